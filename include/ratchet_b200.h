@@ -1,0 +1,172 @@
+/*
+ * ratchet_b200.h — C ABI of the B200 (sm_100a) ratchet-linear train-step library.
+ *
+ * Every entry point takes caller-owned device pointers, element strides and an explicit
+ * cudaStream_t (passed as void*), allocates nothing, never synchronises the host and returns an
+ * int status (RT_OK == 0).  On failure rt_last_error() returns a thread-local message.  Device-side
+ * problems that are found while a kernel runs (non-finite gradients, a bounded wait that ran out)
+ * are recorded in a sticky device status word read with rt_device_status().
+ *
+ * Reference interface each function replaces is cited as file:line inside the reference project
+ * (LoomNode/local-ai-training, package src/local_ai_training).
+ */
+#ifndef RATCHET_B200_H
+#define RATCHET_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RT_ABI_VERSION 1
+
+/* status codes */
+#define RT_OK 0
+#define RT_ERR_INVALID_ARGUMENT 1 /* shapes, strides, null pointers  -> ValueError   */
+#define RT_ERR_DTYPE 2            /* unsupported element type        -> TypeError    */
+#define RT_ERR_ALIGNMENT 3        /* pointer/stride alignment        -> ValueError   */
+#define RT_ERR_CUDA 4             /* launch or driver failure        -> RuntimeError */
+#define RT_ERR_UNSUPPORTED 5      /* valid request this build cannot serve           */
+
+/* element types */
+#define RT_F32 0
+#define RT_BF16 1
+#define RT_I8 2
+#define RT_U8 3
+
+/* bits of the sticky device status word */
+#define RT_STATUS_NONFINITE_GRADIENT 0x1u /* ratchet gradient held NaN/Inf (row left unchanged) */
+#define RT_STATUS_WAIT_TIMEOUT 0x2u       /* a bounded pipeline wait gave up                     */
+#define RT_STATUS_CODE_RANGE 0x4u         /* validate: code escaped [-max_code, max_code]        */
+#define RT_STATUS_PRESSURE_RANGE 0x8u     /* validate: |pressure| > 7                            */
+#define RT_STATUS_SCALE_INVALID 0x10u     /* validate: a row scale is <= 0 or non-finite         */
+
+int rt_abi_version(void);
+const char *rt_last_error(void);
+
+/* Reads the sticky device status word into *out (host memory) after the work queued on `stream`
+ * so far; optionally clears it.  This call synchronises `stream` (eval-cadence use only). */
+int rt_device_status(uint32_t *out, int clear, void *stream);
+
+/* Number of SMs of the current device (cached per device). */
+int rt_sm_count(int *out);
+
+/* ---------------------------------------------------------------------------------------------
+ * Row quantisation.  Replaces int8_matmul.py:_quantize_rows_kernel (106-150) through
+ * quantize_rows (251-259) and quantize_rows_colscaled (262-277).
+ *   v[m,k]   = float(x[m,k]) * col_scale[k]          (col_scale optional)
+ *   scale[m] = max(max_k |v[m,k]| / 127, FLT_MIN)
+ *   RN: q = clamp(rint(v / scale), -127, 127)
+ *   SR: q = clamp(floor(v / scale + u), -127, 127), u = Philox4x32-10 uniform keyed by
+ *       (seed, layer) with counter (element index / 4, step)  [own mapping, not Triton's tl.rand]
+ * x_bf16_out (optional) receives bf16(x) (unscaled) — the grad_weight GEMM operand of
+ * ratchet.py:162 — so the gradient is read from HBM once.
+ * ------------------------------------------------------------------------------------------- */
+int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_t cols, int64_t stride_row,
+                     int64_t stride_col, const float *col_scale, int stochastic, uint64_t seed,
+                     uint32_t step, uint32_t layer, int8_t *q, int64_t ldq, float *row_scale,
+                     void *x_bf16_out, int64_t ld_xbf16, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Scaled int8 GEMM.  Replaces int8_matmul.py:scaled_int8_mm (289-343) / _scaled_int8_kernel
+ * (26-79).  out[m,n] = bf16((float(sum_k lhs[m,k]*rhs[k,n]) * lhs_scale[m]) * rhs_scale[n]);
+ * rhs_scale may be NULL (== 1.0, the grad_input call of ratchet.py:133-134).  Operands are
+ * addressed by element strides exactly like the reference kernel: lhs (M,K), rhs (K,N).
+ * out_dtype RT_BF16 stores the bf16 value, RT_F32 stores the same bf16-rounded value widened to
+ * fp32 (the `.to(inputs.dtype)` of ratchet.py:67 fused into the epilogue).
+ * 16-byte-aligned unit-stride operands run the tcgen05 kind::i8 TMA kernel; anything else runs a
+ * SIMT kernel with identical arithmetic.
+ * ------------------------------------------------------------------------------------------- */
+int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_t lhs_stride_k,
+                      const int8_t *rhs, int64_t rhs_stride_k, int64_t rhs_stride_n,
+                      const float *lhs_scale, const float *rhs_scale, void *out, int out_dtype,
+                      int64_t ldo, int64_t M, int64_t N, int64_t K, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * grad_weight GEMM.  Replaces the per-tile cuBLAS BF16 GEMM of ratchet.py:148-163:
+ *   gw[n,k] (+)= sum_m g[m,n] * x[m,k]     (bf16 operands, fp32 accumulation)
+ * g is (M_tok, N) and x is (M_tok, K), both row-major with unit column stride.  out_dtype RT_F32
+ * (`accumulate` adds into out) or RT_BF16 (`accumulate` must be 0).  The bf16 rounding the
+ * reference applies to the GEMM output is applied by rt_ratchet_update(round_bf16=1), not here.
+ * Small outputs split the token dimension across SMs: each split writes an fp32 partial tile to
+ * `workspace` and the last split of a tile sums the partials in split order (deterministic, no
+ * CTA waits for another).  workspace: 256-byte aligned, its first bytes (one uint32 ticket per
+ * output tile) zero before the first call — calls leave them zero; NULL disables splitting.
+ * Calls sharing a workspace must not overlap on the GPU.
+ * ------------------------------------------------------------------------------------------- */
+int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, int64_t ldx, void *out,
+                        int out_dtype, int64_t ldo, int64_t M_tok, int64_t N, int64_t K,
+                        int accumulate, void *workspace, int64_t workspace_bytes, void *stream);
+/* Workspace bytes rt_grad_weight_bf16 can use for this shape on the current device (0: none). */
+int64_t rt_grad_weight_workspace_bytes(int64_t M_tok, int64_t N, int64_t K);
+
+/* Dequantises saved int8 activations: out[m,k] = bf16(bf16(q[m,k]) * bf16(s[m]))
+ * (ratchet.py:73-76). */
+int rt_dequant_rows_bf16(const int8_t *q, int64_t ldq, const float *row_scale, void *out,
+                         int64_t ldo, int64_t rows, int64_t cols, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Ratchet update, one HBM pass per weight.  Replaces ratchet.py:_capture_weight_gradient
+ * (487-537) -> _normalize (539-556) -> _ratchet_update_core (265-301) -> pack (185-192), and
+ * apply_normalized_gradient (582-611) when normalize == 0.
+ *   grad: (rows, cols) fp32 or bf16; round_bf16 rounds fp32 input to bf16 first (the
+ *         `grad_weight_tile.float()` of ratchet.py:162-163).
+ *   packed: uint8 code|pressure nibbles, updated in place; code_out (optional) receives the new
+ *         int8 codes (the GEMM operand), code_out may alias nothing else.
+ *   rms_ema (optional, rows): per-row second-moment EMA (ratchet.py:543-553), beta in (0,1).
+ *   counts (int64[4], accumulated): positive, negative, blocked positive, blocked negative moves.
+ *   row_rms (optional, rows): sqrt(mean(g^2)) of each row (ratchet.py:534-537 statistics).
+ *   grad_scale (optional, rows): sum_k g[r,k] * code_before[r,k] (ratchet.py:167-169).
+ * Rows holding NaN/Inf are left unchanged and set RT_STATUS_NONFINITE_GRADIENT.
+ * The row mean-square uses a fixed reduction order (documented in the kernel) mirrored by the
+ * CPU oracle, so results are bit-reproducible.
+ * ------------------------------------------------------------------------------------------- */
+int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf16, int64_t ldg, int64_t rows,
+                      int64_t cols, uint8_t *packed, int64_t ldp, int8_t *code_out, int64_t ldc,
+                      int normalize, float *rms_ema, double ema_beta, int max_code, int threshold,
+                      double bucket_low, double bucket_high, double eps, int64_t *counts,
+                      float *row_rms, float *grad_scale, void *stream);
+
+/* Pressure leak: every nonzero pressure moves one unit toward zero (ratchet.py:613-625).
+ * code_out, when given, is refreshed with the (unchanged) codes. */
+int rt_ratchet_leak(uint8_t *packed, int64_t ldp, int64_t rows, int64_t cols, int max_code,
+                    void *stream);
+
+/* Unpacks nibbles (ratchet.py:195-199); code or pressure may be NULL. */
+int rt_unpack_code_pressure(const uint8_t *packed, int64_t ldp, int64_t rows, int64_t cols,
+                            int max_code, int8_t *code, int64_t ldc, int8_t *pressure,
+                            int64_t ldpr, void *stream);
+
+/* State validation (ratchet.py:672-679) into the sticky device status word: code range,
+ * pressure nibble range and, when scale != NULL, positive finite row scales. */
+int rt_ratchet_validate(const uint8_t *packed, int64_t ldp, int64_t rows, int64_t cols,
+                        int max_code, const float *scale, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Fused producers of pre-quantised layer inputs (int8_fused.py / int8_backward.py).
+ * ------------------------------------------------------------------------------------------- */
+/* y = x * rsqrt(mean(x^2) + eps) * w, then RN row quant (int8_fused.py:14-56). */
+int rt_rmsnorm_quantize(const void *x, int x_dtype, int64_t ldx, const float *weight, double eps,
+                        int64_t rows, int64_t cols, int8_t *q, int64_t ldq, float *row_scale,
+                        void *stream);
+/* tanh-GELU then RN row quant (int8_fused.py:58-101). */
+int rt_gelu_quantize(const void *x, int x_dtype, int64_t ldx, int64_t rows, int64_t cols,
+                     int8_t *q, int64_t ldq, float *row_scale, void *stream);
+/* [B,H,T,D] (any strides) -> rows b*T+t of H*D channels, RN row quant (int8_fused.py:103-151). */
+int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, int64_t heads, int64_t seq,
+                          int64_t head_dim, int64_t stride_b, int64_t stride_h, int64_t stride_s,
+                          int64_t stride_d, int8_t *q, int64_t ldq, float *row_scale,
+                          void *stream);
+/* RMSNorm backward, dx only (int8_backward.py:7-51); dx written in dx_dtype. */
+int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
+                        const float *weight, double eps, int64_t rows, int64_t cols, void *dx,
+                        int dx_dtype, void *stream);
+/* tanh-GELU backward (int8_backward.py:53-89); dx written in dx_dtype. */
+int rt_gelu_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype, int64_t rows,
+                     int64_t cols, void *dx, int dx_dtype, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RATCHET_B200_H */

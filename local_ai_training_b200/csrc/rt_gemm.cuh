@@ -1,0 +1,702 @@
+// rt_gemm.cuh — tcgen05 GEMMs for sm_100a.
+//
+//   int8  (kind::i8, s32 accumulate in TMEM):  forward  out = q · codeᵀ       (K-major × K-major)
+//                                              grad_in  out = g_q · code       (K-major × MN-major)
+//   bf16  (kind::f16, f32 accumulate in TMEM): grad_W   gw  = g_bf16ᵀ · x̂      (MN-major × MN-major)
+//
+// One persistent, warp-specialised kernel per configuration:
+//   warp 0      TMA producer (one elected thread): 128-byte-swizzled tiles into a STAGES-deep ring
+//   warp 1      TMEM allocator + MMA issuer (one thread): 4 tcgen05.mma per stage, commit frees the
+//               stage, a final commit hands the accumulator to the epilogue
+//   warps 2..5  epilogue: tcgen05.ld 32x32b → fp32 → dequant/round → global stores (or fp32
+//               reductions for split-K), running on one TMEM accumulator while the MMA fills the
+//               other (2 × BN columns).
+// Tiles are BM=128 rows × BN columns; each stage covers 128 bytes of K (128 int8 or 64 bf16).
+// Every CTA loads its own tiles (no clusters, no shared-tile loads between CTAs).
+#pragma once
+
+#include <mutex>
+
+#include "rt_common.cuh"
+
+namespace rt {
+
+// EPI_SPLIT: split-K partial tiles go to a workspace; the last split of a tile to finish (an
+// atomic ticket per tile, no waiting) sums all partials in split order 0..S-1 and stores the
+// result with `final_epi` — deterministic, and no CTA ever waits for another.
+enum EpiMode : int { EPI_SCALED = 0, EPI_SPLIT = 1, EPI_F32_STORE = 2, EPI_BF16_STORE = 3 };
+
+struct GemmArgs {
+  int M, N, K;  // out is M × N, contraction over K
+  int tiles_m, tiles_n, splits, kblocks;
+  const float *a_scale;  // EPI_SCALED: per-row scale (M)
+  const float *b_scale;  // EPI_SCALED: per-column scale (N) or null (== 1)
+  void *out;
+  int64_t ldo;
+  int out_dtype;  // EPI_SCALED: RT_BF16 or RT_F32 (bf16-rounded value widened)
+  int epi;
+  int accumulate;  // EPI_F32_STORE: out += result
+  int vec_store;   // out rows are 16-byte aligned
+  int final_epi;   // EPI_SPLIT: EPI_F32_STORE or EPI_BF16_STORE for the reduced tile
+  float *workspace;       // EPI_SPLIT: [splits][tiles][BM][BN] fp32 partial tiles
+  unsigned *counters;     // EPI_SPLIT: one ticket per tile, zero between launches
+};
+
+template <typename T>
+struct KindOf;
+template <>
+struct KindOf<int8_t> {
+  static constexpr uint32_t dfmt = 2;  // S32
+  static constexpr uint32_t abfmt = 1; // signed 8-bit
+};
+template <>
+struct KindOf<__nv_bfloat16> {
+  static constexpr uint32_t dfmt = 1;  // F32
+  static constexpr uint32_t abfmt = 1; // BF16
+};
+
+template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int ES = sizeof(T);
+  static constexpr int KE = 128 / ES;  // K elements per stage
+  static constexpr int UK = 32 / ES;   // K elements per tcgen05.mma
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  // Instruction descriptor: D format, A/B formats, majorness, N>>3 at [17,23), M>>4 at [24,29).
+  static constexpr uint32_t IDESC = (KindOf<T>::dfmt << 4) | (KindOf<T>::abfmt << 7) |
+                                    (KindOf<T>::abfmt << 10) | ((A_MN ? 1u : 0u) << 15) |
+                                    ((B_MN ? 1u : 0u) << 16) |
+                                    (static_cast<uint32_t>(BN >> 3) << 17) |
+                                    (static_cast<uint32_t>(BM >> 4) << 24);
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+  static_assert(TMEM_COLS <= 512, "TMEM");
+};
+
+// K-major operand tile (rows × 128 B, 128B swizzle): 8-row groups 1024 B apart (SBO); the k-th
+// MMA step starts 32 bytes further inside the swizzle atom.
+// MN-major operand tile: boxes of (KE k-rows × 128 B) side by side along MN (LBO = KE·128 B);
+// 8-k-row groups 1024 B apart (SBO); the k-th MMA step starts UK k-rows (UK·128 B) further.
+template <bool MN, int KE, int UK>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t tile_addr, int kstep) {
+  if constexpr (MN) {
+    return make_sw128_desc(tile_addr + kstep * UK * 128, KE * 128, 1024);
+  } else {
+    return make_sw128_desc(tile_addr + kstep * 32, 16, 1024);
+  }
+}
+
+template <bool MN, int ROWS, int KE, int ES>
+__device__ __forceinline__ void load_operand(const CUtensorMap *map, uint64_t *bar, uint8_t *dst,
+                                             int row0, int k0) {
+  if constexpr (MN) {
+    constexpr int PER_BOX = 128 / ES;  // MN elements per 128-byte box row
+#pragma unroll
+    for (int j = 0; j < ROWS / PER_BOX; ++j)
+      tma_load_2d(map, bar, dst + j * (KE * 128), row0 + j * PER_BOX, k0);
+  } else {
+    tma_load_2d(map, bar, dst, k0, row0);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float acc_to_float(uint32_t bits) {
+  if constexpr (sizeof(T) == 1)
+    return __int2float_rn(static_cast<int>(bits));
+  else
+    return __uint_as_float(bits);
+}
+
+template <typename T>
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs &p, int epi, int row, int n0,
+                                               const uint32_t (&r)[32]) {
+  if (row >= p.M) return;
+  const bool full = p.vec_store && (n0 + 32 <= p.N);
+  if (epi == EPI_SCALED) {
+    const float ls = __ldg(p.a_scale + row);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(acc_to_float<T>(r[j]), ls);
+    if (p.b_scale != nullptr) {
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 s4 = __ldg(reinterpret_cast<const float4 *>(p.b_scale + n0 + j));
+          v[j] = __fmul_rn(v[j], s4.x);
+          v[j + 1] = __fmul_rn(v[j + 1], s4.y);
+          v[j + 2] = __fmul_rn(v[j + 2], s4.z);
+          v[j + 3] = __fmul_rn(v[j + 3], s4.w);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (n0 + j < p.N) v[j] = __fmul_rn(v[j], __ldg(p.b_scale + n0 + j));
+      }
+    }
+    if (p.out_dtype == RT_BF16) {
+      uint16_t *o = static_cast<uint16_t *>(p.out) + static_cast<int64_t>(row) * p.ldo + n0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 w;
+          w.x = bf16_bits(v[j]) | (uint32_t(bf16_bits(v[j + 1])) << 16);
+          w.y = bf16_bits(v[j + 2]) | (uint32_t(bf16_bits(v[j + 3])) << 16);
+          w.z = bf16_bits(v[j + 4]) | (uint32_t(bf16_bits(v[j + 5])) << 16);
+          w.w = bf16_bits(v[j + 6]) | (uint32_t(bf16_bits(v[j + 7])) << 16);
+          *reinterpret_cast<uint4 *>(o + j) = w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (n0 + j < p.N) o[j] = bf16_bits(v[j]);
+      }
+    } else {
+      float *o = static_cast<float *>(p.out) + static_cast<int64_t>(row) * p.ldo + n0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<float4 *>(o + j) =
+              make_float4(bf16_round(v[j]), bf16_round(v[j + 1]), bf16_round(v[j + 2]),
+                          bf16_round(v[j + 3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (n0 + j < p.N) o[j] = bf16_round(v[j]);
+      }
+    }
+    return;
+  }
+  if (epi == EPI_BF16_STORE) {
+    uint16_t *o = static_cast<uint16_t *>(p.out) + static_cast<int64_t>(row) * p.ldo + n0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 w;
+        w.x = bf16_bits(acc_to_float<T>(r[j])) | (uint32_t(bf16_bits(acc_to_float<T>(r[j + 1]))) << 16);
+        w.y = bf16_bits(acc_to_float<T>(r[j + 2])) | (uint32_t(bf16_bits(acc_to_float<T>(r[j + 3]))) << 16);
+        w.z = bf16_bits(acc_to_float<T>(r[j + 4])) | (uint32_t(bf16_bits(acc_to_float<T>(r[j + 5]))) << 16);
+        w.w = bf16_bits(acc_to_float<T>(r[j + 6])) | (uint32_t(bf16_bits(acc_to_float<T>(r[j + 7]))) << 16);
+        *reinterpret_cast<uint4 *>(o + j) = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) o[j] = bf16_bits(acc_to_float<T>(r[j]));
+    }
+    return;
+  }
+  float *o = static_cast<float *>(p.out) + static_cast<int64_t>(row) * p.ldo + n0;
+  // EPI_F32_STORE
+  if (full) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      float4 w = make_float4(acc_to_float<T>(r[j]), acc_to_float<T>(r[j + 1]),
+                             acc_to_float<T>(r[j + 2]), acc_to_float<T>(r[j + 3]));
+      if (p.accumulate) {
+        const float4 old = *reinterpret_cast<const float4 *>(o + j);
+        w.x = __fadd_rn(old.x, w.x), w.y = __fadd_rn(old.y, w.y);
+        w.z = __fadd_rn(old.z, w.z), w.w = __fadd_rn(old.w, w.w);
+      }
+      *reinterpret_cast<float4 *>(o + j) = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < p.N) o[j] = p.accumulate ? __fadd_rn(o[j], acc_to_float<T>(r[j]))
+                                            : acc_to_float<T>(r[j]);
+  }
+}
+
+template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                     const __grid_constant__ CUtensorMap tma_b, GemmArgs p) {
+  using C = GemmCfg<T, A_MN, B_MN, BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *a_tiles = smem;
+  uint8_t *b_tiles = smem + STAGES * C::A_BYTES;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + STAGES;
+  uint64_t *tfull = bars + 2 * STAGES;
+  uint64_t *tempty = bars + 2 * STAGES + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+  __shared__ int s_last_split;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  const int units = p.tiles_m * p.tiles_n * p.splits;
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int tn = u % p.tiles_n, rest = u / p.tiles_n;
+        const int tm = rest % p.tiles_m, split = rest / p.tiles_m;
+        const int kb0 = static_cast<int>(static_cast<int64_t>(split) * p.kblocks / p.splits);
+        const int kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * p.kblocks / p.splits);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          load_operand<A_MN, C::BM, C::KE, C::ES>(&tma_a, &full[stage],
+                                                  a_tiles + stage * C::A_BYTES, tm * C::BM,
+                                                  kb * C::KE);
+          load_operand<B_MN, BN, C::KE, C::ES>(&tma_b, &full[stage],
+                                               b_tiles + stage * C::B_BYTES, tn * BN, kb * C::KE);
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool ok = true;
+      const uint32_t a_base = smem_u32(a_tiles), b_base = smem_u32(b_tiles);
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int rest = u / p.tiles_n;
+        const int split = rest / p.tiles_m;
+        const int kb0 = static_cast<int>(static_cast<int64_t>(split) * p.kblocks / p.splits);
+        const int kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * p.kblocks / p.splits);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full[stage], phase)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = a_base + stage * C::A_BYTES;
+          const uint32_t b_addr = b_base + stage * C::B_BYTES;
+#pragma unroll
+          for (int j = 0; j < C::KE / C::UK; ++j) {
+            const uint64_t ad = operand_desc<A_MN, C::KE, C::UK>(a_addr, j);
+            const uint64_t bd = operand_desc<B_MN, C::KE, C::UK>(b_addr, j);
+            const uint32_t accumulate = (kb > kb0 || j > 0) ? 1u : 0u;
+            if constexpr (sizeof(T) == 1)
+              umma_i8(d_tmem, ad, bd, C::IDESC, accumulate);
+            else
+              umma_f16(d_tmem, ad, bd, C::IDESC, accumulate);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) acc = 0, acc_phase ^= 1;
+      }
+    }
+  } else {
+    // epilogue warps 2..5: TMEM sub-partition (warp % 4) holds accumulator rows 32·(warp%4)..+31
+    const int sub = warp & 3;
+    const int ep_tid = threadIdx.x - 64;  // 0..127 across the four epilogue warps
+    const bool split_mode = p.epi == EPI_SPLIT;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int tn = u % p.tiles_n, rest = u / p.tiles_n;
+      const int tm = rest % p.tiles_m, split = rest / p.tiles_m;
+      const int tile = tm * p.tiles_n + tn;
+      // every lane polls; the warp proceeds only if all lanes saw the phase complete, so the
+      // .sync.aligned TMEM loads below are always executed by the full warp
+      const bool lane_ok = mbar_wait(&tfull[acc], acc_phase);
+      // the four epilogue warps agree (barrier 1, 128 threads), so a timed-out wait can never
+      // leave some of them inside the split-K barriers below
+      uint32_t all_ok;
+      asm volatile(
+          "{\n\t.reg .pred p, q;\n\t"
+          "setp.ne.u32 p, %1, 0;\n\t"
+          "bar.red.and.pred q, 1, 128, p;\n\t"
+          "selp.u32 %0, 1, 0, q;\n\t}"
+          : "=r"(all_ok)
+          : "r"(static_cast<uint32_t>(lane_ok))
+          : "memory");
+      if (!all_ok) break;
+      tc_fence_after();
+      const int trow = sub * 32 + lane;
+      const int row = tm * C::BM + trow;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN);
+      float *part = nullptr;
+      if (split_mode)
+        part = p.workspace +
+               ((static_cast<int64_t>(split) * p.tiles_m * p.tiles_n + tile) * C::BM + trow) * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n0 = tn * BN + c * 32;
+        if (!split_mode && n0 >= p.N) break;
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
+        tmem_ld_wait();
+        if (split_mode) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4 *>(part + c * 32 + j) =
+                make_float4(acc_to_float<T>(r[j]), acc_to_float<T>(r[j + 1]),
+                            acc_to_float<T>(r[j + 2]), acc_to_float<T>(r[j + 3]));
+        } else {
+          epilogue_chunk<T>(p, p.epi, row, n0, r);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) acc = 0, acc_phase ^= 1;
+      if (split_mode) {
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (ep_tid == 0)
+          s_last_split = atomicAdd(p.counters + tile, 1u) == static_cast<unsigned>(p.splits - 1);
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (s_last_split) {
+          __threadfence();
+          const float *base =
+              p.workspace + (static_cast<int64_t>(tile) * C::BM + trow) * BN;
+          const int64_t split_stride = static_cast<int64_t>(p.tiles_m) * p.tiles_n * C::BM * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            const int n0 = tn * BN + c * 32;
+            if (n0 >= p.N) break;
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 f = __ldcg(reinterpret_cast<const float4 *>(base + c * 32 + j));
+              v[j] = f.x, v[j + 1] = f.y, v[j + 2] = f.z, v[j + 3] = f.w;
+            }
+            for (int sp = 1; sp < p.splits; ++sp) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                const float4 f = __ldcg(
+                    reinterpret_cast<const float4 *>(base + sp * split_stride + c * 32 + j));
+                v[j] = __fadd_rn(v[j], f.x), v[j + 1] = __fadd_rn(v[j + 1], f.y);
+                v[j + 2] = __fadd_rn(v[j + 2], f.z), v[j + 3] = __fadd_rn(v[j + 3], f.w);
+              }
+            }
+            uint32_t r[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(v[j]);
+            epilogue_chunk<__nv_bfloat16>(p, p.final_epi, row, n0, r);
+          }
+          if (ep_tid == 0) p.counters[tile] = 0u;  // leave the ticket zero for the next launch
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// -------------------------------------------------------------------------------------------
+// SIMT kernels with the same arithmetic, for operands TMA cannot address (unaligned strides).
+// -------------------------------------------------------------------------------------------
+__global__ void simt_scaled_i8_kernel(const int8_t *lhs, int64_t slm, int64_t slk,
+                                      const int8_t *rhs, int64_t srk, int64_t srn,
+                                      const float *ls, const float *rs, void *out, int out_dtype,
+                                      int64_t ldo, int64_t M, int64_t N, int64_t K) {
+  const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t m = blockIdx.y * static_cast<int64_t>(blockDim.y) + threadIdx.y;
+  if (m >= M || n >= N) return;
+  int acc = 0;
+  for (int64_t k = 0; k < K; ++k)
+    acc += static_cast<int>(lhs[m * slm + k * slk]) * static_cast<int>(rhs[k * srk + n * srn]);
+  float v = __fmul_rn(__int2float_rn(acc), __ldg(ls + m));
+  if (rs != nullptr) v = __fmul_rn(v, __ldg(rs + n));
+  if (out_dtype == RT_BF16)
+    static_cast<uint16_t *>(out)[m * ldo + n] = bf16_bits(v);
+  else
+    static_cast<float *>(out)[m * ldo + n] = bf16_round(v);
+}
+
+__global__ void simt_gradw_kernel(const uint16_t *g, int64_t ldg, const uint16_t *x, int64_t ldx,
+                                  void *out, int out_dtype, int64_t ldo, int64_t Mt, int64_t N,
+                                  int64_t K, int accumulate) {
+  const int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t n = blockIdx.y * static_cast<int64_t>(blockDim.y) + threadIdx.y;
+  if (n >= N || k >= K) return;
+  float acc = 0.0f;
+  for (int64_t m = 0; m < Mt; ++m)
+    acc = __fadd_rn(acc, __fmul_rn(bf16_from_bits(g[m * ldg + n]), bf16_from_bits(x[m * ldx + k])));
+  if (out_dtype == RT_F32) {
+    float *o = static_cast<float *>(out) + n * ldo + k;
+    *o = accumulate ? __fadd_rn(*o, acc) : acc;
+  } else {
+    static_cast<uint16_t *>(out)[n * ldo + k] = bf16_bits(acc);
+  }
+}
+
+// -------------------------------------------------------------------------------------------
+// Host side: tensor maps (driver entry point fetched once), launch helpers.
+// -------------------------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 2-D map over a row-major matrix: `inner` contiguous elements per row, `outer` rows,
+// `row_bytes` between rows; box = box_inner × box_outer with 128-byte swizzle, zero OOB fill.
+static int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner,
+                    uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return fail(RT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(RT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return RT_OK;
+}
+
+// Operand description for the UMMA path.  A is (M,K), B is (N,K) in GEMM terms.
+struct Operand {
+  const void *ptr;
+  bool mn;           // MN-major (MN index contiguous) vs K-major
+  int64_t ld;        // elements between consecutive rows of the stored matrix
+  int64_t rows_mn;   // extent along M (or N)
+  int64_t extent_k;  // extent along K
+};
+
+template <typename T, bool MN>
+static int operand_map(CUtensorMap *map, const Operand &o, int tile_rows) {
+  using Cfg = GemmCfg<T, false, false, 128, 1>;
+  const CUtensorMapDataType dt =
+      sizeof(T) == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if constexpr (MN)
+    return make_map(map, dt, o.ptr, o.rows_mn, o.extent_k, o.ld * sizeof(T), 128 / sizeof(T),
+                    Cfg::KE);
+  else
+    return make_map(map, dt, o.ptr, o.extent_k, o.rows_mn, o.ld * sizeof(T), Cfg::KE, tile_rows);
+}
+
+template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
+static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaStream_t s) {
+  using C = GemmCfg<T, A_MN, B_MN, BN, STAGES>;
+  CUtensorMap ma, mb;
+  int rc = operand_map<T, A_MN>(&ma, a, C::BM);
+  if (rc) return rc;
+  rc = operand_map<T, B_MN>(&mb, b, BN);
+  if (rc) return rc;
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  if ((rc = rt_sm_count(&sms)) != RT_OK) return rc;
+  static std::mutex mu;
+  static bool configured[64] = {false};
+  auto kernel = umma_gemm_kernel<T, A_MN, B_MN, BN, STAGES>;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+      cudaError_t e =
+          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+      if (e != cudaSuccess)
+        return fail(RT_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      configured[dev] = true;
+    }
+  }
+  args.tiles_m = static_cast<int>((args.M + C::BM - 1) / C::BM);
+  args.tiles_n = static_cast<int>((args.N + BN - 1) / BN);
+  args.kblocks = static_cast<int>((args.K + C::KE - 1) / C::KE);
+  if (args.splits < 1) args.splits = 1;
+  if (args.splits > args.kblocks) args.splits = args.kblocks;
+  const int64_t units = static_cast<int64_t>(args.tiles_m) * args.tiles_n * args.splits;
+  const int grid = static_cast<int>(units < sms ? units : sms);
+  kernel<<<grid, 192, C::SMEM_BYTES, s>>>(ma, mb, args);
+  return check_launch("umma_gemm_kernel");
+}
+
+template <typename T>
+static int kblocks_of(int64_t K) {
+  return static_cast<int>((K + (128 / sizeof(T)) - 1) / (128 / sizeof(T)));
+}
+
+}  // namespace rt
+
+// ===========================================================================================
+// C ABI
+// ===========================================================================================
+using namespace rt;
+
+extern "C" int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_t lhs_stride_k,
+                                 const int8_t *rhs, int64_t rhs_stride_k, int64_t rhs_stride_n,
+                                 const float *lhs_scale, const float *rhs_scale, void *out,
+                                 int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                                 void *stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(RT_ERR_INVALID_ARGUMENT, "scaled_int8_mm: negative shape");
+  if (out_dtype != RT_BF16 && out_dtype != RT_F32)
+    return fail(RT_ERR_DTYPE, "scaled_int8_mm: output must be bfloat16 or float32");
+  if (M == 0 || N == 0) return RT_OK;
+  if (lhs == nullptr || rhs == nullptr || lhs_scale == nullptr || out == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "scaled_int8_mm: null pointer");
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2)
+    return fail(RT_ERR_UNSUPPORTED, "scaled_int8_mm: dimension too large");
+  cudaStream_t s = as_stream(stream);
+  const size_t osz = out_dtype == RT_BF16 ? 2 : 4;
+  GemmArgs args{};
+  args.M = static_cast<int>(M), args.N = static_cast<int>(N), args.K = static_cast<int>(K);
+  args.a_scale = lhs_scale, args.b_scale = rhs_scale, args.out = out, args.ldo = ldo;
+  args.out_dtype = out_dtype, args.epi = EPI_SCALED, args.splits = 1;
+  args.vec_store = aligned16(out) && (ldo * static_cast<int64_t>(osz)) % 16 == 0 &&
+                   (rhs_scale == nullptr || aligned16(rhs_scale));
+  // operand majorness from strides, as the reference kernel addresses them
+  const bool a_k = lhs_stride_k == 1, a_mn = !a_k && lhs_stride_m == 1;
+  const bool b_k = rhs_stride_k == 1, b_mn = !b_k && rhs_stride_n == 1;
+  const bool a_ok = aligned16(lhs) && K > 0 &&
+                    ((a_k && lhs_stride_m % 16 == 0) || (a_mn && lhs_stride_k % 16 == 0));
+  const bool b_ok = aligned16(rhs) && K > 0 &&
+                    ((b_k && rhs_stride_n % 16 == 0) || (b_mn && rhs_stride_k % 16 == 0));
+  if (a_ok && b_ok) {
+    Operand A{lhs, a_mn, a_k ? lhs_stride_m : lhs_stride_k, M, K};
+    Operand B{rhs, b_mn, b_k ? rhs_stride_n : rhs_stride_k, N, K};
+    const bool narrow = N <= 128;
+#define RT_GO(AMN, BMN)                                                              \
+  return narrow ? launch_umma<int8_t, AMN, BMN, 128, 6>(A, B, args, s)               \
+                : launch_umma<int8_t, AMN, BMN, 256, 4>(A, B, args, s)
+    if (!a_mn && !b_mn) RT_GO(false, false);
+    if (!a_mn && b_mn) RT_GO(false, true);
+    if (a_mn && !b_mn) RT_GO(true, false);
+    RT_GO(true, true);
+#undef RT_GO
+  }
+  const dim3 block(32, 8);
+  const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((M + 7) / 8));
+  simt_scaled_i8_kernel<<<grid, block, 0, s>>>(lhs, lhs_stride_m, lhs_stride_k, rhs, rhs_stride_k,
+                                                rhs_stride_n, lhs_scale, rhs_scale, out, out_dtype,
+                                                ldo, M, N, K);
+  return check_launch("simt_scaled_i8_kernel");
+}
+
+namespace rt {
+constexpr int GW_BN = 256;
+constexpr int64_t GW_TILE_BYTES = 128 * GW_BN * 4;
+static int64_t gw_tiles(int64_t N, int64_t K) { return ((N + 127) / 128) * ((K + GW_BN - 1) / GW_BN); }
+static int64_t gw_counter_bytes(int64_t tiles) { return ((tiles * 4 + 255) / 256) * 256; }
+// split count: enough units to cover every SM, bounded by the K blocks and the workspace
+static int gw_splits(int64_t M_tok, int64_t N, int64_t K, int sms, int64_t workspace_bytes) {
+  const int64_t tiles = gw_tiles(N, K);
+  const int64_t kb = (M_tok + 63) / 64;
+  if (tiles >= sms) return 1;
+  int64_t s = sms / tiles;
+  if (s > kb) s = kb;
+  const int64_t room = workspace_bytes - gw_counter_bytes(tiles);
+  const int64_t fit = room > 0 ? room / (tiles * GW_TILE_BYTES) : 0;
+  if (s > fit) s = fit;
+  return s < 2 ? 1 : static_cast<int>(s);
+}
+}  // namespace rt
+
+extern "C" int64_t rt_grad_weight_workspace_bytes(int64_t M_tok, int64_t N, int64_t K) {
+  int sms = 0;
+  if (rt_sm_count(&sms) != RT_OK || M_tok <= 0 || N <= 0 || K <= 0) return 0;
+  const int s = gw_splits(M_tok, N, K, sms, INT64_MAX / 4);
+  if (s <= 1) return 0;
+  const int64_t tiles = gw_tiles(N, K);
+  return gw_counter_bytes(tiles) + static_cast<int64_t>(s) * tiles * GW_TILE_BYTES;
+}
+
+extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, int64_t ldx,
+                                   void *out, int out_dtype, int64_t ldo, int64_t M_tok, int64_t N,
+                                   int64_t K, int accumulate, void *workspace,
+                                   int64_t workspace_bytes, void *stream) {
+  if (M_tok < 0 || N < 0 || K < 0) return fail(RT_ERR_INVALID_ARGUMENT, "grad_weight: shape");
+  if (out_dtype != RT_F32 && out_dtype != RT_BF16)
+    return fail(RT_ERR_DTYPE, "grad_weight: output must be float32 or bfloat16");
+  if (out_dtype == RT_BF16 && accumulate)
+    return fail(RT_ERR_UNSUPPORTED, "grad_weight: accumulate needs a float32 output");
+  if (N == 0 || K == 0) return RT_OK;
+  if (g == nullptr || x == nullptr || out == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "grad_weight: null pointer");
+  if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(RT_ERR_ALIGNMENT, "grad_weight: workspace must be 256-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  const size_t osz = out_dtype == RT_BF16 ? 2 : 4;
+  if (M_tok == 0) {
+    if (accumulate) return RT_OK;
+    cudaError_t e = cudaMemset2DAsync(out, ldo * osz, 0, K * osz, N, s);
+    return e == cudaSuccess ? RT_OK : fail(RT_ERR_CUDA, "grad_weight memset: %s", cudaGetErrorString(e));
+  }
+  const bool tma_ok = aligned16(g) && aligned16(x) && (ldg * 2) % 16 == 0 && (ldx * 2) % 16 == 0 &&
+                      N <= INT32_MAX / 2 && K <= INT32_MAX / 2 && M_tok <= INT32_MAX / 2;
+  if (tma_ok) {
+    int sms = 0;
+    int rc = rt_sm_count(&sms);
+    if (rc) return rc;
+    GemmArgs args{};
+    args.M = static_cast<int>(N), args.N = static_cast<int>(K), args.K = static_cast<int>(M_tok);
+    args.out = out, args.ldo = ldo, args.out_dtype = out_dtype, args.accumulate = accumulate;
+    args.vec_store = aligned16(out) && (ldo * static_cast<int64_t>(osz)) % 16 == 0;
+    const int splits =
+        workspace == nullptr ? 1 : gw_splits(M_tok, N, K, sms, workspace_bytes);
+    const int final_epi = out_dtype == RT_F32 ? EPI_F32_STORE : EPI_BF16_STORE;
+    args.splits = splits;
+    if (splits > 1) {
+      args.epi = EPI_SPLIT;
+      args.final_epi = final_epi;
+      args.counters = static_cast<unsigned *>(workspace);
+      args.workspace = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) +
+                                                 gw_counter_bytes(gw_tiles(N, K)));
+    } else {
+      args.epi = final_epi;
+    }
+    // A = gᵀ: (N × M_tok) with N contiguous (MN-major); B = x: (K × M_tok) with K contiguous.
+    Operand A{g, true, ldg, N, M_tok};
+    Operand B{x, true, ldx, K, M_tok};
+    return launch_umma<__nv_bfloat16, true, true, GW_BN, 4>(A, B, args, s);
+  }
+  const dim3 block(32, 8);
+  const dim3 grid(static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>((N + 7) / 8));
+  simt_gradw_kernel<<<grid, block, 0, s>>>(static_cast<const uint16_t *>(g), ldg,
+                                            static_cast<const uint16_t *>(x), ldx, out, out_dtype,
+                                            ldo, M_tok, N, K, accumulate);
+  return check_launch("simt_gradw_kernel");
+}

@@ -1,0 +1,49 @@
+"""Backward kernels of the fused producers (reference int8_backward.py) on sm_100a."""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+
+def _contig(t: Tensor) -> Tensor:
+    t = t.contiguous()
+    return t if t.dtype in (torch.float32, torch.bfloat16) else t.float()
+
+
+def rmsnorm_backward(grad_y: Tensor, x: Tensor, w: Tensor, eps: float = 1e-5) -> tuple[Tensor, Tensor]:
+    """dx from the CUDA kernel (int8_backward.py:7-27; stored through bf16 into x's dtype);
+    dw = sum_m grad_y * x * rsqrt(mean(x^2) + eps) over tokens, as the reference computes it."""
+    if not x.is_cuda:
+        raise RuntimeError("CUDA required")
+    x_flat = _contig(x.flatten(0, -2))
+    gy_flat = _contig(grad_y.flatten(0, -2))
+    m, k = x_flat.shape
+    grad_x = torch.empty(x_flat.shape, device=x.device,
+                         dtype=x.dtype if x.dtype in (torch.float32, torch.bfloat16) else torch.float32)
+    wf = w.detach().float().contiguous()
+    _lib.check(_lib.lib().rt_rmsnorm_backward(
+        gy_flat.data_ptr(), _lib.dtype_code(gy_flat), x_flat.data_ptr(), _lib.dtype_code(x_flat),
+        wf.data_ptr(), float(eps), m, k, grad_x.data_ptr(), _lib.dtype_code(grad_x),
+        _lib.stream_of(x_flat)))
+    variance = (x_flat.float() ** 2).mean(dim=1, keepdim=True)
+    rsqrt = torch.rsqrt(variance + eps)
+    grad_w = torch.sum(gy_flat.float() * x_flat.float() * rsqrt, dim=0)
+    return grad_x.reshape(x.shape).to(x.dtype), grad_w.to(w.dtype)
+
+
+def gelu_backward(grad_y: Tensor, x: Tensor) -> Tensor:
+    """tanh-GELU backward (int8_backward.py:53-89), stored through bf16 into x's dtype."""
+    if not x.is_cuda:
+        raise RuntimeError("CUDA required")
+    x_flat = _contig(x.flatten(0, -2))
+    gy_flat = _contig(grad_y.flatten(0, -2))
+    m, k = x_flat.shape
+    grad_x = torch.empty(x_flat.shape, device=x.device,
+                         dtype=x.dtype if x.dtype in (torch.float32, torch.bfloat16) else torch.float32)
+    _lib.check(_lib.lib().rt_gelu_backward(
+        gy_flat.data_ptr(), _lib.dtype_code(gy_flat), x_flat.data_ptr(), _lib.dtype_code(x_flat),
+        m, k, grad_x.data_ptr(), _lib.dtype_code(grad_x), _lib.stream_of(x_flat)))
+    return grad_x.reshape(x.shape).to(x.dtype)

@@ -1,0 +1,114 @@
+"""Fused producers of pre-quantised ratchet inputs (reference int8_fused.py) on sm_100a.
+
+Each producer reads its input once per row and writes the int8 row plus its fp32 scale; the
+autograd wrappers return (int8, scale, dummy) exactly like the reference so that the ratchet
+layer receives pre-quantised inputs and the gradient flows back through the dummy.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from . import _lib
+from .int8_backward import gelu_backward, rmsnorm_backward
+
+
+def _rows(x: Tensor) -> Tensor:
+    flat = x.flatten(0, -2)
+    if flat.stride(-1) != 1:
+        flat = flat.contiguous()
+    if flat.dtype not in (torch.float32, torch.bfloat16):
+        flat = flat.float()
+    return flat
+
+
+def fused_rmsnorm_quantize(x: Tensor, weight: Tensor, eps: float = 1e-5) -> tuple[Tensor, Tensor]:
+    """RMSNorm -> per-token int8 (int8_fused.py:14-56)."""
+    if not x.is_cuda:
+        raise RuntimeError("CUDA required")
+    flat = _rows(x)
+    m, k = flat.shape
+    out = torch.empty((m, k), device=x.device, dtype=torch.int8)
+    scale = torch.empty((m,), device=x.device, dtype=torch.float32)
+    w = weight.detach().float().contiguous()
+    _lib.check(_lib.lib().rt_rmsnorm_quantize(
+        flat.data_ptr(), _lib.dtype_code(flat), flat.stride(0), w.data_ptr(), float(eps), m, k,
+        out.data_ptr(), out.stride(0), scale.data_ptr(), _lib.stream_of(flat)))
+    return out.reshape(x.shape), scale.reshape(x.shape[:-1])
+
+
+def fused_gelu_quantize(x: Tensor) -> tuple[Tensor, Tensor]:
+    """tanh-GELU -> per-token int8 (int8_fused.py:58-101)."""
+    if not x.is_cuda:
+        raise RuntimeError("CUDA required")
+    flat = _rows(x)
+    m, k = flat.shape
+    out = torch.empty((m, k), device=x.device, dtype=torch.int8)
+    scale = torch.empty((m,), device=x.device, dtype=torch.float32)
+    _lib.check(_lib.lib().rt_gelu_quantize(
+        flat.data_ptr(), _lib.dtype_code(flat), flat.stride(0), m, k, out.data_ptr(),
+        out.stride(0), scale.data_ptr(), _lib.stream_of(flat)))
+    return out.reshape(x.shape), scale.reshape(x.shape[:-1])
+
+
+def fused_transpose_quantize(x: Tensor) -> tuple[Tensor, Tensor]:
+    """[B, H, T, D] heads -> (B*T, H*D) per-token int8 (int8_fused.py:103-151)."""
+    if not x.is_cuda:
+        raise RuntimeError("CUDA required")
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        x = x.float()
+    b, h, t, d = x.shape
+    out = torch.empty((b * t, h * d), device=x.device, dtype=torch.int8)
+    scale = torch.empty((b * t,), device=x.device, dtype=torch.float32)
+    _lib.check(_lib.lib().rt_transpose_quantize(
+        x.data_ptr(), _lib.dtype_code(x), b, h, t, d, x.stride(0), x.stride(1), x.stride(2),
+        x.stride(3), out.data_ptr(), out.stride(0), scale.data_ptr(), _lib.stream_of(x)))
+    return out, scale
+
+
+class FusedRMSNormQuantizeFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: Tensor, weight: Tensor, eps: float = 1e-5):
+        int8_out, scale_out = fused_rmsnorm_quantize(x, weight, eps)
+        ctx.save_for_backward(x, weight)
+        ctx.eps = eps
+        dummy = torch.empty_like(x)
+        return int8_out, scale_out, dummy
+
+    @staticmethod
+    def backward(ctx, grad_int8, grad_scale, grad_dummy):
+        x, weight = ctx.saved_tensors
+        grad_x, grad_w = rmsnorm_backward(grad_dummy, x, weight, ctx.eps)
+        return grad_x, grad_w, None
+
+
+class FusedGELUQuantizeFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: Tensor):
+        int8_out, scale_out = fused_gelu_quantize(x)
+        ctx.save_for_backward(x)
+        dummy = torch.empty_like(x)
+        return int8_out, scale_out, dummy
+
+    @staticmethod
+    def backward(ctx, grad_int8, grad_scale, grad_dummy):
+        (x,) = ctx.saved_tensors
+        return gelu_backward(grad_dummy, x)
+
+
+class FusedTransposeQuantizeFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, attended: Tensor):
+        int8_out, scale_out = fused_transpose_quantize(attended)
+        ctx.save_for_backward(attended)
+        batch_size, n_head, seq_len, head_dim = attended.shape
+        dummy = torch.empty((batch_size, seq_len, n_head * head_dim), device=attended.device,
+                            dtype=attended.dtype)
+        return int8_out, scale_out, dummy
+
+    @staticmethod
+    def backward(ctx, grad_int8, grad_scale, grad_dummy):
+        (attended,) = ctx.saved_tensors
+        batch_size, n_head, seq_len, head_dim = attended.shape
+        return grad_dummy.view(batch_size, seq_len, n_head, head_dim).transpose(1, 2)

@@ -1,0 +1,188 @@
+"""int8 GEMM with row/column dequantisation and per-token int8 quantisation on sm_100a.
+
+API-compatible with the reference module int8_matmul.py (quantize_rows, quantize_rows_colscaled,
+quantize_columns, scaled_int8_mm); every op runs the CUDA library through the C ABI and raises
+on CPU tensors with the reference's messages.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor
+
+from . import _lib
+
+_TINY = torch.finfo(torch.float32).tiny
+
+
+def _as_quantizable(values: Tensor) -> Tensor:
+    if values.dtype in (torch.float32, torch.bfloat16):
+        return values
+    if values.is_floating_point():
+        return values.float()
+    raise TypeError("row quantization requires a floating-point tensor")
+
+
+def _quantize_rows_fused(
+    values: Tensor,
+    col_scale: Tensor | None = None,
+    *,
+    stochastic: bool = False,
+    seed: int | None = None,
+    step: int = 0,
+    layer: int = 0,
+    bf16_copy: Tensor | None = None,
+) -> tuple[Tensor, Tensor]:
+    """Row quantisation kernel (int8_matmul.py:106-150, 181-207).
+
+    stochastic=True draws the seed from the host RNG when none is given (the reference's
+    `torch.randint(0, 2**31 - 1, (1,))`, int8_matmul.py:200); (seed, step, layer) key the Philox
+    stream.  bf16_copy, when given (rows × cols bf16, unit column stride), receives bf16(values).
+    """
+    if values.ndim != 2:
+        raise ValueError("row quantization requires a 2D tensor")
+    values = _as_quantizable(values)
+    m, k = values.shape
+    out = torch.empty((m, k), device=values.device, dtype=torch.int8)
+    scale = torch.empty((m,), device=values.device, dtype=torch.float32)
+    if m == 0:
+        return out, scale
+    if col_scale is not None:
+        col_scale = col_scale.contiguous()
+    if stochastic and seed is None:
+        seed = int(torch.randint(0, 2**31 - 1, (1,)).item())
+    _lib.check(
+        _lib.lib().rt_quantize_rows(
+            values.data_ptr(), _lib.dtype_code(values), m, k, values.stride(0), values.stride(1),
+            _lib.ptr(col_scale), int(stochastic), int(seed or 0) & (2**64 - 1), int(step) & 0xFFFFFFFF,
+            int(layer) & 0xFFFFFFFF, out.data_ptr(), out.stride(0), scale.data_ptr(),
+            _lib.ptr(bf16_copy), 0 if bf16_copy is None else bf16_copy.stride(0),
+            _lib.stream_of(values),
+        )
+    )
+    return out, scale
+
+
+def quantize_rows(values: Tensor) -> tuple[Tensor, Tensor]:
+    """Symmetrically quantize each row and return int8 values plus FP32 scales (CUDA-only)."""
+    if not values.is_cuda:
+        raise RuntimeError("quantize_rows requires CUDA; the int8 path is GPU-only")
+    return _quantize_rows_fused(values)
+
+
+def quantize_rows_colscaled(
+    values: Tensor, col_scale: Tensor, *, stochastic: bool = False, seed: int | None = None,
+    step: int = 0, layer: int = 0,
+) -> tuple[Tensor, Tensor]:
+    """Row-quantize values after per-column scaling, fused in one pass (CUDA-only)."""
+    if not values.is_cuda:
+        raise RuntimeError("quantize_rows_colscaled requires CUDA; the int8 path is GPU-only")
+    if col_scale.ndim != 1 or values.ndim != 2 or col_scale.shape[0] != values.shape[1]:
+        raise ValueError("col_scale must be 1-D with length values.shape[1]")
+    if col_scale.dtype != torch.float32:
+        raise TypeError("col_scale must be float32")
+    return _quantize_rows_fused(values, col_scale, stochastic=stochastic, seed=seed, step=step,
+                                layer=layer)
+
+
+def quantize_columns(values: Tensor) -> tuple[Tensor, Tensor]:
+    """Per-column symmetric quantisation (int8_matmul.py:153-178 semantics, fp32 arithmetic)."""
+    if not values.is_cuda:
+        raise RuntimeError("quantize_columns requires CUDA; the int8 path is GPU-only")
+    if values.ndim != 2:
+        raise ValueError("column quantization requires a 2D tensor")
+    q_t, scale = _quantize_rows_fused(values.t())
+    return q_t.t().contiguous(), scale
+
+
+def _scaled_int8_mm_into(
+    lhs: Tensor, rhs: Tensor, lhs_scale: Tensor, rhs_scale: Tensor | None, out: Tensor
+) -> Tensor:
+    """No-sync core: out = bf16((float(lhs @ rhs) * lhs_scale[m]) * rhs_scale[n]).
+
+    `out` is (M, N) bf16, or fp32 receiving the bf16-rounded values (the widening cast of
+    ratchet.py:67 fused into the epilogue).  Operands are passed with their strides.
+    """
+    m, k = lhs.shape
+    _, n = rhs.shape
+    _lib.check(
+        _lib.lib().rt_scaled_int8_mm(
+            lhs.data_ptr(), lhs.stride(0), lhs.stride(1), rhs.data_ptr(), rhs.stride(0),
+            rhs.stride(1), lhs_scale.data_ptr(), _lib.ptr(rhs_scale), out.data_ptr(),
+            _lib.dtype_code(out), out.stride(0), m, n, k, _lib.stream_of(lhs),
+        )
+    )
+    return out
+
+
+def scaled_int8_mm(lhs: Tensor, rhs: Tensor, lhs_scale: Tensor, rhs_scale: Tensor) -> Tensor:
+    """Multiply int8 matrices and fuse row/column scale dequantization into BF16 output."""
+    if not lhs.is_cuda or not rhs.is_cuda:
+        raise RuntimeError("scaled_int8_mm requires CUDA operands")
+    if lhs.ndim != 2 or rhs.ndim != 2:
+        raise ValueError("scaled_int8_mm operands must be 2D")
+    if lhs.dtype != torch.int8 or rhs.dtype != torch.int8:
+        raise TypeError("scaled_int8_mm operands must be int8")
+    if lhs.shape[1] != rhs.shape[0]:
+        raise ValueError("scaled_int8_mm inner dimensions must match")
+    if lhs.device != rhs.device:
+        raise ValueError("scaled_int8_mm operands must share a device")
+    m, k = lhs.shape
+    _, n = rhs.shape
+    if lhs_scale.shape != (m,) or rhs_scale.shape != (n,):
+        raise ValueError("scaled_int8_mm scales must match output rows and columns")
+    for name, scale in (("lhs", lhs_scale), ("rhs", rhs_scale)):
+        if scale.device != lhs.device or scale.dtype != torch.float32:
+            raise TypeError(f"{name} scale must be FP32 on the operand device")
+        if not torch.isfinite(scale).all() or torch.any(scale <= 0):
+            raise ValueError(f"{name} scale must be finite and positive")
+    if 1 not in lhs.stride():
+        lhs = lhs.contiguous()
+    if 1 not in rhs.stride():
+        rhs = rhs.contiguous()
+    out = torch.empty((m, n), device=lhs.device, dtype=torch.bfloat16)
+    return _scaled_int8_mm_into(lhs, rhs, lhs_scale.contiguous(), rhs_scale.contiguous(), out)
+
+
+def grad_weight_bf16(grad: Tensor, inputs: Tensor, out: Tensor | None = None, *,
+                     accumulate: bool = False) -> Tensor:
+    """gw[n, k] (+)= sum_m grad[m, n] * inputs[m, k]: bf16 operands, fp32 accumulation/output
+    (the per-tile grad_weight GEMM of ratchet.py:148-163 as one tcgen05 launch)."""
+    if grad.dtype != torch.bfloat16 or inputs.dtype != torch.bfloat16:
+        raise TypeError("grad_weight_bf16 operands must be bfloat16")
+    if grad.stride(1) != 1:
+        grad = grad.contiguous()
+    if inputs.stride(1) != 1:
+        inputs = inputs.contiguous()
+    mt, n = grad.shape
+    mt2, k = inputs.shape
+    if mt != mt2:
+        raise ValueError("grad_weight_bf16 token dimensions must match")
+    if out is None:
+        out = torch.empty((n, k), device=grad.device, dtype=torch.float32)
+        accumulate = False
+    need = _lib.lib().rt_grad_weight_workspace_bytes(mt, n, k)
+    ws = _lib.workspace(grad.device, need)
+    _lib.check(
+        _lib.lib().rt_grad_weight_bf16(
+            grad.data_ptr(), grad.stride(0), inputs.data_ptr(), inputs.stride(0), out.data_ptr(),
+            _lib.dtype_code(out), out.stride(0), mt, n, k, int(accumulate), _lib.ptr(ws),
+            0 if ws is None else ws.numel(), _lib.stream_of(grad),
+        )
+    )
+    return out
+
+
+def dequant_rows_bf16(q: Tensor, scale: Tensor) -> Tensor:
+    """bf16(bf16(q) * bf16(scale[:, None])) (ratchet.py:73-76)."""
+    if q.stride(1) != 1:
+        q = q.contiguous()
+    rows, cols = q.shape
+    out = torch.empty((rows, cols), device=q.device, dtype=torch.bfloat16)
+    _lib.check(
+        _lib.lib().rt_dequant_rows_bf16(
+            q.data_ptr(), q.stride(0), scale.contiguous().data_ptr(), out.data_ptr(), out.stride(0),
+            rows, cols, _lib.stream_of(q),
+        )
+    )
+    return out

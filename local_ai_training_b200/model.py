@@ -1,0 +1,238 @@
+"""GPT decoder whose dense matrices are ratchet layers (reference model.py) on sm_100a.
+
+Same configuration fields, module tree, parameter names and initialisation order as the reference
+(so seeded models and state_dicts match); the int8 path routes through the fused producers and
+the ratchet layers of this package.  Attention (SDPA), RMSNorm weights, embeddings and the loss
+stay PyTorch ops.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Literal
+
+import torch
+from torch import Tensor, nn
+from torch.nn import functional as F
+
+from .int8_fused import FusedGELUQuantizeFn, FusedRMSNormQuantizeFn, FusedTransposeQuantizeFn
+from .ratchet import DiscreteRatchetLinear, RatchetEmbedding, RatchetUpdateStats
+
+
+@dataclass(frozen=True)
+class ModelConfig:
+    vocab_size: int
+    block_size: int = 128
+    n_layer: int = 2
+    n_head: int = 4
+    n_embd: int = 128
+    dropout: float = 0.0
+    pressure_threshold: int = 8
+    bucket_low: float = 0.5
+    bucket_high: float = 1.5
+    trainable_scale: bool = False
+    rms_ema_beta: float = 0.0
+    pressure_leak_period: int = 0
+    compile_update: bool = False
+    gradient_checkpointing: bool = False
+    matmul_mode: Literal["fp32", "bf16", "int8"] = "fp32"
+    int8_backward: bool = False
+    qat: bool = False
+    ratchet_embedding: bool = False
+
+    def __post_init__(self) -> None:
+        if min(self.vocab_size, self.block_size, self.n_layer, self.n_head, self.n_embd) <= 0:
+            raise ValueError("model dimensions must be positive")
+        if self.n_embd % self.n_head != 0:
+            raise ValueError("n_embd must be divisible by n_head")
+        if not 0 <= self.dropout < 1:
+            raise ValueError("dropout must be in [0, 1)")
+        if self.matmul_mode not in {"fp32", "bf16", "int8"}:
+            raise ValueError("matmul_mode must be fp32, bf16, or int8")
+
+
+def _sinusoidal_positions(block_size: int, n_embd: int) -> Tensor:
+    positions = torch.arange(block_size, dtype=torch.float32)[:, None]
+    even_dimensions = torch.arange(0, n_embd, 2, dtype=torch.float32)
+    frequencies = torch.exp(-math.log(10_000.0) * even_dimensions / n_embd)
+    encoding = torch.zeros(block_size, n_embd, dtype=torch.float32)
+    encoding[:, 0::2] = torch.sin(positions * frequencies)
+    if n_embd > 1:
+        encoding[:, 1::2] = torch.cos(positions * frequencies[: encoding[:, 1::2].shape[1]])
+    return encoding
+
+
+def _linear(config: ModelConfig, in_features: int, out_features: int, max_code: int | None):
+    if max_code is None:
+        return nn.Linear(in_features, out_features, bias=False)
+    if config.qat:
+        raise ValueError("the QAT control arm (master weights) is not part of this build")
+    return DiscreteRatchetLinear(
+        in_features,
+        out_features,
+        max_code=max_code,
+        pressure_threshold=config.pressure_threshold,
+        bucket_low=config.bucket_low,
+        bucket_high=config.bucket_high,
+        trainable_scale=config.trainable_scale,
+        rms_ema_beta=config.rms_ema_beta,
+        pressure_leak_period=config.pressure_leak_period,
+        compile_update=config.compile_update,
+        matmul_mode=config.matmul_mode,
+        fuse_backward_update=True,
+        int8_backward=config.int8_backward,
+    )
+
+
+class CausalSelfAttention(nn.Module):
+    def __init__(self, config: ModelConfig, *, max_code: int | None) -> None:
+        super().__init__()
+        self.qkv = _linear(config, config.n_embd, 3 * config.n_embd, max_code)
+        self.projection = _linear(config, config.n_embd, config.n_embd, max_code)
+        self.n_head = config.n_head
+        self.head_size = config.n_embd // config.n_head
+        self.dropout = config.dropout
+
+    def forward(self, inputs: Tensor, *, inputs_int8: Tensor | None = None,
+                inputs_scale: Tensor | None = None) -> Tensor:
+        batch_size, sequence_length, channels = inputs.shape
+        if inputs_int8 is not None:
+            query, key, value = self.qkv(inputs, inputs_int8=inputs_int8,
+                                         inputs_scale=inputs_scale).chunk(3, dim=-1)
+        else:
+            query, key, value = self.qkv(inputs).chunk(3, dim=-1)
+
+        def heads(tensor: Tensor) -> Tensor:
+            return tensor.view(batch_size, sequence_length, self.n_head, self.head_size).transpose(1, 2)
+
+        attended = F.scaled_dot_product_attention(
+            heads(query), heads(key), heads(value),
+            dropout_p=self.dropout if self.training else 0.0, is_causal=True,
+        )
+        if getattr(self.projection, "matmul_mode", "fp32") == "int8":
+            attn_int8, attn_scale, dummy_joined = FusedTransposeQuantizeFn.apply(attended)
+            return self.projection(dummy_joined, inputs_int8=attn_int8, inputs_scale=attn_scale)
+        joined = attended.transpose(1, 2).contiguous().view(batch_size, sequence_length, channels)
+        return self.projection(joined)
+
+
+class FeedForward(nn.Module):
+    def __init__(self, config: ModelConfig, *, max_code: int | None) -> None:
+        super().__init__()
+        hidden_size = 4 * config.n_embd
+        self.expand = _linear(config, config.n_embd, hidden_size, max_code)
+        self.contract = _linear(config, hidden_size, config.n_embd, max_code)
+        self.dropout = config.dropout
+
+    def forward(self, inputs: Tensor, *, inputs_int8: Tensor | None = None,
+                inputs_scale: Tensor | None = None) -> Tensor:
+        if inputs_int8 is not None:
+            expanded = self.expand(inputs, inputs_int8=inputs_int8, inputs_scale=inputs_scale)
+        else:
+            expanded = self.expand(inputs)
+        if getattr(self.contract, "matmul_mode", "fp32") == "int8":
+            gelu_int8, gelu_scale, dummy_gelu = FusedGELUQuantizeFn.apply(expanded)
+            contracted = self.contract(dummy_gelu, inputs_int8=gelu_int8, inputs_scale=gelu_scale)
+        else:
+            contracted = self.contract(F.gelu(expanded))
+        return F.dropout(contracted, p=self.dropout, training=self.training)
+
+
+class TransformerBlock(nn.Module):
+    def __init__(self, config: ModelConfig, *, max_code: int | None) -> None:
+        super().__init__()
+        self.attention_norm = nn.RMSNorm(config.n_embd)
+        self.attention = CausalSelfAttention(config, max_code=max_code)
+        self.feed_forward_norm = nn.RMSNorm(config.n_embd)
+        self.feed_forward = FeedForward(config, max_code=max_code)
+
+    def forward(self, inputs: Tensor) -> Tensor:
+        if getattr(self.attention.qkv, "matmul_mode", "fp32") == "int8":
+            attn_int8, attn_scale, dummy_in = FusedRMSNormQuantizeFn.apply(
+                inputs, self.attention_norm.weight, 1e-5)
+            inputs = inputs + self.attention(dummy_in, inputs_int8=attn_int8, inputs_scale=attn_scale)
+        else:
+            inputs = inputs + self.attention(self.attention_norm(inputs))
+        if getattr(self.feed_forward.expand, "matmul_mode", "fp32") == "int8":
+            ffn_int8, ffn_scale, dummy_in = FusedRMSNormQuantizeFn.apply(
+                inputs, self.feed_forward_norm.weight, 1e-5)
+            inputs = inputs + self.feed_forward(dummy_in, inputs_int8=ffn_int8, inputs_scale=ffn_scale)
+        else:
+            inputs = inputs + self.feed_forward(self.feed_forward_norm(inputs))
+        return inputs
+
+
+class RatchetGPT(nn.Module):
+    def __init__(self, config: ModelConfig, *, max_code: int | None) -> None:
+        super().__init__()
+        self.config = config
+        self.max_code = max_code
+        if max_code is not None and config.ratchet_embedding:
+            self.token_embedding = RatchetEmbedding(
+                config.vocab_size, config.n_embd, max_code=max_code,
+                pressure_threshold=config.pressure_threshold, bucket_low=config.bucket_low,
+                bucket_high=config.bucket_high, trainable_scale=config.trainable_scale,
+                compile_update=config.compile_update, rms_ema_beta=config.rms_ema_beta,
+                pressure_leak_period=config.pressure_leak_period,
+            )
+        else:
+            self.token_embedding = nn.Embedding(config.vocab_size, config.n_embd)
+        self.register_buffer("position_encoding", _sinusoidal_positions(config.block_size, config.n_embd))
+        self.blocks = nn.ModuleList(TransformerBlock(config, max_code=max_code)
+                                    for _ in range(config.n_layer))
+        self.final_norm = nn.RMSNorm(config.n_embd)
+        self.lm_head = _linear(config, config.n_embd, config.vocab_size, max_code)
+        # distinct Philox layer ids for the stochastic rounding of each ratchet layer
+        for index, module in enumerate(m for m in self.modules() if isinstance(m, DiscreteRatchetLinear)):
+            module.sr_layer = index
+
+    def forward(self, tokens: Tensor, targets: Tensor | None = None) -> tuple[Tensor, Tensor | None]:
+        if tokens.ndim != 2:
+            raise ValueError("tokens must have shape (batch, sequence)")
+        sequence_length = tokens.shape[1]
+        if sequence_length > self.config.block_size:
+            raise ValueError("token sequence exceeds configured block_size")
+        hidden = self.token_embedding(tokens) + self.position_encoding[:sequence_length]
+        for block in self.blocks:
+            if self.config.gradient_checkpointing and self.training:
+                import torch.utils.checkpoint
+
+                hidden = torch.utils.checkpoint.checkpoint(block, hidden, use_reentrant=False)
+            else:
+                hidden = block(hidden)
+        logits = self.lm_head(self.final_norm(hidden))
+        loss = None
+        if targets is not None:
+            if targets.shape != tokens.shape:
+                raise ValueError("targets must have the same shape as tokens")
+            loss = F.cross_entropy(logits.flatten(0, 1), targets.flatten())
+        return logits, loss
+
+    def ratchet_layers(self) -> list[DiscreteRatchetLinear]:
+        return [m for m in self.modules() if isinstance(m, DiscreteRatchetLinear)]
+
+    def ratchet_update(self, *, validate: bool = True) -> RatchetUpdateStats:
+        updates = [module.ratchet_update(validate=validate) for module in self.ratchet_layers()]
+        total_weights = sum(update.total_weights for update in updates)
+        aggregated = RatchetUpdateStats(
+            total_weights=total_weights,
+            positive_moves=sum(update.positive_moves for update in updates),
+            negative_moves=sum(update.negative_moves for update in updates),
+            blocked_positive_moves=sum(update.blocked_positive_moves for update in updates),
+            blocked_negative_moves=sum(update.blocked_negative_moves for update in updates),
+            gradient_rms_mean=(sum(update.gradient_rms_mean for update in updates) / len(updates)
+                               if updates else 0.0),
+        )
+        return aggregated.materialize() if validate else aggregated
+
+    def discard_pending_gradients(self) -> None:
+        for module in self.ratchet_layers():
+            module.discard_pending_gradient()
+
+
+def build_seeded_model(config: ModelConfig, *, max_code: int | None, seed: int) -> RatchetGPT:
+    """Build matched arms without changing the caller's global CPU RNG state."""
+    with torch.random.fork_rng(devices=[]):
+        torch.manual_seed(seed)
+        return RatchetGPT(config, max_code=max_code)
