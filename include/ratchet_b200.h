@@ -62,11 +62,14 @@ int rt_sm_count(int *out);
  *       (seed, layer) with counter (element index / 4, step)  [own mapping, not Triton's tl.rand]
  * x_bf16_out (optional) receives bf16(x) (unscaled) — the grad_weight GEMM operand of
  * ratchet.py:162 — so the gradient is read from HBM once.
+ * step_dev (optional): device address of a uint32 read in place of `step`, so a captured CUDA
+ * graph can advance the stream between replays.
  * ------------------------------------------------------------------------------------------- */
 int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_t cols, int64_t stride_row,
                      int64_t stride_col, const float *col_scale, int stochastic, uint64_t seed,
-                     uint32_t step, uint32_t layer, int8_t *q, int64_t ldq, float *row_scale,
-                     void *x_bf16_out, int64_t ld_xbf16, void *stream);
+                     uint32_t step, uint32_t layer, const uint32_t *step_dev, int8_t *q,
+                     int64_t ldq, float *row_scale, void *x_bf16_out, int64_t ld_xbf16,
+                     void *stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Scaled int8 GEMM.  Replaces int8_matmul.py:scaled_int8_mm (289-343) / _scaled_int8_kernel
@@ -117,6 +120,7 @@ int rt_dequant_rows_bf16(const int8_t *q, int64_t ldq, const float *row_scale, v
  *   rms_ema (optional, rows): per-row second-moment EMA (ratchet.py:543-553), beta in (0,1).
  *   counts (int64[4], accumulated): positive, negative, blocked positive, blocked negative moves.
  *   row_rms (optional, rows): sqrt(mean(g^2)) of each row (ratchet.py:534-537 statistics).
+ *   rms_sum (optional, one float, accumulated): the sum of those row values.
  *   grad_scale (optional, rows): sum_k g[r,k] * code_before[r,k] (ratchet.py:167-169).
  * Rows holding NaN/Inf are left unchanged and set RT_STATUS_NONFINITE_GRADIENT.
  * The row mean-square uses a fixed reduction order (documented in the kernel) mirrored by the
@@ -126,7 +130,7 @@ int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf16, int64_t 
                       int64_t cols, uint8_t *packed, int64_t ldp, int8_t *code_out, int64_t ldc,
                       int normalize, float *rms_ema, double ema_beta, int max_code, int threshold,
                       double bucket_low, double bucket_high, double eps, int64_t *counts,
-                      float *row_rms, float *grad_scale, void *stream);
+                      float *row_rms, float *rms_sum, float *grad_scale, void *stream);
 
 /* Pressure leak: every nonzero pressure moves one unit toward zero (ratchet.py:613-625).
  * code_out, when given, is refreshed with the (unchanged) codes. */
@@ -158,10 +162,11 @@ int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, int64_t hea
                           int64_t head_dim, int64_t stride_b, int64_t stride_h, int64_t stride_s,
                           int64_t stride_d, int8_t *q, int64_t ldq, float *row_scale,
                           void *stream);
-/* RMSNorm backward, dx only (int8_backward.py:7-51); dx written in dx_dtype. */
+/* RMSNorm backward (int8_backward.py:7-51): dx written in dx_dtype (through bf16, as the
+ * reference stores it); dw (optional, cols floats, accumulated) += sum over rows of gy*x*rsqrt. */
 int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
                         const float *weight, double eps, int64_t rows, int64_t cols, void *dx,
-                        int dx_dtype, void *stream);
+                        int dx_dtype, float *dw, void *stream);
 /* tanh-GELU backward (int8_backward.py:53-89); dx written in dx_dtype. */
 int rt_gelu_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype, int64_t rows,
                      int64_t cols, void *dx, int dx_dtype, void *stream);

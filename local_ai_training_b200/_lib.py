@@ -41,8 +41,8 @@ _SIGNATURES = {
     "rt_last_error": ([], ctypes.c_char_p),
     "rt_device_status": ([_p, _i, _p], _i),
     "rt_sm_count": ([_p], _i),
-    "rt_quantize_rows": ([_p, _i, _i64, _i64, _i64, _i64, _p, _i, _u64, _u32, _u32, _p, _i64, _p,
-                          _p, _i64, _p], _i),
+    "rt_quantize_rows": ([_p, _i, _i64, _i64, _i64, _i64, _p, _i, _u64, _u32, _u32, _p, _p, _i64,
+                          _p, _p, _i64, _p], _i),
     "rt_scaled_int8_mm": ([_p, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i, _i64, _i64, _i64, _i64,
                            _p], _i),
     "rt_grad_weight_bf16": ([_p, _i64, _p, _i64, _p, _i, _i64, _i64, _i64, _i64, _i, _p, _i64, _p],
@@ -50,7 +50,7 @@ _SIGNATURES = {
     "rt_grad_weight_workspace_bytes": ([_i64, _i64, _i64], _i64),
     "rt_dequant_rows_bf16": ([_p, _i64, _p, _p, _i64, _i64, _i64, _p], _i),
     "rt_ratchet_update": ([_p, _i, _i, _i64, _i64, _i64, _p, _i64, _p, _i64, _i, _p, _d, _i, _i,
-                           _d, _d, _d, _p, _p, _p, _p], _i),
+                           _d, _d, _d, _p, _p, _p, _p, _p], _i),
     "rt_ratchet_leak": ([_p, _i64, _i64, _i64, _i, _p], _i),
     "rt_unpack_code_pressure": ([_p, _i64, _i64, _i64, _i, _p, _i64, _p, _i64, _p], _i),
     "rt_ratchet_validate": ([_p, _i64, _i64, _i64, _i, _p, _p], _i),
@@ -58,7 +58,7 @@ _SIGNATURES = {
     "rt_gelu_quantize": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p], _i),
     "rt_transpose_quantize": ([_p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64,
                                _p, _p], _i),
-    "rt_rmsnorm_backward": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p], _i),
+    "rt_rmsnorm_backward": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p, _p], _i),
     "rt_gelu_backward": ([_p, _i, _p, _i, _i64, _i64, _p, _i, _p], _i),
 }
 
@@ -142,6 +142,30 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor | None:
         ws = torch.zeros(nbytes, device=device, dtype=torch.uint8)
         _WORKSPACES[device] = ws
     return ws
+
+
+# Opt-in timing of library calls: when PROFILE is a dict, each wrapped call records a pair of CUDA
+# events on its stream plus its algorithmic flops and bytes under a kernel-family name.
+PROFILE: dict | None = None
+# When True the events are created as external events, so that a CUDA graph captured while
+# profiling holds event-record nodes and each replay re-times every library call.
+PROFILE_EXTERNAL = False
+
+
+def prof_start(t: torch.Tensor):
+    if PROFILE is None:
+        return None
+    ev = torch.cuda.Event(enable_timing=True, external=PROFILE_EXTERNAL)
+    ev.record(torch.cuda.current_stream(t.device))
+    return ev
+
+
+def prof_stop(start, name: str, t: torch.Tensor, flops: float, nbytes: float) -> None:
+    if start is None or PROFILE is None:
+        return
+    end = torch.cuda.Event(enable_timing=True, external=PROFILE_EXTERNAL)
+    end.record(torch.cuda.current_stream(t.device))
+    PROFILE.setdefault(name, []).append((start, end, float(flops), float(nbytes)))
 
 
 def sm_count() -> int:

@@ -1,14 +1,21 @@
 // rt_rowops.cuh — HBM-bound row kernels: per-token int8 quantisation (round-to-nearest and
 // Philox stochastic rounding), the ratchet update, pressure leak, unpack, validation, the
-// activation dequant of the grad_weight operand and the fused producers of pre-quantised inputs.
+// activation dequant of the grad_weight operand and the fused producers of pre-quantised inputs
+// with their backwards.
 //
-// Canonical row reduction order (mirrored bit-for-bit by oracle/ratchet_oracle.c):
-//   a row of `cols` elements is split into 4-element groups; group g belongs to slot g % 256;
-//   each slot sums its elements in increasing index order starting from +0.0f (fp32, RN);
-//   slots 32w..32w+31 are combined by an xor butterfly (offsets 16,8,4,2,1);
-//   the 8 warp sums w0..w7 are combined as ((w0+w1)+(w2+w3))+((w4+w5)+(w6+w7)).
-// Every kernel that needs a row sum (mean square for the ratchet normalisation, RMSNorm) uses one
-// 256-thread CTA per row and this order.
+// Layout: a row is cut into 8-element chunks (one 16-byte load for bf16, two for fp32).  RT
+// threads serve a row (32: a warp per row, 8 rows per 256-thread CTA; 128: 2 rows per CTA; 256: one
+// row per CTA) and each thread keeps VPT chunks in registers (chunk c = t + RT·i), so HBM sees one
+// read of every input and one write of every output.  Rows whose pointers or strides do not allow
+// 16-byte access, or that are longer than 256·8·8 elements, run the generic kernels (one CTA per
+// row, chunk loop) with identical arithmetic.
+//
+// Canonical row sum (mirrored bit-for-bit by oracle/ratchet_oracle.c canonical_sum):
+//   level 1  256 partials T_t; T_t adds the elements of chunks c ≡ t (mod 256) in index order from
+//            +0.0f (a warp-per-row lane keeps 8 of them, a CTA-per-row thread one);
+//   level 2  S_s = ((T_s+T_s+32)+(T_s+64+T_s+96)) + ((T_s+128+T_s+160)+(T_s+192+T_s+224)), s<32;
+//   level 3  xor butterfly over S_0..S_31 (offsets 16, 8, 4, 2, 1).
+// Every sum a kernel here takes over a row (mean squares, dot products) uses this order.
 #pragma once
 
 #include <cfloat>
@@ -17,11 +24,43 @@
 
 namespace rt {
 
-constexpr int ROW_THREADS = 256;
+constexpr int CTA = 256;
 
-// -------------------------------------------------------------------------------------------
-// Generic element access.
-// -------------------------------------------------------------------------------------------
+// ------------------------------------------------------------------------------------ chunk I/O
+__device__ __forceinline__ void ld8(const float *p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4 *>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4 *>(p) + 1);
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void ld8(const __nv_bfloat16 *p, float (&v)[8]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4 *>(p));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = __uint_as_float(w[j] << 16);
+    v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+}
+__device__ __forceinline__ void st8(float *p, const float (&v)[8]) {
+  reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ void st8(__nv_bfloat16 *p, const float (&v)[8]) {
+  uint4 u;
+  u.x = bf16_bits(v[0]) | (uint32_t(bf16_bits(v[1])) << 16);
+  u.y = bf16_bits(v[2]) | (uint32_t(bf16_bits(v[3])) << 16);
+  u.z = bf16_bits(v[4]) | (uint32_t(bf16_bits(v[5])) << 16);
+  u.w = bf16_bits(v[6]) | (uint32_t(bf16_bits(v[7])) << 16);
+  *reinterpret_cast<uint4 *>(p) = u;
+}
+__device__ __forceinline__ uint2 pack_i8x8(const int8_t (&q)[8]) {
+  uint2 o;
+  o.x = uint32_t(uint8_t(q[0])) | (uint32_t(uint8_t(q[1])) << 8) | (uint32_t(uint8_t(q[2])) << 16) |
+        (uint32_t(uint8_t(q[3])) << 24);
+  o.y = uint32_t(uint8_t(q[4])) | (uint32_t(uint8_t(q[5])) << 8) | (uint32_t(uint8_t(q[6])) << 16) |
+        (uint32_t(uint8_t(q[7])) << 24);
+  return o;
+}
 __device__ __forceinline__ float load_elem(const void *p, int dtype, int64_t idx) {
   if (dtype == RT_F32) return __ldg(static_cast<const float *>(p) + idx);
   return bf16_from_bits(__ldg(static_cast<const unsigned short *>(p) + idx));
@@ -33,43 +72,153 @@ __device__ __forceinline__ void store_elem(void *p, int dtype, int64_t idx, floa
     static_cast<unsigned short *>(p)[idx] = bf16_bits(v);
 }
 
-// Fixed-order CTA sum (see header).  `red` is 8 floats of shared memory.
-__device__ __forceinline__ float cta_sum_canonical(float partial, float *red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float w = warp_sum_butterfly(partial);
-  __syncthreads();  // protect `red` from a previous use
-  if (lane == 0) red[warp] = w;
-  __syncthreads();
-  const float a = __fadd_rn(red[0], red[1]), b = __fadd_rn(red[2], red[3]);
-  const float c = __fadd_rn(red[4], red[5]), d = __fadd_rn(red[6], red[7]);
-  return __fadd_rn(__fadd_rn(a, b), __fadd_rn(c, d));
+// --------------------------------------------------------------------------- row reductions
+__device__ __forceinline__ float tree8(const float (&a)[8]) {
+  return __fadd_rn(__fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3])),
+                   __fadd_rn(__fadd_rn(a[4], a[5]), __fadd_rn(a[6], a[7])));
 }
-__device__ __forceinline__ float cta_max(float v, float *red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_max(v);
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float m = red[0];
+// acc[k] is the level-1 partial T_{t + RT·k}.  `sm` holds (CTA/RT)·CTA floats and `smb` CTA/RT
+// floats when RT > 32.  Every thread of the CTA must call it (it synchronises the CTA).
+template <int RT>
+__device__ __forceinline__ float row_sum(const float (&acc)[CTA / RT], float *sm, float *smb,
+                                         int sub, int t) {
+  if constexpr (RT == 32) {
+    return warp_sum_butterfly(tree8(acc));
+  } else {
+    constexpr int NT = CTA / RT;
+    float *rowsm = sm + sub * CTA;
 #pragma unroll
-  for (int i = 1; i < ROW_THREADS / 32; ++i) m = fmaxf(m, red[i]);
-  return m;
+    for (int k = 0; k < NT; ++k) rowsm[t + RT * k] = acc[k];
+    __syncthreads();
+    if (t < 32) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = rowsm[t + 32 * j];
+      const float s = warp_sum_butterfly(tree8(v));
+      if (t == 0) smb[sub] = s;
+    }
+    __syncthreads();
+    return smb[sub];
+  }
+}
+// row maximum (order-free); `smx` holds (CTA/RT)·8 floats when RT > 32.
+template <int RT>
+__device__ __forceinline__ float row_max(float v, float *smx, int sub, int t) {
+  v = warp_max(v);
+  if constexpr (RT == 32) {
+    return v;
+  } else {
+    __syncthreads();
+    if ((t & 31) == 0) smx[sub * 8 + (t >> 5)] = v;
+    __syncthreads();
+    float m = smx[sub * 8];
+#pragma unroll
+    for (int w = 1; w < RT / 32; ++w) m = fmaxf(m, smx[sub * 8 + w]);
+    return m;
+  }
+}
+// CTA-per-row versions (RT = 256, one level-1 partial per thread) for the generic kernels.
+__device__ __forceinline__ float cta_row_sum(float partial, float *sm, float *smb) {
+  const float acc[1] = {partial};
+  return row_sum<CTA>(acc, sm, smb, 0, threadIdx.x);
+}
+__device__ __forceinline__ float cta_max(float v, float *smx) {
+  return row_max<CTA>(v, smx, 0, threadIdx.x);
 }
 
-// quantisation of one value given the row scale (int8_matmul.py:139-148).
-__device__ __forceinline__ int8_t quant_rn(float v, float scale) {
-  float r = rintf(__fdiv_rn(v, scale));
+// --------------------------------------------------------------------------- quantisation
+// int8_matmul.py:139-148.  The reference rounds RN(v / scale); only its rounding decision
+// matters, so the quotient is first formed as v · RN(1/scale) (within 1.5 ulp of RN(v / scale),
+// i.e. below 2^-15 since |v / scale| <= 127.5) and the IEEE division is taken only when that
+// estimate lies within 2^-12 of a rounding boundary (a half-integer for rint, an integer after
+// adding u for stochastic rounding) — the result is the one of the exact quotient.
+constexpr float kBoundaryWindow = 2.44140625e-4f;  // 2^-12
+__device__ __forceinline__ int8_t quant_rn(float v, float scale, float rcp) {
+  float y = __fmul_rn(v, rcp);
+  if (fabsf(__fsub_rn(__fsub_rn(y, floorf(y)), 0.5f)) <= kBoundaryWindow) y = __fdiv_rn(v, scale);
+  float r = rintf(y);
   r = fminf(fmaxf(r, -127.0f), 127.0f);
   return static_cast<int8_t>(static_cast<int>(r));
 }
-__device__ __forceinline__ int8_t quant_sr(float v, float scale, float u) {
-  float r = floorf(__fadd_rn(__fdiv_rn(v, scale), u));
+__device__ __forceinline__ int8_t quant_sr(float v, float scale, float rcp, float u) {
+  float t = __fadd_rn(__fmul_rn(v, rcp), u);
+  const float f = __fsub_rn(t, floorf(t));
+  if (f <= kBoundaryWindow || f >= 1.0f - kBoundaryWindow) t = __fadd_rn(__fdiv_rn(v, scale), u);
+  float r = floorf(t);
   r = fminf(fmaxf(r, -127.0f), 127.0f);
   return static_cast<int8_t>(static_cast<int>(r));
 }
 __device__ __forceinline__ float row_scale_of(float amax) {
   return fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN);
 }
+
+// Row-kernel configuration: threads per row and chunks per thread for a row of `nch` chunks.
+struct RowCfg {
+  int rt, vpt;  // rt == 0: generic kernel
+};
+static inline int pow2_at_least(int64_t v) {
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+// Few rows get more threads each (up to a CTA per row) so that the grid fills the GPU.
+static inline RowCfg row_cfg(int64_t nch, int64_t rows = INT64_MAX) {
+  const int64_t want_threads = 148 * 2048;
+  int rt = nch <= 32 * 8 ? 32 : (nch <= 128 * 8 ? 128 : (nch <= 256 * 8 ? 256 : 0));
+  if (rt == 0) return {0, 0};
+  while (rt < 256 && rows * rt < want_threads && nch > rt) rt = rt == 32 ? 128 : 256;
+  return {rt, pow2_at_least((nch + rt - 1) / rt)};
+}
+// Kernels holding four row arrays per chunk (RMSNorm backward) keep at most 2 chunks per thread.
+static inline RowCfg row_cfg_narrow(int64_t nch) {
+  if (nch <= 32) return {32, 1};
+  if (nch <= 64) return {32, 2};
+  if (nch <= 256) return {128, 2};
+  if (nch <= 512) return {256, 2};
+  return {0, 0};
+}
+static inline unsigned row_grid(int64_t rows, int rt) {
+  const int64_t rpc = CTA / rt;
+  return static_cast<unsigned>((rows + rpc - 1) / rpc);
+}
+
+#define RT_DISPATCH_ROW(cfg, KERNEL, T, GRID, ...)                                 \
+  do {                                                                               \
+    switch ((cfg).rt * 16 + (cfg).vpt) {                                             \
+      case 32 * 16 + 1: KERNEL<T, 32, 1><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
+      case 32 * 16 + 2: KERNEL<T, 32, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
+      case 32 * 16 + 4: KERNEL<T, 32, 4><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
+      case 32 * 16 + 8: KERNEL<T, 32, 8><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
+      case 128 * 16 + 1: KERNEL<T, 128, 1><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
+      case 128 * 16 + 2: KERNEL<T, 128, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
+      case 128 * 16 + 4: KERNEL<T, 128, 4><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
+      case 128 * 16 + 8: KERNEL<T, 128, 8><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
+      case 256 * 16 + 1: KERNEL<T, 256, 1><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
+      case 256 * 16 + 2: KERNEL<T, 256, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
+      case 256 * 16 + 4: KERNEL<T, 256, 4><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
+      default: KERNEL<T, 256, 8><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;           \
+    }                                                                                \
+  } while (0)
+
+#define RT_DISPATCH_ROW_NARROW(cfg, KERNEL, T, GRID, ...)                           \
+  do {                                                                               \
+    switch ((cfg).rt * 16 + (cfg).vpt) {                                             \
+      case 32 * 16 + 1: KERNEL<T, 32, 1><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
+      case 32 * 16 + 2: KERNEL<T, 32, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
+      case 128 * 16 + 2: KERNEL<T, 128, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
+      default: KERNEL<T, 256, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;           \
+    }                                                                                \
+  } while (0)
+
+#define RT_DISPATCH_ROW_NARROW_SMEM(cfg, KERNEL, T, GRID, SMEM, ...)                        \
+  do {                                                                                        \
+    switch ((cfg).rt * 16 + (cfg).vpt) {                                                      \
+      case 32 * 16 + 1: KERNEL<T, 32, 1><<<GRID, CTA, SMEM, s>>>(__VA_ARGS__); break;         \
+      case 32 * 16 + 2: KERNEL<T, 32, 2><<<GRID, CTA, SMEM, s>>>(__VA_ARGS__); break;         \
+      case 128 * 16 + 2: KERNEL<T, 128, 2><<<GRID, CTA, SMEM, s>>>(__VA_ARGS__); break;       \
+      default: KERNEL<T, 256, 2><<<GRID, CTA, SMEM, s>>>(__VA_ARGS__); break;                 \
+    }                                                                                         \
+  } while (0)
 
 // ===========================================================================================
 // Row quantisation (int8_matmul.py:106-150).
@@ -81,6 +230,7 @@ struct QuantArgs {
   int stochastic;
   uint64_t seed;
   uint32_t step, layer;
+  const uint32_t *step_dev;
   int8_t *q;
   int64_t ldq;
   float *row_scale;
@@ -88,199 +238,120 @@ struct QuantArgs {
   int64_t ld_xbf16;
 };
 
-// Vectorised, register-resident variant: RT threads per row, each holding VPT vectors of W
-// consecutive elements (16-byte loads).  Rows, columns and outputs are 16-byte aligned.
 template <typename T, int RT, int VPT>
-__global__ void __launch_bounds__(256) quant_rows_vec_kernel(QuantArgs a) {
-  constexpr int W = 16 / sizeof(T);
-  constexpr int RPC = 256 / RT;  // rows per CTA
-  constexpr int NW = RT / 32;    // warps per row
-  __shared__ float red[256 / 32];
+__global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
+  constexpr int RPC = CTA / RT;
+  __shared__ float smx[RPC * 8];
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * RPC + sub;
   const bool live = row < a.rows;
-  const int64_t nchunk = a.cols / W;
+  const int64_t nch = a.cols / 8;
   const T *xr = static_cast<const T *>(a.x) + (live ? row : 0) * a.stride_row;
-
-  float v[VPT][W];
+  float v[VPT][8];
   float amax = 0.0f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
-    if (live && c < nchunk) {
-      const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(xr + c * W));
-      if constexpr (sizeof(T) == 4) {
-        v[i][0] = __uint_as_float(raw.x);
-        v[i][1] = __uint_as_float(raw.y);
-        v[i][2] = __uint_as_float(raw.z);
-        v[i][3] = __uint_as_float(raw.w);
-      } else {
-        const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          v[i][2 * j] = __uint_as_float(w4[j] << 16);
-          v[i][2 * j + 1] = __uint_as_float(w4[j] & 0xFFFF0000u);
-        }
-      }
-      if (a.xbf16 != nullptr) {  // bf16(x), unscaled: the grad_weight GEMM operand
-        unsigned short hb[W];
-#pragma unroll
-        for (int j = 0; j < W; ++j) hb[j] = bf16_bits(v[i][j]);
-        unsigned short *dst = a.xbf16 + row * a.ld_xbf16 + c * W;
-        if constexpr (W == 8) {
-          uint4 o;
-          o.x = hb[0] | (uint32_t(hb[1]) << 16);
-          o.y = hb[2] | (uint32_t(hb[3]) << 16);
-          o.z = hb[4] | (uint32_t(hb[5]) << 16);
-          o.w = hb[6] | (uint32_t(hb[7]) << 16);
-          *reinterpret_cast<uint4 *>(dst) = o;
-        } else {
-          uint2 o;
-          o.x = hb[0] | (uint32_t(hb[1]) << 16);
-          o.y = hb[2] | (uint32_t(hb[3]) << 16);
-          *reinterpret_cast<uint2 *>(dst) = o;
-        }
-      }
+    if (live && c < nch) {
+      ld8(xr + 8 * c, v[i]);
+      if (a.xbf16 != nullptr)
+        st8(reinterpret_cast<__nv_bfloat16 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c), v[i]);
       if (a.col_scale != nullptr) {
+        float cs[8];
+        ld8(a.col_scale + 8 * c, cs);
 #pragma unroll
-        for (int j = 0; j < W; j += 4) {
-          const float4 cs = __ldg(reinterpret_cast<const float4 *>(a.col_scale + c * W + j));
-          v[i][j] = __fmul_rn(v[i][j], cs.x);
-          v[i][j + 1] = __fmul_rn(v[i][j + 1], cs.y);
-          v[i][j + 2] = __fmul_rn(v[i][j + 2], cs.z);
-          v[i][j + 3] = __fmul_rn(v[i][j + 3], cs.w);
-        }
+        for (int j = 0; j < 8; ++j) v[i][j] = __fmul_rn(v[i][j], cs[j]);
       }
 #pragma unroll
-      for (int j = 0; j < W; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
     } else {
 #pragma unroll
-      for (int j = 0; j < W; ++j) v[i][j] = 0.0f;
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
     }
   }
-  // row amax across the RT threads of this row
-  amax = warp_max(amax);
-  if constexpr (NW > 1) {
-    __syncthreads();
-    if ((t & 31) == 0) red[sub * NW + (t >> 5)] = amax;
-    __syncthreads();
-    amax = red[sub * NW];
-#pragma unroll
-    for (int w = 1; w < NW; ++w) amax = fmaxf(amax, red[sub * NW + w]);
-  }
+  amax = row_max<RT>(amax, smx, sub, t);
   if (!live) return;
   const float scale = row_scale_of(amax);
+  const float rcp = __frcp_rn(scale);
   if (t == 0) a.row_scale[row] = scale;
+  const uint32_t step = a.step_dev != nullptr ? __ldg(a.step_dev) : a.step;
   int8_t *qr = a.q + row * a.ldq;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
-    if (c >= nchunk) continue;
-    int8_t o[W];
+    if (c >= nch) continue;
+    int8_t o[8];
     if (a.stochastic) {
-      const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + c * W;  // multiple of 4
-#pragma unroll
-      for (int j = 0; j < W; j += 4) {
-        const Philox4 p = sr_block(a.seed, a.step, a.layer, (e0 + j) >> 2);
-        o[j] = quant_sr(v[i][j], scale, u24(p.x));
-        o[j + 1] = quant_sr(v[i][j + 1], scale, u24(p.y));
-        o[j + 2] = quant_sr(v[i][j + 2], scale, u24(p.z));
-        o[j + 3] = quant_sr(v[i][j + 3], scale, u24(p.w));
-      }
+      const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;  // multiple of 8
+      const Philox4 p0 = sr_block(a.seed, step, a.layer, e0 >> 2);
+      const Philox4 p1 = sr_block(a.seed, step, a.layer, (e0 >> 2) + 1);
+      o[0] = quant_sr(v[i][0], scale, rcp, u24(p0.x));
+      o[1] = quant_sr(v[i][1], scale, rcp, u24(p0.y));
+      o[2] = quant_sr(v[i][2], scale, rcp, u24(p0.z));
+      o[3] = quant_sr(v[i][3], scale, rcp, u24(p0.w));
+      o[4] = quant_sr(v[i][4], scale, rcp, u24(p1.x));
+      o[5] = quant_sr(v[i][5], scale, rcp, u24(p1.y));
+      o[6] = quant_sr(v[i][6], scale, rcp, u24(p1.z));
+      o[7] = quant_sr(v[i][7], scale, rcp, u24(p1.w));
     } else {
 #pragma unroll
-      for (int j = 0; j < W; ++j) o[j] = quant_rn(v[i][j], scale);
+      for (int j = 0; j < 8; ++j) o[j] = quant_rn(v[i][j], scale, rcp);
     }
-    if constexpr (W == 8) {
-      uint2 packed8;
-      packed8.x = uint32_t(uint8_t(o[0])) | (uint32_t(uint8_t(o[1])) << 8) |
-                  (uint32_t(uint8_t(o[2])) << 16) | (uint32_t(uint8_t(o[3])) << 24);
-      packed8.y = uint32_t(uint8_t(o[4])) | (uint32_t(uint8_t(o[5])) << 8) |
-                  (uint32_t(uint8_t(o[6])) << 16) | (uint32_t(uint8_t(o[7])) << 24);
-      *reinterpret_cast<uint2 *>(qr + c * W) = packed8;
-    } else {
-      *reinterpret_cast<uint32_t *>(qr + c * W) =
-          uint32_t(uint8_t(o[0])) | (uint32_t(uint8_t(o[1])) << 8) |
-          (uint32_t(uint8_t(o[2])) << 16) | (uint32_t(uint8_t(o[3])) << 24);
-    }
+    *reinterpret_cast<uint2 *>(qr + 8 * c) = pack_i8x8(o);
   }
 }
 
-// Generic variant: any strides/alignment, one 256-thread CTA per row, two passes (the second
-// pass re-reads the row, normally from L2).
+// Generic: any strides, one CTA per row, two passes (the second normally hits L2).
 template <typename T>
-__global__ void __launch_bounds__(256) quant_rows_generic_kernel(QuantArgs a) {
-  __shared__ float red[8];
+__global__ void __launch_bounds__(CTA) quant_rows_generic_kernel(QuantArgs a) {
+  __shared__ float smx[8];
   const int64_t row = blockIdx.x;
   const T *xr = static_cast<const T *>(a.x) + row * a.stride_row;
   float amax = 0.0f;
-  for (int64_t k = threadIdx.x; k < a.cols; k += 256) {
+  for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
     float v = load_as_float<T>(xr + k * a.stride_col);
     if (a.xbf16 != nullptr) a.xbf16[row * a.ld_xbf16 + k] = bf16_bits(v);
     if (a.col_scale != nullptr) v = __fmul_rn(v, __ldg(a.col_scale + k));
     amax = fmaxf(amax, fabsf(v));
   }
-  amax = cta_max(amax, red);
+  amax = cta_max(amax, smx);
   const float scale = row_scale_of(amax);
+  const float rcp = __frcp_rn(scale);
   if (threadIdx.x == 0) a.row_scale[row] = scale;
-  for (int64_t k = threadIdx.x; k < a.cols; k += 256) {
+  const uint32_t step = a.step_dev != nullptr ? __ldg(a.step_dev) : a.step;
+  for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
     float v = load_as_float<T>(xr + k * a.stride_col);
     if (a.col_scale != nullptr) v = __fmul_rn(v, __ldg(a.col_scale + k));
     int8_t o;
     if (a.stochastic) {
       const uint64_t e = static_cast<uint64_t>(row) * a.cols + k;
-      const Philox4 p = sr_block(a.seed, a.step, a.layer, e >> 2);
-      o = quant_sr(v, scale, u24(philox_word(p, static_cast<int>(e & 3))));
+      const Philox4 p = sr_block(a.seed, step, a.layer, e >> 2);
+      o = quant_sr(v, scale, rcp, u24(philox_word(p, static_cast<int>(e & 3))));
     } else {
-      o = quant_rn(v, scale);
+      o = quant_rn(v, scale, rcp);
     }
     a.q[row * a.ldq + k] = o;
   }
 }
 
-template <typename T, int RT>
-static void launch_quant_vec(const QuantArgs &a, int vpt, cudaStream_t s) {
-  const int rpc = 256 / RT;
-  const dim3 grid(static_cast<unsigned>((a.rows + rpc - 1) / rpc));
-  switch (vpt) {
-    case 1: quant_rows_vec_kernel<T, RT, 1><<<grid, 256, 0, s>>>(a); break;
-    case 2: quant_rows_vec_kernel<T, RT, 2><<<grid, 256, 0, s>>>(a); break;
-    case 4: quant_rows_vec_kernel<T, RT, 4><<<grid, 256, 0, s>>>(a); break;
-    case 8: quant_rows_vec_kernel<T, RT, 8><<<grid, 256, 0, s>>>(a); break;
-    default: quant_rows_vec_kernel<T, RT, 16><<<grid, 256, 0, s>>>(a); break;
-  }
-}
-
-static inline int pow2_at_least(int64_t v) {
-  int p = 1;
-  while (p < v) p <<= 1;
-  return p;
-}
-
 template <typename T>
 static int quant_rows_dispatch(const QuantArgs &a, cudaStream_t s) {
-  constexpr int W = 16 / sizeof(T);
-  const bool vec = a.stride_col == 1 && aligned16(a.x) &&
-                   (a.stride_row * static_cast<int64_t>(sizeof(T))) % 16 == 0 && a.cols % W == 0 &&
-                   (reinterpret_cast<uintptr_t>(a.q) % W) == 0 && a.ldq % W == 0 &&
+  const size_t es = sizeof(T);
+  const bool vec = a.stride_col == 1 && aligned16(a.x) && (a.stride_row * es) % 16 == 0 &&
+                   a.cols % 8 == 0 && (reinterpret_cast<uintptr_t>(a.q) & 7) == 0 && a.ldq % 8 == 0 &&
                    (a.col_scale == nullptr || aligned16(a.col_scale)) &&
-                   (a.xbf16 == nullptr ||
-                    ((reinterpret_cast<uintptr_t>(a.xbf16) % (2 * W)) == 0 && a.ld_xbf16 % W == 0));
-  const int64_t nchunk = a.cols / W;
-  if (vec && nchunk <= 32 * 8) {
-    launch_quant_vec<T, 32>(a, pow2_at_least((nchunk + 31) / 32), s);
-  } else if (vec && nchunk <= 256 * 16) {
-    launch_quant_vec<T, 256>(a, pow2_at_least((nchunk + 255) / 256), s);
+                   (a.xbf16 == nullptr || (aligned16(a.xbf16) && a.ld_xbf16 % 8 == 0));
+  const RowCfg cfg = vec ? row_cfg(a.cols / 8, a.rows) : RowCfg{0, 0};
+  if (cfg.rt != 0) {
+    RT_DISPATCH_ROW(cfg, quant_rows_kernel, T, row_grid(a.rows, cfg.rt), a);
   } else {
-    quant_rows_generic_kernel<T><<<static_cast<unsigned>(a.rows), 256, 0, s>>>(a);
+    quant_rows_generic_kernel<T><<<static_cast<unsigned>(a.rows), CTA, 0, s>>>(a);
   }
   return check_launch("rt_quantize_rows");
 }
 
 // ===========================================================================================
-// Ratchet update (ratchet.py:248-301, 487-556, 582-611): one 256-thread CTA per row; the row's
-// 4-element groups are held in registers (VPT groups per thread), so HBM sees one read of the
-// gradient and of `packed`, one write of `packed` and (optionally) of the int8 code mirror.
+// Ratchet update (ratchet.py:248-301, 487-556, 582-611).
 // ===========================================================================================
 struct UpdateArgs {
   const void *grad;
@@ -296,20 +367,33 @@ struct UpdateArgs {
   int max_code, threshold;
   float low, high, eps;
   unsigned long long *counts;
-  float *row_rms, *grad_scale;
+  float *row_rms, *rms_sum, *grad_scale;
 };
 
 struct Moves {
   int pos, neg, bpos, bneg;
 };
 
-// One weight: returns the new packed byte (ratchet.py:277-294).
-__device__ __forceinline__ uint8_t ratchet_one(uint8_t old, float z, const UpdateArgs &a,
+// Pressure increment of one weight (ratchet.py:248-262): -sign(z) · bucket(|z|) with
+// z = RN(g / denom).  Only the two threshold comparisons depend on the quotient, so it is formed
+// as g · RN(1/denom) (relative error below 2^-22) and the IEEE division is taken only when that
+// estimate lies within a relative 2^-20 of a threshold.  sign(z) = sign(g) since denom > 0.
+__device__ __forceinline__ int pressure_increment(float g, float denom, float rcp, int normalize,
+                                                  float low, float high) {
+  float mag = normalize ? fabsf(__fmul_rn(g, rcp)) : fabsf(g);
+  if (normalize) {
+    const float win = __fmul_rn(mag, 9.5367431640625e-07f);  // 2^-20
+    if (fabsf(__fsub_rn(mag, high)) <= win || fabsf(__fsub_rn(mag, low)) <= win)
+      mag = fabsf(__fdiv_rn(g, denom));
+  }
+  const int bucket = mag >= high ? 2 : (mag >= low ? 1 : 0);
+  const int sgn = (g > 0.0f) - (g < 0.0f);
+  return -sgn * bucket;
+}
+
+// One weight: the new packed byte (ratchet.py:277-294).
+__device__ __forceinline__ uint8_t ratchet_one(uint8_t old, int inc, const UpdateArgs &a,
                                                Moves &m) {
-  const float mag = fabsf(z);
-  const int bucket = mag >= a.high ? 2 : (mag >= a.low ? 1 : 0);
-  const int sgn = (z > 0.0f) - (z < 0.0f);
-  const int inc = -sgn * bucket;
   int code = static_cast<int>(old & 0x0F) - a.max_code;
   int p = static_cast<int>(old >> 4) - 7 + inc;
   const bool pos_req = p >= a.threshold, neg_req = p <= -a.threshold;
@@ -324,228 +408,196 @@ __device__ __forceinline__ uint8_t ratchet_one(uint8_t old, float z, const Updat
   m.bneg += neg_req && !neg_mv;
   return static_cast<uint8_t>(((code + a.max_code) & 0x0F) | (((p + 7) & 0x0F) << 4));
 }
-
-__device__ __forceinline__ float grad_value(const UpdateArgs &a, int64_t idx) {
-  float g = load_elem(a.grad, a.grad_dtype, idx);
-  if (a.round_bf16) g = bf16_round(g);
-  return g;
+__device__ __forceinline__ int8_t code_of(uint8_t packed, int max_code) {
+  return static_cast<int8_t>(static_cast<int>(packed & 0x0F) - max_code);
 }
 
-// VEC: fp32/bf16 gradient rows, `packed` and `code_out` allow 4-element vector access.
-template <int VPT, bool VEC>
-__global__ void __launch_bounds__(256) ratchet_update_kernel(UpdateArgs a) {
-  __shared__ float red[8];
-  __shared__ int redi[8][4];
-  __shared__ float bcast[2];
-  const int t = threadIdx.x;
-  const int64_t row = blockIdx.x;
-  const int64_t ngroups = (a.cols + 3) / 4;
+// Per-row normaliser (ratchet.py:539-556); returns rms + eps.  Only `writer` stores rms_ema.
+__device__ __forceinline__ float row_denominator(const UpdateArgs &a, int64_t row, float ms,
+                                                 float ema_old, bool bad, bool writer) {
+  float rms = __fsqrt_rn(ms);
+  if (a.rms_ema != nullptr && !bad) {
+    const float upd = ema_old == 0.0f
+                          ? ms
+                          : __fadd_rn(__fmul_rn(a.beta, ema_old), __fmul_rn(a.one_minus_beta, ms));
+    const float ema = ms > 0.0f ? upd : ema_old;
+    if (writer) a.rms_ema[row] = ema;
+    rms = __fsqrt_rn(ema);
+  }
+  return __fadd_rn(rms, a.eps);
+}
 
-  float g[VPT][4];
-  uint32_t pk[VPT];
+__device__ __forceinline__ void publish_moves(Moves m, int (*redi)[4], const UpdateArgs &a) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  m.pos = warp_isum(m.pos), m.neg = warp_isum(m.neg);
+  m.bpos = warp_isum(m.bpos), m.bneg = warp_isum(m.bneg);
+  __syncthreads();
+  if (lane == 0) {
+    redi[warp][0] = m.pos, redi[warp][1] = m.neg, redi[warp][2] = m.bpos, redi[warp][3] = m.bneg;
+  }
+  __syncthreads();
+  if (threadIdx.x < 4 && a.counts != nullptr) {
+    int sum = 0;
+#pragma unroll
+    for (int w = 0; w < CTA / 32; ++w) sum += redi[w][threadIdx.x];
+    if (sum != 0) atomicAdd(a.counts + threadIdx.x, static_cast<unsigned long long>(sum));
+  }
+}
+
+template <typename G, int RT, int VPT>
+__global__ void __launch_bounds__(CTA) ratchet_update_kernel(UpdateArgs a) {
+  constexpr int RPC = CTA / RT, NT = CTA / RT;
+  __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
+  __shared__ float smb[RPC];
+  __shared__ float smx[RPC * 8];
+  __shared__ int redi[CTA / 32][4];
+  const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * RPC + sub;
+  const bool live = row < a.rows;
+  const int64_t nch = a.cols / 8;
+  const G *gr = static_cast<const G *>(a.grad) + (live ? row : 0) * a.ldg;
+  const uint8_t *pr = a.packed + (live ? row : 0) * a.ldp;
+
+  float g[VPT][8];
+  uint2 pk[VPT];
   bool bad = false;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    const int64_t grp = t + static_cast<int64_t>(i) * ROW_THREADS;
-    const int64_t c0 = grp * 4;
-    pk[i] = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) g[i][j] = 0.0f;
-    if (grp >= ngroups) continue;
-    if constexpr (VEC) {
-      if (a.grad_dtype == RT_F32) {
-        const float4 f = __ldg(
-            reinterpret_cast<const float4 *>(static_cast<const float *>(a.grad) + row * a.ldg + c0));
-        g[i][0] = f.x, g[i][1] = f.y, g[i][2] = f.z, g[i][3] = f.w;
-      } else {
-        const uint2 h = __ldg(reinterpret_cast<const uint2 *>(
-            static_cast<const unsigned short *>(a.grad) + row * a.ldg + c0));
-        g[i][0] = __uint_as_float(h.x << 16), g[i][1] = __uint_as_float(h.x & 0xFFFF0000u);
-        g[i][2] = __uint_as_float(h.y << 16), g[i][3] = __uint_as_float(h.y & 0xFFFF0000u);
-      }
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    pk[i] = make_uint2(0, 0);
+    if (live && c < nch) {
+      ld8(gr + 8 * c, g[i]);
       if (a.round_bf16) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) g[i][j] = bf16_round(g[i][j]);
+        for (int j = 0; j < 8; ++j) g[i][j] = bf16_round(g[i][j]);
       }
-      pk[i] = *reinterpret_cast<const uint32_t *>(a.packed + row * a.ldp + c0);
+      pk[i] = *reinterpret_cast<const uint2 *>(pr + 8 * c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bad |= !isfinite(g[i][j]);
     } else {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (c0 + j < a.cols) {
-          g[i][j] = grad_value(a, row * a.ldg + c0 + j);
-          pk[i] |= static_cast<uint32_t>(a.packed[row * a.ldp + c0 + j]) << (8 * j);
-        }
-      }
+      for (int j = 0; j < 8; ++j) g[i][j] = 0.0f;
     }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) bad |= !isfinite(g[i][j]);
   }
-  bad = __syncthreads_or(bad) != 0;
+  const float ema_old = (a.rms_ema != nullptr && live) ? a.rms_ema[row] : 0.0f;
+  bad = row_max<RT>(bad ? 1.0f : 0.0f, smx, sub, t) > 0.0f;
 
-  // mean square in the canonical order; the trainable-scale gradient uses the same order.
-  float ss = 0.0f, gs = 0.0f;
+  float ss[NT], gsa[NT];
+#pragma unroll
+  for (int k = 0; k < NT; ++k) ss[k] = 0.0f, gsa[k] = 0.0f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      ss = __fadd_rn(ss, __fmul_rn(g[i][j], g[i][j]));
+    for (int j = 0; j < 8; ++j) {
+      ss[i % NT] = __fadd_rn(ss[i % NT], __fmul_rn(g[i][j], g[i][j]));
       if (a.grad_scale != nullptr) {
-        const int code = static_cast<int>((pk[i] >> (8 * j)) & 0x0Fu) - a.max_code;
-        gs = __fadd_rn(gs, __fmul_rn(g[i][j], static_cast<float>(code)));
+        const uint32_t word = j < 4 ? pk[i].x : pk[i].y;
+        const float code = static_cast<float>(code_of(static_cast<uint8_t>(word >> (8 * (j & 3))),
+                                                      a.max_code));
+        gsa[i % NT] = __fadd_rn(gsa[i % NT], __fmul_rn(g[i][j], code));
       }
     }
   }
-  const float total = cta_sum_canonical(ss, red);
-  float gsum = 0.0f;
-  if (a.grad_scale != nullptr) gsum = cta_sum_canonical(gs, red);
+  const float total = row_sum<RT>(ss, sm, smb, sub, t);
+  const float gsum = a.grad_scale != nullptr ? row_sum<RT>(gsa, sm, smb, sub, t) : 0.0f;
   const float ms = __fdiv_rn(total, static_cast<float>(a.cols));
-
-  if (t == 0) {
-    float denom_rms = __fsqrt_rn(ms);
-    if (a.rms_ema != nullptr && !bad) {
-      const float ema_old = a.rms_ema[row];
-      const float upd = ema_old == 0.0f
-                            ? ms
-                            : __fadd_rn(__fmul_rn(a.beta, ema_old), __fmul_rn(a.one_minus_beta, ms));
-      const float ema = ms > 0.0f ? upd : ema_old;
-      a.rms_ema[row] = ema;
-      denom_rms = __fsqrt_rn(ema);
-    }
-    bcast[0] = __fadd_rn(denom_rms, a.eps);
-    if (a.row_rms != nullptr) a.row_rms[row] = __fsqrt_rn(ms);
+  if (RT == 32) __syncwarp();
+  const float denom = row_denominator(a, row, ms, ema_old, bad, live && t == 0);
+  const float rcp = __frcp_rn(denom);
+  if (live && t == 0) {
+    const float rr = __fsqrt_rn(ms);
+    if (a.row_rms != nullptr) a.row_rms[row] = rr;
+    if (a.rms_sum != nullptr) atomicAdd(a.rms_sum, rr);
     if (a.grad_scale != nullptr) a.grad_scale[row] = gsum;
     if (bad) raise_status(RT_STATUS_NONFINITE_GRADIENT);
   }
-  __syncthreads();
-  const float denom = bcast[0];
 
   Moves m = {0, 0, 0, 0};
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
-    const int64_t grp = t + static_cast<int64_t>(i) * ROW_THREADS;
-    const int64_t c0 = grp * 4;
-    if (grp >= ngroups) continue;
-    uint32_t out = pk[i];
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (!live || c >= nch) continue;
+    uint2 out = pk[i];
     if (!bad) {
-      out = 0;
+      uint32_t w[2] = {0, 0};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint8_t old = static_cast<uint8_t>(pk[i] >> (8 * j));
-        if (c0 + j < a.cols) {
-          const float z = a.normalize ? __fdiv_rn(g[i][j], denom) : g[i][j];
-          out |= static_cast<uint32_t>(ratchet_one(old, z, a, m)) << (8 * j);
-        }
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t word = j < 4 ? pk[i].x : pk[i].y;
+        const uint8_t old = static_cast<uint8_t>(word >> (8 * (j & 3)));
+        const int inc = pressure_increment(g[i][j], denom, rcp, a.normalize, a.low, a.high);
+        w[j >> 2] |= static_cast<uint32_t>(ratchet_one(old, inc, a, m)) << (8 * (j & 3));
       }
+      out = make_uint2(w[0], w[1]);
+      *reinterpret_cast<uint2 *>(a.packed + row * a.ldp + 8 * c) = out;
     }
-    uint32_t codes = 0;
+    if (a.code_out != nullptr) {
+      uint32_t cw[2] = {0, 0};
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      codes |= static_cast<uint32_t>(static_cast<uint8_t>(
-                   static_cast<int8_t>(static_cast<int>((out >> (8 * j)) & 0x0Fu) - a.max_code)))
-               << (8 * j);
-    if constexpr (VEC) {
-      if (!bad) *reinterpret_cast<uint32_t *>(a.packed + row * a.ldp + c0) = out;
-      if (a.code_out != nullptr)
-        *reinterpret_cast<uint32_t *>(a.code_out + row * a.ldc + c0) = codes;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (c0 + j >= a.cols) break;
-        if (!bad) a.packed[row * a.ldp + c0 + j] = static_cast<uint8_t>(out >> (8 * j));
-        if (a.code_out != nullptr)
-          a.code_out[row * a.ldc + c0 + j] = static_cast<int8_t>(codes >> (8 * j));
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t word = j < 4 ? out.x : out.y;
+        cw[j >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(
+                          code_of(static_cast<uint8_t>(word >> (8 * (j & 3))), a.max_code)))
+                      << (8 * (j & 3));
       }
+      *reinterpret_cast<uint2 *>(a.code_out + row * a.ldc + 8 * c) = make_uint2(cw[0], cw[1]);
     }
   }
-  // move counters: warp sums, then one atomic per counter per CTA
-  const int lane = t & 31, warp = t >> 5;
-  m.pos = warp_isum(m.pos), m.neg = warp_isum(m.neg);
-  m.bpos = warp_isum(m.bpos), m.bneg = warp_isum(m.bneg);
-  if (lane == 0) {
-    redi[warp][0] = m.pos, redi[warp][1] = m.neg, redi[warp][2] = m.bpos, redi[warp][3] = m.bneg;
-  }
-  __syncthreads();
-  if (t < 4 && a.counts != nullptr) {
-    int s = 0;
-    for (int w = 0; w < 8; ++w) s += redi[w][t];
-    if (s != 0) atomicAdd(a.counts + t, static_cast<unsigned long long>(s));
-  }
+  publish_moves(m, redi, a);
 }
 
-// Rows longer than 8192: same arithmetic and reduction order, gradient re-read per pass.
-__global__ void __launch_bounds__(256) ratchet_update_long_kernel(UpdateArgs a) {
-  __shared__ float red[8];
-  __shared__ int redi[8][4];
-  __shared__ float bcast[1];
+// Generic update: any alignment and row length, one CTA per row, same arithmetic and order.
+__global__ void __launch_bounds__(CTA) ratchet_update_generic_kernel(UpdateArgs a) {
+  __shared__ float sm[CTA];
+  __shared__ float smb[1];
+  __shared__ float smx[8];
+  __shared__ int redi[CTA / 32][4];
   const int t = threadIdx.x;
   const int64_t row = blockIdx.x;
-  const int64_t ngroups = (a.cols + 3) / 4;
+  const int64_t nch = (a.cols + 7) / 8;
   float ss = 0.0f, gs = 0.0f;
   bool bad = false;
-  for (int64_t grp = t; grp < ngroups; grp += ROW_THREADS) {
-    for (int j = 0; j < 4; ++j) {
-      const int64_t c = grp * 4 + j;
-      if (c >= a.cols) break;
-      const float g = grad_value(a, row * a.ldg + c);
-      bad |= !isfinite(g);
-      ss = __fadd_rn(ss, __fmul_rn(g, g));
-      if (a.grad_scale != nullptr) {
-        const int code = static_cast<int>(a.packed[row * a.ldp + c] & 0x0F) - a.max_code;
-        gs = __fadd_rn(gs, __fmul_rn(g, static_cast<float>(code)));
-      }
+  for (int64_t c = t; c < nch; c += CTA)
+    for (int j = 0; j < 8; ++j) {
+      const int64_t k = 8 * c + j;
+      if (k >= a.cols) break;
+      float gv = load_elem(a.grad, a.grad_dtype, row * a.ldg + k);
+      if (a.round_bf16) gv = bf16_round(gv);
+      bad |= !isfinite(gv);
+      ss = __fadd_rn(ss, __fmul_rn(gv, gv));
+      if (a.grad_scale != nullptr)
+        gs = __fadd_rn(gs, __fmul_rn(gv, static_cast<float>(code_of(a.packed[row * a.ldp + k],
+                                                                      a.max_code))));
     }
-  }
-  bad = __syncthreads_or(bad) != 0;
-  const float total = cta_sum_canonical(ss, red);
-  float gsum = 0.0f;
-  if (a.grad_scale != nullptr) gsum = cta_sum_canonical(gs, red);
+  const float ema_old = a.rms_ema != nullptr ? a.rms_ema[row] : 0.0f;
+  bad = cta_max(bad ? 1.0f : 0.0f, smx) > 0.0f;
+  const float total = cta_row_sum(ss, sm, smb);
+  const float gsum = a.grad_scale != nullptr ? cta_row_sum(gs, sm, smb) : 0.0f;
   const float ms = __fdiv_rn(total, static_cast<float>(a.cols));
+  const float denom = row_denominator(a, row, ms, ema_old, bad, t == 0);
+  const float rcp = __frcp_rn(denom);
   if (t == 0) {
-    float denom_rms = __fsqrt_rn(ms);
-    if (a.rms_ema != nullptr && !bad) {
-      const float ema_old = a.rms_ema[row];
-      const float upd = ema_old == 0.0f
-                            ? ms
-                            : __fadd_rn(__fmul_rn(a.beta, ema_old), __fmul_rn(a.one_minus_beta, ms));
-      const float ema = ms > 0.0f ? upd : ema_old;
-      a.rms_ema[row] = ema;
-      denom_rms = __fsqrt_rn(ema);
-    }
-    bcast[0] = __fadd_rn(denom_rms, a.eps);
-    if (a.row_rms != nullptr) a.row_rms[row] = __fsqrt_rn(ms);
+    const float rr = __fsqrt_rn(ms);
+    if (a.row_rms != nullptr) a.row_rms[row] = rr;
+    if (a.rms_sum != nullptr) atomicAdd(a.rms_sum, rr);
     if (a.grad_scale != nullptr) a.grad_scale[row] = gsum;
     if (bad) raise_status(RT_STATUS_NONFINITE_GRADIENT);
   }
-  __syncthreads();
-  const float denom = bcast[0];
   Moves m = {0, 0, 0, 0};
-  for (int64_t c = t; c < a.cols; c += ROW_THREADS) {
-    uint8_t v = a.packed[row * a.ldp + c];
+  for (int64_t k = t; k < a.cols; k += CTA) {
+    uint8_t v = a.packed[row * a.ldp + k];
     if (!bad) {
-      const float g = grad_value(a, row * a.ldg + c);
-      const float z = a.normalize ? __fdiv_rn(g, denom) : g;
-      v = ratchet_one(v, z, a, m);
-      a.packed[row * a.ldp + c] = v;
+      float gv = load_elem(a.grad, a.grad_dtype, row * a.ldg + k);
+      if (a.round_bf16) gv = bf16_round(gv);
+      v = ratchet_one(v, pressure_increment(gv, denom, rcp, a.normalize, a.low, a.high), a, m);
+      a.packed[row * a.ldp + k] = v;
     }
-    if (a.code_out != nullptr)
-      a.code_out[row * a.ldc + c] = static_cast<int8_t>(static_cast<int>(v & 0x0F) - a.max_code);
+    if (a.code_out != nullptr) a.code_out[row * a.ldc + k] = code_of(v, a.max_code);
   }
-  const int lane = t & 31, warp = t >> 5;
-  m.pos = warp_isum(m.pos), m.neg = warp_isum(m.neg);
-  m.bpos = warp_isum(m.bpos), m.bneg = warp_isum(m.bneg);
-  if (lane == 0) {
-    redi[warp][0] = m.pos, redi[warp][1] = m.neg, redi[warp][2] = m.bpos, redi[warp][3] = m.bneg;
-  }
-  __syncthreads();
-  if (t < 4 && a.counts != nullptr) {
-    int s = 0;
-    for (int w = 0; w < 8; ++w) s += redi[w][t];
-    if (s != 0) atomicAdd(a.counts + t, static_cast<unsigned long long>(s));
-  }
+  publish_moves(m, redi, a);
 }
 
 // ===========================================================================================
-// Small elementwise state kernels.
+// Small state kernels.
 // ===========================================================================================
 __global__ void leak_kernel(uint8_t *packed, int64_t ldp, int64_t rows, int64_t cols) {
   const int64_t n = rows * cols;
@@ -567,20 +619,19 @@ __global__ void unpack_kernel(const uint8_t *packed, int64_t ldp, int64_t rows, 
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t r = i / cols, c = i % cols;
     const uint8_t v = __ldg(packed + r * ldp + c);
-    if (code) code[r * ldc + c] = static_cast<int8_t>(static_cast<int>(v & 0x0F) - max_code);
+    if (code) code[r * ldc + c] = code_of(v, max_code);
     if (pressure) pressure[r * ldpr + c] = static_cast<int8_t>(static_cast<int>(v >> 4) - 7);
   }
 }
 
-// Contiguous fast path of the unpack used to refresh the int8 code mirror (16 weights / thread).
+// Contiguous fast path of the unpack used to refresh the int8 code mirror (16 weights/thread).
 __global__ void unpack_codes_vec_kernel(const uint4 *packed, int64_t n16, int max_code,
                                         uint4 *code) {
   const uint32_t bias = 0x01010101u * static_cast<uint32_t>(max_code);
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     uint4 v = __ldg(packed + i);
-    // per byte: (v & 0x0F) - max_code; the low nibble is >= 0, so a bytewise subtraction with a
-    // borrow-free formulation is done via __vsub4.
+    // per byte (v & 0x0F) - max_code, as a bytewise modular subtraction
     v.x = __vsub4(v.x & 0x0F0F0F0Fu, bias);
     v.y = __vsub4(v.y & 0x0F0F0F0Fu, bias);
     v.z = __vsub4(v.z & 0x0F0F0F0Fu, bias);
@@ -605,33 +656,32 @@ __global__ void validate_kernel(const uint8_t *packed, int64_t ldp, int64_t rows
   if (scale != nullptr) {
     for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; r < rows;
          r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-      const float s = scale[r];
-      if (!(s > 0.0f) || !isfinite(s)) bits |= RT_STATUS_SCALE_INVALID;
+      const float sv = scale[r];
+      if (!(sv > 0.0f) || !isfinite(sv)) bits |= RT_STATUS_SCALE_INVALID;
     }
   }
   bits = __reduce_or_sync(0xffffffffu, bits);
   if ((threadIdx.x & 31) == 0 && bits) raise_status(bits);
 }
 
-// out[m,k] = bf16(bf16(q) * bf16(s[m])) (ratchet.py:73-76); 8 elements per thread when aligned.
-__global__ void dequant_vec_kernel(const int8_t *q, int64_t ldq, const float *s, uint16_t *out,
-                                   int64_t ldo, int64_t rows, int64_t cols8) {
-  const int64_t n = rows * cols8;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = i / cols8, c = (i % cols8) * 8;
+// out[m,k] = bf16(bf16(q) * bf16(s[m])) (ratchet.py:73-76); 8 elements per thread, 32-bit
+// indexing when the tensor allows it.
+template <typename I>
+__global__ void dequant_vec_kernel(const int8_t *q, int64_t ldq, const float *s, __nv_bfloat16 *out,
+                                   int64_t ldo, I rows, I cols8) {
+  const I n = rows * cols8;
+  for (I i = blockIdx.x * static_cast<I>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<I>(gridDim.x) * blockDim.x) {
+    const I r = i / cols8, c = (i - r * cols8) * 8;
     const float sb = bf16_round(__ldg(s + r));
     const uint2 raw = __ldg(reinterpret_cast<const uint2 *>(q + r * ldq + c));
-    const uint32_t w[2] = {raw.x, raw.y};
-    uint32_t o[4];
+    float v[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int8_t lo = static_cast<int8_t>((w[j >> 1] >> (16 * (j & 1))) & 0xFF);
-      const int8_t hi = static_cast<int8_t>((w[j >> 1] >> (16 * (j & 1) + 8)) & 0xFF);
-      o[j] = bf16_bits(__fmul_rn(static_cast<float>(lo), sb)) |
-             (static_cast<uint32_t>(bf16_bits(__fmul_rn(static_cast<float>(hi), sb))) << 16);
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t word = j < 4 ? raw.x : raw.y;
+      v[j] = __fmul_rn(static_cast<float>(static_cast<int8_t>(word >> (8 * (j & 3)))), sb);
     }
-    *reinterpret_cast<uint4 *>(out + r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    st8(out + r * ldo + c, v);
   }
 }
 __global__ void dequant_kernel(const int8_t *q, int64_t ldq, const float *s, uint16_t *out,
@@ -646,41 +696,8 @@ __global__ void dequant_kernel(const int8_t *q, int64_t ldq, const float *s, uin
 }
 
 // ===========================================================================================
-// Fused producers (int8_fused.py, int8_backward.py).  One 256-thread CTA per row, row values
-// re-read from L2 for the second pass.
+// Fused producers (int8_fused.py) and their backwards (int8_backward.py).
 // ===========================================================================================
-// rmsnorm: y = (x * r) * w with r = 1 / sqrt(mean(x^2) + eps) (IEEE sqrt and division).
-__global__ void __launch_bounds__(256)
-    rmsnorm_quant_kernel(const void *x, int dtype, int64_t ldx, const float *w, float eps,
-                         int64_t cols, int8_t *q, int64_t ldq, float *row_scale) {
-  __shared__ float red[8];
-  const int64_t row = blockIdx.x;
-  const int64_t ngroups = (cols + 3) / 4;
-  float ss = 0.0f;
-  for (int64_t grp = threadIdx.x; grp < ngroups; grp += 256)
-    for (int j = 0; j < 4; ++j) {
-      const int64_t c = grp * 4 + j;
-      if (c >= cols) break;
-      const float v = load_elem(x, dtype, row * ldx + c);
-      ss = __fadd_rn(ss, __fmul_rn(v, v));
-    }
-  const float total = cta_sum_canonical(ss, red);
-  const float var = __fdiv_rn(total, static_cast<float>(cols));
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-  float amax = 0.0f;
-  for (int64_t c = threadIdx.x; c < cols; c += 256) {
-    const float y = __fmul_rn(__fmul_rn(load_elem(x, dtype, row * ldx + c), r), __ldg(w + c));
-    amax = fmaxf(amax, fabsf(y));
-  }
-  amax = cta_max(amax, red);
-  const float scale = row_scale_of(amax);
-  if (threadIdx.x == 0) row_scale[row] = scale;
-  for (int64_t c = threadIdx.x; c < cols; c += 256) {
-    const float y = __fmul_rn(__fmul_rn(load_elem(x, dtype, row * ldx + c), r), __ldg(w + c));
-    q[row * ldq + c] = quant_rn(y, scale);
-  }
-}
-
 // tanh-approximate GELU with the reference's operation order (int8_fused.py:70-75).
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float c = 0.7978845608028654f;
@@ -689,92 +706,413 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   const float th = tanhf(inner);
   return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, th));
 }
-
-__global__ void __launch_bounds__(256)
-    gelu_quant_kernel(const void *x, int dtype, int64_t ldx, int64_t cols, int8_t *q, int64_t ldq,
-                      float *row_scale) {
-  __shared__ float red[8];
-  const int64_t row = blockIdx.x;
-  float amax = 0.0f;
-  for (int64_t c = threadIdx.x; c < cols; c += 256)
-    amax = fmaxf(amax, fabsf(gelu_tanh(load_elem(x, dtype, row * ldx + c))));
-  amax = cta_max(amax, red);
-  const float scale = row_scale_of(amax);
-  if (threadIdx.x == 0) row_scale[row] = scale;
-  for (int64_t c = threadIdx.x; c < cols; c += 256)
-    q[row * ldq + c] = quant_rn(gelu_tanh(load_elem(x, dtype, row * ldx + c)), scale);
+// its derivative times the incoming gradient, stored through bf16 (int8_backward.py:66-75)
+__device__ __forceinline__ float gelu_tanh_grad(float xv, float g) {
+  const float c = 0.7978845608028654f;
+  const float x2 = __fmul_rn(xv, xv);
+  const float inner = __fmul_rn(c, __fadd_rn(xv, __fmul_rn(__fmul_rn(0.044715f, xv), x2)));
+  const float th = tanhf(inner);
+  const float t1 = __fmul_rn(0.5f, __fadd_rn(1.0f, th));
+  const float t2 =
+      __fmul_rn(__fmul_rn(__fmul_rn(__fmul_rn(0.5f, xv), __fsub_rn(1.0f, __fmul_rn(th, th))), c),
+                __fadd_rn(1.0f, __fmul_rn(0.134145f, x2)));
+  return bf16_round(__fmul_rn(g, __fadd_rn(t1, t2)));
 }
 
-__global__ void __launch_bounds__(256)
-    transpose_quant_kernel(const void *x, int dtype, int64_t heads, int64_t seq, int64_t head_dim,
-                           int64_t sb, int64_t sh, int64_t ss, int64_t sd, int8_t *q, int64_t ldq,
-                           float *row_scale) {
-  __shared__ float red[8];
-  const int64_t row = blockIdx.x;  // row = b * seq + s
-  const int64_t b = row / seq, s = row % seq;
-  const int64_t channels = heads * head_dim;
-  float amax = 0.0f;
-  for (int64_t c = threadIdx.x; c < channels; c += 256) {
-    const int64_t h = c / head_dim, d = c % head_dim;
-    amax = fmaxf(amax, fabsf(load_elem(x, dtype, b * sb + h * sh + s * ss + d * sd)));
+struct ProdArgs {
+  const void *x;
+  int64_t ldx, rows, cols;
+  const float *w;
+  float eps;
+  int8_t *q;
+  int64_t ldq;
+  float *row_scale;
+};
+
+// RMSNorm -> quant: y = (x · r) · w, r = 1 / sqrt(mean(x²) + eps) (IEEE sqrt and division).
+template <typename T, int RT, int VPT>
+__global__ void __launch_bounds__(CTA) rmsnorm_quant_kernel(ProdArgs a) {
+  constexpr int RPC = CTA / RT, NT = CTA / RT;
+  __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
+  __shared__ float smb[RPC];
+  __shared__ float smx[RPC * 8];
+  const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * RPC + sub;
+  const bool live = row < a.rows;
+  const int64_t nch = a.cols / 8;
+  const T *xr = static_cast<const T *>(a.x) + (live ? row : 0) * a.ldx;
+  float v[VPT][8];
+  float ss[NT];
+#pragma unroll
+  for (int k = 0; k < NT; ++k) ss[k] = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (live && c < nch) {
+      ld8(xr + 8 * c, v[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss[i % NT] = __fadd_rn(ss[i % NT], __fmul_rn(v[i][j], v[i][j]));
   }
-  amax = cta_max(amax, red);
+  const float total = row_sum<RT>(ss, sm, smb, sub, t);
+  const float var = __fdiv_rn(total, static_cast<float>(a.cols));
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (c < nch) {
+      float wv[8];
+      ld8(a.w + 8 * c, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[i][j] = __fmul_rn(__fmul_rn(v[i][j], r), wv[j]);
+        amax = fmaxf(amax, fabsf(v[i][j]));
+      }
+    }
+  }
+  amax = row_max<RT>(amax, smx, sub, t);
+  if (!live) return;
   const float scale = row_scale_of(amax);
-  if (threadIdx.x == 0) row_scale[row] = scale;
-  for (int64_t c = threadIdx.x; c < channels; c += 256) {
-    const int64_t h = c / head_dim, d = c % head_dim;
-    q[row * ldq + c] = quant_rn(load_elem(x, dtype, b * sb + h * sh + s * ss + d * sd), scale);
+  const float rcp = __frcp_rn(scale);
+  if (t == 0) a.row_scale[row] = scale;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (c >= nch) continue;
+    int8_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = quant_rn(v[i][j], scale, rcp);
+    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = pack_i8x8(o);
   }
 }
 
-// RMSNorm backward dx (int8_backward.py:7-27), stored through bf16 as the reference does.
-__global__ void __launch_bounds__(256)
-    rmsnorm_bwd_kernel(const void *gy, int gdt, const void *x, int xdt, const float *w, float eps,
-                       int64_t cols, void *dx, int dxdt) {
-  __shared__ float red[8];
+template <typename T, int RT, int VPT>
+__global__ void __launch_bounds__(CTA) gelu_quant_kernel(ProdArgs a) {
+  constexpr int RPC = CTA / RT;
+  __shared__ float smx[RPC * 8];
+  const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * RPC + sub;
+  const bool live = row < a.rows;
+  const int64_t nch = a.cols / 8;
+  const T *xr = static_cast<const T *>(a.x) + (live ? row : 0) * a.ldx;
+  float v[VPT][8];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (live && c < nch) {
+      ld8(xr + 8 * c, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[i][j] = gelu_tanh(v[i][j]);
+        amax = fmaxf(amax, fabsf(v[i][j]));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+    }
+  }
+  amax = row_max<RT>(amax, smx, sub, t);
+  if (!live) return;
+  const float scale = row_scale_of(amax);
+  const float rcp = __frcp_rn(scale);
+  if (t == 0) a.row_scale[row] = scale;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (c >= nch) continue;
+    int8_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = quant_rn(v[i][j], scale, rcp);
+    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = pack_i8x8(o);
+  }
+}
+
+// Generic producers: one CTA per row, the row re-read from L2 between passes.
+__global__ void __launch_bounds__(CTA)
+    rmsnorm_quant_generic_kernel(ProdArgs a, int dtype) {
+  __shared__ float sm[CTA];
+  __shared__ float smb[1];
+  __shared__ float smx[8];
   const int64_t row = blockIdx.x;
-  const int64_t ngroups = (cols + 3) / 4;
+  const int64_t nch = (a.cols + 7) / 8;
+  float ss = 0.0f;
+  for (int64_t c = threadIdx.x; c < nch; c += CTA)
+    for (int j = 0; j < 8; ++j) {
+      const int64_t k = 8 * c + j;
+      if (k >= a.cols) break;
+      const float v = load_elem(a.x, dtype, row * a.ldx + k);
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
+  const float total = cta_row_sum(ss, sm, smb);
+  const float var = __fdiv_rn(total, static_cast<float>(a.cols));
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+  float amax = 0.0f;
+  for (int64_t k = threadIdx.x; k < a.cols; k += CTA)
+    amax = fmaxf(amax, fabsf(__fmul_rn(__fmul_rn(load_elem(a.x, dtype, row * a.ldx + k), r),
+                                       __ldg(a.w + k))));
+  amax = cta_max(amax, smx);
+  const float scale = row_scale_of(amax);
+  const float rcp = __frcp_rn(scale);
+  if (threadIdx.x == 0) a.row_scale[row] = scale;
+  for (int64_t k = threadIdx.x; k < a.cols; k += CTA)
+    a.q[row * a.ldq + k] = quant_rn(
+        __fmul_rn(__fmul_rn(load_elem(a.x, dtype, row * a.ldx + k), r), __ldg(a.w + k)), scale,
+        rcp);
+}
+
+__global__ void __launch_bounds__(CTA) gelu_quant_generic_kernel(ProdArgs a, int dtype) {
+  __shared__ float smx[8];
+  const int64_t row = blockIdx.x;
+  float amax = 0.0f;
+  for (int64_t k = threadIdx.x; k < a.cols; k += CTA)
+    amax = fmaxf(amax, fabsf(gelu_tanh(load_elem(a.x, dtype, row * a.ldx + k))));
+  amax = cta_max(amax, smx);
+  const float scale = row_scale_of(amax);
+  const float rcp = __frcp_rn(scale);
+  if (threadIdx.x == 0) a.row_scale[row] = scale;
+  for (int64_t k = threadIdx.x; k < a.cols; k += CTA)
+    a.q[row * a.ldq + k] = quant_rn(gelu_tanh(load_elem(a.x, dtype, row * a.ldx + k)), scale, rcp);
+}
+
+// [B,H,T,D] heads -> rows b·T+t of H·D channels (int8_fused.py:103-131).
+struct TransArgs {
+  const void *x;
+  int64_t batch, heads, seq, head_dim, sb, sh, ss, sd;
+  int8_t *q;
+  int64_t ldq;
+  float *row_scale;
+};
+template <typename T, int RT, int VPT>
+__global__ void __launch_bounds__(CTA) transpose_quant_kernel(TransArgs a) {
+  constexpr int RPC = CTA / RT;
+  __shared__ float smx[RPC * 8];
+  const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * RPC + sub;
+  const bool live = row < a.batch * a.seq;
+  const int64_t b = live ? row / a.seq : 0, s = live ? row % a.seq : 0;
+  const int64_t nch = a.heads * a.head_dim / 8;
+  const T *base = static_cast<const T *>(a.x) + b * a.sb + s * a.ss;
+  float v[VPT][8];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (live && c < nch) {
+      const int64_t ch = 8 * c, h = ch / a.head_dim, d = ch % a.head_dim;
+      ld8(base + h * a.sh + d, v[i]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+    }
+  }
+  amax = row_max<RT>(amax, smx, sub, t);
+  if (!live) return;
+  const float scale = row_scale_of(amax);
+  const float rcp = __frcp_rn(scale);
+  if (t == 0) a.row_scale[row] = scale;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (c >= nch) continue;
+    int8_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = quant_rn(v[i][j], scale, rcp);
+    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = pack_i8x8(o);
+  }
+}
+__global__ void __launch_bounds__(CTA) transpose_quant_generic_kernel(TransArgs a, int dtype) {
+  __shared__ float smx[8];
+  const int64_t row = blockIdx.x;
+  const int64_t b = row / a.seq, s = row % a.seq;
+  const int64_t channels = a.heads * a.head_dim;
+  float amax = 0.0f;
+  for (int64_t c = threadIdx.x; c < channels; c += CTA) {
+    const int64_t h = c / a.head_dim, d = c % a.head_dim;
+    amax = fmaxf(amax, fabsf(load_elem(a.x, dtype, b * a.sb + h * a.sh + s * a.ss + d * a.sd)));
+  }
+  amax = cta_max(amax, smx);
+  const float scale = row_scale_of(amax);
+  const float rcp = __frcp_rn(scale);
+  if (threadIdx.x == 0) a.row_scale[row] = scale;
+  for (int64_t c = threadIdx.x; c < channels; c += CTA) {
+    const int64_t h = c / a.head_dim, d = c % a.head_dim;
+    a.q[row * a.ldq + c] =
+        quant_rn(load_elem(a.x, dtype, b * a.sb + h * a.sh + s * a.ss + d * a.sd), scale, rcp);
+  }
+}
+
+// RMSNorm backward (int8_backward.py:7-27): dx stored through bf16 (the reference stores the
+// Triton kernel's bf16 value); dw[k] += Σ_rows (gy·x)·r accumulated with fp32 reductions.
+struct RmsBwdArgs {
+  const void *gy;
+  const void *x;
+  const float *w;
+  float eps;
+  int64_t rows, cols;
+  void *dx;
+  int dx_dtype;
+  float *dw;
+};
+template <typename T, int RT, int VPT>
+__global__ void __launch_bounds__(CTA) rmsnorm_bwd_kernel(RmsBwdArgs a) {
+  constexpr int RPC = CTA / RT, NT = CTA / RT;
+  __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
+  __shared__ float smb[RPC];
+  const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
+  const int64_t nch = a.cols / 8;
+  const int64_t groups = (a.rows + RPC - 1) / RPC;
+  float dwp[VPT][8], wv[VPT][8];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (c < nch) {
+      ld8(a.w + 8 * c, wv[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) wv[i][j] = 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dwp[i][j] = 0.0f;
+  }
+  // rows are visited in groups of RPC by a grid-stride loop (uniform across the CTA), so each
+  // thread accumulates the weight gradient of its own columns over many rows
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t row = grp * RPC + sub;
+    const bool live = row < a.rows;
+    const T *xr = static_cast<const T *>(a.x) + (live ? row : 0) * a.cols;
+    const T *gr = static_cast<const T *>(a.gy) + (live ? row : 0) * a.cols;
+    float xv[VPT][8], gv[VPT][8];
+    float ss[NT], dot[NT];
+#pragma unroll
+    for (int k = 0; k < NT; ++k) ss[k] = 0.0f, dot[k] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      if (live && c < nch) {
+        ld8(xr + 8 * c, xv[i]);
+        ld8(gr + 8 * c, gv[i]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xv[i][j] = 0.0f, gv[i][j] = 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float dh = __fmul_rn(gv[i][j], wv[i][j]);
+        ss[i % NT] = __fadd_rn(ss[i % NT], __fmul_rn(xv[i][j], xv[i][j]));
+        dot[i % NT] = __fadd_rn(dot[i % NT], __fmul_rn(dh, xv[i][j]));
+      }
+    }
+    const float total = row_sum<RT>(ss, sm, smb, sub, t);
+    const float dsum = row_sum<RT>(dot, sm, smb, sub, t);
+    const float var = __fdiv_rn(total, static_cast<float>(a.cols));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
+    const float dvar = __fmul_rn(__fmul_rn(dsum, -0.5f), __fmul_rn(__fmul_rn(r, r), r));
+    if (!live) continue;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      if (c >= nch) continue;
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float dh = __fmul_rn(gv[i][j], wv[i][j]);
+        o[j] = bf16_round(__fadd_rn(__fmul_rn(dh, r),
+                                    __fdiv_rn(__fmul_rn(__fmul_rn(dvar, 2.0f), xv[i][j]),
+                                              static_cast<float>(a.cols))));
+        dwp[i][j] = __fadd_rn(dwp[i][j], __fmul_rn(__fmul_rn(gv[i][j], xv[i][j]), r));
+      }
+      if (a.dx_dtype == RT_F32)
+        st8(static_cast<float *>(a.dx) + row * a.cols + 8 * c, o);
+      else
+        st8(static_cast<__nv_bfloat16 *>(a.dx) + row * a.cols + 8 * c, o);
+    }
+  }
+  if (a.dw != nullptr) {
+    // sum the RPC row-partials of the CTA in shared memory, then one reduction per column per
+    // CTA (the grid is about one CTA per SM, so the tiny dw buffer sees few atomics)
+    extern __shared__ float dws[];  // [RPC][cols] when RPC > 1
+    if constexpr (RPC > 1) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t c = t + static_cast<int64_t>(i) * RT;
+        if (c >= nch) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dws[sub * a.cols + 8 * c + j] = dwp[i][j];
+      }
+      __syncthreads();
+      for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
+        float acc = dws[k];
+        for (int r2 = 1; r2 < RPC; ++r2) acc = __fadd_rn(acc, dws[r2 * a.cols + k]);
+        atomicAdd(a.dw + k, acc);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t c = t + static_cast<int64_t>(i) * RT;
+        if (c >= nch) continue;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) atomicAdd(a.dw + 8 * c + j, dwp[i][j]);
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(CTA)
+    rmsnorm_bwd_generic_kernel(RmsBwdArgs a, int gdt, int xdt) {
+  __shared__ float sm[CTA];
+  __shared__ float smb[1];
+  const int64_t row = blockIdx.x;
+  const int64_t nch = (a.cols + 7) / 8;
   float ss = 0.0f, dot = 0.0f;
-  for (int64_t grp = threadIdx.x; grp < ngroups; grp += 256)
-    for (int j = 0; j < 4; ++j) {
-      const int64_t c = grp * 4 + j;
-      if (c >= cols) break;
-      const float xv = load_elem(x, xdt, row * cols + c);
-      const float dh = __fmul_rn(load_elem(gy, gdt, row * cols + c), __ldg(w + c));
+  for (int64_t c = threadIdx.x; c < nch; c += CTA)
+    for (int j = 0; j < 8; ++j) {
+      const int64_t k = 8 * c + j;
+      if (k >= a.cols) break;
+      const float xv = load_elem(a.x, xdt, row * a.cols + k);
+      const float dh = __fmul_rn(load_elem(a.gy, gdt, row * a.cols + k), __ldg(a.w + k));
       ss = __fadd_rn(ss, __fmul_rn(xv, xv));
       dot = __fadd_rn(dot, __fmul_rn(dh, xv));
     }
-  const float total = cta_sum_canonical(ss, red);
-  const float dsum = cta_sum_canonical(dot, red);
-  const float var = __fdiv_rn(total, static_cast<float>(cols));
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  const float total = cta_row_sum(ss, sm, smb);
+  const float dsum = cta_row_sum(dot, sm, smb);
+  const float var = __fdiv_rn(total, static_cast<float>(a.cols));
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
   const float dvar = __fmul_rn(__fmul_rn(dsum, -0.5f), __fmul_rn(__fmul_rn(r, r), r));
-  for (int64_t c = threadIdx.x; c < cols; c += 256) {
-    const float xv = load_elem(x, xdt, row * cols + c);
-    const float dh = __fmul_rn(load_elem(gy, gdt, row * cols + c), __ldg(w + c));
-    const float v = __fadd_rn(__fmul_rn(dh, r),
-                              __fdiv_rn(__fmul_rn(__fmul_rn(dvar, 2.0f), xv), static_cast<float>(cols)));
-    store_elem(dx, dxdt, row * cols + c, bf16_round(v));
+  for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
+    const float xv = load_elem(a.x, xdt, row * a.cols + k);
+    const float g = load_elem(a.gy, gdt, row * a.cols + k);
+    const float dh = __fmul_rn(g, __ldg(a.w + k));
+    const float v = __fadd_rn(__fmul_rn(dh, r), __fdiv_rn(__fmul_rn(__fmul_rn(dvar, 2.0f), xv),
+                                                          static_cast<float>(a.cols)));
+    store_elem(a.dx, a.dx_dtype, row * a.cols + k, bf16_round(v));
+    if (a.dw != nullptr) atomicAdd(a.dw + k, __fmul_rn(__fmul_rn(g, xv), r));
   }
 }
 
-// tanh-GELU backward (int8_backward.py:53-74), stored through bf16 as the reference does.
+template <typename T>
+__global__ void gelu_bwd_vec_kernel(const T *gy, const T *x, int64_t n8, T *dx) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float xv[8], g[8], o[8];
+    ld8(x + 8 * i, xv);
+    ld8(gy + 8 * i, g);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = gelu_tanh_grad(xv[j], g[j]);
+    st8(dx + 8 * i, o);
+  }
+}
 __global__ void gelu_bwd_kernel(const void *gy, int gdt, const void *x, int xdt, int64_t n,
                                 void *dx, int dxdt) {
-  const float c = 0.7978845608028654f;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const float xv = load_elem(x, xdt, i);
-    const float g = load_elem(gy, gdt, i);
-    const float x2 = __fmul_rn(xv, xv);
-    const float inner = __fmul_rn(c, __fadd_rn(xv, __fmul_rn(__fmul_rn(0.044715f, xv), x2)));
-    const float th = tanhf(inner);
-    const float t1 = __fmul_rn(0.5f, __fadd_rn(1.0f, th));
-    const float t2 = __fmul_rn(
-        __fmul_rn(__fmul_rn(__fmul_rn(0.5f, xv), __fsub_rn(1.0f, __fmul_rn(th, th))), c),
-        __fadd_rn(1.0f, __fmul_rn(0.134145f, x2)));
-    store_elem(dx, dxdt, i, bf16_round(__fmul_rn(g, __fadd_rn(t1, t2))));
-  }
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    store_elem(dx, dxdt, i, gelu_tanh_grad(load_elem(x, xdt, i), load_elem(gy, gdt, i)));
 }
 
 static inline unsigned grid_for(int64_t n, int threads) {
@@ -794,8 +1132,9 @@ using namespace rt;
 extern "C" int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_t cols,
                                 int64_t stride_row, int64_t stride_col, const float *col_scale,
                                 int stochastic, uint64_t seed, uint32_t step, uint32_t layer,
-                                int8_t *q, int64_t ldq, float *row_scale, void *x_bf16_out,
-                                int64_t ld_xbf16, void *stream) {
+                                const uint32_t *step_dev, int8_t *q, int64_t ldq,
+                                float *row_scale, void *x_bf16_out, int64_t ld_xbf16,
+                                void *stream) {
   if (rows < 0 || cols < 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_quantize_rows: negative shape");
   if (rows == 0) return RT_OK;
   if (x == nullptr || q == nullptr || row_scale == nullptr)
@@ -803,8 +1142,8 @@ extern "C" int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_
   if (x_dtype != RT_F32 && x_dtype != RT_BF16)
     return fail(RT_ERR_DTYPE, "rt_quantize_rows: input must be float32 or bfloat16");
   if (cols == 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_quantize_rows: zero columns");
-  QuantArgs a{x,   rows,      cols,      stride_row, stride_col, col_scale,
-              stochastic, seed, step, layer, q, ldq, row_scale,
+  QuantArgs a{x,          rows, cols, stride_row, stride_col, col_scale, stochastic, seed,
+              step,       layer, step_dev, q, ldq, row_scale,
               static_cast<unsigned short *>(x_bf16_out), ld_xbf16};
   cudaStream_t s = as_stream(stream);
   return x_dtype == RT_F32 ? quant_rows_dispatch<float>(a, s)
@@ -817,14 +1156,19 @@ extern "C" int rt_dequant_rows_bf16(const int8_t *q, int64_t ldq, const float *r
   if (rows < 0 || cols < 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_dequant_rows_bf16: shape");
   if (rows == 0 || cols == 0) return RT_OK;
   cudaStream_t s = as_stream(stream);
-  uint16_t *o = static_cast<uint16_t *>(out);
   if (cols % 8 == 0 && ldq % 8 == 0 && ldo % 8 == 0 &&
       (reinterpret_cast<uintptr_t>(q) & 7) == 0 && aligned16(out)) {
-    dequant_vec_kernel<<<grid_for(rows * (cols / 8), 256), 256, 0, s>>>(q, ldq, row_scale, o, ldo,
-                                                                         rows, cols / 8);
+    const int64_t n8 = rows * (cols / 8);
+    auto *o = static_cast<__nv_bfloat16 *>(out);
+    if (n8 < (int64_t(1) << 30) && rows * ldq < (int64_t(1) << 31) && rows * ldo < (int64_t(1) << 31))
+      dequant_vec_kernel<int32_t><<<grid_for(n8, 256), 256, 0, s>>>(
+          q, ldq, row_scale, o, ldo, static_cast<int32_t>(rows), static_cast<int32_t>(cols / 8));
+    else
+      dequant_vec_kernel<int64_t><<<grid_for(n8, 256), 256, 0, s>>>(q, ldq, row_scale, o, ldo,
+                                                                    rows, cols / 8);
   } else {
-    dequant_kernel<<<grid_for(rows * cols, 256), 256, 0, s>>>(q, ldq, row_scale, o, ldo, rows,
-                                                              cols);
+    dequant_kernel<<<grid_for(rows * cols, 256), 256, 0, s>>>(
+        q, ldq, row_scale, static_cast<uint16_t *>(out), ldo, rows, cols);
   }
   return check_launch("rt_dequant_rows_bf16");
 }
@@ -834,7 +1178,7 @@ extern "C" int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf1
                                  int8_t *code_out, int64_t ldc, int normalize, float *rms_ema,
                                  double ema_beta, int max_code, int threshold, double bucket_low,
                                  double bucket_high, double eps, int64_t *counts, float *row_rms,
-                                 float *grad_scale, void *stream) {
+                                 float *rms_sum, float *grad_scale, void *stream) {
   if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_ratchet_update: shape");
   if (rows == 0) return RT_OK;
   if (grad == nullptr || packed == nullptr)
@@ -857,30 +1201,22 @@ extern "C" int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf1
   a.low = static_cast<float>(bucket_low), a.high = static_cast<float>(bucket_high);
   a.eps = static_cast<float>(eps);
   a.counts = reinterpret_cast<unsigned long long *>(counts);
-  a.row_rms = row_rms, a.grad_scale = grad_scale;
+  a.row_rms = row_rms, a.rms_sum = rms_sum, a.grad_scale = grad_scale;
   cudaStream_t s = as_stream(stream);
-  const size_t esz = grad_dtype == RT_F32 ? 4 : 2;
-  const bool vec = cols % 4 == 0 && ldg % 4 == 0 && ldp % 4 == 0 &&
-                   (reinterpret_cast<uintptr_t>(grad) % (4 * esz)) == 0 &&
-                   (reinterpret_cast<uintptr_t>(packed) & 3) == 0 &&
-                   (code_out == nullptr || ((reinterpret_cast<uintptr_t>(code_out) & 3) == 0 &&
-                                            ldc % 4 == 0));
-  const int64_t per_thread = (cols + 4 * ROW_THREADS - 1) / (4 * ROW_THREADS);
-  const dim3 grid(static_cast<unsigned>(rows));
-#define RT_UPD(VPT)                                                      \
-  (vec ? (ratchet_update_kernel<VPT, true><<<grid, ROW_THREADS, 0, s>>>(a)) \
-       : (ratchet_update_kernel<VPT, false><<<grid, ROW_THREADS, 0, s>>>(a)))
-  if (per_thread <= 1)
-    RT_UPD(1);
-  else if (per_thread <= 2)
-    RT_UPD(2);
-  else if (per_thread <= 4)
-    RT_UPD(4);
-  else if (per_thread <= 8)
-    RT_UPD(8);
-  else
-    ratchet_update_long_kernel<<<grid, ROW_THREADS, 0, s>>>(a);
-#undef RT_UPD
+  const bool vec = cols % 8 == 0 && ldg % 8 == 0 && ldp % 8 == 0 && aligned16(grad) &&
+                   (reinterpret_cast<uintptr_t>(packed) & 7) == 0 &&
+                   (code_out == nullptr ||
+                    ((reinterpret_cast<uintptr_t>(code_out) & 7) == 0 && ldc % 8 == 0));
+  const RowCfg cfg = vec ? row_cfg(cols / 8, rows) : RowCfg{0, 0};
+  if (cfg.rt != 0) {
+    const unsigned grid = row_grid(rows, cfg.rt);
+    if (grad_dtype == RT_F32)
+      RT_DISPATCH_ROW(cfg, ratchet_update_kernel, float, grid, a);
+    else
+      RT_DISPATCH_ROW(cfg, ratchet_update_kernel, __nv_bfloat16, grid, a);
+  } else {
+    ratchet_update_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a);
+  }
   return check_launch("rt_ratchet_update");
 }
 
@@ -926,8 +1262,20 @@ extern "C" int rt_rmsnorm_quantize(const void *x, int x_dtype, int64_t ldx, cons
   if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_rmsnorm_quantize: shape");
   if (x_dtype != RT_F32 && x_dtype != RT_BF16) return fail(RT_ERR_DTYPE, "rt_rmsnorm_quantize: dtype");
   if (rows == 0) return RT_OK;
-  rmsnorm_quant_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(
-      x, x_dtype, ldx, weight, static_cast<float>(eps), cols, q, ldq, row_scale);
+  cudaStream_t s = as_stream(stream);
+  ProdArgs a{x, ldx, rows, cols, weight, static_cast<float>(eps), q, ldq, row_scale};
+  const size_t es = x_dtype == RT_F32 ? 4 : 2;
+  const bool vec = cols % 8 == 0 && aligned16(x) && (ldx * es) % 16 == 0 && aligned16(weight) &&
+                   (reinterpret_cast<uintptr_t>(q) & 7) == 0 && ldq % 8 == 0;
+  const RowCfg cfg = vec ? row_cfg(cols / 8) : RowCfg{0, 0};
+  if (cfg.rt != 0) {
+    if (x_dtype == RT_F32)
+      RT_DISPATCH_ROW(cfg, rmsnorm_quant_kernel, float, row_grid(rows, cfg.rt), a);
+    else
+      RT_DISPATCH_ROW(cfg, rmsnorm_quant_kernel, __nv_bfloat16, row_grid(rows, cfg.rt), a);
+  } else {
+    rmsnorm_quant_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a, x_dtype);
+  }
   return check_launch("rt_rmsnorm_quantize");
 }
 
@@ -937,9 +1285,20 @@ extern "C" int rt_gelu_quantize(const void *x, int x_dtype, int64_t ldx, int64_t
   if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_gelu_quantize: shape");
   if (x_dtype != RT_F32 && x_dtype != RT_BF16) return fail(RT_ERR_DTYPE, "rt_gelu_quantize: dtype");
   if (rows == 0) return RT_OK;
-  gelu_quant_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(x, x_dtype, ldx,
-                                                                                cols, q, ldq,
-                                                                                row_scale);
+  cudaStream_t s = as_stream(stream);
+  ProdArgs a{x, ldx, rows, cols, nullptr, 0.0f, q, ldq, row_scale};
+  const size_t es = x_dtype == RT_F32 ? 4 : 2;
+  const bool vec = cols % 8 == 0 && aligned16(x) && (ldx * es) % 16 == 0 &&
+                   (reinterpret_cast<uintptr_t>(q) & 7) == 0 && ldq % 8 == 0;
+  const RowCfg cfg = vec ? row_cfg(cols / 8) : RowCfg{0, 0};
+  if (cfg.rt != 0) {
+    if (x_dtype == RT_F32)
+      RT_DISPATCH_ROW(cfg, gelu_quant_kernel, float, row_grid(rows, cfg.rt), a);
+    else
+      RT_DISPATCH_ROW(cfg, gelu_quant_kernel, __nv_bfloat16, row_grid(rows, cfg.rt), a);
+  } else {
+    gelu_quant_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a, x_dtype);
+  }
   return check_launch("rt_gelu_quantize");
 }
 
@@ -952,26 +1311,75 @@ extern "C" int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, 
   if (x_dtype != RT_F32 && x_dtype != RT_BF16)
     return fail(RT_ERR_DTYPE, "rt_transpose_quantize: dtype");
   if (batch * seq == 0) return RT_OK;
-  transpose_quant_kernel<<<static_cast<unsigned>(batch * seq), 256, 0, as_stream(stream)>>>(
-      x, x_dtype, heads, seq, head_dim, stride_b, stride_h, stride_s, stride_d, q, ldq, row_scale);
+  cudaStream_t s = as_stream(stream);
+  TransArgs a{x, batch, heads, seq, head_dim, stride_b, stride_h, stride_s, stride_d, q, ldq,
+              row_scale};
+  const int64_t es = x_dtype == RT_F32 ? 4 : 2;
+  const bool vec = stride_d == 1 && head_dim % 8 == 0 && aligned16(x) &&
+                   (stride_b * es) % 16 == 0 && (stride_h * es) % 16 == 0 &&
+                   (stride_s * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(q) & 7) == 0 &&
+                   ldq % 8 == 0;
+  const RowCfg cfg = vec ? row_cfg(heads * head_dim / 8) : RowCfg{0, 0};
+  const int64_t rows = batch * seq;
+  if (cfg.rt != 0) {
+    if (x_dtype == RT_F32)
+      RT_DISPATCH_ROW(cfg, transpose_quant_kernel, float, row_grid(rows, cfg.rt), a);
+    else
+      RT_DISPATCH_ROW(cfg, transpose_quant_kernel, __nv_bfloat16, row_grid(rows, cfg.rt), a);
+  } else {
+    transpose_quant_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a, x_dtype);
+  }
   return check_launch("rt_transpose_quantize");
 }
 
 extern "C" int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
                                    const float *weight, double eps, int64_t rows, int64_t cols,
-                                   void *dx, int dx_dtype, void *stream) {
+                                   void *dx, int dx_dtype, float *dw, void *stream) {
   if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_rmsnorm_backward: shape");
   if (rows == 0) return RT_OK;
-  rmsnorm_bwd_kernel<<<static_cast<unsigned>(rows), 256, 0, as_stream(stream)>>>(
-      grad_y, gy_dtype, x, x_dtype, weight, static_cast<float>(eps), cols, dx, dx_dtype);
+  cudaStream_t s = as_stream(stream);
+  RmsBwdArgs a{grad_y, x, weight, static_cast<float>(eps), rows, cols, dx, dx_dtype, dw};
+  const int64_t es = x_dtype == RT_F32 ? 4 : 2;
+  const bool vec = gy_dtype == x_dtype && cols % 8 == 0 && aligned16(x) && aligned16(grad_y) &&
+                   aligned16(dx) && aligned16(weight) && (cols * es) % 16 == 0 &&
+                   (dw == nullptr || aligned16(dw));
+  const RowCfg cfg = vec ? row_cfg_narrow(cols / 8) : RowCfg{0, 0};
+  if (cfg.rt != 0) {
+    int sms = 0;
+    rt_sm_count(&sms);
+    const int64_t groups = (rows + (CTA / cfg.rt) - 1) / (CTA / cfg.rt);
+    const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 2;
+    const unsigned grid = static_cast<unsigned>(groups < cap ? groups : cap);
+    const size_t dsm = (dw != nullptr && cfg.rt < CTA) ? (CTA / cfg.rt) * cols * sizeof(float) : 0;
+    if (dsm > 48 * 1024) return fail(RT_ERR_UNSUPPORTED, "rt_rmsnorm_backward: row too long");
+    if (x_dtype == RT_F32)
+      RT_DISPATCH_ROW_NARROW_SMEM(cfg, rmsnorm_bwd_kernel, float, grid, dsm, a);
+    else
+      RT_DISPATCH_ROW_NARROW_SMEM(cfg, rmsnorm_bwd_kernel, __nv_bfloat16, grid, dsm, a);
+  } else {
+    rmsnorm_bwd_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a, gy_dtype, x_dtype);
+  }
   return check_launch("rt_rmsnorm_backward");
 }
 
 extern "C" int rt_gelu_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
                                 int64_t rows, int64_t cols, void *dx, int dx_dtype, void *stream) {
   if (rows < 0 || cols < 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_gelu_backward: shape");
-  if (rows * cols == 0) return RT_OK;
-  gelu_bwd_kernel<<<grid_for(rows * cols, 256), 256, 0, as_stream(stream)>>>(
-      grad_y, gy_dtype, x, x_dtype, rows * cols, dx, dx_dtype);
+  const int64_t n = rows * cols;
+  if (n == 0) return RT_OK;
+  cudaStream_t s = as_stream(stream);
+  if (gy_dtype == x_dtype && dx_dtype == x_dtype && n % 8 == 0 && aligned16(grad_y) &&
+      aligned16(x) && aligned16(dx)) {
+    if (x_dtype == RT_F32)
+      gelu_bwd_vec_kernel<float><<<grid_for(n / 8, 256), 256, 0, s>>>(
+          static_cast<const float *>(grad_y), static_cast<const float *>(x), n / 8,
+          static_cast<float *>(dx));
+    else
+      gelu_bwd_vec_kernel<__nv_bfloat16><<<grid_for(n / 8, 256), 256, 0, s>>>(
+          static_cast<const __nv_bfloat16 *>(grad_y), static_cast<const __nv_bfloat16 *>(x), n / 8,
+          static_cast<__nv_bfloat16 *>(dx));
+  } else {
+    gelu_bwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(grad_y, gy_dtype, x, x_dtype, n, dx, dx_dtype);
+  }
   return check_launch("rt_gelu_backward");
 }

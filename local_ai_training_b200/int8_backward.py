@@ -14,8 +14,9 @@ def _contig(t: Tensor) -> Tensor:
 
 
 def rmsnorm_backward(grad_y: Tensor, x: Tensor, w: Tensor, eps: float = 1e-5) -> tuple[Tensor, Tensor]:
-    """dx from the CUDA kernel (int8_backward.py:7-27; stored through bf16 into x's dtype);
-    dw = sum_m grad_y * x * rsqrt(mean(x^2) + eps) over tokens, as the reference computes it."""
+    """RMSNorm backward in one kernel (int8_backward.py:7-51): dx (stored through bf16 into x's
+    dtype, as the reference's Triton kernel stores it) and dw = sum over tokens of
+    grad_y * x * rsqrt(mean(x^2) + eps), accumulated per column with fp32 reductions."""
     if not x.is_cuda:
         raise RuntimeError("CUDA required")
     x_flat = _contig(x.flatten(0, -2))
@@ -24,13 +25,18 @@ def rmsnorm_backward(grad_y: Tensor, x: Tensor, w: Tensor, eps: float = 1e-5) ->
     grad_x = torch.empty(x_flat.shape, device=x.device,
                          dtype=x.dtype if x.dtype in (torch.float32, torch.bfloat16) else torch.float32)
     wf = w.detach().float().contiguous()
+    if gy_flat.dtype != x_flat.dtype:
+        gy_flat = gy_flat.to(x_flat.dtype) if x_flat.dtype == torch.float32 else gy_flat.float()
+        if gy_flat.dtype != x_flat.dtype:
+            x_flat = x_flat.float()
+    grad_w = torch.zeros(k, device=x.device, dtype=torch.float32)
+    ev = _lib.prof_start(x_flat)
     _lib.check(_lib.lib().rt_rmsnorm_backward(
         gy_flat.data_ptr(), _lib.dtype_code(gy_flat), x_flat.data_ptr(), _lib.dtype_code(x_flat),
         wf.data_ptr(), float(eps), m, k, grad_x.data_ptr(), _lib.dtype_code(grad_x),
-        _lib.stream_of(x_flat)))
-    variance = (x_flat.float() ** 2).mean(dim=1, keepdim=True)
-    rsqrt = torch.rsqrt(variance + eps)
-    grad_w = torch.sum(gy_flat.float() * x_flat.float() * rsqrt, dim=0)
+        grad_w.data_ptr(), _lib.stream_of(x_flat)))
+    _lib.prof_stop(ev, "rmsnorm_bwd", x_flat, 0.0,
+                   m * k * (gy_flat.element_size() + x_flat.element_size() + grad_x.element_size()))
     return grad_x.reshape(x.shape).to(x.dtype), grad_w.to(w.dtype)
 
 
@@ -43,7 +49,10 @@ def gelu_backward(grad_y: Tensor, x: Tensor) -> Tensor:
     m, k = x_flat.shape
     grad_x = torch.empty(x_flat.shape, device=x.device,
                          dtype=x.dtype if x.dtype in (torch.float32, torch.bfloat16) else torch.float32)
+    ev = _lib.prof_start(x_flat)
     _lib.check(_lib.lib().rt_gelu_backward(
         gy_flat.data_ptr(), _lib.dtype_code(gy_flat), x_flat.data_ptr(), _lib.dtype_code(x_flat),
         m, k, grad_x.data_ptr(), _lib.dtype_code(grad_x), _lib.stream_of(x_flat)))
+    _lib.prof_stop(ev, "gelu_bwd", x_flat, 0.0,
+                   m * k * (gy_flat.element_size() + x_flat.element_size() + grad_x.element_size()))
     return grad_x.reshape(x.shape).to(x.dtype)

@@ -32,9 +32,11 @@ def fused_rmsnorm_quantize(x: Tensor, weight: Tensor, eps: float = 1e-5) -> tupl
     out = torch.empty((m, k), device=x.device, dtype=torch.int8)
     scale = torch.empty((m,), device=x.device, dtype=torch.float32)
     w = weight.detach().float().contiguous()
+    ev = _lib.prof_start(flat)
     _lib.check(_lib.lib().rt_rmsnorm_quantize(
         flat.data_ptr(), _lib.dtype_code(flat), flat.stride(0), w.data_ptr(), float(eps), m, k,
         out.data_ptr(), out.stride(0), scale.data_ptr(), _lib.stream_of(flat)))
+    _lib.prof_stop(ev, "rmsnorm_quant", flat, 0.0, m * k * (flat.element_size() + 1) + 4 * m)
     return out.reshape(x.shape), scale.reshape(x.shape[:-1])
 
 
@@ -46,9 +48,11 @@ def fused_gelu_quantize(x: Tensor) -> tuple[Tensor, Tensor]:
     m, k = flat.shape
     out = torch.empty((m, k), device=x.device, dtype=torch.int8)
     scale = torch.empty((m,), device=x.device, dtype=torch.float32)
+    ev = _lib.prof_start(flat)
     _lib.check(_lib.lib().rt_gelu_quantize(
         flat.data_ptr(), _lib.dtype_code(flat), flat.stride(0), m, k, out.data_ptr(),
         out.stride(0), scale.data_ptr(), _lib.stream_of(flat)))
+    _lib.prof_stop(ev, "gelu_quant", flat, 0.0, m * k * (flat.element_size() + 1) + 4 * m)
     return out.reshape(x.shape), scale.reshape(x.shape[:-1])
 
 
@@ -61,9 +65,11 @@ def fused_transpose_quantize(x: Tensor) -> tuple[Tensor, Tensor]:
     b, h, t, d = x.shape
     out = torch.empty((b * t, h * d), device=x.device, dtype=torch.int8)
     scale = torch.empty((b * t,), device=x.device, dtype=torch.float32)
+    ev = _lib.prof_start(x)
     _lib.check(_lib.lib().rt_transpose_quantize(
         x.data_ptr(), _lib.dtype_code(x), b, h, t, d, x.stride(0), x.stride(1), x.stride(2),
         x.stride(3), out.data_ptr(), out.stride(0), scale.data_ptr(), _lib.stream_of(x)))
+    _lib.prof_stop(ev, "transpose_quant", x, 0.0, b * h * t * d * (x.element_size() + 1) + 4 * b * t)
     return out, scale
 
 

@@ -32,12 +32,14 @@ def _quantize_rows_fused(
     step: int = 0,
     layer: int = 0,
     bf16_copy: Tensor | None = None,
+    step_dev: Tensor | None = None,
 ) -> tuple[Tensor, Tensor]:
     """Row quantisation kernel (int8_matmul.py:106-150, 181-207).
 
     stochastic=True draws the seed from the host RNG when none is given (the reference's
     `torch.randint(0, 2**31 - 1, (1,))`, int8_matmul.py:200); (seed, step, layer) key the Philox
     stream.  bf16_copy, when given (rows × cols bf16, unit column stride), receives bf16(values).
+    step_dev (int32 [1] on the device), when given, is read by the kernel instead of `step`.
     """
     if values.ndim != 2:
         raise ValueError("row quantization requires a 2D tensor")
@@ -51,15 +53,20 @@ def _quantize_rows_fused(
         col_scale = col_scale.contiguous()
     if stochastic and seed is None:
         seed = int(torch.randint(0, 2**31 - 1, (1,)).item())
+    ev = _lib.prof_start(values)
     _lib.check(
         _lib.lib().rt_quantize_rows(
             values.data_ptr(), _lib.dtype_code(values), m, k, values.stride(0), values.stride(1),
             _lib.ptr(col_scale), int(stochastic), int(seed or 0) & (2**64 - 1), int(step) & 0xFFFFFFFF,
-            int(layer) & 0xFFFFFFFF, out.data_ptr(), out.stride(0), scale.data_ptr(),
+            int(layer) & 0xFFFFFFFF, _lib.ptr(step_dev), out.data_ptr(), out.stride(0),
+            scale.data_ptr(),
             _lib.ptr(bf16_copy), 0 if bf16_copy is None else bf16_copy.stride(0),
             _lib.stream_of(values),
         )
     )
+    if ev is not None:
+        nbytes = m * k * (values.element_size() + 1 + (2 if bf16_copy is not None else 0)) + 4 * m
+        _lib.prof_stop(ev, "quant_rows_sr" if stochastic else "quant_rows", values, 0.0, nbytes)
     return out, scale
 
 
@@ -105,6 +112,7 @@ def _scaled_int8_mm_into(
     """
     m, k = lhs.shape
     _, n = rhs.shape
+    ev = _lib.prof_start(lhs)
     _lib.check(
         _lib.lib().rt_scaled_int8_mm(
             lhs.data_ptr(), lhs.stride(0), lhs.stride(1), rhs.data_ptr(), rhs.stride(0),
@@ -112,6 +120,9 @@ def _scaled_int8_mm_into(
             _lib.dtype_code(out), out.stride(0), m, n, k, _lib.stream_of(lhs),
         )
     )
+    if ev is not None:
+        _lib.prof_stop(ev, "gemm_i8", lhs, 2.0 * m * n * k,
+                       m * k + n * k + 4 * (m + n) + m * n * out.element_size())
     return out
 
 
@@ -163,6 +174,7 @@ def grad_weight_bf16(grad: Tensor, inputs: Tensor, out: Tensor | None = None, *,
         accumulate = False
     need = _lib.lib().rt_grad_weight_workspace_bytes(mt, n, k)
     ws = _lib.workspace(grad.device, need)
+    ev = _lib.prof_start(grad)
     _lib.check(
         _lib.lib().rt_grad_weight_bf16(
             grad.data_ptr(), grad.stride(0), inputs.data_ptr(), inputs.stride(0), out.data_ptr(),
@@ -170,6 +182,8 @@ def grad_weight_bf16(grad: Tensor, inputs: Tensor, out: Tensor | None = None, *,
             0 if ws is None else ws.numel(), _lib.stream_of(grad),
         )
     )
+    if ev is not None:
+        _lib.prof_stop(ev, "gemm_gradw_bf16", grad, 2.0 * mt * n * k, 2 * mt * (n + k) + 4 * n * k)
     return out
 
 
@@ -179,10 +193,13 @@ def dequant_rows_bf16(q: Tensor, scale: Tensor) -> Tensor:
         q = q.contiguous()
     rows, cols = q.shape
     out = torch.empty((rows, cols), device=q.device, dtype=torch.bfloat16)
+    ev = _lib.prof_start(q)
     _lib.check(
         _lib.lib().rt_dequant_rows_bf16(
             q.data_ptr(), q.stride(0), scale.contiguous().data_ptr(), out.data_ptr(), out.stride(0),
             rows, cols, _lib.stream_of(q),
         )
     )
+    if ev is not None:
+        _lib.prof_stop(ev, "dequant", q, 0.0, 3 * rows * cols + 4 * rows)
     return out

@@ -1,0 +1,239 @@
+"""Kernel microbenchmarks of the ratchet-linear hot path (BASELINE configs 2 and 3).
+
+    python -m local_ai_training_b200.kernel_bench all              # every kernel, three shapes
+    python -m local_ai_training_b200.kernel_bench gradw --m 16384 --n 1536 --k 512 --reps 3
+
+Each case times R launches with CUDA events after warm-up (L2 flushed between launches unless
+--no-flush) and prints one JSON line: mean launch time, algorithmic bytes and flops per launch,
+and the fractions of the measured HBM / tensor peaks.  Used as the small, single-kernel command
+for ncu captures.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import torch
+
+from . import _lib
+from .int8_matmul import (
+    _quantize_rows_fused,
+    _scaled_int8_mm_into,
+    dequant_rows_bf16,
+    grad_weight_bf16,
+)
+
+SHAPES = [(512, 512), (512, 2048), (2048, 512)]  # (K in, N out) of BASELINE configs 2/3
+
+
+def _peaks() -> dict:
+    path = Path(__file__).resolve().parent.parent / "MEASURED_PEAKS.json"
+    peaks = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+    if path.exists():
+        data = json.loads(path.read_text())
+        peaks.update({k: data[k] for k in ("hbm_gbs", "bf16_tflops") if k in data})
+        peaks["source"] = "MEASURED_PEAKS.json"
+    return peaks
+
+
+class _Flusher:
+    def __init__(self, device):
+        self.buf = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+
+    def __call__(self):
+        self.buf.zero_()
+
+
+def _time(fn, reps: int, flush: _Flusher | None) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(reps):
+        if flush is not None:
+            flush()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        total += s.elapsed_time(e) / 1e3
+    return total / reps
+
+
+def _report(name, shape, t, nbytes, flops, peak_tensor, peaks):
+    out = {"kernel": name, "shape": shape, "us": round(t * 1e6, 2),
+           "GB_per_s": round(nbytes / t / 1e9, 1), "hbm_frac": round(nbytes / t / 1e9 / peaks["hbm_gbs"], 3)}
+    if flops:
+        tf = flops / t / 1e12
+        out["TFLOP_per_s"] = round(tf, 1)
+        out["tensor_peak"] = peak_tensor
+        out["tensor_frac"] = round(tf / peak_tensor, 3)
+        out["roofline_time_frac"] = round(max(flops / (peak_tensor * 1e12), nbytes / (peaks["hbm_gbs"] * 1e9)) / t, 3)
+    print(json.dumps(out), flush=True)
+    return out
+
+
+def bench_gemm_fwd(m, k, n, reps, flush, peaks, int8_peak, out_dtype=torch.bfloat16):
+    dev = torch.device("cuda")
+    q = torch.randint(-127, 128, (m, k), device=dev, dtype=torch.int8)
+    s = torch.rand(m, device=dev) + 0.01
+    code = torch.randint(-3, 4, (n, k), device=dev, dtype=torch.int8)
+    scale = torch.rand(n, device=dev) * 0.045 + 0.005
+    out = torch.empty((m, n), device=dev, dtype=out_dtype)
+    t = _time(lambda: _scaled_int8_mm_into(q, code.t(), s, scale, out), reps, flush)
+    nbytes = m * k + n * k + 4 * (m + n) + m * n * out.element_size()
+    return _report("gemm_i8_fwd", [m, k, n], t, nbytes, 2.0 * m * n * k, int8_peak, peaks)
+
+
+def bench_gemm_grad_input(m, k, n, reps, flush, peaks, int8_peak):
+    dev = torch.device("cuda")
+    gq = torch.randint(-127, 128, (m, n), device=dev, dtype=torch.int8)
+    gs = torch.rand(m, device=dev) + 0.01
+    code = torch.randint(-2, 3, (n, k), device=dev, dtype=torch.int8)
+    out = torch.empty((m, k), device=dev, dtype=torch.bfloat16)
+    t = _time(lambda: _scaled_int8_mm_into(gq, code, gs, None, out), reps, flush)
+    nbytes = m * n + n * k + 4 * m + 2 * m * k
+    return _report("gemm_i8_grad_input", [m, n, k], t, nbytes, 2.0 * m * n * k, int8_peak, peaks)
+
+
+def bench_gradw(m, k, n, reps, flush, peaks):
+    dev = torch.device("cuda")
+    g = (torch.randn(m, n, device=dev) * 1e-3).to(torch.bfloat16)
+    x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+    out = torch.empty((n, k), device=dev, dtype=torch.float32)
+    t = _time(lambda: grad_weight_bf16(g, x, out=out), reps, flush)
+    nbytes = 2 * m * (n + k) + 4 * n * k
+    return _report("gemm_gradw_bf16", [m, n, k], t, nbytes, 2.0 * m * n * k, peaks["bf16_tflops"], peaks)
+
+
+def bench_quant_sr(m, n, reps, flush, peaks, dtype=torch.float32):
+    dev = torch.device("cuda")
+    g = (torch.randn(m, n, device=dev) * 1e-3).to(dtype)
+    cs = torch.rand(n, device=dev) * 0.04 + 0.01
+    gbf = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+    t = _time(lambda: _quantize_rows_fused(g, cs, stochastic=True, seed=7, step=1, layer=0,
+                                           bf16_copy=gbf), reps, flush)
+    nbytes = m * n * (g.element_size() + 1 + 2) + 4 * m + 4 * n
+    return _report(f"quant_rows_sr_{str(dtype).split('.')[-1]}", [m, n], t, nbytes, 0, 0, peaks)
+
+
+def bench_quant_rn(m, k, reps, flush, peaks, dtype=torch.bfloat16):
+    dev = torch.device("cuda")
+    x = torch.randn(m, k, device=dev).to(dtype)
+    t = _time(lambda: _quantize_rows_fused(x), reps, flush)
+    return _report(f"quant_rows_rn_{str(dtype).split('.')[-1]}", [m, k], t,
+                   m * k * (x.element_size() + 1) + 4 * m, 0, 0, peaks)
+
+
+def bench_dequant(m, k, reps, flush, peaks):
+    dev = torch.device("cuda")
+    q = torch.randint(-127, 128, (m, k), device=dev, dtype=torch.int8)
+    s = torch.rand(m, device=dev)
+    t = _time(lambda: dequant_rows_bf16(q, s), reps, flush)
+    return _report("dequant", [m, k], t, 3 * m * k + 4 * m, 0, 0, peaks)
+
+
+def bench_update(rows, cols, reps, flush, peaks, grad_dtype=torch.float32):
+    dev = torch.device("cuda")
+    grad = (torch.randn(rows, cols, device=dev) * 1e-3).to(grad_dtype)
+    packed = torch.randint(0, 256, (rows, cols), device=dev, dtype=torch.uint8)
+    packed = (packed & 0x0F).clamp(max=4) | (torch.randint(0, 15, (rows, cols), device=dev, dtype=torch.uint8) << 4)
+    code = torch.empty((rows, cols), device=dev, dtype=torch.int8)
+    counts = torch.zeros(4, device=dev, dtype=torch.int64)
+    rr = torch.empty(rows, device=dev)
+
+    def run():
+        _lib.check(_lib.lib().rt_ratchet_update(
+            grad.data_ptr(), _lib.dtype_code(grad), 1, cols, rows, cols, packed.data_ptr(), cols,
+            code.data_ptr(), cols, 1, None, 0.0, 2, 8, 0.5, 1.5, 1e-8, counts.data_ptr(),
+            rr.data_ptr(), None, None, _lib.stream_of(grad)))
+
+    t = _time(run, reps, flush)
+    nbytes = rows * cols * (grad.element_size() + 3) + 4 * rows
+    return _report(f"ratchet_update_{str(grad_dtype).split('.')[-1]}", [rows, cols], t, nbytes, 0, 0, peaks)
+
+
+def bench_rmsnorm_bwd(m, k, reps, flush, peaks, dtype=torch.float32):
+    from .int8_backward import rmsnorm_backward
+
+    dev = torch.device("cuda")
+    x = torch.randn(m, k, device=dev).to(dtype)
+    gy = (torch.randn(m, k, device=dev) * 1e-2).to(dtype)
+    w = torch.rand(k, device=dev) + 0.5
+    t = _time(lambda: rmsnorm_backward(gy, x, w), reps, flush)
+    return _report(f"rmsnorm_bwd_{str(dtype).split('.')[-1]}", [m, k], t, 3 * m * k * x.element_size(),
+                   0, 0, peaks)
+
+
+def bench_producers(m, k, reps, flush, peaks, dtype=torch.float32):
+    from .int8_fused import fused_gelu_quantize, fused_rmsnorm_quantize, fused_transpose_quantize
+
+    dev = torch.device("cuda")
+    x = torch.randn(m, k, device=dev).to(dtype)
+    w = torch.rand(k, device=dev) + 0.5
+    es = x.element_size()
+    t = _time(lambda: fused_rmsnorm_quantize(x, w), reps, flush)
+    _report(f"rmsnorm_quant_{str(dtype).split('.')[-1]}", [m, k], t, m * k * (es + 1), 0, 0, peaks)
+    xg = torch.randn(m, 4 * k, device=dev).to(dtype)
+    t = _time(lambda: fused_gelu_quantize(xg), reps, flush)
+    _report(f"gelu_quant_{str(dtype).split('.')[-1]}", [m, 4 * k], t, m * 4 * k * (es + 1), 0, 0, peaks)
+    heads = k // 64
+    xt = torch.randn(m // 512, heads, 512, 64, device=dev, dtype=torch.bfloat16)
+    t = _time(lambda: fused_transpose_quantize(xt), reps, flush)
+    _report("transpose_quant_bfloat16", list(xt.shape), t, xt.numel() * 3, 0, 0, peaks)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("kernel", choices=["all", "fwd", "grad_input", "gradw", "quant_sr", "quant_rn",
+                                           "dequant", "update", "rmsnorm_bwd", "producers"])
+    parser.add_argument("--m", type=int, default=16384)
+    parser.add_argument("--k", type=int, default=512)
+    parser.add_argument("--n", type=int, default=2048)
+    parser.add_argument("--reps", type=int, default=20)
+    parser.add_argument("--no-flush", action="store_true")
+    parser.add_argument("--int8-peak", type=float, default=4500.0,
+                        help="INT8 dense peak (TOPS) for the fractions; datasheet by default")
+    args = parser.parse_args()
+    peaks = _peaks()
+    flush = None if args.no_flush else _Flusher(torch.device("cuda"))
+    m = args.m
+    if args.kernel == "all":
+        for k, n in SHAPES:
+            bench_gemm_fwd(m, k, n, args.reps, flush, peaks, args.int8_peak)
+            bench_gemm_grad_input(m, k, n, args.reps, flush, peaks, args.int8_peak)
+            bench_gradw(m, k, n, args.reps, flush, peaks)
+            bench_quant_sr(m, n, args.reps, flush, peaks, torch.float32)
+            bench_quant_sr(m, n, args.reps, flush, peaks, torch.bfloat16)
+            bench_quant_rn(m, k, args.reps, flush, peaks)
+            bench_dequant(m, k, args.reps, flush, peaks)
+            bench_update(n, k, args.reps, flush, peaks)
+        bench_update(8192, 2048, args.reps, flush, peaks)
+        bench_rmsnorm_bwd(m, 512, args.reps, flush, peaks)
+        bench_producers(m, 512, args.reps, flush, peaks)
+        return
+    if args.kernel == "fwd":
+        bench_gemm_fwd(m, args.k, args.n, args.reps, flush, peaks, args.int8_peak)
+    elif args.kernel == "grad_input":
+        bench_gemm_grad_input(m, args.k, args.n, args.reps, flush, peaks, args.int8_peak)
+    elif args.kernel == "gradw":
+        bench_gradw(m, args.k, args.n, args.reps, flush, peaks)
+    elif args.kernel == "quant_sr":
+        bench_quant_sr(m, args.n, args.reps, flush, peaks)
+    elif args.kernel == "quant_rn":
+        bench_quant_rn(m, args.k, args.reps, flush, peaks)
+    elif args.kernel == "dequant":
+        bench_dequant(m, args.k, args.reps, flush, peaks)
+    elif args.kernel == "update":
+        bench_update(args.n, args.k, args.reps, flush, peaks)
+    elif args.kernel == "rmsnorm_bwd":
+        bench_rmsnorm_bwd(m, args.k, args.reps, flush, peaks)
+    elif args.kernel == "producers":
+        bench_producers(m, args.k, args.reps, flush, peaks)
+
+
+if __name__ == "__main__":
+    main()

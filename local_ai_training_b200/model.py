@@ -13,6 +13,7 @@ from dataclasses import dataclass
 from typing import Literal
 
 import torch
+import torch.utils.checkpoint
 from torch import Tensor, nn
 from torch.nn import functional as F
 
@@ -186,6 +187,7 @@ class RatchetGPT(nn.Module):
         # distinct Philox layer ids for the stochastic rounding of each ratchet layer
         for index, module in enumerate(m for m in self.modules() if isinstance(m, DiscreteRatchetLinear)):
             module.sr_layer = index
+        self._step_stats: Tensor | None = None
 
     def forward(self, tokens: Tensor, targets: Tensor | None = None) -> tuple[Tensor, Tensor | None]:
         if tokens.ndim != 2:
@@ -193,11 +195,11 @@ class RatchetGPT(nn.Module):
         sequence_length = tokens.shape[1]
         if sequence_length > self.config.block_size:
             raise ValueError("token sequence exceeds configured block_size")
+        if self.training and torch.is_grad_enabled():
+            self._assign_stats_slots(tokens.device)
         hidden = self.token_embedding(tokens) + self.position_encoding[:sequence_length]
         for block in self.blocks:
             if self.config.gradient_checkpointing and self.training:
-                import torch.utils.checkpoint
-
                 hidden = torch.utils.checkpoint.checkpoint(block, hidden, use_reentrant=False)
             else:
                 hidden = block(hidden)
@@ -210,10 +212,43 @@ class RatchetGPT(nn.Module):
         return logits, loss
 
     def ratchet_layers(self) -> list[DiscreteRatchetLinear]:
-        return [m for m in self.modules() if isinstance(m, DiscreteRatchetLinear)]
+        if getattr(self, "_ratchet_layers", None) is None:
+            self._ratchet_layers = [m for m in self.modules() if isinstance(m, DiscreteRatchetLinear)]
+        return self._ratchet_layers
+
+    def _assign_stats_slots(self, device: torch.device) -> None:
+        """One int64 [layers, 5] buffer per train step collects every fused layer's move counters
+        and gradient-rms sum, so the unvalidated model update reduces them in one pass."""
+        layers = self.ratchet_layers()
+        if device.type != "cuda" or not layers or self._step_stats is not None:
+            return
+        if not all(l.fuse_backward_update and l._pending_counts is None for l in layers):
+            return
+        self._step_stats = torch.zeros(len(layers), 5, device=device, dtype=torch.int64)
+        for i, layer in enumerate(layers):
+            layer._stats_slot = self._step_stats[i]
+        if getattr(self, "_out_features_dev", None) is None or self._out_features_dev.device != device:
+            self._out_features_dev = torch.tensor([float(max(1, l.out_features)) for l in layers],
+                                                  device=device)
 
     def ratchet_update(self, *, validate: bool = True) -> RatchetUpdateStats:
-        updates = [module.ratchet_update(validate=validate) for module in self.ratchet_layers()]
+        layers = self.ratchet_layers()
+        buf = self._step_stats
+        self._step_stats = None
+        if (not validate and buf is not None
+                and all(l._stats_slot is not None and l._pending_counts is not None for l in layers)):
+            counts = buf[:, :4].sum(dim=0)
+            rms = buf[:, 4:].contiguous().view(torch.float32)[:, 0]
+            total_weights = 0
+            for layer in layers:
+                total_weights += layer._pending_stats_total_weights
+                layer._reset_pending_stats()
+                layer._maybe_leak_pressure()
+            return RatchetUpdateStats(
+                total_weights=total_weights, positive_moves=counts[0], negative_moves=counts[1],
+                blocked_positive_moves=counts[2], blocked_negative_moves=counts[3],
+                gradient_rms_mean=(rms / self._out_features_dev).mean())
+        updates = [module.ratchet_update(validate=validate) for module in layers]
         total_weights = sum(update.total_weights for update in updates)
         aggregated = RatchetUpdateStats(
             total_weights=total_weights,

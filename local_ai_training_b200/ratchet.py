@@ -118,10 +118,12 @@ class _RatchetMatmul(torch.autograd.Function):
             # also writes bf16(gradient) for grad_weight), int8 GEMM against the codes
             grad_bf16 = torch.empty(flat_gradient.shape, device=flat_gradient.device,
                                     dtype=torch.bfloat16)
-            sink = ctx.gradient_sink
-            seed, step, layer = _sr_key(sink)
+            seed, step, layer, step_dev = _sr_key(ctx.gradient_sink)
             gq, gs = _quantize_rows_fused(flat_gradient, scale.float(), stochastic=True, seed=seed,
-                                          step=step, layer=layer, bf16_copy=grad_bf16)
+                                          step=step, layer=layer, bf16_copy=grad_bf16,
+                                          step_dev=step_dev)
+            if step_dev is not None:
+                step_dev.add_(1)
             gi_dtype = ctx.input_dtype if ctx.input_dtype in (torch.float32, torch.bfloat16) else torch.bfloat16
             grad_input = torch.empty((gq.shape[0], in_features), device=gq.device, dtype=gi_dtype)
             _scaled_int8_mm_into(gq, code, gs, None, grad_input)
@@ -153,11 +155,11 @@ class _RatchetMatmul(torch.autograd.Function):
                 grad_scale, None, None, None, None, None)
 
 
-def _sr_key(sink) -> tuple[int | None, int, int]:
+def _sr_key(sink) -> tuple[int | None, int, int, Tensor | None]:
     layer = getattr(sink, "__self__", None)
     if isinstance(layer, DiscreteRatchetLinear):
         return layer._next_sr_key()
-    return None, 0, 0
+    return None, 0, 0, None
 
 
 def pack_code_pressure(code: Tensor, pressure: Tensor, max_code: int) -> Tensor:
@@ -333,10 +335,13 @@ class DiscreteRatchetLinear(nn.Module):
         # int8 code mirror of `packed` (not a buffer: derived, rebuilt on demand)
         self._code_mirror: Tensor | None = None
         self._code_mirror_key: tuple | None = None
-        # stochastic-rounding key of the int8 grad_input quant: (seed, step, layer)
+        # Stochastic-rounding key of the int8 grad_input quant: (seed, step, layer).  With
+        # sr_seed None the seed is drawn from the host RNG per call, as the reference does; a fixed
+        # sr_seed keeps the step counter in device memory (graph-capturable, advanced per call).
         self.sr_seed: int | None = None
         self.sr_layer: int = 0
         self._sr_step = 0
+        self._sr_step_dev: Tensor | None = None
 
     # ------------------------------------------------------------------ construction helpers
     @classmethod
@@ -353,11 +358,18 @@ class DiscreteRatchetLinear(nn.Module):
         self._pending_stats_total_weights = 0
         self._pending_counts: Tensor | None = None
         self._pending_stats_rms_sum = 0.0
+        # optional int64[5] row of a caller-owned per-step buffer (RatchetGPT hands one to every
+        # layer so that one reduction aggregates the whole model); cleared with the stats
+        self._stats_slot: Tensor | None = None
 
-    def _next_sr_key(self) -> tuple[int | None, int, int]:
-        step = self._sr_step
-        self._sr_step += 1
-        return self.sr_seed, step, self.sr_layer
+    def _next_sr_key(self) -> tuple[int | None, int, int, Tensor | None]:
+        if self.sr_seed is None:
+            step = self._sr_step
+            self._sr_step += 1
+            return None, step, self.sr_layer, None
+        if self._sr_step_dev is None or self._sr_step_dev.device != self.packed.device:
+            self._sr_step_dev = torch.zeros(1, device=self.packed.device, dtype=torch.int32)
+        return self.sr_seed, 0, self.sr_layer, self._sr_step_dev
 
     # ------------------------------------------------------------------ state views
     @property
@@ -424,7 +436,7 @@ class DiscreteRatchetLinear(nn.Module):
     # ------------------------------------------------------------------ update
     def _run_update(self, gradient: Tensor, row_start: int, row_end: int, *, normalize: bool,
                     round_bf16: bool, counts: Tensor, want_grad_scale: bool = False,
-                    row_rms: Tensor | None = None) -> Tensor | None:
+                    row_rms: Tensor | None = None, rms_sum: Tensor | None = None) -> Tensor | None:
         """One launch of the update kernel over rows [row_start, row_end)."""
         pk = self.packed
         _require_cuda(pk, "the ratchet update")
@@ -444,6 +456,7 @@ class DiscreteRatchetLinear(nn.Module):
         grad_scale = torch.empty(rows, device=pk.device, dtype=torch.float32) if want_grad_scale else None
         pk_rows = pk[row_start:row_end]
         mirror_rows = mirror[row_start:row_end]
+        ev = _lib.prof_start(pk)
         _lib.check(_lib.lib().rt_ratchet_update(
             gradient.data_ptr(), _lib.dtype_code(gradient), int(round_bf16), gradient.stride(0),
             rows, self.in_features, pk_rows.data_ptr(), pk.stride(0), mirror_rows.data_ptr(),
@@ -451,7 +464,10 @@ class DiscreteRatchetLinear(nn.Module):
             None if ema is None else ema[row_start:row_end].data_ptr(), float(self.rms_ema_beta),
             self.max_code, self.pressure_threshold, float(self.bucket_low),
             float(self.bucket_high), float(self.eps), counts.data_ptr(),
-            _lib.ptr(row_rms), _lib.ptr(grad_scale), _lib.stream_of(pk)))
+            _lib.ptr(row_rms), _lib.ptr(rms_sum), _lib.ptr(grad_scale), _lib.stream_of(pk)))
+        if ev is not None:
+            _lib.prof_stop(ev, "ratchet_update", pk, 0.0,
+                           rows * self.in_features * (gradient.element_size() + 3) + 4 * rows)
         return grad_scale
 
     def _capture_weight_gradient(self, gradient: Tensor, tile_start: int | None,
@@ -468,14 +484,17 @@ class DiscreteRatchetLinear(nn.Module):
         assert tile_start is not None and tile_end is not None
         if gradient.shape != (tile_end - tile_start, self.in_features):
             raise ValueError("fused tile gradient shape mismatch")
-        row_rms = torch.empty(tile_end - tile_start, device=gradient.device, dtype=torch.float32)
         if self._pending_counts is None:
-            self._pending_counts = torch.zeros(4, device=gradient.device, dtype=torch.int64)
+            # one buffer for the four move counters and the rms sum (bit pattern of a float)
+            self._pending_buf = (self._stats_slot if self._stats_slot is not None else
+                                 torch.zeros(5, device=gradient.device, dtype=torch.int64))
+            self._pending_counts = self._pending_buf[:4]
+            self._pending_rms = self._pending_buf[4:].view(torch.float32)[:1]
         grad_scale = self._run_update(gradient, tile_start, tile_end, normalize=True,
                                       round_bf16=round_bf16, counts=self._pending_counts,
-                                      want_grad_scale=want_grad_scale, row_rms=row_rms)
+                                      want_grad_scale=want_grad_scale, rms_sum=self._pending_rms)
         self._pending_stats_total_weights += (tile_end - tile_start) * self.in_features
-        self._pending_stats_rms_sum = self._pending_stats_rms_sum + row_rms.sum()
+        self._pending_stats_rms_sum = self._pending_rms[0]
         return grad_scale
 
     @torch.no_grad()
@@ -569,6 +588,8 @@ class DiscreteRatchetLinear(nn.Module):
                 gradient_rms_mean=self._pending_stats_rms_sum / max(1, self.out_features),
             )
             self._reset_pending_stats()
+            self._maybe_leak_pressure()
+            return stats.materialize() if validate else stats
         elif self.matmul_mode != "fp32":
             if self._pending_weight_gradient is None:
                 raise RuntimeError("ratchet layer has no pending effective-weight gradient")

@@ -66,30 +66,34 @@ float or_sr_uniform(uint64_t seed, uint32_t step, uint32_t layer, uint64_t e) {
 }
 
 /* ---------- canonical row sum ----------
- * Elements are grouped in fours; group g feeds slot g % 256; a slot adds its elements in index
- * order from +0.0f; slots 32w..32w+31 are combined by an xor butterfly (16, 8, 4, 2, 1); the eight
- * results combine as ((w0+w1)+(w2+w3))+((w4+w5)+(w6+w7)).  All arithmetic fp32 round-to-nearest. */
+ * The row is cut into 8-element chunks (chunk c = elements 8c..8c+7).
+ *   level 1: 256 partials T_t (t = 0..255); T_t adds the elements of chunks c = t (mod 256) in
+ *            increasing index order, starting from +0.0f;
+ *   level 2: 32 partials S_s = ((T_s + T_s+32) + (T_s+64 + T_s+96)) + ((T_s+128 + T_s+160) +
+ *            (T_s+192 + T_s+224));
+ *   level 3: xor butterfly over S_0..S_31 (offsets 16, 8, 4, 2, 1); the result is lane 0's value.
+ * All arithmetic fp32 round-to-nearest.  A warp per row (each lane keeping 8 level-1 partials) and
+ * a CTA per row (one partial per thread) both realise this order exactly. */
 static float canonical_sum(const float *terms, int64_t n) {
-  float slot[256];
-  for (int i = 0; i < 256; ++i) slot[i] = 0.0f;
-  const int64_t groups = (n + 3) / 4;
-  for (int64_t g = 0; g < groups; ++g)
-    for (int j = 0; j < 4; ++j) {
-      const int64_t i = 4 * g + j;
-      if (i < n) slot[g % 256] = slot[g % 256] + terms[i];
+  float T[256];
+  for (int i = 0; i < 256; ++i) T[i] = 0.0f;
+  const int64_t chunks = (n + 7) / 8;
+  for (int64_t c = 0; c < chunks; ++c)
+    for (int j = 0; j < 8; ++j) {
+      const int64_t i = 8 * c + j;
+      if (i < n) T[c % 256] = T[c % 256] + terms[i];
     }
-  float w[8];
-  for (int wi = 0; wi < 8; ++wi) {
-    float v[32], nv[32];
-    for (int l = 0; l < 32; ++l) v[l] = slot[32 * wi + l];
-    for (int o = 16; o > 0; o >>= 1) {
-      for (int l = 0; l < 32; ++l) nv[l] = v[l] + v[l ^ o];
-      for (int l = 0; l < 32; ++l) v[l] = nv[l];
-    }
-    w[wi] = v[0];
+  float v[32], nv[32];
+  for (int s = 0; s < 32; ++s) {
+    const float a = T[s] + T[s + 32], b = T[s + 64] + T[s + 96];
+    const float c = T[s + 128] + T[s + 160], d = T[s + 192] + T[s + 224];
+    v[s] = (a + b) + (c + d);
   }
-  const float a = w[0] + w[1], b = w[2] + w[3], c = w[4] + w[5], d = w[6] + w[7];
-  return (a + b) + (c + d);
+  for (int o = 16; o > 0; o >>= 1) {
+    for (int l = 0; l < 32; ++l) nv[l] = v[l] + v[l ^ o];
+    for (int l = 0; l < 32; ++l) v[l] = nv[l];
+  }
+  return v[0];
 }
 
 /* ---------- row quantisation: int8_matmul.py:82-84, 106-150, 225-239 ----------

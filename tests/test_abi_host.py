@@ -56,7 +56,7 @@ def test_status_codes_map_to_reference_exceptions():
                                                 1, 1, 1, None))
     with pytest.raises(ValueError, match="max_code"):
         _lib.check(_lib.lib().rt_ratchet_update(1, 0, 0, 1, 1, 1, 1, 1, None, 1, 1, None, 0.0, 9,
-                                                8, 0.5, 1.5, 1e-8, None, None, None, None))
+                                                8, 0.5, 1.5, 1e-8, None, None, None, None, None))
 
 
 def test_cpu_operands_are_rejected_like_the_reference():

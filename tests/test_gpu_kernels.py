@@ -208,15 +208,17 @@ def _update_gpu(grad, packed, *, max_code, threshold=8, low=0.5, high=1.5, eps=1
     code = torch.empty_like(pk, dtype=torch.int8)
     counts = torch.zeros(4, device=dev, dtype=torch.int64)
     row_rms = torch.empty(rows, device=dev)
+    rms_sum = torch.zeros(1, device=dev)
     gs = torch.empty(rows, device=dev) if want_gs else None
     ema_t = None if ema is None else ema.clone()
     _lib.check(_lib.lib().rt_ratchet_update(
         grad.data_ptr(), _lib.dtype_code(grad), int(round_bf16), grad.stride(0), rows, cols,
         pk.data_ptr(), pk.stride(0), code.data_ptr(), code.stride(0), int(normalize),
         None if ema_t is None else ema_t.data_ptr(), beta, max_code, threshold, low, high, eps,
-        counts.data_ptr(), row_rms.data_ptr(), None if gs is None else gs.data_ptr(),
-        _lib.stream_of(grad)))
-    return dict(packed=pk, code=code, counts=counts, row_rms=row_rms, rms_ema=ema_t, grad_scale=gs)
+        counts.data_ptr(), row_rms.data_ptr(), rms_sum.data_ptr(),
+        None if gs is None else gs.data_ptr(), _lib.stream_of(grad)))
+    return dict(packed=pk, code=code, counts=counts, row_rms=row_rms, rms_ema=ema_t, grad_scale=gs,
+                rms_sum=rms_sum)
 
 
 @pytest.mark.parametrize("idx", range(7))
@@ -238,6 +240,8 @@ def test_update_matches_oracle_bit_exact(cuda_device, idx):
     np.testing.assert_array_equal(_np(out["counts"]), ref["counts"])
     np.testing.assert_array_equal(_np(out["row_rms"]), ref["row_rms"])
     np.testing.assert_array_equal(_np(out["grad_scale"]), ref["grad_scale"])
+    np.testing.assert_allclose(_np(out["rms_sum"])[0], ref["row_rms"].astype(np.float64).sum(),
+                               rtol=1e-5)
     if beta > 0:
         np.testing.assert_array_equal(_np(out["rms_ema"]), ref["rms_ema"])
     # and against the reference's own result (reduction order may flip a boundary weight)

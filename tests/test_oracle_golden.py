@@ -93,7 +93,7 @@ def test_bucket_pressure_known_answers():
     # tests/test_ratchet.py:17-22 of the reference
     z = np.array([[-1.5, -1.49, -0.5, -0.49, 0.0, 0.49, 0.5, 1.49, 1.5]], np.float32)
     packed = O.pack_code_pressure(np.zeros_like(z, np.int8), np.zeros_like(z, np.int8), 2)
-    out = O.ratchet_update(z, packed, max_code=2, threshold=100 if False else 8, normalize=False)
+    out = O.ratchet_update(z, packed, max_code=2, threshold=8, normalize=False)
     _, pressure = O.unpack_code_pressure(out["packed"], 2)
     assert pressure.tolist() == [[2, 1, 1, 0, 0, 0, -1, -1, -2]]
 
@@ -211,3 +211,30 @@ def test_dequant_matches_torch_bf16_product():
     s = (rng.random(7) * 0.1 + 1e-3).astype(np.float32)
     ref = (torch.from_numpy(q).to(torch.bfloat16) * torch.from_numpy(s)[:, None].to(torch.bfloat16))
     np.testing.assert_array_equal(O.dequant_rows(q, s), ref.float().numpy())
+
+
+# ---------------------------------------------------------------- model-level fp32 restatement
+def test_fp32_model_step_matches_reference_tiny_model():
+    """oracle/model_fp32.py (CPU baseline) reproduces the reference RatchetGPT fp32 step:
+    identical seeded state, logits, loss and packed states after one fused-update step."""
+    import torch
+
+    from oracle.model_fp32 import Config, build_seeded
+
+    g = load_golden("model_tiny.npz")
+    model = build_seeded(Config(vocab_size=11, block_size=8, n_layer=2, n_head=2, n_embd=16,
+                                max_code=3), seed=5)
+    state = model.state_dict()
+    for key, value in state.items():
+        np.testing.assert_array_equal(value.numpy(), g[f"state0::{key}"], err_msg=key)
+    tokens = torch.from_numpy(g["tokens"])
+    logits, loss = model(tokens[:, :8], tokens[:, 1:])
+    np.testing.assert_allclose(logits.detach().numpy(), g["logits"], rtol=1e-5, atol=1e-6)
+    assert abs(float(loss) - float(g["loss"])) < 1e-5
+    loss.backward()
+    for key, value in model.state_dict().items():
+        if key.endswith("packed"):
+            np.testing.assert_array_equal(value.numpy(), g[f"state1::{key}"], err_msg=key)
+    moves = sum((layer.moves for layer in model.ratchet_layers()), torch.zeros(4, dtype=torch.int64))
+    np.testing.assert_array_equal(moves.numpy(), g["moves"])
+    np.testing.assert_allclose(model.token_embedding.weight.grad.numpy(), g["emb_grad"], rtol=1e-5, atol=1e-7)
