@@ -72,14 +72,15 @@ __host__ __device__ __forceinline__ Philox4 philox4x32_10(uint32_t c0, uint32_t 
   const uint32_t A = 0xD2511F53u, B = 0xCD9E8D57u;
 #pragma unroll
   for (int r = 0; r < 10; ++r) {
-    const uint32_t n0 = umulhi32(B, c2) ^ c1 ^ k0;
-    const uint32_t n2 = umulhi32(A, c0) ^ c3 ^ k1;
-    const uint32_t n1 = B * c2;
-    const uint32_t n3 = A * c0;
+    // one 32x32->64 multiply per product gives both halves
+    const uint64_t pb = static_cast<uint64_t>(B) * c2;
+    const uint64_t pa = static_cast<uint64_t>(A) * c0;
+    const uint32_t n0 = static_cast<uint32_t>(pb >> 32) ^ c1 ^ k0;
+    const uint32_t n2 = static_cast<uint32_t>(pa >> 32) ^ c3 ^ k1;
     c0 = n0;
-    c1 = n1;
+    c1 = static_cast<uint32_t>(pb);
     c2 = n2;
-    c3 = n3;
+    c3 = static_cast<uint32_t>(pa);
     k0 += 0x9E3779B9u;
     k1 += 0xBB67AE85u;
   }
@@ -177,6 +178,29 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap *map, uint64_t *ba
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+// TMA: 2-D tiled bulk tensor store shared -> global (bulk async-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int32_t x,
+                                             int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// wait until at most one committed bulk group of this thread is still reading shared memory
+__device__ __forceinline__ void bulk_wait_read_le1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// order generic-proxy shared-memory writes before async-proxy (TMA) reads of them
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -45,12 +45,16 @@ __device__ __forceinline__ void st8(float *p, const float (&v)[8]) {
   reinterpret_cast<float4 *>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
   reinterpret_cast<float4 *>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
+__device__ __forceinline__ uint32_t bf16x2_bits(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);  // one paired RN conversion
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
 __device__ __forceinline__ void st8(__nv_bfloat16 *p, const float (&v)[8]) {
   uint4 u;
-  u.x = bf16_bits(v[0]) | (uint32_t(bf16_bits(v[1])) << 16);
-  u.y = bf16_bits(v[2]) | (uint32_t(bf16_bits(v[3])) << 16);
-  u.z = bf16_bits(v[4]) | (uint32_t(bf16_bits(v[5])) << 16);
-  u.w = bf16_bits(v[6]) | (uint32_t(bf16_bits(v[7])) << 16);
+  u.x = bf16x2_bits(v[0], v[1]);
+  u.y = bf16x2_bits(v[2], v[3]);
+  u.z = bf16x2_bits(v[4], v[5]);
+  u.w = bf16x2_bits(v[6], v[7]);
   *reinterpret_cast<uint4 *>(p) = u;
 }
 __device__ __forceinline__ uint2 pack_i8x8(const int8_t (&q)[8]) {
@@ -133,20 +137,35 @@ __device__ __forceinline__ float cta_max(float v, float *smx) {
 // estimate lies within 2^-12 of a rounding boundary (a half-integer for rint, an integer after
 // adding u for stochastic rounding) — the result is the one of the exact quotient.
 constexpr float kBoundaryWindow = 2.44140625e-4f;  // 2^-12
+constexpr float kRoundMagic = 12582912.0f;            // 1.5 * 2^23
+// Round-to-nearest-even quant of one value, as an int in [-127, 127].  The estimate is clamped
+// first (clamping commutes with rounding at the integer bounds) and rounded by adding 1.5·2^23,
+// whose low mantissa bits then hold the integer.
+__device__ __forceinline__ int quant_rn_i(float v, float scale, float rcp) {
+  const float y = fminf(fmaxf(__fmul_rn(v, rcp), -127.0f), 127.0f);
+  const float t = __fadd_rn(y, kRoundMagic);
+  if (fabsf(__fsub_rn(y, __fsub_rn(t, kRoundMagic))) >= 0.5f - kBoundaryWindow)
+    return static_cast<int>(rintf(fminf(fmaxf(__fdiv_rn(v, scale), -127.0f), 127.0f)));
+  return __float_as_int(t) - 0x4B400000;
+}
+// Stochastic rounding floor(RN(v / scale) + u), as an int in [-127, 127].
+__device__ __forceinline__ int quant_sr_i(float v, float scale, float rcp, float u) {
+  float t = __fadd_rn(__fmul_rn(v, rcp), u);
+  if (fabsf(__fsub_rn(__fsub_rn(t, floorf(t)), 0.5f)) >= 0.5f - kBoundaryWindow)
+    t = __fadd_rn(__fdiv_rn(v, scale), u);
+  return min(max(__float2int_rd(t), -127), 127);
+}
 __device__ __forceinline__ int8_t quant_rn(float v, float scale, float rcp) {
-  float y = __fmul_rn(v, rcp);
-  if (fabsf(__fsub_rn(__fsub_rn(y, floorf(y)), 0.5f)) <= kBoundaryWindow) y = __fdiv_rn(v, scale);
-  float r = rintf(y);
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(r));
+  return static_cast<int8_t>(quant_rn_i(v, scale, rcp));
 }
 __device__ __forceinline__ int8_t quant_sr(float v, float scale, float rcp, float u) {
-  float t = __fadd_rn(__fmul_rn(v, rcp), u);
-  const float f = __fsub_rn(t, floorf(t));
-  if (f <= kBoundaryWindow || f >= 1.0f - kBoundaryWindow) t = __fadd_rn(__fdiv_rn(v, scale), u);
-  float r = floorf(t);
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(r));
+  return static_cast<int8_t>(quant_sr_i(v, scale, rcp, u));
+}
+// Four ints in [-128, 127] -> one word of int8 bytes (two byte permutes and a merge).
+__device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
+  const uint32_t lo = __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040);
+  const uint32_t hi = __byte_perm(static_cast<uint32_t>(c), static_cast<uint32_t>(d), 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
 }
 __device__ __forceinline__ float row_scale_of(float amax) {
   return fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN);
@@ -280,24 +299,26 @@ __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     if (c >= nch) continue;
-    int8_t o[8];
+    uint2 o;
     if (a.stochastic) {
       const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;  // multiple of 8
       const Philox4 p0 = sr_block(a.seed, step, a.layer, e0 >> 2);
       const Philox4 p1 = sr_block(a.seed, step, a.layer, (e0 >> 2) + 1);
-      o[0] = quant_sr(v[i][0], scale, rcp, u24(p0.x));
-      o[1] = quant_sr(v[i][1], scale, rcp, u24(p0.y));
-      o[2] = quant_sr(v[i][2], scale, rcp, u24(p0.z));
-      o[3] = quant_sr(v[i][3], scale, rcp, u24(p0.w));
-      o[4] = quant_sr(v[i][4], scale, rcp, u24(p1.x));
-      o[5] = quant_sr(v[i][5], scale, rcp, u24(p1.y));
-      o[6] = quant_sr(v[i][6], scale, rcp, u24(p1.z));
-      o[7] = quant_sr(v[i][7], scale, rcp, u24(p1.w));
+      o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, u24(p0.x)),
+                     quant_sr_i(v[i][1], scale, rcp, u24(p0.y)),
+                     quant_sr_i(v[i][2], scale, rcp, u24(p0.z)),
+                     quant_sr_i(v[i][3], scale, rcp, u24(p0.w)));
+      o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, u24(p1.x)),
+                     quant_sr_i(v[i][5], scale, rcp, u24(p1.y)),
+                     quant_sr_i(v[i][6], scale, rcp, u24(p1.z)),
+                     quant_sr_i(v[i][7], scale, rcp, u24(p1.w)));
     } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = quant_rn(v[i][j], scale, rcp);
+      o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
+                     quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
+      o.y = pack4_i8(quant_rn_i(v[i][4], scale, rcp), quant_rn_i(v[i][5], scale, rcp),
+                     quant_rn_i(v[i][6], scale, rcp), quant_rn_i(v[i][7], scale, rcp));
     }
-    *reinterpret_cast<uint2 *>(qr + 8 * c) = pack_i8x8(o);
+    *reinterpret_cast<uint2 *>(qr + 8 * c) = o;
   }
 }
 
@@ -783,10 +804,12 @@ __global__ void __launch_bounds__(CTA) rmsnorm_quant_kernel(ProdArgs a) {
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     if (c >= nch) continue;
-    int8_t o[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = quant_rn(v[i][j], scale, rcp);
-    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = pack_i8x8(o);
+    uint2 o;
+    o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
+                   quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
+    o.y = pack4_i8(quant_rn_i(v[i][4], scale, rcp), quant_rn_i(v[i][5], scale, rcp),
+                   quant_rn_i(v[i][6], scale, rcp), quant_rn_i(v[i][7], scale, rcp));
+    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = o;
   }
 }
 
@@ -825,10 +848,12 @@ __global__ void __launch_bounds__(CTA) gelu_quant_kernel(ProdArgs a) {
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     if (c >= nch) continue;
-    int8_t o[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = quant_rn(v[i][j], scale, rcp);
-    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = pack_i8x8(o);
+    uint2 o;
+    o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
+                   quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
+    o.y = pack4_i8(quant_rn_i(v[i][4], scale, rcp), quant_rn_i(v[i][5], scale, rcp),
+                   quant_rn_i(v[i][6], scale, rcp), quant_rn_i(v[i][7], scale, rcp));
+    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = o;
   }
 }
 
@@ -921,10 +946,12 @@ __global__ void __launch_bounds__(CTA) transpose_quant_kernel(TransArgs a) {
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     if (c >= nch) continue;
-    int8_t o[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = quant_rn(v[i][j], scale, rcp);
-    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = pack_i8x8(o);
+    uint2 o;
+    o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
+                   quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
+    o.y = pack4_i8(quant_rn_i(v[i][4], scale, rcp), quant_rn_i(v[i][5], scale, rcp),
+                   quant_rn_i(v[i][6], scale, rcp), quant_rn_i(v[i][7], scale, rcp));
+    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = o;
   }
 }
 __global__ void __launch_bounds__(CTA) transpose_quant_generic_kernel(TransArgs a, int dtype) {
@@ -960,7 +987,8 @@ struct RmsBwdArgs {
   int dx_dtype;
   float *dw;
 };
-template <typename T, int RT, int VPT>
+// X: input dtype, G: incoming-gradient dtype (fp32 or bf16 each).
+template <typename X, typename G, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) rmsnorm_bwd_kernel(RmsBwdArgs a) {
   constexpr int RPC = CTA / RT, NT = CTA / RT;
   __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
@@ -986,8 +1014,8 @@ __global__ void __launch_bounds__(CTA) rmsnorm_bwd_kernel(RmsBwdArgs a) {
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
     const int64_t row = grp * RPC + sub;
     const bool live = row < a.rows;
-    const T *xr = static_cast<const T *>(a.x) + (live ? row : 0) * a.cols;
-    const T *gr = static_cast<const T *>(a.gy) + (live ? row : 0) * a.cols;
+    const X *xr = static_cast<const X *>(a.x) + (live ? row : 0) * a.cols;
+    const G *gr = static_cast<const G *>(a.gy) + (live ? row : 0) * a.cols;
     float xv[VPT][8], gv[VPT][8];
     float ss[NT], dot[NT];
 #pragma unroll
@@ -1339,10 +1367,8 @@ extern "C" int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void 
   if (rows == 0) return RT_OK;
   cudaStream_t s = as_stream(stream);
   RmsBwdArgs a{grad_y, x, weight, static_cast<float>(eps), rows, cols, dx, dx_dtype, dw};
-  const int64_t es = x_dtype == RT_F32 ? 4 : 2;
-  const bool vec = gy_dtype == x_dtype && cols % 8 == 0 && aligned16(x) && aligned16(grad_y) &&
-                   aligned16(dx) && aligned16(weight) && (cols * es) % 16 == 0 &&
-                   (dw == nullptr || aligned16(dw));
+  const bool vec = cols % 8 == 0 && aligned16(x) && aligned16(grad_y) && aligned16(dx) &&
+                   aligned16(weight) && (dw == nullptr || aligned16(dw));
   const RowCfg cfg = vec ? row_cfg_narrow(cols / 8) : RowCfg{0, 0};
   if (cfg.rt != 0) {
     int sms = 0;
@@ -1352,10 +1378,21 @@ extern "C" int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void 
     const unsigned grid = static_cast<unsigned>(groups < cap ? groups : cap);
     const size_t dsm = (dw != nullptr && cfg.rt < CTA) ? (CTA / cfg.rt) * cols * sizeof(float) : 0;
     if (dsm > 48 * 1024) return fail(RT_ERR_UNSUPPORTED, "rt_rmsnorm_backward: row too long");
-    if (x_dtype == RT_F32)
-      RT_DISPATCH_ROW_NARROW_SMEM(cfg, rmsnorm_bwd_kernel, float, grid, dsm, a);
-    else
-      RT_DISPATCH_ROW_NARROW_SMEM(cfg, rmsnorm_bwd_kernel, __nv_bfloat16, grid, dsm, a);
+    const int combo = (x_dtype == RT_F32 ? 0 : 2) + (gy_dtype == RT_F32 ? 0 : 1);
+#define RT_RMSB(X, G)                                                                        \
+  switch (cfg.rt * 16 + cfg.vpt) {                                                           \
+    case 32 * 16 + 1: rmsnorm_bwd_kernel<X, G, 32, 1><<<grid, CTA, dsm, s>>>(a); break;       \
+    case 32 * 16 + 2: rmsnorm_bwd_kernel<X, G, 32, 2><<<grid, CTA, dsm, s>>>(a); break;       \
+    case 128 * 16 + 2: rmsnorm_bwd_kernel<X, G, 128, 2><<<grid, CTA, dsm, s>>>(a); break;     \
+    default: rmsnorm_bwd_kernel<X, G, 256, 2><<<grid, CTA, dsm, s>>>(a); break;               \
+  }
+    switch (combo) {
+      case 0: RT_RMSB(float, float) break;
+      case 1: RT_RMSB(float, __nv_bfloat16) break;
+      case 2: RT_RMSB(__nv_bfloat16, float) break;
+      default: RT_RMSB(__nv_bfloat16, __nv_bfloat16) break;
+    }
+#undef RT_RMSB
   } else {
     rmsnorm_bwd_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a, gy_dtype, x_dtype);
   }

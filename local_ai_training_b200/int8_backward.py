@@ -25,10 +25,6 @@ def rmsnorm_backward(grad_y: Tensor, x: Tensor, w: Tensor, eps: float = 1e-5) ->
     grad_x = torch.empty(x_flat.shape, device=x.device,
                          dtype=x.dtype if x.dtype in (torch.float32, torch.bfloat16) else torch.float32)
     wf = w.detach().float().contiguous()
-    if gy_flat.dtype != x_flat.dtype:
-        gy_flat = gy_flat.to(x_flat.dtype) if x_flat.dtype == torch.float32 else gy_flat.float()
-        if gy_flat.dtype != x_flat.dtype:
-            x_flat = x_flat.float()
     grad_w = torch.zeros(k, device=x.device, dtype=torch.float32)
     ev = _lib.prof_start(x_flat)
     _lib.check(_lib.lib().rt_rmsnorm_backward(
@@ -47,6 +43,8 @@ def gelu_backward(grad_y: Tensor, x: Tensor) -> Tensor:
     x_flat = _contig(x.flatten(0, -2))
     gy_flat = _contig(grad_y.flatten(0, -2))
     m, k = x_flat.shape
+    if gy_flat.dtype != x_flat.dtype:  # the vector kernel takes one dtype for both operands
+        gy_flat = gy_flat.to(x_flat.dtype)
     grad_x = torch.empty(x_flat.shape, device=x.device,
                          dtype=x.dtype if x.dtype in (torch.float32, torch.bfloat16) else torch.float32)
     ev = _lib.prof_start(x_flat)

@@ -74,33 +74,38 @@ def fused_transpose_quantize(x: Tensor) -> tuple[Tensor, Tensor]:
 
 
 class FusedRMSNormQuantizeFn(torch.autograd.Function):
+    """(int8, scale, dummy) like the reference.  `dummy_dtype` (default: x's dtype, the
+    reference) sets the dtype of the dummy, i.e. of the consuming layer's input gradient."""
+
     @staticmethod
-    def forward(ctx, x: Tensor, weight: Tensor, eps: float = 1e-5):
+    def forward(ctx, x: Tensor, weight: Tensor, eps: float = 1e-5, dummy_dtype=None):
         int8_out, scale_out = fused_rmsnorm_quantize(x, weight, eps)
         ctx.save_for_backward(x, weight)
         ctx.eps = eps
-        dummy = torch.empty_like(x)
+        dummy = torch.empty(x.shape, device=x.device, dtype=dummy_dtype or x.dtype)
         return int8_out, scale_out, dummy
 
     @staticmethod
     def backward(ctx, grad_int8, grad_scale, grad_dummy):
         x, weight = ctx.saved_tensors
         grad_x, grad_w = rmsnorm_backward(grad_dummy, x, weight, ctx.eps)
-        return grad_x, grad_w, None
+        return grad_x, grad_w, None, None
 
 
 class FusedGELUQuantizeFn(torch.autograd.Function):
+    """(int8, scale, dummy) like the reference; `dummy_dtype` as in FusedRMSNormQuantizeFn."""
+
     @staticmethod
-    def forward(ctx, x: Tensor):
+    def forward(ctx, x: Tensor, dummy_dtype=None):
         int8_out, scale_out = fused_gelu_quantize(x)
         ctx.save_for_backward(x)
-        dummy = torch.empty_like(x)
+        dummy = torch.empty(x.shape, device=x.device, dtype=dummy_dtype or x.dtype)
         return int8_out, scale_out, dummy
 
     @staticmethod
     def backward(ctx, grad_int8, grad_scale, grad_dummy):
         (x,) = ctx.saved_tensors
-        return gelu_backward(grad_dummy, x)
+        return gelu_backward(grad_dummy, x), None
 
 
 class FusedTransposeQuantizeFn(torch.autograd.Function):

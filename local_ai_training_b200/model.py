@@ -41,6 +41,11 @@ class ModelConfig:
     int8_backward: bool = False
     qat: bool = False
     ratchet_embedding: bool = False
+    # int8 mode: carry the producer dummies (and so the qkv/expand outputs and every ratchet
+    # grad_input) in bf16.  Those tensors hold bf16-rounded values in the reference too (GEMM
+    # epilogue, SDPA, GELU backward), so results are identical while HBM traffic halves; the
+    # contract layer keeps an fp32 output so the residual-stream gradient stays fp32.
+    bf16_activations: bool = True
 
     def __post_init__(self) -> None:
         if min(self.vocab_size, self.block_size, self.n_layer, self.n_head, self.n_embd) <= 0:
@@ -125,6 +130,10 @@ class FeedForward(nn.Module):
         self.expand = _linear(config, config.n_embd, hidden_size, max_code)
         self.contract = _linear(config, hidden_size, config.n_embd, max_code)
         self.dropout = config.dropout
+        self.dummy_dtype = None
+        if config.matmul_mode == "int8" and config.bf16_activations and max_code is not None:
+            self.dummy_dtype = torch.bfloat16
+            self.contract.output_dtype = torch.float32
 
     def forward(self, inputs: Tensor, *, inputs_int8: Tensor | None = None,
                 inputs_scale: Tensor | None = None) -> Tensor:
@@ -133,7 +142,7 @@ class FeedForward(nn.Module):
         else:
             expanded = self.expand(inputs)
         if getattr(self.contract, "matmul_mode", "fp32") == "int8":
-            gelu_int8, gelu_scale, dummy_gelu = FusedGELUQuantizeFn.apply(expanded)
+            gelu_int8, gelu_scale, dummy_gelu = FusedGELUQuantizeFn.apply(expanded, self.dummy_dtype)
             contracted = self.contract(dummy_gelu, inputs_int8=gelu_int8, inputs_scale=gelu_scale)
         else:
             contracted = self.contract(F.gelu(expanded))
@@ -147,17 +156,19 @@ class TransformerBlock(nn.Module):
         self.attention = CausalSelfAttention(config, max_code=max_code)
         self.feed_forward_norm = nn.RMSNorm(config.n_embd)
         self.feed_forward = FeedForward(config, max_code=max_code)
+        self.dummy_dtype = (torch.bfloat16 if config.matmul_mode == "int8" and config.bf16_activations
+                            and max_code is not None else None)
 
     def forward(self, inputs: Tensor) -> Tensor:
         if getattr(self.attention.qkv, "matmul_mode", "fp32") == "int8":
             attn_int8, attn_scale, dummy_in = FusedRMSNormQuantizeFn.apply(
-                inputs, self.attention_norm.weight, 1e-5)
+                inputs, self.attention_norm.weight, 1e-5, self.dummy_dtype)
             inputs = inputs + self.attention(dummy_in, inputs_int8=attn_int8, inputs_scale=attn_scale)
         else:
             inputs = inputs + self.attention(self.attention_norm(inputs))
         if getattr(self.feed_forward.expand, "matmul_mode", "fp32") == "int8":
             ffn_int8, ffn_scale, dummy_in = FusedRMSNormQuantizeFn.apply(
-                inputs, self.feed_forward_norm.weight, 1e-5)
+                inputs, self.feed_forward_norm.weight, 1e-5, self.dummy_dtype)
             inputs = inputs + self.feed_forward(dummy_in, inputs_int8=ffn_int8, inputs_scale=ffn_scale)
         else:
             inputs = inputs + self.feed_forward(self.feed_forward_norm(inputs))

@@ -57,6 +57,9 @@ class _RatchetMatmul(torch.autograd.Function):
         out_features = code.shape[0]
         ctx.input_shape = input_shape
         ctx.input_dtype = inputs.dtype
+        # the reference returns `.to(inputs.dtype)`; a layer may ask for another output dtype
+        layer = getattr(gradient_sink, "__self__", None)
+        result_dtype = getattr(layer, "output_dtype", None) or inputs.dtype
         ctx.mode = mode
         ctx.fuse_backward_update = fuse_backward_update
         ctx.int8_backward = int8_backward
@@ -76,11 +79,11 @@ class _RatchetMatmul(torch.autograd.Function):
                 q, s = quantize_rows(flat_inputs)
                 ctx.save_for_backward(flat_inputs, code, scale)
                 ctx.used_fused_int8 = False
-            out_dtype = inputs.dtype if inputs.dtype in (torch.float32, torch.bfloat16) else torch.bfloat16
+            out_dtype = result_dtype if result_dtype in (torch.float32, torch.bfloat16) else torch.bfloat16
             output = torch.empty((q.shape[0], out_features), device=q.device, dtype=out_dtype)
             # rhs = codeᵀ: (in, out) view of the [out, in] code tensor, K-major for the GEMM
             _scaled_int8_mm_into(q, code.t(), s, scale.float().contiguous(), output)
-            return output.reshape(*input_shape[:-1], out_features).to(inputs.dtype)
+            return output.reshape(*input_shape[:-1], out_features).to(result_dtype)
 
         _require_cuda(inputs, "the ratchet matmul")
         ctx.save_for_backward(flat_inputs, code, scale)
@@ -93,7 +96,7 @@ class _RatchetMatmul(torch.autograd.Function):
             output = flat_inputs.to(torch.bfloat16) @ effective.t()
         else:
             raise ValueError("matmul_mode must be fp32, bf16, or int8")
-        return output.reshape(*input_shape[:-1], out_features).to(inputs.dtype)
+        return output.reshape(*input_shape[:-1], out_features).to(result_dtype)
 
     @staticmethod
     def backward(ctx, grad_output):
@@ -335,6 +338,8 @@ class DiscreteRatchetLinear(nn.Module):
         # int8 code mirror of `packed` (not a buffer: derived, rebuilt on demand)
         self._code_mirror: Tensor | None = None
         self._code_mirror_key: tuple | None = None
+        # None: the output follows the input dtype (the reference's `.to(inputs.dtype)`)
+        self.output_dtype: torch.dtype | None = None
         # Stochastic-rounding key of the int8 grad_input quant: (seed, step, layer).  With
         # sr_seed None the seed is drawn from the host RNG per call, as the reference does; a fixed
         # sr_seed keeps the step counter in device memory (graph-capturable, advanced per call).

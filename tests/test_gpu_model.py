@@ -87,3 +87,41 @@ def test_int8_25m_shape_step_runs_and_matches_fp32_loss(cuda_device):
     stats = m8.ratchet_update()
     assert stats.total_weights == 25_165_824 + 4_194_304
     assert stats.code_moves >= 0 and math.isfinite(stats.gradient_rms_mean)
+
+
+def test_bf16_activation_plumbing_matches_reference_plumbing(cuda_device):
+    """bf16 producer dummies (the default) against the reference's fp32 dummies: logits, loss,
+    every packed state and the embedding gradient are bit-identical over three steps (the
+    RMSNorm weight gradients use fp32 reductions and are compared to 1e-5)."""
+    from local_ai_training_b200 import ModelConfig, build_seeded_model
+
+    kw = dict(vocab_size=512, block_size=64, n_layer=2, n_head=4, n_embd=128, dropout=0.0,
+              matmul_mode="int8", int8_backward=True)
+    models = []
+    for bf16 in (False, True):
+        m = build_seeded_model(ModelConfig(**kw, bf16_activations=bf16), max_code=2,
+                               seed=3).to(cuda_device).train()
+        for layer in m.ratchet_layers():
+            layer.sr_seed = 11
+        models.append(m)
+    gen = torch.Generator().manual_seed(4)
+    for step in range(3):
+        tokens = torch.randint(0, 512, (4, 65), generator=gen).to(cuda_device)
+        outs = []
+        for m in models:
+            for p in m.parameters():
+                p.grad = None
+            with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+                logits, loss = m(tokens[:, :-1], tokens[:, 1:])
+            loss.backward()
+            m.ratchet_update(validate=False)
+            outs.append((logits.float(), loss.detach()))
+        assert torch.equal(outs[0][0], outs[1][0]), step
+        assert torch.equal(outs[0][1], outs[1][1]), step
+        for la, lb in zip(models[0].ratchet_layers(), models[1].ratchet_layers(), strict=True):
+            assert torch.equal(la.packed, lb.packed), step
+        ga = models[0].token_embedding.weight.grad
+        gb = models[1].token_embedding.weight.grad
+        assert torch.equal(ga, gb), step
+        for (na, pa), (_, pb) in zip(models[0].named_parameters(), models[1].named_parameters()):
+            torch.testing.assert_close(pa.grad, pb.grad, rtol=1e-5, atol=1e-7, msg=na)
