@@ -15,6 +15,7 @@
 // Every CTA loads its own tiles (no clusters, no shared-tile loads between CTAs).
 #pragma once
 
+#include <cstring>
 #include <mutex>
 
 #include "rt_common.cuh"
@@ -38,6 +39,7 @@ struct GemmArgs {
   int accumulate;  // EPI_F32_STORE: out += result
   int vec_store;   // out rows are 16-byte aligned
   int final_epi;   // EPI_SPLIT: EPI_F32_STORE or EPI_BF16_STORE for the reduced tile
+  int tma_store;   // epilogue stages 32-row groups in shared memory and stores them with TMA
   float *workspace;       // EPI_SPLIT: [splits][tiles][BM][BN] fp32 partial tiles
   unsigned *counters;     // EPI_SPLIT: one ticket per tile, zero between launches
 };
@@ -65,7 +67,9 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+  // per epilogue warp: two 32-row x 128-byte staging buffers for TMA stores
+  static constexpr int EPI_BYTES = 4 * 2 * 4096;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   // Instruction descriptor: D format, A/B formats, majorness, N>>3 at [17,23), M>>4 at [24,29).
   static constexpr uint32_t IDESC = (KindOf<T>::dfmt << 4) | (KindOf<T>::abfmt << 7) |
                                     (KindOf<T>::abfmt << 10) | ((A_MN ? 1u : 0u) << 15) |
@@ -210,23 +214,48 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &p, int epi, int r
   }
 }
 
+// One 32-row group of up to 64 bf16 / 32 fp32 output columns through the warp's staging buffer:
+// 128-byte swizzled rows (conflict-free 16-byte shared stores), then one TMA store that clips
+// rows/columns outside the output.  `words` holds the 32 packed words of this lane's row.
+__device__ __forceinline__ void stage_and_store(const CUtensorMap *map, uint8_t *staging, int &buf,
+                                                int lane, const uint32_t (&words)[32], int x,
+                                                int y) {
+  uint8_t *b = staging + buf * 4096;
+  if (lane == 0) bulk_wait_read_le1();  // the store that last used this buffer has read it
+  __syncwarp();
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<uint4 *>(b + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+        make_uint4(words[4 * c], words[4 * c + 1], words[4 * c + 2], words[4 * c + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(map, b, x, y);
+    bulk_commit_group();
+  }
+  buf ^= 1;
+}
+
 template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
-                     const __grid_constant__ CUtensorMap tma_b, GemmArgs p) {
+                     const __grid_constant__ CUtensorMap tma_b,
+                     const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
   using C = GemmCfg<T, A_MN, B_MN, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *a_tiles = smem;
   uint8_t *b_tiles = smem + STAGES * C::A_BYTES;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES);
+  uint8_t *staging_all = smem + STAGES * C::STAGE_BYTES;  // 1024-byte aligned
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + STAGES * C::STAGE_BYTES + C::EPI_BYTES);
   uint64_t *full = bars;
   uint64_t *empty = bars + STAGES;
   uint64_t *tfull = bars + 2 * STAGES;
   uint64_t *tempty = bars + 2 * STAGES + 2;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
   __shared__ int s_last_split;
+  __shared__ float s_bscale[BN];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0 && lane == 0) {
@@ -241,6 +270,7 @@ __global__ void __launch_bounds__(192, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
+    if (p.tma_store) tma_prefetch_desc(&tma_c);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, C::TMEM_COLS);
@@ -321,6 +351,7 @@ __global__ void __launch_bounds__(192, 1)
     const int sub = warp & 3;
     const int ep_tid = threadIdx.x - 64;  // 0..127 across the four epilogue warps
     const bool split_mode = p.epi == EPI_SPLIT;
+    int stage_buf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
@@ -347,6 +378,65 @@ __global__ void __launch_bounds__(192, 1)
       const int row = tm * C::BM + trow;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN);
+      if (p.tma_store) {
+        // column scales of this tile, once, in shared memory (barrier 1: the epilogue warps)
+        const bool scaled = p.epi == EPI_SCALED;
+        if (scaled) {
+          for (int j = ep_tid; j < BN; j += 128) {
+            const int n = tn * BN + j;
+            s_bscale[j] = (p.b_scale != nullptr && n < p.N) ? __ldg(p.b_scale + n) : 1.0f;
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+        const float a_s = (scaled && row < p.M) ? __ldg(p.a_scale + row) : 1.0f;
+        const bool bf16_out = p.out_dtype == RT_BF16 || p.epi == EPI_BF16_STORE;
+        const int y = tm * C::BM + sub * 32;
+        if (y >= p.M) {
+          // this warp's 32 rows lie past the output: nothing to store
+        } else if (bf16_out) {
+#pragma unroll 1
+          for (int g = 0; g < BN / 64; ++g) {
+            const int n0 = tn * BN + g * 64;
+            if (n0 >= p.N) break;
+            uint32_t r0[32], r1[32];
+            tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64), r0);
+            tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64 + 32), r1);
+            tmem_ld_wait();
+            uint32_t w[32];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float v0 = acc_to_float<T>(r0[2 * j]), v1 = acc_to_float<T>(r0[2 * j + 1]);
+              float v2 = acc_to_float<T>(r1[2 * j]), v3 = acc_to_float<T>(r1[2 * j + 1]);
+              if (scaled) {
+                v0 = __fmul_rn(__fmul_rn(v0, a_s), s_bscale[g * 64 + 2 * j]);
+                v1 = __fmul_rn(__fmul_rn(v1, a_s), s_bscale[g * 64 + 2 * j + 1]);
+                v2 = __fmul_rn(__fmul_rn(v2, a_s), s_bscale[g * 64 + 32 + 2 * j]);
+                v3 = __fmul_rn(__fmul_rn(v3, a_s), s_bscale[g * 64 + 32 + 2 * j + 1]);
+              }
+              w[j] = bf16_bits(v0) | (uint32_t(bf16_bits(v1)) << 16);
+              w[16 + j] = bf16_bits(v2) | (uint32_t(bf16_bits(v3)) << 16);
+            }
+            stage_and_store(&tma_c, staging_all + (warp - 2) * 8192, stage_buf, lane, w, n0, y);
+          }
+        } else {
+#pragma unroll 1
+          for (int g = 0; g < BN / 32; ++g) {
+            const int n0 = tn * BN + g * 32;
+            if (n0 >= p.N) break;
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 32), r);
+            tmem_ld_wait();
+            uint32_t w[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float v = acc_to_float<T>(r[j]);
+              if (scaled) v = bf16_round(__fmul_rn(__fmul_rn(v, a_s), s_bscale[g * 32 + j]));
+              w[j] = __float_as_uint(v);
+            }
+            stage_and_store(&tma_c, staging_all + (warp - 2) * 8192, stage_buf, lane, w, n0, y);
+          }
+        }
+      } else {
       float *part = nullptr;
       if (split_mode)
         part = p.workspace +
@@ -367,6 +457,7 @@ __global__ void __launch_bounds__(192, 1)
         } else {
           epilogue_chunk<T>(p, p.epi, row, n0, r);
         }
+      }
       }
       tc_fence_before();
       __syncwarp();
@@ -412,6 +503,7 @@ __global__ void __launch_bounds__(192, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
     }
+    if (p.tma_store && lane == 0) bulk_wait_all();  // staged stores done before the CTA exits
   }
   __syncwarp();
   tc_fence_before();
@@ -523,11 +615,23 @@ static int operand_map(CUtensorMap *map, const Operand &o, int tile_rows) {
 template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
 static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaStream_t s) {
   using C = GemmCfg<T, A_MN, B_MN, BN, STAGES>;
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mc;
+  memset(&mc, 0, sizeof(mc));
   int rc = operand_map<T, A_MN>(&ma, a, C::BM);
   if (rc) return rc;
   rc = operand_map<T, B_MN>(&mb, b, BN);
   if (rc) return rc;
+  // TMA-store epilogue: 16-byte aligned rows, a plain store (no accumulate, no split)
+  const bool out_bf16 = args.out_dtype == RT_BF16 || args.epi == EPI_BF16_STORE;
+  args.tma_store = args.vec_store && (args.epi == EPI_SCALED || args.epi == EPI_BF16_STORE ||
+                                      (args.epi == EPI_F32_STORE && !args.accumulate));
+  if (args.tma_store) {
+    const size_t es = out_bf16 ? 2 : 4;
+    rc = make_map(&mc, out_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                  args.out, static_cast<uint64_t>(args.N), static_cast<uint64_t>(args.M),
+                  static_cast<uint64_t>(args.ldo) * es, static_cast<uint32_t>(128 / es), 32);
+    if (rc) return rc;
+  }
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   if ((rc = rt_sm_count(&sms)) != RT_OK) return rc;
@@ -551,7 +655,7 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
   if (args.splits > args.kblocks) args.splits = args.kblocks;
   const int64_t units = static_cast<int64_t>(args.tiles_m) * args.tiles_n * args.splits;
   const int grid = static_cast<int>(units < sms ? units : sms);
-  kernel<<<grid, 192, C::SMEM_BYTES, s>>>(ma, mb, args);
+  kernel<<<grid, 192, C::SMEM_BYTES, s>>>(ma, mb, mc, args);
   return check_launch("umma_gemm_kernel");
 }
 
@@ -700,3 +804,4 @@ extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, in
                                             ldo, M_tok, N, K, accumulate);
   return check_launch("simt_gradw_kernel");
 }
+
