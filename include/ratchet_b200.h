@@ -104,6 +104,21 @@ int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, int64_t ldx, 
 /* Workspace bytes rt_grad_weight_bf16 can use for this shape on the current device (0: none). */
 int64_t rt_grad_weight_workspace_bytes(int64_t M_tok, int64_t N, int64_t K);
 
+/* rt_grad_weight_bf16 that allocates nothing and takes no workspace (no counterpart in the
+ * reference, whose grad_weight GEMM is a cuBLAS call).  For callers that bind the C ABI without
+ * a device allocator of their own (an FFI host with no caching allocator, where cudaMalloc would
+ * synchronise the device in the middle of a step) or that have budgeted all HBM to resident
+ * state.  The split-K partial tiles live in a 20 MiB device array of this library (one copy per
+ * device); shapes whose workspace (rt_grad_weight_workspace_bytes) exceeds it fail with
+ * RT_ERR_UNSUPPORTED.  The first call on each device looks up that array's address with the
+ * device current; make it before any stream capture.  Each call clears the per-tile tickets on
+ * `stream` first.  All calls on one device share the array: calls that overlap on the GPU
+ * (different streams, no ordering between them) race and give wrong results.  Results equal
+ * rt_grad_weight_bf16 with a workspace of rt_grad_weight_workspace_bytes bytes. */
+int rt_grad_weight_bf16_noalloc(const void *g, int64_t ldg, const void *x, int64_t ldx, void *out,
+                                int out_dtype, int64_t ldo, int64_t M_tok, int64_t N, int64_t K,
+                                int accumulate, void *stream);
+
 /* Dequantises saved int8 activations: out[m,k] = bf16(bf16(q[m,k]) * bf16(s[m]))
  * (ratchet.py:73-76). */
 int rt_dequant_rows_bf16(const int8_t *q, int64_t ldq, const float *row_scale, void *out,

@@ -805,3 +805,59 @@ extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, in
   return check_launch("simt_gradw_kernel");
 }
 
+// ---------------------------------------------------------------------------------------------
+// rt_grad_weight_bf16 without a caller-provided workspace: the split-K partial tiles and tickets
+// live in a fixed device array of this library.  Nothing is allocated per call.
+namespace rt {
+constexpr int64_t kGwScratchBytes = int64_t(20) << 20;  // >= SMs x 128 KiB tiles + tickets
+constexpr int kGwScratchDevices = 64;
+static __device__ __align__(256) uint8_t g_gw_scratch[kGwScratchBytes];
+
+// Address of this device's copy of g_gw_scratch, looked up once per device.
+static int gw_scratch_address(int dev, void **out) {
+  static std::mutex mu;
+  static void *addr[kGwScratchDevices] = {};
+  if (dev < 0 || dev >= kGwScratchDevices)
+    return fail(RT_ERR_UNSUPPORTED, "grad_weight_noalloc: device ordinal %d beyond %d", dev,
+                kGwScratchDevices);
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_gw_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(RT_ERR_CUDA, "grad_weight_noalloc: scratch address lookup failed: %s",
+                  cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return RT_OK;
+}
+}  // namespace rt
+
+extern "C" int rt_grad_weight_bf16_noalloc(const void *g, int64_t ldg, const void *x, int64_t ldx,
+                                           void *out, int out_dtype, int64_t ldo, int64_t M_tok,
+                                           int64_t N, int64_t K, int accumulate, void *stream) {
+  if (M_tok <= 0 || N <= 0 || K <= 0)  // nothing to split: the plain path handles it
+    return rt_grad_weight_bf16(g, ldg, x, ldx, out, out_dtype, ldo, M_tok, N, K, accumulate,
+                               nullptr, 0, stream);
+  const int64_t need = rt_grad_weight_workspace_bytes(M_tok, N, K);
+  if (need > kGwScratchBytes)
+    return fail(RT_ERR_UNSUPPORTED,
+                "grad_weight_noalloc: this shape needs %lld bytes of scratch, the static scratch "
+                "holds %lld",
+                static_cast<long long>(need), static_cast<long long>(kGwScratchBytes));
+  void *scratch = nullptr;
+  if (need > 0) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, "grad_weight_noalloc: %s", cudaGetErrorString(e));
+    int rc = gw_scratch_address(dev, &scratch);
+    if (rc) return rc;
+    // the per-tile tickets must start at zero; a call that ended early may have left some set
+    e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(gw_counter_bytes(gw_tiles(N, K))),
+                        as_stream(stream));
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, "grad_weight_noalloc: %s", cudaGetErrorString(e));
+  }
+  return rt_grad_weight_bf16(g, ldg, x, ldx, out, out_dtype, ldo, M_tok, N, K, accumulate, scratch,
+                             need, stream);
+}
