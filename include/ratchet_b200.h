@@ -93,10 +93,9 @@ int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_t lhs_strid
  * (`accumulate` adds into out) or RT_BF16 (`accumulate` must be 0).  The bf16 rounding the
  * reference applies to the GEMM output is applied by rt_ratchet_update(round_bf16=1), not here.
  * Small outputs split the token dimension across SMs: each split writes an fp32 partial tile to
- * `workspace` and the last split of a tile sums the partials in split order (deterministic, no
- * CTA waits for another).  workspace: 256-byte aligned, its first bytes (one uint32 ticket per
- * output tile) zero before the first call — calls leave them zero; NULL disables splitting.
- * Calls sharing a workspace must not overlap on the GPU.
+ * `workspace` and a second launch sums the partials in split order (deterministic, no CTA waits
+ * for another).  workspace: 256-byte aligned, no initial contents needed; NULL disables
+ * splitting.  Calls sharing a workspace must not overlap on the GPU.
  * ------------------------------------------------------------------------------------------- */
 int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, int64_t ldx, void *out,
                         int out_dtype, int64_t ldo, int64_t M_tok, int64_t N, int64_t K,
@@ -111,8 +110,8 @@ int64_t rt_grad_weight_workspace_bytes(int64_t M_tok, int64_t N, int64_t K);
  * state.  The split-K partial tiles live in a 20 MiB device array of this library (one copy per
  * device); shapes whose workspace (rt_grad_weight_workspace_bytes) exceeds it fail with
  * RT_ERR_UNSUPPORTED.  The first call on each device looks up that array's address with the
- * device current; make it before any stream capture.  Each call clears the per-tile tickets on
- * `stream` first.  All calls on one device share the array: calls that overlap on the GPU
+ * device current; make it before any stream capture.  Nothing in the array needs to start at
+ * zero (every partial tile is written before it is read, within a call).  All calls on one device share the array: calls that overlap on the GPU
  * (different streams, no ordering between them) race and give wrong results.  Results equal
  * rt_grad_weight_bf16 with a workspace of rt_grad_weight_workspace_bytes bytes. */
 int rt_grad_weight_bf16_noalloc(const void *g, int64_t ldg, const void *x, int64_t ldx, void *out,

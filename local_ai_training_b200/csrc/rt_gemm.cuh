@@ -8,9 +8,10 @@
 //   warp 0      TMA producer (one elected thread): 128-byte-swizzled tiles into a STAGES-deep ring
 //   warp 1      TMEM allocator + MMA issuer (one thread): 4 tcgen05.mma per stage, commit frees the
 //               stage, a final commit hands the accumulator to the epilogue
-//   warps 2..5  epilogue: tcgen05.ld 32x32b → fp32 → dequant/round → global stores (or fp32
-//               reductions for split-K), running on one TMEM accumulator while the MMA fills the
-//               other (2 × BN columns).
+//   warps 2..5  epilogue: tcgen05.ld 32x32b → fp32 → dequant/round → 128-byte-swizzled staging
+//               in shared memory → TMA stores (plain lane-per-row stores when the output rows
+//               are not 16-byte aligned or it accumulates), running on one TMEM accumulator
+//               while the MMA fills the other (2 × BN columns).
 // Tiles are BM=128 rows × BN columns; each stage covers 128 bytes of K (128 int8 or 64 bf16).
 // Every CTA loads its own tiles (no clusters, no shared-tile loads between CTAs).
 #pragma once
@@ -22,9 +23,8 @@
 
 namespace rt {
 
-// EPI_SPLIT: split-K partial tiles go to a workspace; the last split of a tile to finish (an
-// atomic ticket per tile, no waiting) sums all partials in split order 0..S-1 and stores the
-// result with `final_epi` — deterministic, and no CTA ever waits for another.
+// EPI_SPLIT: split-K partial tiles (fp32) go to a workspace by TMA store; a second kernel sums
+// them in split order 0..S-1 into the output — deterministic, and no CTA ever waits for another.
 enum EpiMode : int { EPI_SCALED = 0, EPI_SPLIT = 1, EPI_F32_STORE = 2, EPI_BF16_STORE = 3 };
 
 struct GemmArgs {
@@ -38,10 +38,8 @@ struct GemmArgs {
   int epi;
   int accumulate;  // EPI_F32_STORE: out += result
   int vec_store;   // out rows are 16-byte aligned
-  int final_epi;   // EPI_SPLIT: EPI_F32_STORE or EPI_BF16_STORE for the reduced tile
   int tma_store;   // epilogue stages 32-row groups in shared memory and stores them with TMA
-  float *workspace;       // EPI_SPLIT: [splits][tiles][BM][BN] fp32 partial tiles
-  unsigned *counters;     // EPI_SPLIT: one ticket per tile, zero between launches
+  float *workspace;  // EPI_SPLIT: [splits][tiles][BM][BN] fp32 partial tiles
 };
 
 template <typename T>
@@ -254,7 +252,6 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t *tfull = bars + 2 * STAGES;
   uint64_t *tempty = bars + 2 * STAGES + 2;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
-  __shared__ int s_last_split;
   __shared__ float s_bscale[BN];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -362,7 +359,7 @@ __global__ void __launch_bounds__(192, 1)
       // .sync.aligned TMEM loads below are always executed by the full warp
       const bool lane_ok = mbar_wait(&tfull[acc], acc_phase);
       // the four epilogue warps agree (barrier 1, 128 threads), so a timed-out wait can never
-      // leave some of them inside the split-K barriers below
+      // leave some of them inside the column-scale barrier below
       uint32_t all_ok;
       asm volatile(
           "{\n\t.reg .pred p, q;\n\t"
@@ -389,9 +386,15 @@ __global__ void __launch_bounds__(192, 1)
           asm volatile("bar.sync 1, 128;" ::: "memory");
         }
         const float a_s = (scaled && row < p.M) ? __ldg(p.a_scale + row) : 1.0f;
-        const bool bf16_out = p.out_dtype == RT_BF16 || p.epi == EPI_BF16_STORE;
-        const int y = tm * C::BM + sub * 32;
-        if (y >= p.M) {
+        const bool bf16_out =
+            !split_mode && (p.out_dtype == RT_BF16 || p.epi == EPI_BF16_STORE);
+        // split mode: the fp32 partial tile goes to its own 128 x BN block of the workspace
+        const int y = split_mode
+                          ? (split * p.tiles_m * p.tiles_n + tile) * C::BM + sub * 32
+                          : tm * C::BM + sub * 32;
+        const int x0 = split_mode ? 0 : tn * BN;
+        const int x_end = split_mode ? BN : p.N;
+        if (!split_mode && y >= p.M) {
           // this warp's 32 rows lie past the output: nothing to store
         } else if (bf16_out) {
 #pragma unroll 1
@@ -421,8 +424,8 @@ __global__ void __launch_bounds__(192, 1)
         } else {
 #pragma unroll 1
           for (int g = 0; g < BN / 32; ++g) {
-            const int n0 = tn * BN + g * 32;
-            if (n0 >= p.N) break;
+            const int n0 = x0 + g * 32;
+            if (n0 >= x_end) break;
             uint32_t r[32];
             tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 32), r);
             tmem_ld_wait();
@@ -437,71 +440,20 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       } else {
-      float *part = nullptr;
-      if (split_mode)
-        part = p.workspace +
-               ((static_cast<int64_t>(split) * p.tiles_m * p.tiles_n + tile) * C::BM + trow) * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int n0 = tn * BN + c * 32;
-        if (!split_mode && n0 >= p.N) break;
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
-        tmem_ld_wait();
-        if (split_mode) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4 *>(part + c * 32 + j) =
-                make_float4(acc_to_float<T>(r[j]), acc_to_float<T>(r[j + 1]),
-                            acc_to_float<T>(r[j + 2]), acc_to_float<T>(r[j + 3]));
-        } else {
+        for (int c = 0; c < BN / 32; ++c) {
+          const int n0 = tn * BN + c * 32;
+          if (n0 >= p.N) break;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
+          tmem_ld_wait();
           epilogue_chunk<T>(p, p.epi, row, n0, r);
         }
-      }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) acc = 0, acc_phase ^= 1;
-      if (split_mode) {
-        __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (ep_tid == 0)
-          s_last_split = atomicAdd(p.counters + tile, 1u) == static_cast<unsigned>(p.splits - 1);
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (s_last_split) {
-          __threadfence();
-          const float *base =
-              p.workspace + (static_cast<int64_t>(tile) * C::BM + trow) * BN;
-          const int64_t split_stride = static_cast<int64_t>(p.tiles_m) * p.tiles_n * C::BM * BN;
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            const int n0 = tn * BN + c * 32;
-            if (n0 >= p.N) break;
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const float4 f = __ldcg(reinterpret_cast<const float4 *>(base + c * 32 + j));
-              v[j] = f.x, v[j + 1] = f.y, v[j + 2] = f.z, v[j + 3] = f.w;
-            }
-            for (int sp = 1; sp < p.splits; ++sp) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                const float4 f = __ldcg(
-                    reinterpret_cast<const float4 *>(base + sp * split_stride + c * 32 + j));
-                v[j] = __fadd_rn(v[j], f.x), v[j + 1] = __fadd_rn(v[j + 1], f.y);
-                v[j + 2] = __fadd_rn(v[j + 2], f.z), v[j + 3] = __fadd_rn(v[j + 3], f.w);
-              }
-            }
-            uint32_t r[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(v[j]);
-            epilogue_chunk<__nv_bfloat16>(p, p.final_epi, row, n0, r);
-          }
-          if (ep_tid == 0) p.counters[tile] = 0u;  // leave the ticket zero for the next launch
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-      }
     }
     if (p.tma_store && lane == 0) bulk_wait_all();  // staged stores done before the CTA exits
   }
@@ -621,11 +573,25 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
   if (rc) return rc;
   rc = operand_map<T, B_MN>(&mb, b, BN);
   if (rc) return rc;
-  // TMA-store epilogue: 16-byte aligned rows, a plain store (no accumulate, no split)
+  args.tiles_m = static_cast<int>((args.M + C::BM - 1) / C::BM);
+  args.tiles_n = static_cast<int>((args.N + BN - 1) / BN);
+  args.kblocks = static_cast<int>((args.K + C::KE - 1) / C::KE);
+  if (args.splits < 1) args.splits = 1;
+  if (args.splits > args.kblocks) args.splits = args.kblocks;
+  // TMA-store epilogue: 16-byte aligned rows and a plain store (no accumulate), or the split-K
+  // partial tiles (fp32, BN columns, one 128-row block per split and tile)
   const bool out_bf16 = args.out_dtype == RT_BF16 || args.epi == EPI_BF16_STORE;
-  args.tma_store = args.vec_store && (args.epi == EPI_SCALED || args.epi == EPI_BF16_STORE ||
-                                      (args.epi == EPI_F32_STORE && !args.accumulate));
-  if (args.tma_store) {
+  if (args.epi == EPI_SPLIT) {
+    args.tma_store = 1;
+    rc = make_map(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, args.workspace, static_cast<uint64_t>(BN),
+                  static_cast<uint64_t>(args.splits) * args.tiles_m * args.tiles_n * C::BM,
+                  static_cast<uint64_t>(BN) * 4, 32, 32);
+    if (rc) return rc;
+  } else {
+    args.tma_store = args.vec_store && (args.epi == EPI_SCALED || args.epi == EPI_BF16_STORE ||
+                                        (args.epi == EPI_F32_STORE && !args.accumulate));
+  }
+  if (args.tma_store && args.epi != EPI_SPLIT) {
     const size_t es = out_bf16 ? 2 : 4;
     rc = make_map(&mc, out_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                   args.out, static_cast<uint64_t>(args.N), static_cast<uint64_t>(args.M),
@@ -648,11 +614,6 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
       configured[dev] = true;
     }
   }
-  args.tiles_m = static_cast<int>((args.M + C::BM - 1) / C::BM);
-  args.tiles_n = static_cast<int>((args.N + BN - 1) / BN);
-  args.kblocks = static_cast<int>((args.K + C::KE - 1) / C::KE);
-  if (args.splits < 1) args.splits = 1;
-  if (args.splits > args.kblocks) args.splits = args.kblocks;
   const int64_t units = static_cast<int64_t>(args.tiles_m) * args.tiles_n * args.splits;
   const int grid = static_cast<int>(units < sms ? units : sms);
   kernel<<<grid, 192, C::SMEM_BYTES, s>>>(ma, mb, mc, args);
@@ -724,7 +685,57 @@ namespace rt {
 constexpr int GW_BN = 256;
 constexpr int64_t GW_TILE_BYTES = 128 * GW_BN * 4;
 static int64_t gw_tiles(int64_t N, int64_t K) { return ((N + 127) / 128) * ((K + GW_BN - 1) / GW_BN); }
-static int64_t gw_counter_bytes(int64_t tiles) { return ((tiles * 4 + 255) / 256) * 256; }
+// Split-K reduction of the grad_weight partial tiles: out[n, k] (+)= sum over splits, in split
+// order, of ws[split][tile(n, k)][n % 128][k % BN].  Four consecutive k per thread, so both the
+// partial-tile reads and the output writes are coalesced.
+template <int BN>
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const float *__restrict__ ws, int splits, int tiles_m, int tiles_n,
+                         int rows, int cols, void *out, int out_dtype, int64_t ldo,
+                         int accumulate, int vec_out) {
+  const int groups = (cols + 3) >> 2;
+  const int64_t total = static_cast<int64_t>(rows) * groups;
+  const int64_t split_stride = static_cast<int64_t>(tiles_m) * tiles_n * 128 * BN;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / groups);
+    const int col = static_cast<int>(i - static_cast<int64_t>(row) * groups) * 4;
+    const int tile = (row >> 7) * tiles_n + col / BN;
+    const float *src = ws + (static_cast<int64_t>(tile) * 128 + (row & 127)) * BN + col % BN;
+    float4 v = __ldcs(reinterpret_cast<const float4 *>(src));
+#pragma unroll 4
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 f = __ldcs(reinterpret_cast<const float4 *>(src + sp * split_stride));
+      v.x = __fadd_rn(v.x, f.x), v.y = __fadd_rn(v.y, f.y);
+      v.z = __fadd_rn(v.z, f.z), v.w = __fadd_rn(v.w, f.w);
+    }
+    const float r[4] = {v.x, v.y, v.z, v.w};
+    if (out_dtype == RT_F32) {
+      float *o = static_cast<float *>(out) + static_cast<int64_t>(row) * ldo + col;
+      if (vec_out && col + 4 <= cols) {
+        float4 w = v;
+        if (accumulate) {
+          const float4 old = *reinterpret_cast<const float4 *>(o);
+          w.x = __fadd_rn(old.x, w.x), w.y = __fadd_rn(old.y, w.y);
+          w.z = __fadd_rn(old.z, w.z), w.w = __fadd_rn(old.w, w.w);
+        }
+        *reinterpret_cast<float4 *>(o) = w;
+      } else {
+        for (int j = 0; j < 4 && col + j < cols; ++j) o[j] = accumulate ? __fadd_rn(o[j], r[j]) : r[j];
+      }
+    } else {
+      uint16_t *o = static_cast<uint16_t *>(out) + static_cast<int64_t>(row) * ldo + col;
+      if (vec_out && col + 4 <= cols) {
+        *reinterpret_cast<uint2 *>(o) =
+            make_uint2(bf16_bits(r[0]) | (uint32_t(bf16_bits(r[1])) << 16),
+                       bf16_bits(r[2]) | (uint32_t(bf16_bits(r[3])) << 16));
+      } else {
+        for (int j = 0; j < 4 && col + j < cols; ++j) o[j] = bf16_bits(r[j]);
+      }
+    }
+  }
+}
+
 // split count: enough units to cover every SM, bounded by the K blocks and the workspace
 static int gw_splits(int64_t M_tok, int64_t N, int64_t K, int sms, int64_t workspace_bytes) {
   const int64_t tiles = gw_tiles(N, K);
@@ -732,8 +743,7 @@ static int gw_splits(int64_t M_tok, int64_t N, int64_t K, int sms, int64_t works
   if (tiles >= sms) return 1;
   int64_t s = sms / tiles;
   if (s > kb) s = kb;
-  const int64_t room = workspace_bytes - gw_counter_bytes(tiles);
-  const int64_t fit = room > 0 ? room / (tiles * GW_TILE_BYTES) : 0;
+  const int64_t fit = workspace_bytes > 0 ? workspace_bytes / (tiles * GW_TILE_BYTES) : 0;
   if (s > fit) s = fit;
   return s < 2 ? 1 : static_cast<int>(s);
 }
@@ -745,7 +755,7 @@ extern "C" int64_t rt_grad_weight_workspace_bytes(int64_t M_tok, int64_t N, int6
   const int s = gw_splits(M_tok, N, K, sms, INT64_MAX / 4);
   if (s <= 1) return 0;
   const int64_t tiles = gw_tiles(N, K);
-  return gw_counter_bytes(tiles) + static_cast<int64_t>(s) * tiles * GW_TILE_BYTES;
+  return static_cast<int64_t>(s) * tiles * GW_TILE_BYTES;
 }
 
 extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, int64_t ldx,
@@ -781,21 +791,28 @@ extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, in
     args.vec_store = aligned16(out) && (ldo * static_cast<int64_t>(osz)) % 16 == 0;
     const int splits =
         workspace == nullptr ? 1 : gw_splits(M_tok, N, K, sms, workspace_bytes);
-    const int final_epi = out_dtype == RT_F32 ? EPI_F32_STORE : EPI_BF16_STORE;
     args.splits = splits;
     if (splits > 1) {
       args.epi = EPI_SPLIT;
-      args.final_epi = final_epi;
-      args.counters = static_cast<unsigned *>(workspace);
-      args.workspace = reinterpret_cast<float *>(static_cast<uint8_t *>(workspace) +
-                                                 gw_counter_bytes(gw_tiles(N, K)));
+      args.workspace = static_cast<float *>(workspace);
     } else {
-      args.epi = final_epi;
+      args.epi = out_dtype == RT_F32 ? EPI_F32_STORE : EPI_BF16_STORE;
     }
     // A = gᵀ: (N × M_tok) with N contiguous (MN-major); B = x: (K × M_tok) with K contiguous.
     Operand A{g, true, ldg, N, M_tok};
     Operand B{x, true, ldx, K, M_tok};
-    return launch_umma<__nv_bfloat16, true, true, GW_BN, 4>(A, B, args, s);
+    rc = launch_umma<__nv_bfloat16, true, true, GW_BN, 4>(A, B, args, s);
+    if (rc || splits == 1) return rc;
+    // the partial tiles, summed in split order into the output
+    const int64_t work = N * ((K + 3) / 4);
+    int64_t blocks = (work + 255) / 256;
+    if (blocks > static_cast<int64_t>(sms) * 8) blocks = static_cast<int64_t>(sms) * 8;
+    const int tiles_m = static_cast<int>((N + 127) / 128);
+    const int tiles_n = static_cast<int>((K + GW_BN - 1) / GW_BN);
+    splitk_reduce_kernel<GW_BN><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+        static_cast<const float *>(workspace), splits, tiles_m, tiles_n, static_cast<int>(N),
+        static_cast<int>(K), out, out_dtype, ldo, accumulate, args.vec_store);
+    return check_launch("splitk_reduce_kernel");
   }
   const dim3 block(32, 8);
   const dim3 grid(static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>((N + 7) / 8));
@@ -806,10 +823,10 @@ extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, in
 }
 
 // ---------------------------------------------------------------------------------------------
-// rt_grad_weight_bf16 without a caller-provided workspace: the split-K partial tiles and tickets
-// live in a fixed device array of this library.  Nothing is allocated per call.
+// rt_grad_weight_bf16 without a caller-provided workspace: the split-K partial tiles live in a
+// fixed device array of this library.  Nothing is allocated per call.
 namespace rt {
-constexpr int64_t kGwScratchBytes = int64_t(20) << 20;  // >= SMs x 128 KiB tiles + tickets
+constexpr int64_t kGwScratchBytes = int64_t(20) << 20;  // >= SMs x 128 KiB partial tiles
 constexpr int kGwScratchDevices = 64;
 static __device__ __align__(256) uint8_t g_gw_scratch[kGwScratchBytes];
 
@@ -853,10 +870,8 @@ extern "C" int rt_grad_weight_bf16_noalloc(const void *g, int64_t ldg, const voi
     if (e != cudaSuccess) return fail(RT_ERR_CUDA, "grad_weight_noalloc: %s", cudaGetErrorString(e));
     int rc = gw_scratch_address(dev, &scratch);
     if (rc) return rc;
-    // the per-tile tickets must start at zero; a call that ended early may have left some set
-    e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(gw_counter_bytes(gw_tiles(N, K))),
-                        as_stream(stream));
-    if (e != cudaSuccess) return fail(RT_ERR_CUDA, "grad_weight_noalloc: %s", cudaGetErrorString(e));
+    // nothing in the scratch needs to start at zero: every partial tile is written before it
+    // is read, within the call
   }
   return rt_grad_weight_bf16(g, ldg, x, ldx, out, out_dtype, ldo, M_tok, N, K, accumulate, scratch,
                              need, stream);
