@@ -58,16 +58,20 @@ int rt_sm_count(int *out);
  *   v[m,k]   = float(x[m,k]) * col_scale[k]          (col_scale optional)
  *   scale[m] = max(max_k |v[m,k]| / 127, FLT_MIN)
  *   RN: q = clamp(rint(v / scale), -127, 127)
- *   SR: q = clamp(floor(v / scale + u), -127, 127), u = Philox4x32-10 uniform keyed by
- *       (seed, layer) with counter (element index / 4, step)  [own mapping, not Triton's tl.rand]
+ *   SR: q = clamp(floor(v / scale + u), -127, 127), u = (h + 1/2)·2^-16 from 16-bit half
+ *       (e & 1) of word (e & 7)/2 of Philox4x32-10 keyed by (seed, layer) with counter
+ *       (element index e / 8, step)  [own mapping, not Triton's tl.rand]
  * x_bf16_out (optional) receives bf16(x) (unscaled) — the grad_weight GEMM operand of
  * ratchet.py:162 — so the gradient is read from HBM once.
- * step_dev (optional): device address of a uint32 read in place of `step`, so a captured CUDA
- * graph can advance the stream between replays.
+ * step_dev (optional): two device uint32s.  step_dev[0] is read in place of `step` and the call
+ * advances it by one once every CTA has read it; step_dev[1] is the call's arrival count and must
+ * be zero between calls (calls leave it zero).  Consecutive calls, and the replays of a captured
+ * CUDA graph, thus draw fresh streams without host work.  Calls sharing a step_dev must not
+ * overlap on the GPU.
  * ------------------------------------------------------------------------------------------- */
 int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_t cols, int64_t stride_row,
                      int64_t stride_col, const float *col_scale, int stochastic, uint64_t seed,
-                     uint32_t step, uint32_t layer, const uint32_t *step_dev, int8_t *q,
+                     uint32_t step, uint32_t layer, uint32_t *step_dev, int8_t *q,
                      int64_t ldq, float *row_scale, void *x_bf16_out, int64_t ld_xbf16,
                      void *stream);
 

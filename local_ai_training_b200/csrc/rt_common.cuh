@@ -87,18 +87,25 @@ __host__ __device__ __forceinline__ Philox4 philox4x32_10(uint32_t c0, uint32_t 
   return {c0, c1, c2, c3};
 }
 // Stochastic-rounding stream of this library: the element with linear index e = row*cols + col
-// of a (rows, cols) tensor draws word (e & 3) of
-//   Philox4x32-10(counter = (e >> 2 low 32, e >> 2 high 32, step, 0x52415443 "RATC"),
+// of a (rows, cols) tensor draws 16-bit half (e & 1) (0 = low) of word ((e & 7) >> 1) of
+//   Philox4x32-10(counter = (e >> 3 low 32, e >> 3 high 32, step, 0x52415443 "RATC"),
 //                 key     = (seed low 32, (seed high 32) ^ layer))
-// and maps it to u = (word >> 8) * 2^-24 in [0, 1).
+// and maps that half h to u = (h + 1/2) * 2^-16 in (0, 1): one Philox block serves 8 elements,
+// and the rounding is unbiased to within 2^-17 of an int8 step (below the fp32 error of the
+// scaled value itself near |127|).
 __host__ __device__ __forceinline__ Philox4 sr_block(uint64_t seed, uint32_t step, uint32_t layer,
-                                                     uint64_t quad) {
-  return philox4x32_10(static_cast<uint32_t>(quad), static_cast<uint32_t>(quad >> 32), step,
+                                                     uint64_t block) {
+  return philox4x32_10(static_cast<uint32_t>(block), static_cast<uint32_t>(block >> 32), step,
                        0x52415443u, static_cast<uint32_t>(seed),
                        static_cast<uint32_t>(seed >> 32) ^ layer);
 }
-__host__ __device__ __forceinline__ float u24(uint32_t word) {
-  return static_cast<float>(word >> 8) * 5.9604644775390625e-08f;  // 2^-24, exact
+// u of the low / high 16 bits of a word, built in the mantissa of a float in [1, 2) (exact,
+// no int->float conversion): 1 + h * 2^-16 + 2^-17, minus 1.
+__device__ __forceinline__ float sr_u_lo(uint32_t word) {
+  return __uint_as_float(((word << 7) & 0x007FFF80u) | 0x3F800040u) - 1.0f;
+}
+__device__ __forceinline__ float sr_u_hi(uint32_t word) {
+  return __uint_as_float(((word >> 9) & 0x007FFF80u) | 0x3F800040u) - 1.0f;
 }
 __host__ __device__ __forceinline__ uint32_t philox_word(const Philox4 &p, int j) {
   return j == 0 ? p.x : (j == 1 ? p.y : (j == 2 ? p.z : p.w));

@@ -148,12 +148,21 @@ __device__ __forceinline__ int quant_rn_i(float v, float scale, float rcp) {
     return static_cast<int>(rintf(fminf(fmaxf(__fdiv_rn(v, scale), -127.0f), 127.0f)));
   return __float_as_int(t) - 0x4B400000;
 }
-// Stochastic rounding floor(RN(v / scale) + u), as an int in [-127, 127].
+// Stochastic rounding floor(RN(RN(v / scale) + u)), as an int in [-127, 127].  The floor is
+// taken with the rounding magic as well (no conversion unit): z = t + 1.5·2^23 holds n = RN(t)
+// in its low mantissa bits, d = t - n is exact, and floor(t) = n - (d < 0).  |d| <= 2^-12 (t
+// within the window of an integer) sends the element to the IEEE division.
 __device__ __forceinline__ int quant_sr_i(float v, float scale, float rcp, float u) {
   float t = __fadd_rn(__fmul_rn(v, rcp), u);
-  if (fabsf(__fsub_rn(__fsub_rn(t, floorf(t)), 0.5f)) >= 0.5f - kBoundaryWindow)
+  float z = __fadd_rn(t, kRoundMagic);
+  float d = __fsub_rn(t, __fsub_rn(z, kRoundMagic));
+  if (fabsf(d) <= kBoundaryWindow) {
     t = __fadd_rn(__fdiv_rn(v, scale), u);
-  return min(max(__float2int_rd(t), -127), 127);
+    z = __fadd_rn(t, kRoundMagic);
+    d = __fsub_rn(t, __fsub_rn(z, kRoundMagic));
+  }
+  const int n = (__float_as_int(z) - 0x4B400000) - (d < 0.0f ? 1 : 0);
+  return min(max(n, -127), 127);
 }
 __device__ __forceinline__ int8_t quant_rn(float v, float scale, float rcp) {
   return static_cast<int8_t>(quant_rn_i(v, scale, rcp));
@@ -180,11 +189,14 @@ static inline int pow2_at_least(int64_t v) {
   while (p < v) p <<= 1;
   return p;
 }
-// Few rows get more threads each (up to a CTA per row) so that the grid fills the GPU.
+// At most two chunks per thread while a CTA per row allows it: the row stays in registers
+// without capping occupancy (eight chunks held 86 registers and left a quarter of the warp
+// slots in use), and more resident warps hide each row's load -> reduce -> store chain.  Few
+// rows get more threads each (up to a CTA per row) so that the grid fills the GPU.
 static inline RowCfg row_cfg(int64_t nch, int64_t rows = INT64_MAX) {
   const int64_t want_threads = 148 * 2048;
-  int rt = nch <= 32 * 8 ? 32 : (nch <= 128 * 8 ? 128 : (nch <= 256 * 8 ? 256 : 0));
-  if (rt == 0) return {0, 0};
+  if (nch > 256 * 8) return {0, 0};
+  int rt = nch <= 32 * 2 ? 32 : (nch <= 128 * 2 ? 128 : 256);
   while (rt < 256 && rows * rt < want_threads && nch > rt) rt = rt == 32 ? 128 : 256;
   return {rt, pow2_at_least((nch + rt - 1) / rt)};
 }
@@ -249,13 +261,35 @@ struct QuantArgs {
   int stochastic;
   uint64_t seed;
   uint32_t step, layer;
-  const uint32_t *step_dev;
+  uint32_t *step_dev;
   int8_t *q;
   int64_t ldq;
   float *row_scale;
   unsigned short *xbf16;
   int64_t ld_xbf16;
 };
+
+// Step of the stochastic-rounding stream: step_dev[0] when given (read by every thread at the
+// start).  After all its threads have used it, each CTA reports on step_dev[1]; the last CTA of
+// the launch resets that count and advances step_dev[0] by one, so consecutive calls draw fresh
+// streams with no host work per call (a captured graph advances it on every replay).
+__device__ __forceinline__ uint32_t sr_step_read(const QuantArgs &a) {
+  return a.step_dev != nullptr ? *reinterpret_cast<const volatile uint32_t *>(a.step_dev)
+                               : a.step;
+}
+// Whole CTA, after the last use of `step`.
+__device__ __forceinline__ void sr_step_arrive(const QuantArgs &a, uint32_t step) {
+  if (a.step_dev == nullptr) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(a.step_dev + 1, 1u) == gridDim.x - 1) {
+      a.step_dev[1] = 0u;
+      __threadfence();
+      atomicExch(a.step_dev, step + 1u);
+    }
+  }
+}
 
 template <typename T, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
@@ -266,6 +300,7 @@ __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
   const bool live = row < a.rows;
   const int64_t nch = a.cols / 8;
   const T *xr = static_cast<const T *>(a.x) + (live ? row : 0) * a.stride_row;
+  const uint32_t step = sr_step_read(a);
   float v[VPT][8];
   float amax = 0.0f;
 #pragma unroll
@@ -289,29 +324,26 @@ __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
     }
   }
   amax = row_max<RT>(amax, smx, sub, t);
-  if (!live) return;
   const float scale = row_scale_of(amax);
   const float rcp = __frcp_rn(scale);
-  if (t == 0) a.row_scale[row] = scale;
-  const uint32_t step = a.step_dev != nullptr ? __ldg(a.step_dev) : a.step;
-  int8_t *qr = a.q + row * a.ldq;
+  if (live && t == 0) a.row_scale[row] = scale;
+  int8_t *qr = a.q + (live ? row : 0) * a.ldq;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
-    if (c >= nch) continue;
+    if (!live || c >= nch) continue;
     uint2 o;
     if (a.stochastic) {
       const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;  // multiple of 8
-      const Philox4 p0 = sr_block(a.seed, step, a.layer, e0 >> 2);
-      const Philox4 p1 = sr_block(a.seed, step, a.layer, (e0 >> 2) + 1);
-      o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, u24(p0.x)),
-                     quant_sr_i(v[i][1], scale, rcp, u24(p0.y)),
-                     quant_sr_i(v[i][2], scale, rcp, u24(p0.z)),
-                     quant_sr_i(v[i][3], scale, rcp, u24(p0.w)));
-      o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, u24(p1.x)),
-                     quant_sr_i(v[i][5], scale, rcp, u24(p1.y)),
-                     quant_sr_i(v[i][6], scale, rcp, u24(p1.z)),
-                     quant_sr_i(v[i][7], scale, rcp, u24(p1.w)));
+      const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
+      o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_u_lo(p.x)),
+                     quant_sr_i(v[i][1], scale, rcp, sr_u_hi(p.x)),
+                     quant_sr_i(v[i][2], scale, rcp, sr_u_lo(p.y)),
+                     quant_sr_i(v[i][3], scale, rcp, sr_u_hi(p.y)));
+      o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_u_lo(p.z)),
+                     quant_sr_i(v[i][5], scale, rcp, sr_u_hi(p.z)),
+                     quant_sr_i(v[i][6], scale, rcp, sr_u_lo(p.w)),
+                     quant_sr_i(v[i][7], scale, rcp, sr_u_hi(p.w)));
     } else {
       o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
                      quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
@@ -320,6 +352,7 @@ __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
     }
     *reinterpret_cast<uint2 *>(qr + 8 * c) = o;
   }
+  sr_step_arrive(a, step);
 }
 
 // Generic: any strides, one CTA per row, two passes (the second normally hits L2).
@@ -328,6 +361,7 @@ __global__ void __launch_bounds__(CTA) quant_rows_generic_kernel(QuantArgs a) {
   __shared__ float smx[8];
   const int64_t row = blockIdx.x;
   const T *xr = static_cast<const T *>(a.x) + row * a.stride_row;
+  const uint32_t step = sr_step_read(a);
   float amax = 0.0f;
   for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
     float v = load_as_float<T>(xr + k * a.stride_col);
@@ -339,20 +373,21 @@ __global__ void __launch_bounds__(CTA) quant_rows_generic_kernel(QuantArgs a) {
   const float scale = row_scale_of(amax);
   const float rcp = __frcp_rn(scale);
   if (threadIdx.x == 0) a.row_scale[row] = scale;
-  const uint32_t step = a.step_dev != nullptr ? __ldg(a.step_dev) : a.step;
   for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
     float v = load_as_float<T>(xr + k * a.stride_col);
     if (a.col_scale != nullptr) v = __fmul_rn(v, __ldg(a.col_scale + k));
     int8_t o;
     if (a.stochastic) {
       const uint64_t e = static_cast<uint64_t>(row) * a.cols + k;
-      const Philox4 p = sr_block(a.seed, step, a.layer, e >> 2);
-      o = quant_sr(v, scale, rcp, u24(philox_word(p, static_cast<int>(e & 3))));
+      const Philox4 p = sr_block(a.seed, step, a.layer, e >> 3);
+      const uint32_t w = philox_word(p, static_cast<int>((e & 7) >> 1));
+      o = quant_sr(v, scale, rcp, (e & 1) ? sr_u_hi(w) : sr_u_lo(w));
     } else {
       o = quant_rn(v, scale, rcp);
     }
     a.q[row * a.ldq + k] = o;
   }
+  sr_step_arrive(a, step);
 }
 
 template <typename T>
@@ -1160,7 +1195,7 @@ using namespace rt;
 extern "C" int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_t cols,
                                 int64_t stride_row, int64_t stride_col, const float *col_scale,
                                 int stochastic, uint64_t seed, uint32_t step, uint32_t layer,
-                                const uint32_t *step_dev, int8_t *q, int64_t ldq,
+                                uint32_t *step_dev, int8_t *q, int64_t ldq,
                                 float *row_scale, void *x_bf16_out, int64_t ld_xbf16,
                                 void *stream) {
   if (rows < 0 || cols < 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_quantize_rows: negative shape");

@@ -73,6 +73,14 @@ def fused_transpose_quantize(x: Tensor) -> tuple[Tensor, Tensor]:
     return out, scale
 
 
+def _no_zero_grads(ctx, int8_out: Tensor, scale_out: Tensor) -> None:
+    """The int8 codes and row scales carry no gradient: mark them so, and let backward see None
+    for gradients nobody produced instead of zero tensors autograd would fill (one fill kernel
+    per output per call)."""
+    ctx.mark_non_differentiable(int8_out, scale_out)
+    ctx.set_materialize_grads(False)
+
+
 class FusedRMSNormQuantizeFn(torch.autograd.Function):
     """(int8, scale, dummy) like the reference.  `dummy_dtype` (default: x's dtype, the
     reference) sets the dtype of the dummy, i.e. of the consuming layer's input gradient."""
@@ -83,10 +91,13 @@ class FusedRMSNormQuantizeFn(torch.autograd.Function):
         ctx.save_for_backward(x, weight)
         ctx.eps = eps
         dummy = torch.empty(x.shape, device=x.device, dtype=dummy_dtype or x.dtype)
+        _no_zero_grads(ctx, int8_out, scale_out)
         return int8_out, scale_out, dummy
 
     @staticmethod
     def backward(ctx, grad_int8, grad_scale, grad_dummy):
+        if grad_dummy is None:
+            return None, None, None, None
         x, weight = ctx.saved_tensors
         grad_x, grad_w = rmsnorm_backward(grad_dummy, x, weight, ctx.eps)
         return grad_x, grad_w, None, None
@@ -100,10 +111,13 @@ class FusedGELUQuantizeFn(torch.autograd.Function):
         int8_out, scale_out = fused_gelu_quantize(x)
         ctx.save_for_backward(x)
         dummy = torch.empty(x.shape, device=x.device, dtype=dummy_dtype or x.dtype)
+        _no_zero_grads(ctx, int8_out, scale_out)
         return int8_out, scale_out, dummy
 
     @staticmethod
     def backward(ctx, grad_int8, grad_scale, grad_dummy):
+        if grad_dummy is None:
+            return None, None
         (x,) = ctx.saved_tensors
         return gelu_backward(grad_dummy, x), None
 
@@ -116,10 +130,13 @@ class FusedTransposeQuantizeFn(torch.autograd.Function):
         batch_size, n_head, seq_len, head_dim = attended.shape
         dummy = torch.empty((batch_size, seq_len, n_head * head_dim), device=attended.device,
                             dtype=attended.dtype)
+        _no_zero_grads(ctx, int8_out, scale_out)
         return int8_out, scale_out, dummy
 
     @staticmethod
     def backward(ctx, grad_int8, grad_scale, grad_dummy):
+        if grad_dummy is None:
+            return None
         (attended,) = ctx.saved_tensors
         batch_size, n_head, seq_len, head_dim = attended.shape
         return grad_dummy.view(batch_size, seq_len, n_head, head_dim).transpose(1, 2)

@@ -39,7 +39,9 @@ def _quantize_rows_fused(
     stochastic=True draws the seed from the host RNG when none is given (the reference's
     `torch.randint(0, 2**31 - 1, (1,))`, int8_matmul.py:200); (seed, step, layer) key the Philox
     stream.  bf16_copy, when given (rows × cols bf16, unit column stride), receives bf16(values).
-    step_dev (int32 [1] on the device), when given, is read by the kernel instead of `step`.
+    step_dev (int32 [2] on the device, zeros to start), when given: element 0 is read by the
+    kernel instead of `step` and advanced by one by the call; element 1 is the kernel's arrival
+    count (zero between calls).
     """
     if values.ndim != 2:
         raise ValueError("row quantization requires a 2D tensor")

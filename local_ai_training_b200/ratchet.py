@@ -124,9 +124,7 @@ class _RatchetMatmul(torch.autograd.Function):
             seed, step, layer, step_dev = _sr_key(ctx.gradient_sink)
             gq, gs = _quantize_rows_fused(flat_gradient, scale.float(), stochastic=True, seed=seed,
                                           step=step, layer=layer, bf16_copy=grad_bf16,
-                                          step_dev=step_dev)
-            if step_dev is not None:
-                step_dev.add_(1)
+                                          step_dev=step_dev)  # the call advances step_dev
             gi_dtype = ctx.input_dtype if ctx.input_dtype in (torch.float32, torch.bfloat16) else torch.bfloat16
             grad_input = torch.empty((gq.shape[0], in_features), device=gq.device, dtype=gi_dtype)
             _scaled_int8_mm_into(gq, code, gs, None, grad_input)
@@ -373,7 +371,7 @@ class DiscreteRatchetLinear(nn.Module):
             self._sr_step += 1
             return None, step, self.sr_layer, None
         if self._sr_step_dev is None or self._sr_step_dev.device != self.packed.device:
-            self._sr_step_dev = torch.zeros(1, device=self.packed.device, dtype=torch.int32)
+            self._sr_step_dev = torch.zeros(2, device=self.packed.device, dtype=torch.int32)
         return self.sr_seed, 0, self.sr_layer, self._sr_step_dev
 
     # ------------------------------------------------------------------ state views

@@ -52,17 +52,20 @@ void or_philox4x32_10(const uint32_t ctr_in[4], const uint32_t key_in[2], uint32
 }
 
 /* This library's stochastic-rounding draw for linear element index e (see the header of the
- * CUDA library): word (e & 3) of Philox(ctr = (e>>2, (e>>2)>>32, step, "RATC"),
- * key = (seed, (seed>>32) ^ layer)), u = (word >> 8) * 2^-24.  The reference draws
- * tl.rand(seed, m*K + n) with a fresh host seed per call (int8_matmul.py:143-145, 200); its
- * stream is not reproducible, so only the distribution of the rounding is shared. */
+ * CUDA library): 16-bit half (e & 1) (0 = low) of word ((e & 7) >> 1) of
+ * Philox(ctr = (e>>3, (e>>3)>>32, step, "RATC"), key = (seed, (seed>>32) ^ layer)), mapped to
+ * u = (h + 1/2) * 2^-16.  The reference draws tl.rand(seed, m*K + n) with a fresh host seed per
+ * call (int8_matmul.py:143-145, 200); its stream is not reproducible, so only the distribution
+ * of the rounding is shared. */
 float or_sr_uniform(uint64_t seed, uint32_t step, uint32_t layer, uint64_t e) {
-  const uint64_t quad = e >> 2;
-  const uint32_t ctr[4] = {(uint32_t)quad, (uint32_t)(quad >> 32), step, 0x52415443u};
+  const uint64_t block = e >> 3;
+  const uint32_t ctr[4] = {(uint32_t)block, (uint32_t)(block >> 32), step, 0x52415443u};
   const uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32) ^ layer};
   uint32_t out[4];
   or_philox4x32_10(ctr, key, out);
-  return (float)(out[e & 3] >> 8) * 5.9604644775390625e-08f;
+  const uint32_t word = out[(e & 7) >> 1];
+  const uint32_t h = (e & 1) ? (word >> 16) : (word & 0xFFFFu);
+  return (float)(2u * h + 1u) * 7.62939453125e-06f; /* 2^-17, exact */
 }
 
 /* ---------- canonical row sum ----------

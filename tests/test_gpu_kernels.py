@@ -82,6 +82,23 @@ def test_stochastic_rounding_matches_philox_replica(cuda_device, shape, dtype):
     np.testing.assert_array_equal(_np(gbf), O.bf16_round(_np(g)))
 
 
+@pytest.mark.parametrize("shape", [(16384, 1536), (67, 35), (3, 8)])
+def test_device_step_is_read_then_advanced_by_each_call(cuda_device, shape):
+    """step_dev[0] replaces `step` and each call advances it once all CTAs have read it."""
+    from local_ai_training_b200.int8_matmul import _quantize_rows_fused
+
+    torch.manual_seed(8)
+    g = torch.randn(shape, device=cuda_device)
+    step_dev = torch.tensor([5, 0], device=cuda_device, dtype=torch.int32)
+    rows = slice(0, min(shape[0], 64))
+    for step in (5, 6, 7):
+        q, _ = _quantize_rows_fused(g, None, stochastic=True, seed=3, step=0, layer=1,
+                                    step_dev=step_dev)
+        qo, _ = O.quantize_rows(_np(g[rows]), stochastic=True, seed=3, step=step, layer=1)
+        np.testing.assert_array_equal(_np(q[rows]), qo)
+    assert step_dev.tolist() == [8, 0]
+
+
 def test_stochastic_rounding_unbiased_over_a_million_draws(cuda_device):
     from local_ai_training_b200.int8_matmul import _quantize_rows_fused
 
