@@ -84,11 +84,15 @@ int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_t cols, int
  * fp32 (the `.to(inputs.dtype)` of ratchet.py:67 fused into the epilogue).
  * 16-byte-aligned unit-stride operands run the tcgen05 kind::i8 TMA kernel; anything else runs a
  * SIMT kernel with identical arithmetic.
+ * rhs_abs_max: a bound the caller guarantees on |rhs| (ratchet codes: 7), or 0 when unknown; it
+ * only selects a cheaper exact int32 -> fp32 conversion when K·128·bound < 2^22 (results are the
+ * same either way as long as the bound holds).
  * ------------------------------------------------------------------------------------------- */
 int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_t lhs_stride_k,
                       const int8_t *rhs, int64_t rhs_stride_k, int64_t rhs_stride_n,
                       const float *lhs_scale, const float *rhs_scale, void *out, int out_dtype,
-                      int64_t ldo, int64_t M, int64_t N, int64_t K, void *stream);
+                      int64_t ldo, int64_t M, int64_t N, int64_t K, int rhs_abs_max,
+                      void *stream);
 
 /* ---------------------------------------------------------------------------------------------
  * grad_weight GEMM.  Replaces the per-tile cuBLAS BF16 GEMM of ratchet.py:148-163:

@@ -44,7 +44,7 @@ _SIGNATURES = {
     "rt_quantize_rows": ([_p, _i, _i64, _i64, _i64, _i64, _p, _i, _u64, _u32, _u32, _p, _p, _i64,
                           _p, _p, _i64, _p], _i),
     "rt_scaled_int8_mm": ([_p, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i, _i64, _i64, _i64, _i64,
-                           _p], _i),
+                           _i, _p], _i),
     "rt_grad_weight_bf16": ([_p, _i64, _p, _i64, _p, _i, _i64, _i64, _i64, _i64, _i, _p, _i64, _p],
                             _i),
     "rt_grad_weight_workspace_bytes": ([_i64, _i64, _i64], _i64),

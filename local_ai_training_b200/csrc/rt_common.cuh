@@ -198,9 +198,9 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void 
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
-// wait until at most one committed bulk group of this thread is still reading shared memory
-__device__ __forceinline__ void bulk_wait_read_le1() {
-  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+// wait until no committed bulk group of this thread is still reading shared memory
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");

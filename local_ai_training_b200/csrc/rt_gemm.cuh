@@ -39,6 +39,7 @@ struct GemmArgs {
   int accumulate;  // EPI_F32_STORE: out += result
   int vec_store;   // out rows are 16-byte aligned
   int tma_store;   // epilogue stages 32-row groups in shared memory and stores them with TMA
+  int acc_small;   // int8: every |accumulator| < 2^22 (K·127·max|rhs| below it), 2-op conversion
   float *workspace;  // EPI_SPLIT: [splits][tiles][BM][BN] fp32 partial tiles
 };
 
@@ -65,8 +66,11 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  // per epilogue warp: two 32-row x 128-byte staging buffers for TMA stores
-  static constexpr int EPI_BYTES = 4 * 2 * 4096;
+  // eight epilogue warps: two per TMEM lane quarter, each taking half of the tile's columns
+  static constexpr int EPI_WARPS = 8;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  // per epilogue warp: one 32-row x 128-byte staging buffer for TMA stores
+  static constexpr int EPI_BYTES = EPI_WARPS * 4096;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
   // Instruction descriptor: D format, A/B formats, majorness, N>>3 at [17,23), M>>4 at [24,29).
   static constexpr uint32_t IDESC = (KindOf<T>::dfmt << 4) | (KindOf<T>::abfmt << 7) |
@@ -104,10 +108,20 @@ __device__ __forceinline__ void load_operand(const CUtensorMap *map, uint64_t *b
   }
 }
 
+// Exact int32 -> fp32 (round to nearest even) on the ALU and FMA pipes instead of the
+// conversion unit, which a 128 x 256 tile's 32K conversions would otherwise saturate: with
+// acc = hi·2^16 + lo (lo in [0, 2^16)) both halves are exact floats built in a mantissa, and one
+// FMA rounds hi·2^16 + lo once.
+__device__ __forceinline__ float i32_to_f32_rn(int acc) {
+  const float hi = __int_as_float((acc >> 16) + 0x4B400000) - 12582912.0f;
+  const float lo = __int_as_float((acc & 0xFFFF) | 0x4B000000) - 8388608.0f;
+  return __fmaf_rn(hi, 65536.0f, lo);
+}
+
 template <typename T>
 __device__ __forceinline__ float acc_to_float(uint32_t bits) {
   if constexpr (sizeof(T) == 1)
-    return __int2float_rn(static_cast<int>(bits));
+    return i32_to_f32_rn(static_cast<int>(bits));
   else
     return __uint_as_float(bits);
 }
@@ -212,14 +226,12 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &p, int epi, int r
   }
 }
 
-// One 32-row group of up to 64 bf16 / 32 fp32 output columns through the warp's staging buffer:
+// One 32-row group of 64 bf16 / 32 fp32 output columns through the warp's staging buffer:
 // 128-byte swizzled rows (conflict-free 16-byte shared stores), then one TMA store that clips
 // rows/columns outside the output.  `words` holds the 32 packed words of this lane's row.
-__device__ __forceinline__ void stage_and_store(const CUtensorMap *map, uint8_t *staging, int &buf,
-                                                int lane, const uint32_t (&words)[32], int x,
-                                                int y) {
-  uint8_t *b = staging + buf * 4096;
-  if (lane == 0) bulk_wait_read_le1();  // the store that last used this buffer has read it
+__device__ __forceinline__ void stage_and_store(const CUtensorMap *map, uint8_t *b, int lane,
+                                                const uint32_t (&words)[32], int x, int y) {
+  if (lane == 0) bulk_wait_read_all();  // the warp's previous store has read the buffer
   __syncwarp();
 #pragma unroll
   for (int c = 0; c < 8; ++c)
@@ -231,11 +243,76 @@ __device__ __forceinline__ void stage_and_store(const CUtensorMap *map, uint8_t 
     tma_store_2d(map, b, x, y);
     bulk_commit_group();
   }
-  buf ^= 1;
+}
+
+// Accumulator word -> fp32.  CONV 0: fp32 bits (kind::f16); 1: int32 known to lie in
+// (-2^22, 2^22), exact through the 1.5·2^23 mantissa (one integer add, one float add);
+// 2: any int32, exact round-to-nearest (i32_to_f32_rn).
+template <int CONV>
+__device__ __forceinline__ float cvt_acc(uint32_t b) {
+  if constexpr (CONV == 0)
+    return __uint_as_float(b);
+  else if constexpr (CONV == 1)
+    return __int_as_float(static_cast<int>(b) + 0x4B400000) - 12582912.0f;
+  else
+    return i32_to_f32_rn(static_cast<int>(b));
+}
+
+// One warp's share of a tile (32 rows, HALF columns from TMEM column t_row) through its staging
+// buffer: bf16 groups of 64 columns or fp32 groups of 32, optionally scaled by the row scale a_s
+// and the column scales bs[] (bf16-rounded like the reference when scaled).
+template <int CONV, int HALF>
+__device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *staging, int lane,
+                                             uint32_t t_row, int x0, int x_end, int y,
+                                             bool bf16_out, bool scaled, float a_s,
+                                             const float *bs) {
+  if (bf16_out) {
+#pragma unroll 1
+    for (int g = 0; g < HALF / 64; ++g) {
+      const int n0 = x0 + g * 64;
+      if (n0 >= x_end) break;
+      uint32_t r0[32], r1[32];
+      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64), r0);
+      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64 + 32), r1);
+      tmem_ld_wait();
+      uint32_t w[32];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float v0 = cvt_acc<CONV>(r0[2 * j]), v1 = cvt_acc<CONV>(r0[2 * j + 1]);
+        float v2 = cvt_acc<CONV>(r1[2 * j]), v3 = cvt_acc<CONV>(r1[2 * j + 1]);
+        if (scaled) {
+          v0 = __fmul_rn(__fmul_rn(v0, a_s), bs[g * 64 + 2 * j]);
+          v1 = __fmul_rn(__fmul_rn(v1, a_s), bs[g * 64 + 2 * j + 1]);
+          v2 = __fmul_rn(__fmul_rn(v2, a_s), bs[g * 64 + 32 + 2 * j]);
+          v3 = __fmul_rn(__fmul_rn(v3, a_s), bs[g * 64 + 32 + 2 * j + 1]);
+        }
+        w[j] = bf16_bits(v0) | (uint32_t(bf16_bits(v1)) << 16);
+        w[16 + j] = bf16_bits(v2) | (uint32_t(bf16_bits(v3)) << 16);
+      }
+      stage_and_store(map, staging, lane, w, n0, y);
+    }
+  } else {
+#pragma unroll 1
+    for (int g = 0; g < HALF / 32; ++g) {
+      const int n0 = x0 + g * 32;
+      if (n0 >= x_end) break;
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 32), r);
+      tmem_ld_wait();
+      uint32_t w[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float v = cvt_acc<CONV>(r[j]);
+        if (scaled) v = bf16_round(__fmul_rn(__fmul_rn(v, a_s), bs[g * 32 + j]));
+        w[j] = __float_as_uint(v);
+      }
+      stage_and_store(map, staging, lane, w, n0, y);
+    }
+  }
 }
 
 template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(64 + 32 * 8, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
@@ -262,7 +339,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], C::EPI_WARPS);
     }
     fence_barrier_init();
     tma_prefetch_desc(&tma_a);
@@ -344,11 +421,14 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    // epilogue warps 2..5: TMEM sub-partition (warp % 4) holds accumulator rows 32·(warp%4)..+31
+    // epilogue warps 2..9: TMEM lane quarter (warp % 4) holds accumulator rows 32·(warp%4)..+31;
+    // warps 2..5 take the tile's first BN/2 columns, warps 6..9 the second half
+    constexpr int HALF = BN / 2;
     const int sub = warp & 3;
-    const int ep_tid = threadIdx.x - 64;  // 0..127 across the four epilogue warps
+    const int col0 = ((warp - 2) >> 2) * HALF;  // first tile column of this warp
+    const int ep_tid = threadIdx.x - 64;        // 0..255 across the epilogue warps
+    uint8_t *staging = staging_all + (warp - 2) * 4096;
     const bool split_mode = p.epi == EPI_SPLIT;
-    int stage_buf = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
@@ -358,32 +438,32 @@ __global__ void __launch_bounds__(192, 1)
       // every lane polls; the warp proceeds only if all lanes saw the phase complete, so the
       // .sync.aligned TMEM loads below are always executed by the full warp
       const bool lane_ok = mbar_wait(&tfull[acc], acc_phase);
-      // the four epilogue warps agree (barrier 1, 128 threads), so a timed-out wait can never
-      // leave some of them inside the column-scale barrier below
+      // the epilogue warps agree (barrier 1), so a timed-out wait can never leave some of them
+      // inside the column-scale barrier below
       uint32_t all_ok;
       asm volatile(
           "{\n\t.reg .pred p, q;\n\t"
           "setp.ne.u32 p, %1, 0;\n\t"
-          "bar.red.and.pred q, 1, 128, p;\n\t"
+          "bar.red.and.pred q, 1, %2, p;\n\t"
           "selp.u32 %0, 1, 0, q;\n\t}"
           : "=r"(all_ok)
-          : "r"(static_cast<uint32_t>(lane_ok))
+          : "r"(static_cast<uint32_t>(lane_ok)), "n"(32 * C::EPI_WARPS)
           : "memory");
       if (!all_ok) break;
       tc_fence_after();
       const int trow = sub * 32 + lane;
       const int row = tm * C::BM + trow;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
-                             static_cast<uint32_t>(acc * BN);
+                             static_cast<uint32_t>(acc * BN + col0);
       if (p.tma_store) {
         // column scales of this tile, once, in shared memory (barrier 1: the epilogue warps)
         const bool scaled = p.epi == EPI_SCALED;
         if (scaled) {
-          for (int j = ep_tid; j < BN; j += 128) {
+          for (int j = ep_tid; j < BN; j += 32 * C::EPI_WARPS) {
             const int n = tn * BN + j;
             s_bscale[j] = (p.b_scale != nullptr && n < p.N) ? __ldg(p.b_scale + n) : 1.0f;
           }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
+          asm volatile("bar.sync 1, %0;" ::"n"(32 * C::EPI_WARPS) : "memory");
         }
         const float a_s = (scaled && row < p.M) ? __ldg(p.a_scale + row) : 1.0f;
         const bool bf16_out =
@@ -392,57 +472,26 @@ __global__ void __launch_bounds__(192, 1)
         const int y = split_mode
                           ? (split * p.tiles_m * p.tiles_n + tile) * C::BM + sub * 32
                           : tm * C::BM + sub * 32;
-        const int x0 = split_mode ? 0 : tn * BN;
+        const int x0 = (split_mode ? 0 : tn * BN) + col0;
         const int x_end = split_mode ? BN : p.N;
+        const float *bs = s_bscale + col0;
         if (!split_mode && y >= p.M) {
           // this warp's 32 rows lie past the output: nothing to store
-        } else if (bf16_out) {
-#pragma unroll 1
-          for (int g = 0; g < BN / 64; ++g) {
-            const int n0 = tn * BN + g * 64;
-            if (n0 >= p.N) break;
-            uint32_t r0[32], r1[32];
-            tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64), r0);
-            tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64 + 32), r1);
-            tmem_ld_wait();
-            uint32_t w[32];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float v0 = acc_to_float<T>(r0[2 * j]), v1 = acc_to_float<T>(r0[2 * j + 1]);
-              float v2 = acc_to_float<T>(r1[2 * j]), v3 = acc_to_float<T>(r1[2 * j + 1]);
-              if (scaled) {
-                v0 = __fmul_rn(__fmul_rn(v0, a_s), s_bscale[g * 64 + 2 * j]);
-                v1 = __fmul_rn(__fmul_rn(v1, a_s), s_bscale[g * 64 + 2 * j + 1]);
-                v2 = __fmul_rn(__fmul_rn(v2, a_s), s_bscale[g * 64 + 32 + 2 * j]);
-                v3 = __fmul_rn(__fmul_rn(v3, a_s), s_bscale[g * 64 + 32 + 2 * j + 1]);
-              }
-              w[j] = bf16_bits(v0) | (uint32_t(bf16_bits(v1)) << 16);
-              w[16 + j] = bf16_bits(v2) | (uint32_t(bf16_bits(v3)) << 16);
-            }
-            stage_and_store(&tma_c, staging_all + (warp - 2) * 8192, stage_buf, lane, w, n0, y);
-          }
+        } else if constexpr (sizeof(T) == 1) {
+          if (p.acc_small)
+            epilogue_tma<1, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out, scaled,
+                                  a_s, bs);
+          else
+            epilogue_tma<2, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out, scaled,
+                                  a_s, bs);
         } else {
-#pragma unroll 1
-          for (int g = 0; g < BN / 32; ++g) {
-            const int n0 = x0 + g * 32;
-            if (n0 >= x_end) break;
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 32), r);
-            tmem_ld_wait();
-            uint32_t w[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float v = acc_to_float<T>(r[j]);
-              if (scaled) v = bf16_round(__fmul_rn(__fmul_rn(v, a_s), s_bscale[g * 32 + j]));
-              w[j] = __float_as_uint(v);
-            }
-            stage_and_store(&tma_c, staging_all + (warp - 2) * 8192, stage_buf, lane, w, n0, y);
-          }
+          epilogue_tma<0, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out, scaled,
+                                a_s, bs);
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          const int n0 = tn * BN + c * 32;
+        for (int c = 0; c < HALF / 32; ++c) {
+          const int n0 = tn * BN + col0 + c * 32;
           if (n0 >= p.N) break;
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
@@ -616,7 +665,7 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
   }
   const int64_t units = static_cast<int64_t>(args.tiles_m) * args.tiles_n * args.splits;
   const int grid = static_cast<int>(units < sms ? units : sms);
-  kernel<<<grid, 192, C::SMEM_BYTES, s>>>(ma, mb, mc, args);
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(ma, mb, mc, args);
   return check_launch("umma_gemm_kernel");
 }
 
@@ -636,7 +685,7 @@ extern "C" int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_
                                  const int8_t *rhs, int64_t rhs_stride_k, int64_t rhs_stride_n,
                                  const float *lhs_scale, const float *rhs_scale, void *out,
                                  int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
-                                 void *stream) {
+                                 int rhs_abs_max, void *stream) {
   if (M < 0 || N < 0 || K < 0) return fail(RT_ERR_INVALID_ARGUMENT, "scaled_int8_mm: negative shape");
   if (out_dtype != RT_BF16 && out_dtype != RT_F32)
     return fail(RT_ERR_DTYPE, "scaled_int8_mm: output must be bfloat16 or float32");
@@ -651,6 +700,8 @@ extern "C" int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_
   args.M = static_cast<int>(M), args.N = static_cast<int>(N), args.K = static_cast<int>(K);
   args.a_scale = lhs_scale, args.b_scale = rhs_scale, args.out = out, args.ldo = ldo;
   args.out_dtype = out_dtype, args.epi = EPI_SCALED, args.splits = 1;
+  const int64_t rhs_bound = (rhs_abs_max <= 0 || rhs_abs_max > 128) ? 128 : rhs_abs_max;
+  args.acc_small = K * 128 * rhs_bound < (int64_t(1) << 22);
   args.vec_store = aligned16(out) && (ldo * static_cast<int64_t>(osz)) % 16 == 0 &&
                    (rhs_scale == nullptr || aligned16(rhs_scale));
   // operand majorness from strides, as the reference kernel addresses them

@@ -105,12 +105,15 @@ def quantize_columns(values: Tensor) -> tuple[Tensor, Tensor]:
 
 
 def _scaled_int8_mm_into(
-    lhs: Tensor, rhs: Tensor, lhs_scale: Tensor, rhs_scale: Tensor | None, out: Tensor
+    lhs: Tensor, rhs: Tensor, lhs_scale: Tensor, rhs_scale: Tensor | None, out: Tensor,
+    rhs_abs_max: int = 0,
 ) -> Tensor:
     """No-sync core: out = bf16((float(lhs @ rhs) * lhs_scale[m]) * rhs_scale[n]).
 
     `out` is (M, N) bf16, or fp32 receiving the bf16-rounded values (the widening cast of
     ratchet.py:67 fused into the epilogue).  Operands are passed with their strides.
+    rhs_abs_max: a guaranteed bound on |rhs| (ratchet codes: 7) or 0; it only lets the epilogue
+    use a cheaper exact accumulator conversion.
     """
     m, k = lhs.shape
     _, n = rhs.shape
@@ -119,7 +122,7 @@ def _scaled_int8_mm_into(
         _lib.lib().rt_scaled_int8_mm(
             lhs.data_ptr(), lhs.stride(0), lhs.stride(1), rhs.data_ptr(), rhs.stride(0),
             rhs.stride(1), lhs_scale.data_ptr(), _lib.ptr(rhs_scale), out.data_ptr(),
-            _lib.dtype_code(out), out.stride(0), m, n, k, _lib.stream_of(lhs),
+            _lib.dtype_code(out), out.stride(0), m, n, k, int(rhs_abs_max), _lib.stream_of(lhs),
         )
     )
     if ev is not None:

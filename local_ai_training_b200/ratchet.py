@@ -82,7 +82,8 @@ class _RatchetMatmul(torch.autograd.Function):
             out_dtype = result_dtype if result_dtype in (torch.float32, torch.bfloat16) else torch.bfloat16
             output = torch.empty((q.shape[0], out_features), device=q.device, dtype=out_dtype)
             # rhs = codeᵀ: (in, out) view of the [out, in] code tensor, K-major for the GEMM
-            _scaled_int8_mm_into(q, code.t(), s, scale.float().contiguous(), output)
+            _scaled_int8_mm_into(q, code.t(), s, scale.float().contiguous(), output,
+                                 rhs_abs_max=_code_bound(gradient_sink))
             return output.reshape(*input_shape[:-1], out_features).to(result_dtype)
 
         _require_cuda(inputs, "the ratchet matmul")
@@ -119,15 +120,22 @@ class _RatchetMatmul(torch.autograd.Function):
         elif ctx.int8_backward and ctx.used_fused_int8 and ctx.fuse_backward_update:
             # fold the per-out scale into the gradient, stochastic-round to int8 (one pass that
             # also writes bf16(gradient) for grad_weight), int8 GEMM against the codes
-            grad_bf16 = torch.empty(flat_gradient.shape, device=flat_gradient.device,
-                                    dtype=torch.bfloat16)
+            # a bf16 gradient with unit column stride is already the grad_weight operand; any
+            # other gets its bf16 copy written by the same pass
+            if flat_gradient.dtype == torch.bfloat16 and flat_gradient.stride(1) == 1:
+                grad_bf16, bf16_copy = flat_gradient, None
+            else:
+                grad_bf16 = torch.empty(flat_gradient.shape, device=flat_gradient.device,
+                                        dtype=torch.bfloat16)
+                bf16_copy = grad_bf16
             seed, step, layer, step_dev = _sr_key(ctx.gradient_sink)
             gq, gs = _quantize_rows_fused(flat_gradient, scale.float(), stochastic=True, seed=seed,
-                                          step=step, layer=layer, bf16_copy=grad_bf16,
+                                          step=step, layer=layer, bf16_copy=bf16_copy,
                                           step_dev=step_dev)  # the call advances step_dev
             gi_dtype = ctx.input_dtype if ctx.input_dtype in (torch.float32, torch.bfloat16) else torch.bfloat16
             grad_input = torch.empty((gq.shape[0], in_features), device=gq.device, dtype=gi_dtype)
-            _scaled_int8_mm_into(gq, code, gs, None, grad_input)
+            _scaled_int8_mm_into(gq, code, gs, None, grad_input,
+                                 rhs_abs_max=_code_bound(ctx.gradient_sink))
         else:
             grad_bf16 = flat_gradient.to(torch.bfloat16)
             effective = code.to(torch.bfloat16) * scale.to(torch.bfloat16)[:, None]
@@ -154,6 +162,13 @@ class _RatchetMatmul(torch.autograd.Function):
             grad_scale = (grad_weight * code.float()).sum(dim=1) if want_scale else None
         return (grad_input.reshape(ctx.input_shape).to(ctx.input_dtype), None, None, None,
                 grad_scale, None, None, None, None, None)
+
+
+def _code_bound(sink) -> int:
+    """|code| bound of the layer behind a gradient sink (its max_code; the layer keeps every code
+    within it), or 0 when the codes come from elsewhere."""
+    layer = getattr(sink, "__self__", None)
+    return int(layer.max_code) if isinstance(layer, DiscreteRatchetLinear) else 0
 
 
 def _sr_key(sink) -> tuple[int | None, int, int, Tensor | None]:

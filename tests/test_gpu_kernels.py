@@ -150,9 +150,33 @@ def test_scaled_int8_mm_tcgen05_layouts_match_oracle(cuda_device, m, k, n, layou
     np.testing.assert_array_equal(_np(out), O.scaled_int8_mm(lhs.numpy(), rhs.numpy(), ls.numpy(), None))
 
 
-@pytest.mark.parametrize("k,n", [(512, 512), (512, 2048), (2048, 512)])
-def test_scaled_int8_mm_full_size_exact(cuda_device, k, n):
-    """BASELINE config 2 shapes, M = 16384: exact integer sums on the device as the checker."""
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_scaled_int8_mm_full_range_accumulators_round_like_oracle(cuda_device, out_dtype):
+    """|acc| up to 127·127·8192 > 2^24: the int32 -> fp32 conversion of the epilogue rounds."""
+    from local_ai_training_b200.int8_matmul import _scaled_int8_mm_into
+
+    torch.manual_seed(21)
+    m, k, n = 256, 8192, 384
+    lhs = torch.randint(-127, 128, (m, k), dtype=torch.int8)
+    lhs[:8] = 127  # rows of maximal sums against the all-127 columns below
+    rhs = torch.randint(-127, 128, (k, n), dtype=torch.int8)
+    rhs[:, :8] = 127
+    rhs[:, 8:16] = -127
+    ls = torch.rand(m) * 0.05 + 1e-3
+    rs = torch.rand(n) * 0.05 + 5e-3
+    expected, acc = O.scaled_int8_mm(lhs.numpy(), rhs.numpy(), ls.numpy(), rs.numpy(), return_acc=True)
+    assert np.abs(acc).max() > 2**24
+    out = torch.empty((m, n), device=cuda_device, dtype=out_dtype)
+    _scaled_int8_mm_into(lhs.to(cuda_device), rhs.t().contiguous().to(cuda_device).t(),
+                         ls.to(cuda_device), rs.to(cuda_device), out)
+    np.testing.assert_array_equal(_np(out), expected)
+
+
+@pytest.mark.parametrize("bound", [0, 7])
+@pytest.mark.parametrize("k,n", [(512, 512), (512, 2048), (2048, 512), (4096, 256)])
+def test_scaled_int8_mm_full_size_exact(cuda_device, k, n, bound):
+    """BASELINE config 2 shapes, M = 16384: exact integer sums on the device as the checker;
+    bound = 7 (the codes' bound) takes the 2-op accumulator conversion up to K·128·7 < 2^22."""
     from local_ai_training_b200.int8_matmul import _scaled_int8_mm_into, quantize_rows
 
     torch.manual_seed(1337)
@@ -161,14 +185,16 @@ def test_scaled_int8_mm_full_size_exact(cuda_device, k, n):
     code = torch.randint(-3, 4, (n, k), device=cuda_device, dtype=torch.int8)
     scale = torch.rand(n, device=cuda_device) * 0.045 + 0.005
     out = torch.empty((16384, n), device=cuda_device, dtype=torch.bfloat16)
-    _scaled_int8_mm_into(q, code.t(), s, scale, out)
-    acc = q.float() @ code.float().t()  # exact: |acc| <= 127*3*2048 < 2^24
+    q[:4] = -128 if k == 4096 else q[:4]  # extreme sums near the conversion bound
+    code[:4] = 7 if k == 4096 else code[:4]
+    _scaled_int8_mm_into(q, code.t(), s, scale, out, rhs_abs_max=bound)
+    acc = q.float() @ code.float().t()  # exact: |acc| <= 128*7*4096 < 2^24
     expected = ((acc * s[:, None]) * scale[None, :]).to(torch.bfloat16)
     assert torch.equal(out, expected)
     # grad_input form: B = code (MN-major), no column scale
     gi = torch.empty((16384, k), device=cuda_device, dtype=torch.bfloat16)
     gq = torch.randint(-127, 128, (16384, n), device=cuda_device, dtype=torch.int8)
-    _scaled_int8_mm_into(gq, code, s, None, gi)
+    _scaled_int8_mm_into(gq, code, s, None, gi, rhs_abs_max=bound)
     acc2 = gq.float() @ code.float()
     assert torch.equal(gi, (acc2 * s[:, None]).to(torch.bfloat16))
 
