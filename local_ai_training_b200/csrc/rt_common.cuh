@@ -39,6 +39,11 @@ __device__ __forceinline__ float bf16_round(float x) {
 __device__ __forceinline__ uint16_t bf16_bits(float x) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
+// Two floats -> one word of RN bf16s (a in the low half): a single paired conversion.
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
 __device__ __forceinline__ float bf16_from_bits(uint16_t b) {
   return __uint_as_float(static_cast<uint32_t>(b) << 16);
 }

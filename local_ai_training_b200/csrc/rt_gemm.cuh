@@ -276,18 +276,26 @@ __device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *st
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64 + 32), r1);
       tmem_ld_wait();
       uint32_t w[32];
+      const float4 *bs4 = reinterpret_cast<const float4 *>(bs + g * 64);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float v0 = cvt_acc<CONV>(r0[2 * j]), v1 = cvt_acc<CONV>(r0[2 * j + 1]);
-        float v2 = cvt_acc<CONV>(r1[2 * j]), v3 = cvt_acc<CONV>(r1[2 * j + 1]);
-        if (scaled) {
-          v0 = __fmul_rn(__fmul_rn(v0, a_s), bs[g * 64 + 2 * j]);
-          v1 = __fmul_rn(__fmul_rn(v1, a_s), bs[g * 64 + 2 * j + 1]);
-          v2 = __fmul_rn(__fmul_rn(v2, a_s), bs[g * 64 + 32 + 2 * j]);
-          v3 = __fmul_rn(__fmul_rn(v3, a_s), bs[g * 64 + 32 + 2 * j + 1]);
+      for (int j = 0; j < 8; ++j) {  // columns 4j..4j+3 of r0 and 32+4j..32+4j+3 of r1
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[e] = cvt_acc<CONV>(r0[4 * j + e]);
+          v[4 + e] = cvt_acc<CONV>(r1[4 * j + e]);
         }
-        w[j] = bf16_bits(v0) | (uint32_t(bf16_bits(v1)) << 16);
-        w[16 + j] = bf16_bits(v2) | (uint32_t(bf16_bits(v3)) << 16);
+        if (scaled) {
+          const float4 sa = bs4[j], sb = bs4[8 + j];  // 16-byte broadcast reads
+          v[0] = __fmul_rn(__fmul_rn(v[0], a_s), sa.x), v[1] = __fmul_rn(__fmul_rn(v[1], a_s), sa.y);
+          v[2] = __fmul_rn(__fmul_rn(v[2], a_s), sa.z), v[3] = __fmul_rn(__fmul_rn(v[3], a_s), sa.w);
+          v[4] = __fmul_rn(__fmul_rn(v[4], a_s), sb.x), v[5] = __fmul_rn(__fmul_rn(v[5], a_s), sb.y);
+          v[6] = __fmul_rn(__fmul_rn(v[6], a_s), sb.z), v[7] = __fmul_rn(__fmul_rn(v[7], a_s), sb.w);
+        }
+        w[2 * j] = pack_bf16x2(v[0], v[1]);
+        w[2 * j + 1] = pack_bf16x2(v[2], v[3]);
+        w[16 + 2 * j] = pack_bf16x2(v[4], v[5]);
+        w[16 + 2 * j + 1] = pack_bf16x2(v[6], v[7]);
       }
       stage_and_store(map, staging, lane, w, n0, y);
     }
@@ -300,11 +308,21 @@ __device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *st
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 32), r);
       tmem_ld_wait();
       uint32_t w[32];
+      const float4 *bs4 = reinterpret_cast<const float4 *>(bs + g * 32);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        float v = cvt_acc<CONV>(r[j]);
-        if (scaled) v = bf16_round(__fmul_rn(__fmul_rn(v, a_s), bs[g * 32 + j]));
-        w[j] = __float_as_uint(v);
+      for (int j = 0; j < 8; ++j) {
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = cvt_acc<CONV>(r[4 * j + e]);
+        if (scaled) {
+          const float4 sc = bs4[j];
+          v[0] = bf16_round(__fmul_rn(__fmul_rn(v[0], a_s), sc.x));
+          v[1] = bf16_round(__fmul_rn(__fmul_rn(v[1], a_s), sc.y));
+          v[2] = bf16_round(__fmul_rn(__fmul_rn(v[2], a_s), sc.z));
+          v[3] = bf16_round(__fmul_rn(__fmul_rn(v[3], a_s), sc.w));
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[4 * j + e] = __float_as_uint(v[e]);
       }
       stage_and_store(map, staging, lane, w, n0, y);
     }
@@ -329,7 +347,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
   uint64_t *tfull = bars + 2 * STAGES;
   uint64_t *tempty = bars + 2 * STAGES + 2;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
-  __shared__ float s_bscale[BN];
+  __shared__ __align__(16) float s_bscale[BN];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0 && lane == 0) {
