@@ -274,7 +274,8 @@ __device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *st
       uint32_t r0[32], r1[32];
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64), r0);
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64 + 32), r1);
-      tmem_ld_wait();
+      tmem_ld_wait_regs(r0);
+      tmem_regs_after_wait(r1);
       uint32_t w[32];
       const float4 *bs4 = reinterpret_cast<const float4 *>(bs + g * 64);
 #pragma unroll
@@ -306,7 +307,7 @@ __device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *st
       if (n0 >= x_end) break;
       uint32_t r[32];
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 32), r);
-      tmem_ld_wait();
+      tmem_ld_wait_regs(r);
       uint32_t w[32];
       const float4 *bs4 = reinterpret_cast<const float4 *>(bs + g * 32);
 #pragma unroll
@@ -453,6 +454,17 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
       const int tn = u % p.tiles_n, rest = u / p.tiles_n;
       const int tm = rest % p.tiles_m, split = rest / p.tiles_m;
       const int tile = tm * p.tiles_n + tn;
+      const int trow = sub * 32 + lane;
+      const int row = tm * C::BM + trow;
+      // this tile's scales, requested before the wait so that their latency overlaps the MMA
+      const bool scaled = p.epi == EPI_SCALED && p.tma_store;
+      static_assert(BN <= 32 * C::EPI_WARPS, "one column scale per epilogue thread");
+      float col_scale = 1.0f, a_s = 1.0f;
+      if (scaled) {
+        const int n = tn * BN + ep_tid;
+        if (ep_tid < BN && p.b_scale != nullptr && n < p.N) col_scale = __ldg(p.b_scale + n);
+        if (row < p.M) a_s = __ldg(p.a_scale + row);
+      }
       // every lane polls; the warp proceeds only if all lanes saw the phase complete, so the
       // .sync.aligned TMEM loads below are always executed by the full warp
       const bool lane_ok = mbar_wait(&tfull[acc], acc_phase);
@@ -469,21 +481,15 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
           : "memory");
       if (!all_ok) break;
       tc_fence_after();
-      const int trow = sub * 32 + lane;
-      const int row = tm * C::BM + trow;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN + col0);
       if (p.tma_store) {
-        // column scales of this tile, once, in shared memory (barrier 1: the epilogue warps)
-        const bool scaled = p.epi == EPI_SCALED;
+        // column scales of this tile in shared memory; the barrier above also guarantees that
+        // every warp has finished reading the previous tile's (barrier 1: the epilogue warps)
         if (scaled) {
-          for (int j = ep_tid; j < BN; j += 32 * C::EPI_WARPS) {
-            const int n = tn * BN + j;
-            s_bscale[j] = (p.b_scale != nullptr && n < p.N) ? __ldg(p.b_scale + n) : 1.0f;
-          }
+          if (ep_tid < BN) s_bscale[ep_tid] = col_scale;
           asm volatile("bar.sync 1, %0;" ::"n"(32 * C::EPI_WARPS) : "memory");
         }
-        const float a_s = (scaled && row < p.M) ? __ldg(p.a_scale + row) : 1.0f;
         const bool bf16_out =
             !split_mode && (p.out_dtype == RT_BF16 || p.epi == EPI_BF16_STORE);
         // split mode: the fp32 partial tile goes to its own 128 x BN block of the workspace
@@ -513,7 +519,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
           if (n0 >= p.N) break;
           uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(c * 32), r);
-          tmem_ld_wait();
+          tmem_ld_wait_regs(r);
           epilogue_chunk<T>(p, p.epi, row, n0, r);
         }
       }
