@@ -240,12 +240,25 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
     tokens_resident = dev_tokens16.long()
     loss_host = torch.zeros(1, dtype=torch.float32).pin_memory()
 
+    ddp = None
+    if world > 1:
+        # data parallel: reduce-scatter of bf16 grad_W by owned rows during backward, rank-local
+        # update, all-gather of the owned packed rows, averaged support gradients
+        from local_ai_training_b200.dist import RatchetDataParallel
+
+        ddp = RatchetDataParallel(model)
+
     def step(tokens):
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
             _, loss = model(tokens[:, :-1], tokens[:, 1:])
         loss.backward()
-        model.ratchet_update(validate=False)
-        opt.step()
+        if ddp is None:
+            model.ratchet_update(validate=False)
+            opt.step()
+        else:
+            ddp.synchronize_gradients()
+            opt.step()
+            ddp.ratchet_update(validate=False)
         return loss
 
     def eager_step(tokens):
@@ -359,6 +372,8 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
     peak_info = int8_peak_probe(torch, device) if rank == 0 and not args.no_peak_probe else {}
     if world > 1:
         dist.barrier(device_ids=[local_rank])
+        graph = None  # a graph holding NCCL work is released before the group goes
+        torch.cuda.synchronize()
         dist.destroy_process_group()
     if rank != 0:
         return

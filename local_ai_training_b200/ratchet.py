@@ -142,6 +142,20 @@ class _RatchetMatmul(torch.autograd.Function):
             grad_input = grad_bf16 @ effective
 
         # ---- grad_weight (ratchet.py:148-163)
+        dp = getattr(getattr(ctx.gradient_sink, "__self__", None), "_dp", None)
+        if dp is not None and ctx.mode != "fp32":
+            # data-parallel: the bf16-rounded grad_W goes to the layer's reduce-scatter buffer and
+            # the update runs later on the owned rows of the summed gradient
+            layer = ctx.gradient_sink.__self__
+            if grad_bf16 is None:
+                grad_bf16 = flat_gradient.to(torch.bfloat16)
+            target = dp.grad_buffer(layer)
+            grad_weight_bf16(grad_bf16, inputs_bf16, out=target)
+            grad_scale = ((target.float() * code.float()).sum(dim=1)
+                          if ctx.needs_input_grad[4] else None)
+            dp.grad_ready(layer)
+            return (grad_input.reshape(ctx.input_shape).to(ctx.input_dtype), None, None, None,
+                    grad_scale, None, None, None, None, None)
         if ctx.mode == "fp32":
             grad_weight = flat_gradient.to(torch.float32).t() @ flat_inputs.to(torch.float32)
             round_bf16 = False
@@ -360,6 +374,8 @@ class DiscreteRatchetLinear(nn.Module):
         self.sr_layer: int = 0
         self._sr_step = 0
         self._sr_step_dev: Tensor | None = None
+        # data-parallel runtime this layer's gradient goes to (local_ai_training_b200.dist)
+        self._dp = None
 
     # ------------------------------------------------------------------ construction helpers
     @classmethod
@@ -414,6 +430,21 @@ class DiscreteRatchetLinear(nn.Module):
 
     def effective_weight(self) -> Tensor:
         return self.code.to(dtype=self.scale.dtype) * self.scale[:, None]
+
+    def _refresh_code_mirror(self) -> None:
+        """Re-derives the int8 code mirror from `packed` in place, for writers of `packed` that do
+        not move its version counter (collectives writing into it)."""
+        pk = self.packed
+        key = (pk.device, pk.data_ptr(), pk._version)
+        if self._code_mirror is None or self._code_mirror.shape != pk.shape or not pk.is_cuda:
+            self._code_mirror = None
+            self.code_int8()
+            return
+        rows, cols = pk.shape
+        _lib.check(_lib.lib().rt_unpack_code_pressure(
+            pk.data_ptr(), pk.stride(0), rows, cols, self.max_code, self._code_mirror.data_ptr(),
+            self._code_mirror.stride(0), None, 0, _lib.stream_of(pk)))
+        self._code_mirror_key = key
 
     def code_int8(self) -> Tensor:
         """The int8 code tensor the GEMMs read, kept in step with `packed`."""
