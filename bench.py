@@ -370,6 +370,7 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
     gpu_launches = sum(f["launches"] for f in fams.values())  # library kernels per K steps
 
     peak_info = int8_peak_probe(torch, device) if rank == 0 and not args.no_peak_probe else {}
+    used_graph = graph is not None
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         graph = None  # a graph holding NCCL work is released before the group goes
@@ -451,7 +452,7 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
         "roofline": roofline,
         "cpu_baseline": cpu,
         "gpu_launches": gpu_launches,
-        "cuda_graph": graph is not None,
+        "cuda_graph": used_graph,
         "cuda_graph_error": graph_error,
         "profile_pass": profile_mode,
         "profile_ms_per_step": p_elapsed / args.steps * 1e3,

@@ -141,21 +141,37 @@ class RatchetDataParallel:
             layer._capture_weight_gradient(shard, state.row_start, state.row_end,
                                            round_bf16=False)
             layer._pending_stats_total_weights = layer.out_features * layer.in_features
-            if self.world > 1:
+        if self.world > 1:
+            # re-replicate: every layer's owned packed rows (and rms_ema rows), as one group of
+            # collectives where the backend can batch them
+            gathers = []
+            for state in self.states:
+                layer = state.layer
                 pk = layer.packed
-                dist.all_gather_into_tensor(pk, pk[state.row_start:state.row_end].contiguous(),
-                                            group=self.group)
+                gathers.append((pk, pk[state.row_start:state.row_end]))
                 if layer.rms_ema_beta > 0.0:
-                    ema = layer.rms_ema
-                    dist.all_gather_into_tensor(ema, ema[state.row_start:state.row_end].contiguous(),
-                                                group=self.group)
-                layer._refresh_code_mirror()
+                    gathers.append((layer.rms_ema, layer.rms_ema[state.row_start:state.row_end]))
+            self._all_gather_many(gathers)
+            for state in self.states:
+                state.layer._refresh_code_mirror()
         if self.world > 1:
             self._reduce_step_stats()
         if hasattr(self.model, "ratchet_update"):
             return self.model.ratchet_update(validate=validate)
         updates = [s.layer.ratchet_update(validate=validate) for s in self.states]
         return _aggregate(updates, validate)
+
+    def _all_gather_many(self, pairs: list[tuple[Tensor, Tensor]]) -> None:
+        """In-place all-gathers (each input is this rank's block of its output)."""
+        if dist.get_backend(self.group) == "nccl":
+            device = pairs[0][0].device
+            with dist._coalescing_manager(group=self.group, device=device, async_ops=True) as cm:
+                for out, inp in pairs:
+                    dist.all_gather_into_tensor(out, inp, group=self.group)
+            cm.wait()
+        else:
+            for out, inp in pairs:
+                dist.all_gather_into_tensor(out, inp.contiguous(), group=self.group)
 
     def _reduce_step_stats(self) -> None:
         """Sums each layer's [4 counters, rms sum] across ranks in one all-reduce (float64 holds

@@ -22,8 +22,10 @@ pytestmark = pytest.mark.gpu
 def _cfg(int8_backward: bool):
     from local_ai_training_b200 import ModelConfig
 
+    # threshold 2 with rms_ema so that codes move within a few steps and the EMA path runs
     return ModelConfig(vocab_size=64, block_size=32, n_layer=2, n_head=2, n_embd=64, dropout=0.0,
-                       matmul_mode="int8", int8_backward=int8_backward)
+                       pressure_threshold=2, rms_ema_beta=0.5, matmul_mode="int8",
+                       int8_backward=int8_backward)
 
 
 def _free_port() -> int:
@@ -58,6 +60,8 @@ def test_single_rank_dp_equals_fused_single_process(cuda_device, int8_backward):
             a.sr_seed = b.sr_seed = 21
         ddp = RatchetDataParallel(dp_model)
         gen = torch.Generator().manual_seed(4)
+        before = [l.packed.clone() for l in plain.ratchet_layers()]
+        moves = 0
         for _ in range(3):
             tokens = torch.randint(0, 64, (4, 33), generator=gen).to(cuda_device)
             la, sa = _step(plain, tokens)
@@ -65,9 +69,13 @@ def test_single_rank_dp_equals_fused_single_process(cuda_device, int8_backward):
             assert la == lb
             assert int(sa.code_moves) == int(sb.code_moves)
             assert int(sa.total_weights) == int(sb.total_weights)
-        for a, b in zip(plain.ratchet_layers(), dp_model.ratchet_layers()):
+            moves += int(sa.code_moves)
+        assert moves > 0
+        for a, b, c in zip(plain.ratchet_layers(), dp_model.ratchet_layers(), before):
             assert torch.equal(a.packed, b.packed)
             assert torch.equal(a.code_int8(), b.code_int8())
+            assert torch.equal(a.rms_ema, b.rms_ema)
+        assert any(not torch.equal(a.packed, c) for a, c in zip(plain.ratchet_layers(), before))
         ddp.detach()
     finally:
         dist.destroy_process_group()
@@ -93,13 +101,14 @@ def _two_rank_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     ddp = RatchetDataParallel(model)
     gen = torch.Generator().manual_seed(100 + rank)
     moves = 0
-    for _ in range(2):
+    for _ in range(3):
         tokens = torch.randint(0, 64, (4, 33), generator=gen).to(device)
         _, stats = _step(model, tokens, ddp)
         moves += int(stats.code_moves)
     changed = sum(int((b != l.packed).sum()) for b, l in zip(before, model.ratchet_layers()))
     torch.save({"packed": [l.packed.cpu() for l in model.ratchet_layers()],
                 "mirror": [l.code_int8().cpu() for l in model.ratchet_layers()],
+                "ema": [l.rms_ema.cpu() for l in model.ratchet_layers()],
                 "moves": moves, "changed": changed},
                os.path.join(out_dir, f"rank{rank}.pt"))
     dist.barrier()
@@ -116,4 +125,7 @@ def test_two_rank_state_stays_replicated(tmp_path):
         assert torch.equal(a, b)
     for a, b in zip(r0["mirror"], r1["mirror"]):
         assert torch.equal(a, b)
+    for a, b in zip(r0["ema"], r1["ema"]):
+        assert torch.equal(a, b)
     assert r0["moves"] == r1["moves"] and r0["moves"] > 0
+    assert r0["changed"] == r1["changed"] and r0["changed"] > 0
