@@ -293,64 +293,69 @@ __device__ __forceinline__ void sr_step_arrive(const QuantArgs &a, uint32_t step
 
 template <typename T, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
+  // grid-stride over groups of RPC rows: a resident-sized grid (few CTAs, so that the step
+  // ticket of sr_step_arrive costs one atomic per resident CTA)
   constexpr int RPC = CTA / RT;
   __shared__ float smx[RPC * 8];
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * RPC + sub;
-  const bool live = row < a.rows;
   const int64_t nch = a.cols / 8;
-  const T *xr = static_cast<const T *>(a.x) + (live ? row : 0) * a.stride_row;
+  const int64_t groups = (a.rows + RPC - 1) / RPC;
   const uint32_t step = sr_step_read(a);
-  float v[VPT][8];
-  float amax = 0.0f;
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t row = grp * RPC + sub;
+    const bool live = row < a.rows;
+    const T *xr = static_cast<const T *>(a.x) + (live ? row : 0) * a.stride_row;
+    float v[VPT][8];
+    float amax = 0.0f;
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int64_t c = t + static_cast<int64_t>(i) * RT;
-    if (live && c < nch) {
-      ld8(xr + 8 * c, v[i]);
-      if (a.xbf16 != nullptr)
-        st8(reinterpret_cast<__nv_bfloat16 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c), v[i]);
-      if (a.col_scale != nullptr) {
-        float cs[8];
-        ld8(a.col_scale + 8 * c, cs);
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      if (live && c < nch) {
+        ld8(xr + 8 * c, v[i]);
+        if (a.xbf16 != nullptr)
+          st8(reinterpret_cast<__nv_bfloat16 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c), v[i]);
+        if (a.col_scale != nullptr) {
+          float cs[8];
+          ld8(a.col_scale + 8 * c, cs);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] = __fmul_rn(v[i][j], cs[j]);
+          for (int j = 0; j < 8; ++j) v[i][j] = __fmul_rn(v[i][j], cs[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
     }
-  }
-  amax = row_max<RT>(amax, smx, sub, t);
-  const float scale = row_scale_of(amax);
-  const float rcp = __frcp_rn(scale);
-  if (live && t == 0) a.row_scale[row] = scale;
-  int8_t *qr = a.q + (live ? row : 0) * a.ldq;
+    amax = row_max<RT>(amax, smx, sub, t);  // CTA-uniform trip count: its barriers are safe
+    const float scale = row_scale_of(amax);
+    const float rcp = __frcp_rn(scale);
+    if (live && t == 0) a.row_scale[row] = scale;
+    int8_t *qr = a.q + (live ? row : 0) * a.ldq;
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int64_t c = t + static_cast<int64_t>(i) * RT;
-    if (!live || c >= nch) continue;
-    uint2 o;
-    if (a.stochastic) {
-      const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;  // multiple of 8
-      const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
-      o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_u_lo(p.x)),
-                     quant_sr_i(v[i][1], scale, rcp, sr_u_hi(p.x)),
-                     quant_sr_i(v[i][2], scale, rcp, sr_u_lo(p.y)),
-                     quant_sr_i(v[i][3], scale, rcp, sr_u_hi(p.y)));
-      o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_u_lo(p.z)),
-                     quant_sr_i(v[i][5], scale, rcp, sr_u_hi(p.z)),
-                     quant_sr_i(v[i][6], scale, rcp, sr_u_lo(p.w)),
-                     quant_sr_i(v[i][7], scale, rcp, sr_u_hi(p.w)));
-    } else {
-      o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
-                     quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
-      o.y = pack4_i8(quant_rn_i(v[i][4], scale, rcp), quant_rn_i(v[i][5], scale, rcp),
-                     quant_rn_i(v[i][6], scale, rcp), quant_rn_i(v[i][7], scale, rcp));
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      if (!live || c >= nch) continue;
+      uint2 o;
+      if (a.stochastic) {
+        const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;  // multiple of 8
+        const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
+        o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_u_lo(p.x)),
+                       quant_sr_i(v[i][1], scale, rcp, sr_u_hi(p.x)),
+                       quant_sr_i(v[i][2], scale, rcp, sr_u_lo(p.y)),
+                       quant_sr_i(v[i][3], scale, rcp, sr_u_hi(p.y)));
+        o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_u_lo(p.z)),
+                       quant_sr_i(v[i][5], scale, rcp, sr_u_hi(p.z)),
+                       quant_sr_i(v[i][6], scale, rcp, sr_u_lo(p.w)),
+                       quant_sr_i(v[i][7], scale, rcp, sr_u_hi(p.w)));
+      } else {
+        o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
+                       quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
+        o.y = pack4_i8(quant_rn_i(v[i][4], scale, rcp), quant_rn_i(v[i][5], scale, rcp),
+                       quant_rn_i(v[i][6], scale, rcp), quant_rn_i(v[i][7], scale, rcp));
+      }
+      *reinterpret_cast<uint2 *>(qr + 8 * c) = o;
     }
-    *reinterpret_cast<uint2 *>(qr + 8 * c) = o;
   }
   sr_step_arrive(a, step);
 }
@@ -399,7 +404,12 @@ static int quant_rows_dispatch(const QuantArgs &a, cudaStream_t s) {
                    (a.xbf16 == nullptr || (aligned16(a.xbf16) && a.ld_xbf16 % 8 == 0));
   const RowCfg cfg = vec ? row_cfg(a.cols / 8, a.rows) : RowCfg{0, 0};
   if (cfg.rt != 0) {
-    RT_DISPATCH_ROW(cfg, quant_rows_kernel, T, row_grid(a.rows, cfg.rt), a);
+    int sms = 0;
+    if (int rc = rt_sm_count(&sms)) return rc;
+    // four CTAs per SM are resident for every configuration up to two chunks per thread
+    const unsigned resident = static_cast<unsigned>(sms) * 4;
+    const unsigned groups = row_grid(a.rows, cfg.rt);
+    RT_DISPATCH_ROW(cfg, quant_rows_kernel, T, groups < resident ? groups : resident, a);
   } else {
     quant_rows_generic_kernel<T><<<static_cast<unsigned>(a.rows), CTA, 0, s>>>(a);
   }
