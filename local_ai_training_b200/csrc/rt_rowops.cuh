@@ -148,21 +148,19 @@ __device__ __forceinline__ int quant_rn_i(float v, float scale, float rcp) {
     return static_cast<int>(rintf(fminf(fmaxf(__fdiv_rn(v, scale), -127.0f), 127.0f)));
   return __float_as_int(t) - 0x4B400000;
 }
-// Stochastic rounding floor(RN(RN(v / scale) + u)), as an int in [-127, 127].  The floor is
-// taken with the rounding magic as well (no conversion unit): z = t + 1.5·2^23 holds n = RN(t)
-// in its low mantissa bits, d = t - n is exact, and floor(t) = n - (d < 0).  |d| <= 2^-12 (t
-// within the window of an integer) sends the element to the IEEE division.
+// Stochastic rounding floor(RN(RN(v / scale) + u)), as an int in [-127, 127].  With
+// t = v·rcp + u, floor(t) is taken as RN(t - 1/2) through the rounding magic (t - 1/2 is exact:
+// |t| < 2^8 and t is a multiple of 2^-17), which equals floor(t) unless t lies within the
+// window of an integer; those elements go to the IEEE division, floor and clamp.  Outside the
+// window the estimate stays within (-128, 128), so the fast path needs no clamp.
 __device__ __forceinline__ int quant_sr_i(float v, float scale, float rcp, float u) {
-  float t = __fadd_rn(__fmul_rn(v, rcp), u);
-  float z = __fadd_rn(t, kRoundMagic);
-  float d = __fsub_rn(t, __fsub_rn(z, kRoundMagic));
-  if (fabsf(d) <= kBoundaryWindow) {
-    t = __fadd_rn(__fdiv_rn(v, scale), u);
-    z = __fadd_rn(t, kRoundMagic);
-    d = __fsub_rn(t, __fsub_rn(z, kRoundMagic));
+  const float th = __fsub_rn(__fadd_rn(__fmul_rn(v, rcp), u), 0.5f);
+  const float z = __fadd_rn(th, kRoundMagic);
+  if (fabsf(__fsub_rn(th, __fsub_rn(z, kRoundMagic))) >= 0.5f - kBoundaryWindow) {
+    const float t = __fadd_rn(__fdiv_rn(v, scale), u);
+    return min(max(__float2int_rd(t), -127), 127);
   }
-  const int n = (__float_as_int(z) - 0x4B400000) - (d < 0.0f ? 1 : 0);
-  return min(max(n, -127), 127);
+  return __float_as_int(z) - 0x4B400000;
 }
 __device__ __forceinline__ int8_t quant_rn(float v, float scale, float rcp) {
   return static_cast<int8_t>(quant_rn_i(v, scale, rcp));
@@ -301,6 +299,18 @@ __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
   const int64_t nch = a.cols / 8;
   const int64_t groups = (a.rows + RPC - 1) / RPC;
   const uint32_t step = sr_step_read(a);
+  // this thread's chunks are the same columns in every row: their scales stay in registers
+  float cs[VPT][8];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (a.col_scale != nullptr && c < nch) {
+      ld8(a.col_scale + 8 * c, cs[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cs[i][j] = 1.0f;
+    }
+  }
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
     const int64_t row = grp * RPC + sub;
     const bool live = row < a.rows;
@@ -315,10 +325,8 @@ __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
         if (a.xbf16 != nullptr)
           st8(reinterpret_cast<__nv_bfloat16 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c), v[i]);
         if (a.col_scale != nullptr) {
-          float cs[8];
-          ld8(a.col_scale + 8 * c, cs);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[i][j] = __fmul_rn(v[i][j], cs[j]);
+          for (int j = 0; j < 8; ++j) v[i][j] = __fmul_rn(v[i][j], cs[i][j]);
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));

@@ -115,13 +115,16 @@ def bench_gradw(m, k, n, reps, flush, peaks):
 
 
 def bench_quant_sr(m, n, reps, flush, peaks, dtype=torch.float32):
+    """The grad_output quantiser as the layer calls it: column-scaled, stochastic, Philox step on
+    the device; an fp32 gradient also gets its bf16 copy written (a bf16 one is used in place)."""
     dev = torch.device("cuda")
     g = (torch.randn(m, n, device=dev) * 1e-3).to(dtype)
     cs = torch.rand(n, device=dev) * 0.04 + 0.01
-    gbf = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
-    t = _time(lambda: _quantize_rows_fused(g, cs, stochastic=True, seed=7, step=1, layer=0,
-                                           bf16_copy=gbf), reps, flush)
-    nbytes = m * n * (g.element_size() + 1 + 2) + 4 * m + 4 * n
+    gbf = torch.empty((m, n), device=dev, dtype=torch.bfloat16) if dtype != torch.bfloat16 else None
+    step_dev = torch.zeros(2, device=dev, dtype=torch.int32)
+    t = _time(lambda: _quantize_rows_fused(g, cs, stochastic=True, seed=7, step=0, layer=0,
+                                           bf16_copy=gbf, step_dev=step_dev), reps, flush)
+    nbytes = m * n * (g.element_size() + 1 + (2 if gbf is not None else 0)) + 4 * m + 4 * n
     return _report(f"quant_rows_sr_{str(dtype).split('.')[-1]}", [m, n], t, nbytes, 0, 0, peaks)
 
 
@@ -200,6 +203,8 @@ def main() -> None:
     parser.add_argument("--n", type=int, default=2048)
     parser.add_argument("--reps", type=int, default=20)
     parser.add_argument("--no-flush", action="store_true")
+    parser.add_argument("--dtype", choices=["f32", "bf16"], default="f32",
+                        help="input dtype of quant_sr / quant_rn")
     parser.add_argument("--int8-peak", type=float, default=4500.0,
                         help="INT8 dense peak (TOPS) for the fractions; datasheet by default")
     args = parser.parse_args()
@@ -227,9 +232,11 @@ def main() -> None:
     elif args.kernel == "gradw":
         bench_gradw(m, args.k, args.n, args.reps, flush, peaks)
     elif args.kernel == "quant_sr":
-        bench_quant_sr(m, args.n, args.reps, flush, peaks)
+        bench_quant_sr(m, args.n, args.reps, flush, peaks,
+                       torch.bfloat16 if args.dtype == "bf16" else torch.float32)
     elif args.kernel == "quant_rn":
-        bench_quant_rn(m, args.k, args.reps, flush, peaks)
+        bench_quant_rn(m, args.k, args.reps, flush, peaks,
+                       torch.bfloat16 if args.dtype == "bf16" else torch.float32)
     elif args.kernel == "dequant":
         bench_dequant(m, args.k, args.reps, flush, peaks)
     elif args.kernel == "update":
