@@ -193,6 +193,24 @@ int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void *x, int x_d
 int rt_gelu_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype, int64_t rows,
                      int64_t cols, void *dx, int dx_dtype, void *stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Token cross-entropy over the lm_head logits.  Replaces F.cross_entropy(logits, targets) of
+ * model.py:244-249 (mean over targets != ignore_index) and the bf16 cast of its gradient before
+ * the lm_head grad GEMMs (ratchet.py:139-141, 161).  Forward, per row: row_max, row_logsum =
+ * log(sum exp(x - max)), row_loss = -((x_t - max) - logsum) (0 for ignored rows).  Backward
+ * writes grad_bf16[r, j] = bf16(RN(exp((x - max) - logsum) * w) - [j == t] * w (+ extra_grad)),
+ * w = grad_loss / count read from device memory (no host sync; capturable).  An out-of-range
+ * target sets RT_STATUS_CODE_RANGE and its row is treated as ignored.
+ * ------------------------------------------------------------------------------------------- */
+int rt_cross_entropy_fwd(const void *logits, int dtype, int64_t ld, int64_t rows, int64_t cols,
+                         const int64_t *targets, int64_t ignore_index, float *row_max,
+                         float *row_logsum, float *row_loss, void *stream);
+int rt_cross_entropy_bwd(const void *logits, int dtype, int64_t ld, int64_t rows, int64_t cols,
+                         const int64_t *targets, int64_t ignore_index, const float *row_max,
+                         const float *row_logsum, const float *grad_loss, const float *count,
+                         const float *extra_grad, int64_t ld_extra, void *grad_bf16, int64_t ldo,
+                         void *stream);
+
 #ifdef __cplusplus
 }
 #endif

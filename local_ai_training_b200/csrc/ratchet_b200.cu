@@ -3,3 +3,4 @@
 #include "rt_api.cuh"
 #include "rt_rowops.cuh"
 #include "rt_gemm.cuh"
+#include "rt_loss.cuh"

@@ -46,6 +46,9 @@ class ModelConfig:
     # epilogue, SDPA, GELU backward), so results are identical while HBM traffic halves; the
     # contract layer keeps an fp32 output so the residual-stream gradient stays fp32.
     bf16_activations: bool = True
+    # int8 mode with targets: the self-quantising lm_head GEMM and the token cross-entropy run as
+    # one autograd step (local_ai_training_b200.cross_entropy); False keeps F.cross_entropy
+    fused_cross_entropy: bool = True
 
     def __post_init__(self) -> None:
         if min(self.vocab_size, self.block_size, self.n_layer, self.n_head, self.n_embd) <= 0:
@@ -214,11 +217,17 @@ class RatchetGPT(nn.Module):
                 hidden = torch.utils.checkpoint.checkpoint(block, hidden, use_reentrant=False)
             else:
                 hidden = block(hidden)
-        logits = self.lm_head(self.final_norm(hidden))
+        normed = self.final_norm(hidden)
+        if targets is not None and targets.shape != tokens.shape:
+            raise ValueError("targets must have the same shape as tokens")
+        if targets is not None and self.config.fused_cross_entropy:
+            from .cross_entropy import fused_lm_head_applies, lm_head_cross_entropy
+
+            if fused_lm_head_applies(self.lm_head, normed):
+                return lm_head_cross_entropy(self.lm_head, normed, targets)
+        logits = self.lm_head(normed)
         loss = None
         if targets is not None:
-            if targets.shape != tokens.shape:
-                raise ValueError("targets must have the same shape as tokens")
             loss = F.cross_entropy(logits.flatten(0, 1), targets.flatten())
         return logits, loss
 

@@ -142,40 +142,46 @@ class _RatchetMatmul(torch.autograd.Function):
             grad_input = grad_bf16 @ effective
 
         # ---- grad_weight (ratchet.py:148-163)
-        dp = getattr(getattr(ctx.gradient_sink, "__self__", None), "_dp", None)
-        if dp is not None and ctx.mode != "fp32":
-            # data-parallel: the bf16-rounded grad_W goes to the layer's reduce-scatter buffer and
-            # the update runs later on the owned rows of the summed gradient
-            layer = ctx.gradient_sink.__self__
-            if grad_bf16 is None:
-                grad_bf16 = flat_gradient.to(torch.bfloat16)
-            target = dp.grad_buffer(layer)
-            grad_weight_bf16(grad_bf16, inputs_bf16, out=target)
-            grad_scale = ((target.float() * code.float()).sum(dim=1)
-                          if ctx.needs_input_grad[4] else None)
-            dp.grad_ready(layer)
-            return (grad_input.reshape(ctx.input_shape).to(ctx.input_dtype), None, None, None,
-                    grad_scale, None, None, None, None, None)
-        if ctx.mode == "fp32":
-            grad_weight = flat_gradient.to(torch.float32).t() @ flat_inputs.to(torch.float32)
-            round_bf16 = False
-        else:
-            if grad_bf16 is None:
-                grad_bf16 = flat_gradient.to(torch.bfloat16)
-            grad_weight = grad_weight_bf16(grad_bf16, inputs_bf16)
-            round_bf16 = True
-
-        want_scale = bool(ctx.needs_input_grad[4])
-        if ctx.fuse_backward_update:
-            grad_scale = ctx.gradient_sink(grad_weight, 0, out_features, round_bf16=round_bf16,
-                                           want_grad_scale=want_scale)
-        else:
-            if round_bf16:
-                grad_weight = grad_weight.to(torch.bfloat16).float()
-            ctx.gradient_sink(grad_weight, None, None)
-            grad_scale = (grad_weight * code.float()).sum(dim=1) if want_scale else None
+        if ctx.mode != "fp32" and grad_bf16 is None:
+            grad_bf16 = flat_gradient.to(torch.bfloat16)
+        grad_scale = _deliver_weight_gradient(
+            ctx.gradient_sink, ctx.mode, ctx.fuse_backward_update, grad_bf16, inputs_bf16,
+            flat_gradient, flat_inputs, code, bool(ctx.needs_input_grad[4]))
         return (grad_input.reshape(ctx.input_shape).to(ctx.input_dtype), None, None, None,
                 grad_scale, None, None, None, None, None)
+
+
+def _deliver_weight_gradient(gradient_sink, mode: str, fuse_backward_update: bool,
+                             grad_bf16: Tensor | None, inputs_bf16: Tensor | None,
+                             flat_gradient: Tensor | None, flat_inputs: Tensor | None,
+                             code: Tensor, want_scale: bool) -> Tensor | None:
+    """grad_W of one ratchet layer (ratchet.py:148-169) handed to where it is consumed: the
+    data-parallel reduce-scatter buffer, the fused update (sink), or the pending gradient.
+    Returns the trainable-scale gradient when asked for."""
+    out_features = code.shape[0]
+    dp = getattr(getattr(gradient_sink, "__self__", None), "_dp", None)
+    if dp is not None and mode != "fp32":
+        # data-parallel: the bf16-rounded grad_W goes to the layer's reduce-scatter buffer and
+        # the update runs later on the owned rows of the summed gradient
+        layer = gradient_sink.__self__
+        target = dp.grad_buffer(layer)
+        grad_weight_bf16(grad_bf16, inputs_bf16, out=target)
+        grad_scale = (target.float() * code.float()).sum(dim=1) if want_scale else None
+        dp.grad_ready(layer)
+        return grad_scale
+    if mode == "fp32":
+        grad_weight = flat_gradient.to(torch.float32).t() @ flat_inputs.to(torch.float32)
+        round_bf16 = False
+    else:
+        grad_weight = grad_weight_bf16(grad_bf16, inputs_bf16)
+        round_bf16 = True
+    if fuse_backward_update:
+        return gradient_sink(grad_weight, 0, out_features, round_bf16=round_bf16,
+                             want_grad_scale=want_scale)
+    if round_bf16:
+        grad_weight = grad_weight.to(torch.bfloat16).float()
+    gradient_sink(grad_weight, None, None)
+    return (grad_weight * code.float()).sum(dim=1) if want_scale else None
 
 
 def _code_bound(sink) -> int:

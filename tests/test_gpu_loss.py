@@ -1,0 +1,124 @@
+"""GPU: the token cross-entropy kernels and the fused lm_head + cross-entropy step.
+
+Reference: torch's F.cross_entropy (mean, ignore_index -100) on the same fp32 logits, on the GPU.
+Bars: loss within 1e-6 relative; per-row loss within 2e-6 absolute; the bf16 logit gradient equal
+to torch's fp32 gradient rounded to bf16 except where the two sums of exponentials round apart
+(at most one bf16 ulp, on under 0.1 % of elements).
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _torch_reference(logits, targets, extra=None):
+    x = logits.detach().float().clone().requires_grad_(True)
+    loss = F.cross_entropy(x, targets)
+    total = loss if extra is None else loss + (x * extra).sum()
+    total.backward()
+    return loss.detach(), x.grad
+
+
+def _ulp_diff(a_bf16, b_bf16):
+    """|a - b| in units of one bf16 step at b's magnitude (0 where equal); differences below
+    1e-10 count as equal (fp32 rounding residue where a gradient cancels to almost zero)."""
+    a, b = a_bf16.float(), b_bf16.float()
+    step = torch.ldexp(torch.ones_like(b), torch.frexp(b.abs().clamp_min(1e-30))[1] - 8)
+    d = ((a - b).abs() / step).round().int()
+    return torch.where((a - b).abs() < 1e-10, torch.zeros_like(d), d)
+
+
+@pytest.mark.parametrize("rows,cols,dtype", [(512, 8192, torch.float32), (300, 1000, torch.float32),
+                                             (64, 8192, torch.bfloat16), (7, 13, torch.float32)])
+def test_cross_entropy_matches_torch(cuda_device, rows, cols, dtype):
+    from local_ai_training_b200.cross_entropy import cross_entropy_grad_bf16, cross_entropy_rows
+
+    torch.manual_seed(rows + cols)
+    logits = (torch.randn(rows, cols, device=cuda_device) * 3).to(dtype)
+    targets = torch.randint(0, cols, (rows,), device=cuda_device)
+    targets[::5] = -100  # ignored rows
+    row_max, row_logsum, row_loss = cross_entropy_rows(logits, targets)
+    count = (targets != -100).sum().float().reshape(1)
+    loss = row_loss.sum() / count[0]
+    ref_loss, ref_grad = _torch_reference(logits, targets)
+    assert torch.allclose(loss, ref_loss, rtol=1e-6, atol=0)
+    ref_rows = F.cross_entropy(logits.float(), targets, reduction="none")
+    assert (row_loss - ref_rows).abs().max().item() < 2e-6
+    grad = cross_entropy_grad_bf16(logits, targets, row_max, row_logsum,
+                                   torch.ones((), device=cuda_device), count)
+    d = _ulp_diff(grad, ref_grad.to(torch.bfloat16))
+    assert d.max().item() <= 1
+    assert (d > 0).float().mean().item() < 1e-3
+    assert torch.equal(grad[::5], torch.zeros_like(grad[::5]))  # ignored rows
+
+
+def test_cross_entropy_extra_gradient_and_scale(cuda_device):
+    from local_ai_training_b200.cross_entropy import cross_entropy_grad_bf16, cross_entropy_rows
+
+    torch.manual_seed(3)
+    logits = torch.randn(128, 4096, device=cuda_device)
+    targets = torch.randint(0, 4096, (128,), device=cuda_device)
+    extra = torch.randn(128, 4096, device=cuda_device) * 1e-4
+    row_max, row_logsum, _ = cross_entropy_rows(logits, targets)
+    count = torch.tensor([128.0], device=cuda_device)
+    grad = cross_entropy_grad_bf16(logits, targets, row_max, row_logsum,
+                                   torch.full((), 2.0, device=cuda_device), count, extra)
+    x = logits.clone().requires_grad_(True)
+    (2.0 * F.cross_entropy(x, targets) + (x * extra).sum()).backward()
+    d = _ulp_diff(grad, x.grad.to(torch.bfloat16))
+    assert d.max().item() <= 1 and (d > 0).float().mean().item() < 1e-3
+
+
+def test_out_of_range_target_flags_and_is_ignored(cuda_device):
+    from local_ai_training_b200 import _lib
+    from local_ai_training_b200.cross_entropy import cross_entropy_rows
+
+    logits = torch.randn(4, 10, device=cuda_device)
+    targets = torch.tensor([1, 2, 10, 3], device=cuda_device)
+    _lib.device_status(cuda_device, clear=True)
+    _, _, row_loss = cross_entropy_rows(logits, targets)
+    assert row_loss[2].item() == 0.0
+    assert _lib.device_status(cuda_device, clear=True) & 0x4
+
+
+@pytest.mark.parametrize("int8_backward", [False, True])
+def test_fused_lm_head_cross_entropy_step_matches_unfused(cuda_device, int8_backward):
+    """One model step with the fused lm_head + cross-entropy and with F.cross_entropy from the
+    same state: identical logits, loss to fp32 rounding, embedding gradients to bf16 rounding,
+    and ratchet states that differ only where a one-ulp bf16 gradient difference crosses a
+    bucket threshold (a small fraction of pressures, fewer codes)."""
+    from local_ai_training_b200 import ModelConfig, build_seeded_model
+    from local_ai_training_b200.ratchet import unpack_code_pressure
+
+    def run(fused):
+        cfg = ModelConfig(vocab_size=512, block_size=64, n_layer=2, n_head=2, n_embd=64,
+                          dropout=0.0, pressure_threshold=2, matmul_mode="int8",
+                          int8_backward=int8_backward, fused_cross_entropy=fused)
+        model = build_seeded_model(cfg, max_code=2, seed=3).to(cuda_device).train()
+        for layer in model.ratchet_layers():
+            layer.sr_seed = 5
+        tokens = torch.randint(0, 512, (8, 65), generator=torch.Generator().manual_seed(8))
+        tokens = tokens.to(cuda_device)
+        logits, loss = model(tokens[:, :-1], tokens[:, 1:])
+        loss.backward()
+        emb_grad = model.token_embedding.weight.grad.clone()
+        moves = int(model.ratchet_update(validate=False).code_moves)
+        return logits.detach(), float(loss), emb_grad, moves, [l.packed.clone() for l in
+                                                              model.ratchet_layers()]
+
+    lf, xf, gf, mf, pf = run(True)
+    lp, xp, gp, mp, pp = run(False)
+    assert torch.equal(lf, lp)
+    assert xf == pytest.approx(xp, rel=1e-6)
+    assert torch.allclose(gf, gp, rtol=1e-2, atol=1e-6)
+    assert mf > 0
+    total = sum(a.numel() for a in pf)
+    mism = sum(int((a != b).sum()) for a, b in zip(pf, pp))
+    code_mism = sum(int((unpack_code_pressure(a, 2)[0] != unpack_code_pressure(b, 2)[0]).sum())
+                    for a, b in zip(pf, pp))
+    assert mism <= total // 200, (mism, total)
+    assert code_mism <= total // 2000, (code_mism, total)
