@@ -41,6 +41,24 @@ WORKLOADS = {
 METRIC = "ratchet train-step tokens/s"
 
 
+# DRAM bytes (read + write) that ncu measured for one launch of a family's kernel, and that
+# launch's algorithmic bytes (profiles/gemm_i8_fwd_16384x512x2048.md,
+# profiles/quant_rows_sr_bf16_16384x2048.md).  The roofline's `traffic` for the dominant family is
+# this ratio times the family's mean algorithmic bytes per launch (traffic grows in proportion
+# with the rows processed).  Below 1: outputs still resident in L2 when the kernel ends.
+NCU_TRAFFIC = {
+    "gemm_i8": ((9.59e6 + 9.11e6), 76.6e6, "profiles/gemm_i8_fwd_16384x512x2048.md"),
+    "quant_rows_sr": ((67.15e6 + 7.62e6), 100.7e6, "profiles/quant_rows_sr_bf16_16384x2048.md"),
+}
+
+
+def _traffic(family: str, bytes_per_launch: float) -> tuple[float | None, str | None]:
+    if family not in NCU_TRAFFIC:
+        return None, None
+    measured, algorithmic, source = NCU_TRAFFIC[family]
+    return round(measured / algorithmic * bytes_per_launch), source
+
+
 def _load_peaks() -> dict:
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -415,19 +433,25 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
             achieved = d["flops_per_launch"] / mean_s / 1e12
             roofline = {"kernel": dominant, "bound": "tensor", "achieved": round(achieved, 1),
                         "peak": round(tensor_peak, 1), "unit": "TFLOP/s",
-                        "frac": round(achieved / tensor_peak, 3), "traffic": None,
+                        "frac": round(achieved / tensor_peak, 3),
+                        "traffic": _traffic(dominant, d["bytes_per_launch"])[0],
+                        "traffic_source": _traffic(dominant, d["bytes_per_launch"])[1],
                         "peak_source": int8_peak_source if dominant == "gemm_i8"
                         else "MEASURED_PEAKS.json bf16_tflops"}
         else:
             achieved = d["bytes_per_launch"] / mean_s / 1e9
             roofline = {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 1),
                         "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 3),
-                        "traffic": None, "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
+                        "traffic": _traffic(dominant, d["bytes_per_launch"])[0],
+                        "traffic_source": _traffic(dominant, d["bytes_per_launch"])[1],
+                        "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
     else:
         achieved = d["bytes_per_launch"] / mean_s / 1e9
         roofline = {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 1),
                     "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 3),
-                    "traffic": None, "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
+                    "traffic": _traffic(dominant, d["bytes_per_launch"])[0],
+                    "traffic_source": _traffic(dominant, d["bytes_per_launch"])[1],
+                    "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
