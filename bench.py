@@ -264,7 +264,7 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
         # update, all-gather of the owned packed rows, averaged support gradients
         from local_ai_training_b200.dist import RatchetDataParallel
 
-        ddp = RatchetDataParallel(model)
+        ddp = RatchetDataParallel(model, bucket_layers=args.dp_bucket_layers)
 
     def step(tokens):
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
@@ -497,6 +497,8 @@ def main() -> None:
     parser.add_argument("--workload", choices=sorted(WORKLOADS), default="25m")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-graph", action="store_true", help="time eager steps (no CUDA graph)")
+    parser.add_argument("--dp-bucket-layers", type=int, default=4,
+                        help="N>1: layers whose grad_W reduce-scatters are batched into one group")
     parser.add_argument("--no-peak-probe", action="store_true",
                         help="skip the 8192^3 int8 GEMM probe (ours vs torch._int_mm)")
     args = parser.parse_args()

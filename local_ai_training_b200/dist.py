@@ -53,13 +53,20 @@ class RatchetDataParallel:
         stats = ddp.ratchet_update()      # owned-row update, state re-replicated, global stats
     """
 
-    def __init__(self, model: torch.nn.Module, group: dist.ProcessGroup | None = None) -> None:
+    def __init__(self, model: torch.nn.Module, group: dist.ProcessGroup | None = None, *,
+                 bucket_layers: int = 4) -> None:
+        """bucket_layers: gradients of this many consecutive layers (in backward order) are
+        reduce-scattered as one batched group of collectives (one NCCL launch), the last group
+        when the first layer's gradient arrives."""
         if not dist.is_initialized():
             raise RuntimeError("RatchetDataParallel needs an initialised torch.distributed group")
         self.model = model
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.bucket_layers = max(1, int(bucket_layers))
+        self._pending: list[_LayerState] = []
+        self._nccl = dist.get_backend(group) == "nccl"
         layers = (model.ratchet_layers() if hasattr(model, "ratchet_layers") else
                   [m for m in model.modules() if isinstance(m, DiscreteRatchetLinear)])
         self.states: list[_LayerState] = []
@@ -102,8 +109,28 @@ class RatchetDataParallel:
         if self.world == 1:
             state.work = _Done()
             return
-        state.work = dist.reduce_scatter_tensor(state.shard, state.grad, op=dist.ReduceOp.SUM,
-                                                group=self.group, async_op=True)
+        state.work = _Pending()
+        self._pending.append(state)
+        if len(self._pending) >= self.bucket_layers or state is self.states[0]:
+            self._flush()
+
+    def _flush(self) -> None:
+        """Starts the reduce-scatters of the pending layers (one batched group under NCCL)."""
+        pending, self._pending = self._pending, []
+        if not pending:
+            return
+        op = dist.ReduceOp.SUM
+        if self._nccl and len(pending) > 1:
+            device = pending[0].grad.device
+            with dist._coalescing_manager(group=self.group, device=device, async_ops=True) as cm:
+                for st in pending:
+                    dist.reduce_scatter_tensor(st.shard, st.grad, op=op, group=self.group)
+            for st in pending:
+                st.work = cm
+        else:
+            for st in pending:
+                st.work = dist.reduce_scatter_tensor(st.shard, st.grad, op=op, group=self.group,
+                                                     async_op=True)
 
     # ------------------------------------------------------------------ after backward
     @torch.no_grad()
@@ -131,9 +158,13 @@ class RatchetDataParallel:
         for state in self.states:
             if state.work is None:
                 raise RuntimeError("ratchet layer has no pending effective-weight gradient")
+        self._flush()  # layers whose gradient arrived after the last full group
+        waited = set()
         for state in self.states:
             layer = state.layer
-            state.work.wait()
+            if id(state.work) not in waited:  # a batched group is waited for once
+                state.work.wait()
+                waited.add(id(state.work))
             state.work = None
             shard = state.shard
             if self.world > 1:
@@ -197,6 +228,13 @@ class RatchetDataParallel:
 class _Done:
     def wait(self) -> None:
         return None
+
+
+class _Pending:
+    """Placeholder until the layer's reduce-scatter group is started."""
+
+    def wait(self) -> None:
+        raise RuntimeError("reduce-scatter was never started")
 
 
 def _aggregate(updates: list[RatchetUpdateStats], validate: bool) -> RatchetUpdateStats:
