@@ -274,9 +274,7 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
             model.ratchet_update(validate=False)
             opt.step()
         else:
-            ddp.synchronize_gradients()
-            opt.step()
-            ddp.ratchet_update(validate=False)
+            ddp.step(opt)  # support all-reduce, owned-row updates, AdamW, re-replication
         return loss
 
     def eager_step(tokens):

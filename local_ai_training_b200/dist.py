@@ -136,13 +136,46 @@ class RatchetDataParallel:
     @torch.no_grad()
     def synchronize_gradients(self) -> None:
         """Averages the support-parameter gradients (one all-reduce of a flat fp32 buffer)."""
+        self._finish_support(self._start_support())
+
+    @torch.no_grad()
+    def ratchet_update(self, *, validate: bool = False) -> RatchetUpdateStats:
+        """Updates the owned rows of every layer from the summed gradient, re-replicates `packed`
+        (and `rms_ema`), sums the step statistics across ranks and returns the model's
+        aggregated update statistics (ratchet.py:627-668 / model.py ratchet_update)."""
+        self._update_owned_rows()
+        self._finish_gathers(self._start_gathers())
+        return self._finish_stats(validate)
+
+    @torch.no_grad()
+    def step(self, optimizer: torch.optim.Optimizer, *,
+             validate: bool = False) -> RatchetUpdateStats:
+        """synchronize_gradients + optimizer.step + ratchet_update with the communication
+        overlapped: the support all-reduce runs during the owned-row updates, the re-replication
+        all-gather during the optimizer step."""
+        support = self._start_support()
+        self._update_owned_rows()
+        gathers = self._start_gathers()
+        self._finish_support(support)
+        optimizer.step()
+        self._finish_gathers(gathers)
+        return self._finish_stats(validate)
+
+    def _start_support(self):
         if self.world == 1:
-            return
+            return None
         grads = [p.grad for p in self.support if p.grad is not None]
         if not grads:
-            return
+            return None
         flat = torch.cat([g.reshape(-1).float() for g in grads])
-        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
+        work = dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        return work, flat, grads
+
+    def _finish_support(self, handle) -> None:
+        if handle is None:
+            return
+        work, flat, grads = handle
+        work.wait()
         flat.mul_(1.0 / self.world)
         offset = 0
         for g in grads:
@@ -150,11 +183,7 @@ class RatchetDataParallel:
             g.copy_(flat[offset:offset + n].view_as(g))
             offset += n
 
-    @torch.no_grad()
-    def ratchet_update(self, *, validate: bool = False) -> RatchetUpdateStats:
-        """Updates the owned rows of every layer from the summed gradient, re-replicates `packed`
-        (and `rms_ema`), sums the step statistics across ranks and returns the model's
-        aggregated update statistics (ratchet.py:627-668 / model.py ratchet_update)."""
+    def _update_owned_rows(self) -> None:
         for state in self.states:
             if state.work is None:
                 raise RuntimeError("ratchet layer has no pending effective-weight gradient")
@@ -172,19 +201,30 @@ class RatchetDataParallel:
             layer._capture_weight_gradient(shard, state.row_start, state.row_end,
                                            round_bf16=False)
             layer._pending_stats_total_weights = layer.out_features * layer.in_features
-        if self.world > 1:
-            # re-replicate: every layer's owned packed rows (and rms_ema rows), as one group of
-            # collectives where the backend can batch them
-            gathers = []
-            for state in self.states:
-                layer = state.layer
-                pk = layer.packed
-                gathers.append((pk, pk[state.row_start:state.row_end]))
-                if layer.rms_ema_beta > 0.0:
-                    gathers.append((layer.rms_ema, layer.rms_ema[state.row_start:state.row_end]))
-            self._all_gather_many(gathers)
-            for state in self.states:
-                state.layer._refresh_code_mirror()
+
+    def _start_gathers(self):
+        """Re-replication: every layer's owned packed rows (and rms_ema rows), as one group of
+        collectives where the backend can batch them."""
+        if self.world == 1:
+            return None
+        pairs = []
+        for state in self.states:
+            layer = state.layer
+            pk = layer.packed
+            pairs.append((pk, pk[state.row_start:state.row_end]))
+            if layer.rms_ema_beta > 0.0:
+                pairs.append((layer.rms_ema, layer.rms_ema[state.row_start:state.row_end]))
+        return self._all_gather_many(pairs)
+
+    def _finish_gathers(self, handle) -> None:
+        if handle is None:
+            return
+        for work in handle:
+            work.wait()
+        for state in self.states:
+            state.layer._refresh_code_mirror()
+
+    def _finish_stats(self, validate: bool) -> RatchetUpdateStats:
         if self.world > 1:
             self._reduce_step_stats()
         if hasattr(self.model, "ratchet_update"):
@@ -192,17 +232,17 @@ class RatchetDataParallel:
         updates = [s.layer.ratchet_update(validate=validate) for s in self.states]
         return _aggregate(updates, validate)
 
-    def _all_gather_many(self, pairs: list[tuple[Tensor, Tensor]]) -> None:
-        """In-place all-gathers (each input is this rank's block of its output)."""
+    def _all_gather_many(self, pairs: list[tuple[Tensor, Tensor]]) -> list:
+        """Starts in-place all-gathers (each input is this rank's block of its output); returns
+        the handles to wait for."""
         if dist.get_backend(self.group) == "nccl":
             device = pairs[0][0].device
             with dist._coalescing_manager(group=self.group, device=device, async_ops=True) as cm:
                 for out, inp in pairs:
                     dist.all_gather_into_tensor(out, inp, group=self.group)
-            cm.wait()
-        else:
-            for out, inp in pairs:
-                dist.all_gather_into_tensor(out, inp.contiguous(), group=self.group)
+            return [cm]
+        return [dist.all_gather_into_tensor(out, inp.contiguous(), group=self.group,
+                                            async_op=True) for out, inp in pairs]
 
     def _reduce_step_stats(self) -> None:
         """Sums each layer's [4 counters, rms sum] across ranks in one all-reduce (float64 holds

@@ -109,11 +109,11 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         ddp.grad_buffer(layer).copy_(_local_grad(rank, n, SHAPES[n][:2]))
         ddp.grad_ready(layer)
     model.norm.grad = torch.full((6,), float(rank + 1))
-    ddp.synchronize_gradients()
-    stats = ddp.ratchet_update()
+    # step(): support all-reduce, owned-row updates, the optimizer, re-replication
+    stats = ddp.step(torch.optim.SGD([model.norm], lr=1.0))
     torch.save({"packed": [l.packed.clone() for l in model.layers],
                 "ema": [l.rms_ema.clone() for l in model.layers],
-                "norm_grad": model.norm.grad.clone(),
+                "norm_grad": model.norm.grad.clone(), "norm": model.norm.detach().clone(),
                 "sr_layer": [l.sr_layer for l in model.layers],
                 "stats": [int(stats.positive_moves), int(stats.negative_moves),
                           int(stats.blocked_positive_moves), int(stats.blocked_negative_moves),
@@ -141,6 +141,8 @@ def test_row_owner_update_equals_single_process_update(tmp_path):
     assert res[0]["stats"] == res[1]["stats"]
     # support gradient averaged
     assert torch.equal(res[0]["norm_grad"], torch.full((6,), 1.5))
+    assert torch.equal(res[0]["norm"], torch.full((6,), -0.5))
+    assert torch.equal(res[1]["norm"], torch.full((6,), -0.5))
     # per-rank stochastic-rounding streams
     assert res[0]["sr_layer"] == [0, 0, 0] and res[1]["sr_layer"] == [1 << 16] * 3
     # single process: the whole matrix, gradient = bf16 sum of the ranks' bf16 grads, halved
