@@ -63,6 +63,8 @@ int rt_sm_count(int *out);
  *       (element index e / 8, step)  [own mapping, not Triton's tl.rand]
  * x_bf16_out (optional) receives bf16(x) (unscaled) — the grad_weight GEMM operand of
  * ratchet.py:162 — so the gradient is read from HBM once.
+ * round_input_bf16 (fp32 input): each value is first rounded to bf16, the cast autograd applies
+ * to the gradient of a bf16 layer output whose consumer was fused into an fp32 residual add.
  * step_dev (optional): two device uint32s.  step_dev[0] is read in place of `step` and the call
  * advances it by one once every CTA has read it; step_dev[1] is the call's arrival count and must
  * be zero between calls (calls leave it zero).  Consecutive calls, and the replays of a captured
@@ -70,8 +72,9 @@ int rt_sm_count(int *out);
  * overlap on the GPU.
  * ------------------------------------------------------------------------------------------- */
 int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_t cols, int64_t stride_row,
-                     int64_t stride_col, const float *col_scale, int stochastic, uint64_t seed,
-                     uint32_t step, uint32_t layer, uint32_t *step_dev, int8_t *q,
+                     int64_t stride_col, const float *col_scale, int stochastic,
+                     int round_input_bf16, uint64_t seed, uint32_t step, uint32_t layer,
+                     uint32_t *step_dev, int8_t *q,
                      int64_t ldq, float *row_scale, void *x_bf16_out, int64_t ld_xbf16,
                      void *stream);
 
@@ -87,12 +90,16 @@ int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_t cols, int
  * rhs_abs_max: a bound the caller guarantees on |rhs| (ratchet codes: 7), or 0 when unknown; it
  * only selects a cheaper exact int32 -> fp32 conversion when K·128·bound < 2^22 (results are the
  * same either way as long as the bound holds).
+ * residual (optional, fp32 out only, M x N with row stride ld_residual; may be `out` itself):
+ * out = residual + (the fp32-widened bf16 value), the residual add of the transformer block
+ * (model.py TransformerBlock.forward: `inputs + attention(...)`, `inputs + feed_forward(...)`) in
+ * the epilogue instead of a separate pass over the residual stream.
  * ------------------------------------------------------------------------------------------- */
 int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_t lhs_stride_k,
                       const int8_t *rhs, int64_t rhs_stride_k, int64_t rhs_stride_n,
                       const float *lhs_scale, const float *rhs_scale, void *out, int out_dtype,
                       int64_t ldo, int64_t M, int64_t N, int64_t K, int rhs_abs_max,
-                      void *stream);
+                      const float *residual, int64_t ld_residual, void *stream);
 
 /* ---------------------------------------------------------------------------------------------
  * grad_weight GEMM.  Replaces the per-tile cuBLAS BF16 GEMM of ratchet.py:148-163:
@@ -185,10 +192,12 @@ int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, int64_t hea
                           int64_t stride_d, int8_t *q, int64_t ldq, float *row_scale,
                           void *stream);
 /* RMSNorm backward (int8_backward.py:7-51): dx written in dx_dtype (through bf16, as the
- * reference stores it); dw (optional, cols floats, accumulated) += sum over rows of gy*x*rsqrt. */
+ * reference stores it); dw (optional, cols floats, accumulated) += sum over rows of gy*x*rsqrt.
+ * dx_add (optional, fp32 dx only, may equal dx): the residual branch's gradient, added to dx the
+ * way autograd accumulates the two branches of the residual stream. */
 int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
                         const float *weight, double eps, int64_t rows, int64_t cols, void *dx,
-                        int dx_dtype, float *dw, void *stream);
+                        int dx_dtype, float *dw, const float *dx_add, void *stream);
 /* tanh-GELU backward (int8_backward.py:53-89); dx written in dx_dtype. */
 int rt_gelu_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype, int64_t rows,
                      int64_t cols, void *dx, int dx_dtype, void *stream);

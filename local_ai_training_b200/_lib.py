@@ -41,10 +41,10 @@ _SIGNATURES = {
     "rt_last_error": ([], ctypes.c_char_p),
     "rt_device_status": ([_p, _i, _p], _i),
     "rt_sm_count": ([_p], _i),
-    "rt_quantize_rows": ([_p, _i, _i64, _i64, _i64, _i64, _p, _i, _u64, _u32, _u32, _p, _p, _i64,
+    "rt_quantize_rows": ([_p, _i, _i64, _i64, _i64, _i64, _p, _i, _i, _u64, _u32, _u32, _p, _p, _i64,
                           _p, _p, _i64, _p], _i),
     "rt_scaled_int8_mm": ([_p, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i, _i64, _i64, _i64, _i64,
-                           _i, _p], _i),
+                           _i, _p, _i64, _p], _i),
     "rt_grad_weight_bf16": ([_p, _i64, _p, _i64, _p, _i, _i64, _i64, _i64, _i64, _i, _p, _i64, _p],
                             _i),
     "rt_grad_weight_workspace_bytes": ([_i64, _i64, _i64], _i64),
@@ -60,7 +60,7 @@ _SIGNATURES = {
     "rt_gelu_quantize": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p], _i),
     "rt_transpose_quantize": ([_p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64,
                                _p, _p], _i),
-    "rt_rmsnorm_backward": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p, _p], _i),
+    "rt_rmsnorm_backward": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p, _p, _p], _i),
     "rt_gelu_backward": ([_p, _i, _p, _i, _i64, _i64, _p, _i, _p], _i),
     "rt_cross_entropy_fwd": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p], _i),
     "rt_cross_entropy_bwd": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _p,

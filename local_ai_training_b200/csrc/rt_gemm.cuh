@@ -32,6 +32,9 @@ struct GemmArgs {
   int tiles_m, tiles_n, splits, kblocks;
   const float *a_scale;  // EPI_SCALED: per-row scale (M)
   const float *b_scale;  // EPI_SCALED: per-column scale (N) or null (== 1)
+  const float *residual;  // EPI_SCALED, fp32 out: out = residual + value (M x N, ld_res) or null
+  int64_t ld_res;
+  int res_vec;            // residual rows are 16-byte aligned
   void *out;
   int64_t ldo;
   int out_dtype;  // EPI_SCALED: RT_BF16 or RT_F32 (bf16-rounded value widened)
@@ -171,16 +174,21 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &p, int epi, int r
       }
     } else {
       float *o = static_cast<float *>(p.out) + static_cast<int64_t>(row) * p.ldo + n0;
+      const float *res =
+          p.residual != nullptr ? p.residual + static_cast<int64_t>(row) * p.ld_res + n0 : nullptr;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        v[j] = bf16_round(v[j]);
+        if (res != nullptr && n0 + j < p.N) v[j] = __fadd_rn(__ldg(res + j), v[j]);
+      }
       if (full) {
 #pragma unroll
         for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4 *>(o + j) =
-              make_float4(bf16_round(v[j]), bf16_round(v[j + 1]), bf16_round(v[j + 2]),
-                          bf16_round(v[j + 3]));
+          *reinterpret_cast<float4 *>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          if (n0 + j < p.N) o[j] = bf16_round(v[j]);
+          if (n0 + j < p.N) o[j] = v[j];
       }
     }
     return;
@@ -261,11 +269,15 @@ __device__ __forceinline__ float cvt_acc(uint32_t b) {
 // One warp's share of a tile (32 rows, HALF columns from TMEM column t_row) through its staging
 // buffer: bf16 groups of 64 columns or fp32 groups of 32, optionally scaled by the row scale a_s
 // and the column scales bs[] (bf16-rounded like the reference when scaled).
+// rmap (fp32 output only, or null): the residual, whose tile of each group is TMA-loaded into
+// the staging buffer (completion on rbar, parity rphase) while the accumulators are read, then
+// added after the rounding.
 template <int CONV, int HALF>
 __device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *staging, int lane,
                                              uint32_t t_row, int x0, int x_end, int y,
                                              bool bf16_out, bool scaled, float a_s,
-                                             const float *bs) {
+                                             const float *bs, const CUtensorMap *rmap,
+                                             uint64_t *rbar, uint32_t &rphase) {
   if (bf16_out) {
 #pragma unroll 1
     for (int g = 0; g < HALF / 64; ++g) {
@@ -305,11 +317,21 @@ __device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *st
     for (int g = 0; g < HALF / 32; ++g) {
       const int n0 = x0 + g * 32;
       if (n0 >= x_end) break;
+      if (rmap != nullptr && lane == 0) {
+        bulk_wait_read_all();  // the previous store has read the staging buffer
+        mbar_arrive_expect_tx(rbar, 4096);
+        tma_load_2d(rmap, rbar, staging, n0, y);
+      }
       uint32_t r[32];
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 32), r);
       tmem_ld_wait_regs(r);
       uint32_t w[32];
       const float4 *bs4 = reinterpret_cast<const float4 *>(bs + g * 32);
+      bool res_ok = true;
+      if (rmap != nullptr) {
+        res_ok = mbar_wait(rbar, rphase);
+        rphase ^= 1u;
+      }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         float v[4];
@@ -321,6 +343,12 @@ __device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *st
           v[1] = bf16_round(__fmul_rn(__fmul_rn(v[1], a_s), sc.y));
           v[2] = bf16_round(__fmul_rn(__fmul_rn(v[2], a_s), sc.z));
           v[3] = bf16_round(__fmul_rn(__fmul_rn(v[3], a_s), sc.w));
+        }
+        if (rmap != nullptr && res_ok) {  // out = residual + value, the reference's fp32 add
+          const float4 r4 = *reinterpret_cast<const float4 *>(staging + lane * 128 +
+                                                              ((j ^ (lane & 7)) << 4));
+          v[0] = __fadd_rn(r4.x, v[0]), v[1] = __fadd_rn(r4.y, v[1]);
+          v[2] = __fadd_rn(r4.z, v[2]), v[3] = __fadd_rn(r4.w, v[3]);
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) w[4 * j + e] = __float_as_uint(v[e]);
@@ -334,7 +362,8 @@ template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
 __global__ void __launch_bounds__(64 + 32 * 8, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b,
-                     const __grid_constant__ CUtensorMap tma_c, GemmArgs p) {
+                     const __grid_constant__ CUtensorMap tma_c,
+                     const __grid_constant__ CUtensorMap tma_r, GemmArgs p) {
   using C = GemmCfg<T, A_MN, B_MN, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
@@ -347,7 +376,8 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
   uint64_t *empty = bars + STAGES;
   uint64_t *tfull = bars + 2 * STAGES;
   uint64_t *tempty = bars + 2 * STAGES + 2;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4);
+  uint64_t *rfull = bars + 2 * STAGES + 4;  // per epilogue warp: its residual tile has landed
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 2 * STAGES + 4 + C::EPI_WARPS);
   __shared__ __align__(16) float s_bscale[BN];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -360,10 +390,12 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], C::EPI_WARPS);
     }
+    for (int w = 0; w < C::EPI_WARPS; ++w) mbar_init(&rfull[w], 1);
     fence_barrier_init();
     tma_prefetch_desc(&tma_a);
     tma_prefetch_desc(&tma_b);
     if (p.tma_store) tma_prefetch_desc(&tma_c);
+    if (p.residual != nullptr && p.tma_store) tma_prefetch_desc(&tma_r);
   }
   if (warp == 1) {
     tmem_alloc(tmem_holder, C::TMEM_COLS);
@@ -450,6 +482,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     const bool split_mode = p.epi == EPI_SPLIT;
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t rphase = 0;  // parity of this warp's residual barrier
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
       const int tn = u % p.tiles_n, rest = u / p.tiles_n;
       const int tm = rest % p.tiles_m, split = rest / p.tiles_m;
@@ -499,18 +532,20 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         const int x0 = (split_mode ? 0 : tn * BN) + col0;
         const int x_end = split_mode ? BN : p.N;
         const float *bs = s_bscale + col0;
+        const CUtensorMap *rmap = (p.residual != nullptr && !bf16_out) ? &tma_r : nullptr;
+        uint64_t *rbar = &rfull[warp - 2];
         if (!split_mode && y >= p.M) {
           // this warp's 32 rows lie past the output: nothing to store
         } else if constexpr (sizeof(T) == 1) {
           if (p.acc_small)
             epilogue_tma<1, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out, scaled,
-                                  a_s, bs);
+                                  a_s, bs, rmap, rbar, rphase);
           else
             epilogue_tma<2, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out, scaled,
-                                  a_s, bs);
+                                  a_s, bs, rmap, rbar, rphase);
         } else {
           epilogue_tma<0, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out, scaled,
-                                a_s, bs);
+                                a_s, bs, rmap, rbar, rphase);
         }
       } else {
 #pragma unroll 1
@@ -545,7 +580,8 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
 __global__ void simt_scaled_i8_kernel(const int8_t *lhs, int64_t slm, int64_t slk,
                                       const int8_t *rhs, int64_t srk, int64_t srn,
                                       const float *ls, const float *rs, void *out, int out_dtype,
-                                      int64_t ldo, int64_t M, int64_t N, int64_t K) {
+                                      int64_t ldo, int64_t M, int64_t N, int64_t K,
+                                      const float *residual, int64_t ld_res) {
   const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t m = blockIdx.y * static_cast<int64_t>(blockDim.y) + threadIdx.y;
   if (m >= M || n >= N) return;
@@ -554,10 +590,13 @@ __global__ void simt_scaled_i8_kernel(const int8_t *lhs, int64_t slm, int64_t sl
     acc += static_cast<int>(lhs[m * slm + k * slk]) * static_cast<int>(rhs[k * srk + n * srn]);
   float v = __fmul_rn(__int2float_rn(acc), __ldg(ls + m));
   if (rs != nullptr) v = __fmul_rn(v, __ldg(rs + n));
-  if (out_dtype == RT_BF16)
+  if (out_dtype == RT_BF16) {
     static_cast<uint16_t *>(out)[m * ldo + n] = bf16_bits(v);
-  else
-    static_cast<float *>(out)[m * ldo + n] = bf16_round(v);
+  } else {
+    v = bf16_round(v);
+    if (residual != nullptr) v = __fadd_rn(residual[m * ld_res + n], v);
+    static_cast<float *>(out)[m * ldo + n] = v;
+  }
 }
 
 __global__ void simt_gradw_kernel(const uint16_t *g, int64_t ldg, const uint16_t *x, int64_t ldx,
@@ -640,7 +679,8 @@ static int operand_map(CUtensorMap *map, const Operand &o, int tile_rows) {
 template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
 static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaStream_t s) {
   using C = GemmCfg<T, A_MN, B_MN, BN, STAGES>;
-  CUtensorMap ma, mb, mc;
+  CUtensorMap ma, mb, mc, mr;
+  memset(&mr, 0, sizeof(mr));
   memset(&mc, 0, sizeof(mc));
   int rc = operand_map<T, A_MN>(&ma, a, C::BM);
   if (rc) return rc;
@@ -671,6 +711,18 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
                   static_cast<uint64_t>(args.ldo) * es, static_cast<uint32_t>(128 / es), 32);
     if (rc) return rc;
   }
+  if (args.tma_store && args.residual != nullptr) {
+    // the residual tile of each fp32 output group, loaded by TMA into the group's staging buffer
+    if (!args.res_vec) {
+      args.tma_store = 0;  // unaligned residual rows: the lane-per-row epilogue adds it
+    } else {
+      rc = make_map(&mr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, args.residual,
+                    static_cast<uint64_t>(args.N), static_cast<uint64_t>(args.M),
+                    static_cast<uint64_t>(args.ld_res) * 4, 32, 32);
+      if (rc) return rc;
+    }
+  }
+
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   if ((rc = rt_sm_count(&sms)) != RT_OK) return rc;
@@ -689,7 +741,7 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
   }
   const int64_t units = static_cast<int64_t>(args.tiles_m) * args.tiles_n * args.splits;
   const int grid = static_cast<int>(units < sms ? units : sms);
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(ma, mb, mc, args);
+  kernel<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(ma, mb, mc, mr, args);
   return check_launch("umma_gemm_kernel");
 }
 
@@ -709,10 +761,13 @@ extern "C" int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_
                                  const int8_t *rhs, int64_t rhs_stride_k, int64_t rhs_stride_n,
                                  const float *lhs_scale, const float *rhs_scale, void *out,
                                  int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
-                                 int rhs_abs_max, void *stream) {
+                                 int rhs_abs_max, const float *residual, int64_t ld_residual,
+                                 void *stream) {
   if (M < 0 || N < 0 || K < 0) return fail(RT_ERR_INVALID_ARGUMENT, "scaled_int8_mm: negative shape");
   if (out_dtype != RT_BF16 && out_dtype != RT_F32)
     return fail(RT_ERR_DTYPE, "scaled_int8_mm: output must be bfloat16 or float32");
+  if (residual != nullptr && out_dtype != RT_F32)
+    return fail(RT_ERR_DTYPE, "scaled_int8_mm: a residual needs a float32 output");
   if (M == 0 || N == 0) return RT_OK;
   if (lhs == nullptr || rhs == nullptr || lhs_scale == nullptr || out == nullptr)
     return fail(RT_ERR_INVALID_ARGUMENT, "scaled_int8_mm: null pointer");
@@ -723,6 +778,8 @@ extern "C" int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_
   GemmArgs args{};
   args.M = static_cast<int>(M), args.N = static_cast<int>(N), args.K = static_cast<int>(K);
   args.a_scale = lhs_scale, args.b_scale = rhs_scale, args.out = out, args.ldo = ldo;
+  args.residual = residual, args.ld_res = ld_residual;
+  args.res_vec = residual != nullptr && aligned16(residual) && ld_residual % 4 == 0;
   args.out_dtype = out_dtype, args.epi = EPI_SCALED, args.splits = 1;
   const int64_t rhs_bound = (rhs_abs_max <= 0 || rhs_abs_max > 128) ? 128 : rhs_abs_max;
   args.acc_small = K * 128 * rhs_bound < (int64_t(1) << 22);
@@ -752,7 +809,7 @@ extern "C" int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_
   const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((M + 7) / 8));
   simt_scaled_i8_kernel<<<grid, block, 0, s>>>(lhs, lhs_stride_m, lhs_stride_k, rhs, rhs_stride_k,
                                                 rhs_stride_n, lhs_scale, rhs_scale, out, out_dtype,
-                                                ldo, M, N, K);
+                                                ldo, M, N, K, residual, ld_residual);
   return check_launch("simt_scaled_i8_kernel");
 }
 

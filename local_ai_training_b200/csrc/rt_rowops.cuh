@@ -257,6 +257,7 @@ struct QuantArgs {
   int64_t rows, cols, stride_row, stride_col;
   const float *col_scale;
   int stochastic;
+  int round_bf16;  // fp32 input rounded to bf16 before anything else
   uint64_t seed;
   uint32_t step, layer;
   uint32_t *step_dev;
@@ -322,6 +323,10 @@ __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
       const int64_t c = t + static_cast<int64_t>(i) * RT;
       if (live && c < nch) {
         ld8(xr + 8 * c, v[i]);
+        if (a.round_bf16) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] = bf16_round(v[i][j]);
+        }
         if (a.xbf16 != nullptr)
           st8(reinterpret_cast<__nv_bfloat16 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c), v[i]);
         if (a.col_scale != nullptr) {
@@ -378,6 +383,7 @@ __global__ void __launch_bounds__(CTA) quant_rows_generic_kernel(QuantArgs a) {
   float amax = 0.0f;
   for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
     float v = load_as_float<T>(xr + k * a.stride_col);
+    if (a.round_bf16) v = bf16_round(v);
     if (a.xbf16 != nullptr) a.xbf16[row * a.ld_xbf16 + k] = bf16_bits(v);
     if (a.col_scale != nullptr) v = __fmul_rn(v, __ldg(a.col_scale + k));
     amax = fmaxf(amax, fabsf(v));
@@ -388,6 +394,7 @@ __global__ void __launch_bounds__(CTA) quant_rows_generic_kernel(QuantArgs a) {
   if (threadIdx.x == 0) a.row_scale[row] = scale;
   for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
     float v = load_as_float<T>(xr + k * a.stride_col);
+    if (a.round_bf16) v = bf16_round(v);
     if (a.col_scale != nullptr) v = __fmul_rn(v, __ldg(a.col_scale + k));
     int8_t o;
     if (a.stochastic) {
@@ -1039,6 +1046,7 @@ struct RmsBwdArgs {
   void *dx;
   int dx_dtype;
   float *dw;
+  const float *dx_add;  // optional fp32 gradient added to dx (the residual branch), may be dx
 };
 // X: input dtype, G: incoming-gradient dtype (fp32 or bf16 each).
 template <typename X, typename G, int RT, int VPT>
@@ -1109,6 +1117,12 @@ __global__ void __launch_bounds__(CTA) rmsnorm_bwd_kernel(RmsBwdArgs a) {
                                               static_cast<float>(a.cols))));
         dwp[i][j] = __fadd_rn(dwp[i][j], __fmul_rn(__fmul_rn(gv[i][j], xv[i][j]), r));
       }
+      if (a.dx_add != nullptr) {  // the residual branch's gradient, summed as autograd would
+        float ad[8];
+        ld8(a.dx_add + row * a.cols + 8 * c, ad);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(ad[j], o[j]);
+      }
       if (a.dx_dtype == RT_F32)
         st8(static_cast<float *>(a.dx) + row * a.cols + 8 * c, o);
       else
@@ -1172,7 +1186,9 @@ __global__ void __launch_bounds__(CTA)
     const float dh = __fmul_rn(g, __ldg(a.w + k));
     const float v = __fadd_rn(__fmul_rn(dh, r), __fdiv_rn(__fmul_rn(__fmul_rn(dvar, 2.0f), xv),
                                                           static_cast<float>(a.cols)));
-    store_elem(a.dx, a.dx_dtype, row * a.cols + k, bf16_round(v));
+    float o = bf16_round(v);
+    if (a.dx_add != nullptr) o = __fadd_rn(a.dx_add[row * a.cols + k], o);
+    store_elem(a.dx, a.dx_dtype, row * a.cols + k, o);
     if (a.dw != nullptr) atomicAdd(a.dw + k, __fmul_rn(__fmul_rn(g, xv), r));
   }
 }
@@ -1212,8 +1228,9 @@ using namespace rt;
 
 extern "C" int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_t cols,
                                 int64_t stride_row, int64_t stride_col, const float *col_scale,
-                                int stochastic, uint64_t seed, uint32_t step, uint32_t layer,
-                                uint32_t *step_dev, int8_t *q, int64_t ldq,
+                                int stochastic, int round_input_bf16, uint64_t seed,
+                                uint32_t step, uint32_t layer, uint32_t *step_dev, int8_t *q,
+                                int64_t ldq,
                                 float *row_scale, void *x_bf16_out, int64_t ld_xbf16,
                                 void *stream) {
   if (rows < 0 || cols < 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_quantize_rows: negative shape");
@@ -1223,9 +1240,9 @@ extern "C" int rt_quantize_rows(const void *x, int x_dtype, int64_t rows, int64_
   if (x_dtype != RT_F32 && x_dtype != RT_BF16)
     return fail(RT_ERR_DTYPE, "rt_quantize_rows: input must be float32 or bfloat16");
   if (cols == 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_quantize_rows: zero columns");
-  QuantArgs a{x,          rows, cols, stride_row, stride_col, col_scale, stochastic, seed,
-              step,       layer, step_dev, q, ldq, row_scale,
-              static_cast<unsigned short *>(x_bf16_out), ld_xbf16};
+  QuantArgs a{x,          rows,   cols,     stride_row, stride_col, col_scale, stochastic,
+              x_dtype == RT_F32 && round_input_bf16, seed, step, layer, step_dev, q, ldq,
+              row_scale,  static_cast<unsigned short *>(x_bf16_out), ld_xbf16};
   cudaStream_t s = as_stream(stream);
   return x_dtype == RT_F32 ? quant_rows_dispatch<float>(a, s)
                            : quant_rows_dispatch<__nv_bfloat16>(a, s);
@@ -1415,13 +1432,17 @@ extern "C" int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, 
 
 extern "C" int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
                                    const float *weight, double eps, int64_t rows, int64_t cols,
-                                   void *dx, int dx_dtype, float *dw, void *stream) {
+                                   void *dx, int dx_dtype, float *dw, const float *dx_add,
+                                   void *stream) {
   if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_rmsnorm_backward: shape");
   if (rows == 0) return RT_OK;
+  if (dx_add != nullptr && dx_dtype != RT_F32)
+    return fail(RT_ERR_DTYPE, "rt_rmsnorm_backward: an added gradient needs a float32 dx");
   cudaStream_t s = as_stream(stream);
-  RmsBwdArgs a{grad_y, x, weight, static_cast<float>(eps), rows, cols, dx, dx_dtype, dw};
+  RmsBwdArgs a{grad_y, x, weight, static_cast<float>(eps), rows, cols, dx, dx_dtype, dw, dx_add};
   const bool vec = cols % 8 == 0 && aligned16(x) && aligned16(grad_y) && aligned16(dx) &&
-                   aligned16(weight) && (dw == nullptr || aligned16(dw));
+                   aligned16(weight) && (dw == nullptr || aligned16(dw)) &&
+                   (dx_add == nullptr || aligned16(dx_add));
   const RowCfg cfg = vec ? row_cfg_narrow(cols / 8) : RowCfg{0, 0};
   if (cfg.rt != 0) {
     int sms = 0;

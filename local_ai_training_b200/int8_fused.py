@@ -83,24 +83,35 @@ def _no_zero_grads(ctx, int8_out: Tensor, scale_out: Tensor) -> None:
 
 class FusedRMSNormQuantizeFn(torch.autograd.Function):
     """(int8, scale, dummy) like the reference.  `dummy_dtype` (default: x's dtype, the
-    reference) sets the dtype of the dummy, i.e. of the consuming layer's input gradient."""
+    reference) sets the dtype of the dummy, i.e. of the consuming layer's input gradient.
+
+    residual_out=True also returns x itself as a fourth output, to be consumed as the residual
+    of the block (`x + sublayer(norm(x))`): its gradient then arrives here and is added to the
+    RMSNorm input gradient by the same kernel, instead of autograd summing the two branches."""
 
     @staticmethod
-    def forward(ctx, x: Tensor, weight: Tensor, eps: float = 1e-5, dummy_dtype=None):
+    def forward(ctx, x: Tensor, weight: Tensor, eps: float = 1e-5, dummy_dtype=None,
+                residual_out: bool = False):
         int8_out, scale_out = fused_rmsnorm_quantize(x, weight, eps)
         ctx.save_for_backward(x, weight)
         ctx.eps = eps
         dummy = torch.empty(x.shape, device=x.device, dtype=dummy_dtype or x.dtype)
         _no_zero_grads(ctx, int8_out, scale_out)
+        if residual_out:
+            return int8_out, scale_out, dummy, x
         return int8_out, scale_out, dummy
 
     @staticmethod
-    def backward(ctx, grad_int8, grad_scale, grad_dummy):
+    def backward(ctx, grad_int8, grad_scale, grad_dummy, grad_residual=None):
         if grad_dummy is None:
-            return None, None, None, None
+            return grad_residual, None, None, None, None
         x, weight = ctx.saved_tensors
-        grad_x, grad_w = rmsnorm_backward(grad_dummy, x, weight, ctx.eps)
-        return grad_x, grad_w, None, None
+        fuse = grad_residual is not None and x.dtype == torch.float32
+        grad_x, grad_w = rmsnorm_backward(grad_dummy, x, weight, ctx.eps,
+                                          residual_grad=grad_residual if fuse else None)
+        if grad_residual is not None and not fuse:
+            grad_x = grad_x + grad_residual
+        return grad_x, grad_w, None, None, None
 
 
 class FusedGELUQuantizeFn(torch.autograd.Function):

@@ -33,6 +33,7 @@ def _quantize_rows_fused(
     layer: int = 0,
     bf16_copy: Tensor | None = None,
     step_dev: Tensor | None = None,
+    round_input_bf16: bool = False,
 ) -> tuple[Tensor, Tensor]:
     """Row quantisation kernel (int8_matmul.py:106-150, 181-207).
 
@@ -41,7 +42,7 @@ def _quantize_rows_fused(
     stream.  bf16_copy, when given (rows × cols bf16, unit column stride), receives bf16(values).
     step_dev (int32 [2] on the device, zeros to start), when given: element 0 is read by the
     kernel instead of `step` and advanced by one by the call; element 1 is the kernel's arrival
-    count (zero between calls).
+    count (zero between calls).  round_input_bf16 (fp32 values): each value is rounded to bf16 first.
     """
     if values.ndim != 2:
         raise ValueError("row quantization requires a 2D tensor")
@@ -59,7 +60,8 @@ def _quantize_rows_fused(
     _lib.check(
         _lib.lib().rt_quantize_rows(
             values.data_ptr(), _lib.dtype_code(values), m, k, values.stride(0), values.stride(1),
-            _lib.ptr(col_scale), int(stochastic), int(seed or 0) & (2**64 - 1), int(step) & 0xFFFFFFFF,
+            _lib.ptr(col_scale), int(stochastic), int(round_input_bf16),
+            int(seed or 0) & (2**64 - 1), int(step) & 0xFFFFFFFF,
             int(layer) & 0xFFFFFFFF, _lib.ptr(step_dev), out.data_ptr(), out.stride(0),
             scale.data_ptr(),
             _lib.ptr(bf16_copy), 0 if bf16_copy is None else bf16_copy.stride(0),
@@ -106,14 +108,14 @@ def quantize_columns(values: Tensor) -> tuple[Tensor, Tensor]:
 
 def _scaled_int8_mm_into(
     lhs: Tensor, rhs: Tensor, lhs_scale: Tensor, rhs_scale: Tensor | None, out: Tensor,
-    rhs_abs_max: int = 0,
+    rhs_abs_max: int = 0, residual: Tensor | None = None,
 ) -> Tensor:
     """No-sync core: out = bf16((float(lhs @ rhs) * lhs_scale[m]) * rhs_scale[n]).
 
     `out` is (M, N) bf16, or fp32 receiving the bf16-rounded values (the widening cast of
     ratchet.py:67 fused into the epilogue).  Operands are passed with their strides.
     rhs_abs_max: a guaranteed bound on |rhs| (ratchet codes: 7) or 0; it only lets the epilogue
-    use a cheaper exact accumulator conversion.
+    use a cheaper exact accumulator conversion.  residual (fp32 `out` only): out = residual + value.
     """
     m, k = lhs.shape
     _, n = rhs.shape
@@ -122,7 +124,8 @@ def _scaled_int8_mm_into(
         _lib.lib().rt_scaled_int8_mm(
             lhs.data_ptr(), lhs.stride(0), lhs.stride(1), rhs.data_ptr(), rhs.stride(0),
             rhs.stride(1), lhs_scale.data_ptr(), _lib.ptr(rhs_scale), out.data_ptr(),
-            _lib.dtype_code(out), out.stride(0), m, n, k, int(rhs_abs_max), _lib.stream_of(lhs),
+            _lib.dtype_code(out), out.stride(0), m, n, k, int(rhs_abs_max), _lib.ptr(residual),
+            0 if residual is None else residual.stride(0), _lib.stream_of(lhs),
         )
     )
     if ev is not None:

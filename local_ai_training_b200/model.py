@@ -49,6 +49,9 @@ class ModelConfig:
     # int8 mode with targets: the self-quantising lm_head GEMM and the token cross-entropy run as
     # one autograd step (local_ai_training_b200.cross_entropy); False keeps F.cross_entropy
     fused_cross_entropy: bool = True
+    # int8 mode: the residual adds of each block run in the epilogue of the sublayer's last GEMM
+    # and in the RMSNorm backward kernel (TransformerBlock.forward); False keeps `x + f(x)`
+    fused_residual: bool = True
 
     def __post_init__(self) -> None:
         if min(self.vocab_size, self.block_size, self.n_layer, self.n_head, self.n_embd) <= 0:
@@ -104,7 +107,9 @@ class CausalSelfAttention(nn.Module):
         self.dropout = config.dropout
 
     def forward(self, inputs: Tensor, *, inputs_int8: Tensor | None = None,
-                inputs_scale: Tensor | None = None) -> Tensor:
+                inputs_scale: Tensor | None = None, residual: Tensor | None = None) -> Tensor:
+        """residual (int8 path): returns residual + attention(...), the add in the projection's
+        GEMM epilogue."""
         batch_size, sequence_length, channels = inputs.shape
         if inputs_int8 is not None:
             query, key, value = self.qkv(inputs, inputs_int8=inputs_int8,
@@ -121,9 +126,11 @@ class CausalSelfAttention(nn.Module):
         )
         if getattr(self.projection, "matmul_mode", "fp32") == "int8":
             attn_int8, attn_scale, dummy_joined = FusedTransposeQuantizeFn.apply(attended)
-            return self.projection(dummy_joined, inputs_int8=attn_int8, inputs_scale=attn_scale)
+            return self.projection(dummy_joined, inputs_int8=attn_int8, inputs_scale=attn_scale,
+                                   residual=residual)
         joined = attended.transpose(1, 2).contiguous().view(batch_size, sequence_length, channels)
-        return self.projection(joined)
+        out = self.projection(joined)
+        return out if residual is None else residual + out
 
 
 class FeedForward(nn.Module):
@@ -139,17 +146,25 @@ class FeedForward(nn.Module):
             self.contract.output_dtype = torch.float32
 
     def forward(self, inputs: Tensor, *, inputs_int8: Tensor | None = None,
-                inputs_scale: Tensor | None = None) -> Tensor:
+                inputs_scale: Tensor | None = None, residual: Tensor | None = None) -> Tensor:
+        """residual (int8 path, no active dropout): returns residual + feed_forward(...), the add
+        in the contraction's GEMM epilogue."""
         if inputs_int8 is not None:
             expanded = self.expand(inputs, inputs_int8=inputs_int8, inputs_scale=inputs_scale)
         else:
             expanded = self.expand(inputs)
+        fuse_residual = residual is not None and (self.dropout == 0.0 or not self.training)
         if getattr(self.contract, "matmul_mode", "fp32") == "int8":
             gelu_int8, gelu_scale, dummy_gelu = FusedGELUQuantizeFn.apply(expanded, self.dummy_dtype)
-            contracted = self.contract(dummy_gelu, inputs_int8=gelu_int8, inputs_scale=gelu_scale)
+            contracted = self.contract(dummy_gelu, inputs_int8=gelu_int8, inputs_scale=gelu_scale,
+                                       residual=residual if fuse_residual else None)
         else:
             contracted = self.contract(F.gelu(expanded))
-        return F.dropout(contracted, p=self.dropout, training=self.training)
+            fuse_residual = False
+        if fuse_residual:
+            return contracted
+        out = F.dropout(contracted, p=self.dropout, training=self.training)
+        return out if residual is None else residual + out
 
 
 class TransformerBlock(nn.Module):
@@ -161,18 +176,37 @@ class TransformerBlock(nn.Module):
         self.feed_forward = FeedForward(config, max_code=max_code)
         self.dummy_dtype = (torch.bfloat16 if config.matmul_mode == "int8" and config.bf16_activations
                             and max_code is not None else None)
+        self.fused_residual = config.fused_residual and max_code is not None
 
     def forward(self, inputs: Tensor) -> Tensor:
+        # int8 path with fused residuals: the RMSNorm producer hands x on as the residual, the
+        # sublayer's last GEMM adds it in its epilogue, and in backward the residual gradient is
+        # added to the RMSNorm input gradient by the same kernel (same values as `x + f(x)`)
+        fused = self.fused_residual and inputs.dtype == torch.float32
         if getattr(self.attention.qkv, "matmul_mode", "fp32") == "int8":
-            attn_int8, attn_scale, dummy_in = FusedRMSNormQuantizeFn.apply(
-                inputs, self.attention_norm.weight, 1e-5, self.dummy_dtype)
-            inputs = inputs + self.attention(dummy_in, inputs_int8=attn_int8, inputs_scale=attn_scale)
+            if fused:
+                attn_int8, attn_scale, dummy_in, res = FusedRMSNormQuantizeFn.apply(
+                    inputs, self.attention_norm.weight, 1e-5, self.dummy_dtype, True)
+                inputs = self.attention(dummy_in, inputs_int8=attn_int8, inputs_scale=attn_scale,
+                                        residual=res)
+            else:
+                attn_int8, attn_scale, dummy_in = FusedRMSNormQuantizeFn.apply(
+                    inputs, self.attention_norm.weight, 1e-5, self.dummy_dtype)
+                inputs = inputs + self.attention(dummy_in, inputs_int8=attn_int8,
+                                                 inputs_scale=attn_scale)
         else:
             inputs = inputs + self.attention(self.attention_norm(inputs))
         if getattr(self.feed_forward.expand, "matmul_mode", "fp32") == "int8":
-            ffn_int8, ffn_scale, dummy_in = FusedRMSNormQuantizeFn.apply(
-                inputs, self.feed_forward_norm.weight, 1e-5, self.dummy_dtype)
-            inputs = inputs + self.feed_forward(dummy_in, inputs_int8=ffn_int8, inputs_scale=ffn_scale)
+            if fused:
+                ffn_int8, ffn_scale, dummy_in, res = FusedRMSNormQuantizeFn.apply(
+                    inputs, self.feed_forward_norm.weight, 1e-5, self.dummy_dtype, True)
+                inputs = self.feed_forward(dummy_in, inputs_int8=ffn_int8, inputs_scale=ffn_scale,
+                                           residual=res)
+            else:
+                ffn_int8, ffn_scale, dummy_in = FusedRMSNormQuantizeFn.apply(
+                    inputs, self.feed_forward_norm.weight, 1e-5, self.dummy_dtype)
+                inputs = inputs + self.feed_forward(dummy_in, inputs_int8=ffn_int8,
+                                                    inputs_scale=ffn_scale)
         else:
             inputs = inputs + self.feed_forward(self.feed_forward_norm(inputs))
         return inputs

@@ -51,7 +51,7 @@ class _RatchetMatmul(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, inputs, inputs_int8, inputs_scale, code, scale, mode, fuse_backward_update,
-                int8_backward, tile_size, gradient_sink):
+                int8_backward, tile_size, gradient_sink, residual=None):
         input_shape = inputs.shape
         flat_inputs = inputs.flatten(0, -2)
         out_features = code.shape[0]
@@ -60,6 +60,10 @@ class _RatchetMatmul(torch.autograd.Function):
         # the reference returns `.to(inputs.dtype)`; a layer may ask for another output dtype
         layer = getattr(gradient_sink, "__self__", None)
         result_dtype = getattr(layer, "output_dtype", None) or inputs.dtype
+        # residual (fp32): the output is residual + the layer output, the block's residual add;
+        # the layer output's own dtype still decides how its gradient is rounded in backward
+        ctx.has_residual = residual is not None
+        ctx.output_dtype = result_dtype
         ctx.mode = mode
         ctx.fuse_backward_update = fuse_backward_update
         ctx.int8_backward = int8_backward
@@ -80,11 +84,22 @@ class _RatchetMatmul(torch.autograd.Function):
                 ctx.save_for_backward(flat_inputs, code, scale)
                 ctx.used_fused_int8 = False
             out_dtype = result_dtype if result_dtype in (torch.float32, torch.bfloat16) else torch.bfloat16
+            res_flat = None
+            if residual is not None and residual.dtype == torch.float32:
+                out_dtype = torch.float32
+                res_flat = residual.reshape(q.shape[0], out_features)
+                if res_flat.stride(1) != 1:
+                    res_flat = res_flat.contiguous()
             output = torch.empty((q.shape[0], out_features), device=q.device, dtype=out_dtype)
             # rhs = codeᵀ: (in, out) view of the [out, in] code tensor, K-major for the GEMM
             _scaled_int8_mm_into(q, code.t(), s, scale.float().contiguous(), output,
-                                 rhs_abs_max=_code_bound(gradient_sink))
-            return output.reshape(*input_shape[:-1], out_features).to(result_dtype)
+                                 rhs_abs_max=_code_bound(gradient_sink), residual=res_flat)
+            output = output.reshape(*input_shape[:-1], out_features)
+            if residual is None:
+                return output.to(result_dtype)
+            if res_flat is None:  # a residual in another dtype: the add the reference performs
+                return residual + output.to(result_dtype)
+            return output
 
         _require_cuda(inputs, "the ratchet matmul")
         ctx.save_for_backward(flat_inputs, code, scale)
@@ -97,10 +112,17 @@ class _RatchetMatmul(torch.autograd.Function):
             output = flat_inputs.to(torch.bfloat16) @ effective.t()
         else:
             raise ValueError("matmul_mode must be fp32, bf16, or int8")
-        return output.reshape(*input_shape[:-1], out_features).to(result_dtype)
+        output = output.reshape(*input_shape[:-1], out_features).to(result_dtype)
+        return output if residual is None else residual + output
 
     @staticmethod
     def backward(ctx, grad_output):
+        grad_residual = grad_output if ctx.has_residual else None
+        # the layer output's own gradient: the residual sum's gradient in the output's dtype (the
+        # cast autograd applies at the add); an fp32 gradient meeting a bf16 output is rounded by
+        # the quantiser on the int8 path, cast here otherwise
+        round_grad_bf16 = (ctx.has_residual and ctx.output_dtype == torch.bfloat16
+                           and grad_output.dtype == torch.float32)
         if ctx.used_fused_int8:
             q, s, code, scale = ctx.saved_tensors
             flat_inputs = None
@@ -111,6 +133,9 @@ class _RatchetMatmul(torch.autograd.Function):
         flat_gradient = grad_output.flatten(0, -2)
         out_features, in_features = code.shape
         grad_bf16 = None
+        if round_grad_bf16 and not (ctx.int8_backward and ctx.used_fused_int8
+                                    and ctx.fuse_backward_update):
+            flat_gradient = flat_gradient.to(torch.bfloat16)
 
         # ---- grad_input (ratchet.py:84-141)
         if ctx.mode == "fp32":
@@ -131,7 +156,8 @@ class _RatchetMatmul(torch.autograd.Function):
             seed, step, layer, step_dev = _sr_key(ctx.gradient_sink)
             gq, gs = _quantize_rows_fused(flat_gradient, scale.float(), stochastic=True, seed=seed,
                                           step=step, layer=layer, bf16_copy=bf16_copy,
-                                          step_dev=step_dev)  # the call advances step_dev
+                                          step_dev=step_dev,  # the call advances step_dev
+                                          round_input_bf16=round_grad_bf16)
             gi_dtype = ctx.input_dtype if ctx.input_dtype in (torch.float32, torch.bfloat16) else torch.bfloat16
             grad_input = torch.empty((gq.shape[0], in_features), device=gq.device, dtype=gi_dtype)
             _scaled_int8_mm_into(gq, code, gs, None, grad_input,
@@ -148,7 +174,7 @@ class _RatchetMatmul(torch.autograd.Function):
             ctx.gradient_sink, ctx.mode, ctx.fuse_backward_update, grad_bf16, inputs_bf16,
             flat_gradient, flat_inputs, code, bool(ctx.needs_input_grad[4]))
         return (grad_input.reshape(ctx.input_shape).to(ctx.input_dtype), None, None, None,
-                grad_scale, None, None, None, None, None)
+                grad_scale, None, None, None, None, None, grad_residual)
 
 
 def _deliver_weight_gradient(gradient_sink, mode: str, fuse_backward_update: bool,
@@ -471,12 +497,14 @@ class DiscreteRatchetLinear(nn.Module):
 
     # ------------------------------------------------------------------ forward
     def forward(self, inputs: Tensor, *, inputs_int8: Tensor | None = None,
-                inputs_scale: Tensor | None = None) -> Tensor:
+                inputs_scale: Tensor | None = None, residual: Tensor | None = None) -> Tensor:
+        """residual (optional): returns residual + layer(inputs), the add fused into the int8
+        GEMM epilogue when residual is fp32."""
         if self.matmul_mode != "fp32" or self.fuse_backward_update:
             return _RatchetMatmul.apply(
                 inputs, inputs_int8, inputs_scale, self.code_int8(), self.scale, self.matmul_mode,
                 self.fuse_backward_update, self.int8_backward, self.tile_size,
-                self._capture_weight_gradient,
+                self._capture_weight_gradient, residual,
             )
         _require_cuda(inputs, "the ratchet layer")
         effective = self.effective_weight().to(dtype=inputs.dtype)
@@ -486,7 +514,8 @@ class DiscreteRatchetLinear(nn.Module):
             else:
                 effective = effective.detach().requires_grad_(True)
             self._effective_weight = effective
-        return F.linear(inputs, effective)
+        output = F.linear(inputs, effective)
+        return output if residual is None else residual + output
 
     # ------------------------------------------------------------------ update
     def _run_update(self, gradient: Tensor, row_start: int, row_end: int, *, normalize: bool,

@@ -50,10 +50,10 @@ def test_status_codes_map_to_reference_exceptions():
     # a shape error straight from the library (no GPU work is launched for negative shapes)
     with pytest.raises(ValueError, match="negative shape"):
         _lib.check(_lib.lib().rt_scaled_int8_mm(None, 0, 0, None, 0, 0, None, None, None, 1, 0,
-                                                -1, 1, 1, 0, None))
+                                                -1, 1, 1, 0, None, 0, None))
     with pytest.raises(TypeError, match="bfloat16 or float32"):
         _lib.check(_lib.lib().rt_scaled_int8_mm(None, 0, 0, None, 0, 0, None, None, None, 7, 0,
-                                                1, 1, 1, 0, None))
+                                                1, 1, 1, 0, None, 0, None))
     with pytest.raises(ValueError, match="max_code"):
         _lib.check(_lib.lib().rt_ratchet_update(1, 0, 0, 1, 1, 1, 1, 1, None, 1, 1, None, 0.0, 9,
                                                 8, 0.5, 1.5, 1e-8, None, None, None, None, None))

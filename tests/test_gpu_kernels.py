@@ -172,6 +172,32 @@ def test_scaled_int8_mm_full_range_accumulators_round_like_oracle(cuda_device, o
     np.testing.assert_array_equal(_np(out), expected)
 
 
+@pytest.mark.parametrize("m,k,n,pad", [(16384, 512, 512, 0), (300, 512, 96, 0), (129, 256, 520, 0),
+                                       (200, 128, 64, 3)])
+@pytest.mark.parametrize("inplace", [False, True])
+def test_scaled_int8_mm_residual_epilogue(cuda_device, m, k, n, pad, inplace):
+    """out = residual + fp32(bf16(...)), the block's residual add in the epilogue: TMA-loaded
+    residual tiles (16-byte rows) and the lane-per-row path (pad breaks the row alignment)."""
+    from local_ai_training_b200.int8_matmul import _scaled_int8_mm_into
+
+    torch.manual_seed(m + n + pad)
+    lhs = torch.randint(-127, 128, (m, k), device=cuda_device, dtype=torch.int8)
+    code = torch.randint(-3, 4, (n, k), device=cuda_device, dtype=torch.int8)
+    ls = torch.rand(m, device=cuda_device) * 0.01 + 1e-3
+    rs = torch.rand(n, device=cuda_device) * 0.05 + 5e-3
+    base = torch.randn(m, n + pad, device=cuda_device)
+    residual = base[:, :n]
+    expected = residual + ((lhs.float() @ code.float().t()) * ls[:, None] * rs[None, :]).to(
+        torch.bfloat16).float()
+    if inplace:
+        out = residual
+        _scaled_int8_mm_into(lhs, code.t(), ls, rs, out, rhs_abs_max=7, residual=residual)
+    else:
+        out = torch.empty(m, n, device=cuda_device)
+        _scaled_int8_mm_into(lhs, code.t(), ls, rs, out, rhs_abs_max=7, residual=residual)
+    assert torch.equal(out, expected)
+
+
 @pytest.mark.parametrize("bound", [0, 7])
 @pytest.mark.parametrize("k,n", [(512, 512), (512, 2048), (2048, 512), (4096, 256)])
 def test_scaled_int8_mm_full_size_exact(cuda_device, k, n, bound):
