@@ -203,6 +203,41 @@ int rt_gelu_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtyp
                      int64_t cols, void *dx, int dx_dtype, void *stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Gradient producers fused with the consuming layer's stochastic-rounding quantisation.  Each
+ * computes the output gradient G of a ratchet layer (the gradient the layer's backward receives)
+ * and, in the same pass, quantises G exactly as rt_quantize_rows(G, col_scale, stochastic=1,
+ * round_input_bf16, seed, step, layer, step_dev, q, ldq, row_scale, x_bf16_out) would: the
+ * ratchet.py:117-134 fold of the layer's row scales into the gradient and its per-token
+ * stochastic rounding, with the same Philox stream and step_dev advance.  They replace the
+ * reference's two passes (the producer's backward, then the layer's quantisation) over G.
+ * Rows must allow 16-byte chunks (RT_ERR_UNSUPPORTED otherwise; the caller then runs the two
+ * passes).
+ *
+ * rt_rmsnorm_backward_sr: rt_rmsnorm_backward (int8_backward.py:7-51) whose dx is G.
+ * rt_gelu_backward_sr: tanh-GELU backward (int8_backward.py:53-89) of contiguous rows whose
+ *   dx (dtype of grad_y and x) is G.
+ * rt_heads_gather_sr: G[b·T+t, p·H·D + h·D + d] = src_p[b, h, t, d] for p = 0, 1, 2 — the
+ *   gradient of a q|k|v projection output split into three [B, H, T, D] head views
+ *   (model.py:61-70, `.chunk(3)` and the head transposes), written to `out` (row stride ldo).
+ *   strides holds (b, h, t, d) element strides of src_0, src_1, src_2; d strides must be 1.
+ * ------------------------------------------------------------------------------------------- */
+int rt_rmsnorm_backward_sr(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
+                           const float *weight, double eps, int64_t rows, int64_t cols, void *dx,
+                           int dx_dtype, float *dw, const float *dx_add, const float *col_scale,
+                           int round_input_bf16, uint64_t seed, uint32_t step, uint32_t layer,
+                           uint32_t *step_dev, int8_t *q, int64_t ldq, float *row_scale,
+                           void *x_bf16_out, int64_t ld_xbf16, void *stream);
+int rt_gelu_backward_sr(const void *grad_y, const void *x, int dtype, int64_t rows, int64_t cols,
+                        void *dx, const float *col_scale, uint64_t seed, uint32_t step,
+                        uint32_t layer, uint32_t *step_dev, int8_t *q, int64_t ldq,
+                        float *row_scale, void *x_bf16_out, int64_t ld_xbf16, void *stream);
+int rt_heads_gather_sr(const void *const *src, const int64_t *strides, int dtype, int64_t batch,
+                       int64_t heads, int64_t seq, int64_t head_dim, void *out, int64_t ldo,
+                       const float *col_scale, uint64_t seed, uint32_t step, uint32_t layer,
+                       uint32_t *step_dev, int8_t *q, int64_t ldq, float *row_scale,
+                       void *x_bf16_out, int64_t ld_xbf16, void *stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Token cross-entropy over the lm_head logits.  Replaces F.cross_entropy(logits, targets) of
  * model.py:244-249 (mean over targets != ignore_index) and the bf16 cast of its gradient before
  * the lm_head grad GEMMs (ratchet.py:139-141, 161).  Forward, per row: row_max, row_logsum =

@@ -62,6 +62,12 @@ _SIGNATURES = {
                                _p, _p], _i),
     "rt_rmsnorm_backward": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p, _p, _p], _i),
     "rt_gelu_backward": ([_p, _i, _p, _i, _i64, _i64, _p, _i, _p], _i),
+    "rt_rmsnorm_backward_sr": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p, _p, _p, _i, _u64,
+                                _u32, _u32, _p, _p, _i64, _p, _p, _i64, _p], _i),
+    "rt_gelu_backward_sr": ([_p, _p, _i, _i64, _i64, _p, _p, _u64, _u32, _u32, _p, _p, _i64, _p,
+                             _p, _i64, _p], _i),
+    "rt_heads_gather_sr": ([_p, _p, _i, _i64, _i64, _i64, _i64, _p, _i64, _p, _u64, _u32, _u32,
+                            _p, _p, _i64, _p, _p, _i64, _p], _i),
     "rt_cross_entropy_fwd": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p], _i),
     "rt_cross_entropy_bwd": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _p,
                               _i64, _p], _i),

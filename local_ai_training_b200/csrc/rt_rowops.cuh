@@ -410,6 +410,75 @@ __global__ void __launch_bounds__(CTA) quant_rows_generic_kernel(QuantArgs a) {
   sr_step_arrive(a, step);
 }
 
+// ---- pieces of the stochastic-rounding row quantisation shared by the fused gradient producers
+// (a producer that already holds a layer's output-gradient row in registers quantises it for
+// the layer's int8 grad_input GEMM in the same pass, with the arithmetic of quant_rows_kernel).
+template <int RT, int VPT>
+__device__ __forceinline__ void sr_load_col_scales(const QuantArgs &a, int t, int64_t nch,
+                                                   float (&cs)[VPT][8]) {
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (a.col_scale != nullptr && c < nch) {
+      ld8(a.col_scale + 8 * c, cs[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cs[i][j] = 1.0f;
+    }
+  }
+}
+// One chunk of the gradient as the layer receives it -> the value the quantiser rounds: the
+// optional bf16 rounding, the bf16 copy (grad_weight operand), the column scale; amax updated.
+__device__ __forceinline__ void sr_prepare_chunk(const QuantArgs &a, int64_t row, int64_t c,
+                                                 float (&v)[8], const float (&cs)[8],
+                                                 float &amax) {
+  if (a.round_bf16) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = bf16_round(v[j]);
+  }
+  if (a.xbf16 != nullptr)
+    st8(reinterpret_cast<__nv_bfloat16 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c), v);
+  if (a.col_scale != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(v[j], cs[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+}
+// Row scale and int8 row from the prepared values (amax already reduced over the row).
+template <int RT, int VPT>
+__device__ __forceinline__ void sr_quant_store_row(const QuantArgs &a, uint32_t step, int64_t row,
+                                                   int t, int64_t nch, const float (&v)[VPT][8],
+                                                   float amax) {
+  const float scale = row_scale_of(amax);
+  const float rcp = __frcp_rn(scale);
+  if (t == 0) a.row_scale[row] = scale;
+  int8_t *qr = a.q + row * a.ldq;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (c >= nch) continue;
+    const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;
+    const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
+    uint2 o;
+    o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_u_lo(p.x)),
+                   quant_sr_i(v[i][1], scale, rcp, sr_u_hi(p.x)),
+                   quant_sr_i(v[i][2], scale, rcp, sr_u_lo(p.y)),
+                   quant_sr_i(v[i][3], scale, rcp, sr_u_hi(p.y)));
+    o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_u_lo(p.z)),
+                   quant_sr_i(v[i][5], scale, rcp, sr_u_hi(p.z)),
+                   quant_sr_i(v[i][6], scale, rcp, sr_u_lo(p.w)),
+                   quant_sr_i(v[i][7], scale, rcp, sr_u_hi(p.w)));
+    *reinterpret_cast<uint2 *>(qr + 8 * c) = o;
+  }
+}
+// Host: the vectorised kernels' layout conditions on the quantiser outputs.
+static inline bool sr_outputs_vec(const QuantArgs &a) {
+  return (reinterpret_cast<uintptr_t>(a.q) & 7) == 0 && a.ldq % 8 == 0 &&
+         (a.col_scale == nullptr || aligned16(a.col_scale)) &&
+         (a.xbf16 == nullptr || (aligned16(a.xbf16) && a.ld_xbf16 % 8 == 0));
+}
+
 template <typename T>
 static int quant_rows_dispatch(const QuantArgs &a, cudaStream_t s) {
   const size_t es = sizeof(T);
@@ -1047,13 +1116,18 @@ struct RmsBwdArgs {
   int dx_dtype;
   float *dw;
   const float *dx_add;  // optional fp32 gradient added to dx (the residual branch), may be dx
+  QuantArgs sq;         // SRQ: stochastic-rounding quantisation of dx for the layer it feeds
 };
-// X: input dtype, G: incoming-gradient dtype (fp32 or bf16 each).
-template <typename X, typename G, int RT, int VPT>
-__global__ void __launch_bounds__(CTA) rmsnorm_bwd_kernel(RmsBwdArgs a) {
+// X: input dtype, G: incoming-gradient dtype (fp32 or bf16 each).  SRQ: dx (the output gradient
+// of the ratchet layer whose output is this norm's input) is also quantised with stochastic
+// rounding for that layer's int8 grad_input GEMM (a.sq: column scales, Philox key, int8 rows,
+// row scales, bf16 copy), exactly as quant_rows_kernel would quantise the stored dx.
+template <typename X, typename G, int RT, int VPT, bool SRQ>
+__global__ void __launch_bounds__(CTA, 2) rmsnorm_bwd_kernel(RmsBwdArgs a) {
   constexpr int RPC = CTA / RT, NT = CTA / RT;
   __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
   __shared__ float smb[RPC];
+  __shared__ float smx[SRQ ? RPC * 8 : 1];
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
   const int64_t nch = a.cols / 8;
   const int64_t groups = (a.rows + RPC - 1) / RPC;
@@ -1070,6 +1144,8 @@ __global__ void __launch_bounds__(CTA) rmsnorm_bwd_kernel(RmsBwdArgs a) {
 #pragma unroll
     for (int j = 0; j < 8; ++j) dwp[i][j] = 0.0f;
   }
+  // column scales are re-read per row (L1 hits) rather than held: two CTAs per SM stay resident
+  const uint32_t step = SRQ ? sr_step_read(a.sq) : 0u;
   // rows are visited in groups of RPC by a grid-stride loop (uniform across the CTA), so each
   // thread accumulates the weight gradient of its own columns over many rows
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
@@ -1103,30 +1179,45 @@ __global__ void __launch_bounds__(CTA) rmsnorm_bwd_kernel(RmsBwdArgs a) {
     const float var = __fdiv_rn(total, static_cast<float>(a.cols));
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.eps)));
     const float dvar = __fmul_rn(__fmul_rn(dsum, -0.5f), __fmul_rn(__fmul_rn(r, r), r));
-    if (!live) continue;
+    float qv[SRQ ? VPT : 1][8];
+    float amax = 0.0f;
+    if (live) {
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int64_t c = t + static_cast<int64_t>(i) * RT;
-      if (c >= nch) continue;
-      float o[8];
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t c = t + static_cast<int64_t>(i) * RT;
+        if (c >= nch) continue;
+        float o[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float dh = __fmul_rn(gv[i][j], wv[i][j]);
-        o[j] = bf16_round(__fadd_rn(__fmul_rn(dh, r),
-                                    __fdiv_rn(__fmul_rn(__fmul_rn(dvar, 2.0f), xv[i][j]),
-                                              static_cast<float>(a.cols))));
-        dwp[i][j] = __fadd_rn(dwp[i][j], __fmul_rn(__fmul_rn(gv[i][j], xv[i][j]), r));
+        for (int j = 0; j < 8; ++j) {
+          const float dh = __fmul_rn(gv[i][j], wv[i][j]);
+          o[j] = bf16_round(__fadd_rn(__fmul_rn(dh, r),
+                                      __fdiv_rn(__fmul_rn(__fmul_rn(dvar, 2.0f), xv[i][j]),
+                                                static_cast<float>(a.cols))));
+          dwp[i][j] = __fadd_rn(dwp[i][j], __fmul_rn(__fmul_rn(gv[i][j], xv[i][j]), r));
+        }
+        if (a.dx_add != nullptr) {  // the residual branch's gradient, summed as autograd would
+          float ad[8];
+          ld8(a.dx_add + row * a.cols + 8 * c, ad);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(ad[j], o[j]);
+        }
+        if (a.dx_dtype == RT_F32)
+          st8(static_cast<float *>(a.dx) + row * a.cols + 8 * c, o);
+        else
+          st8(static_cast<__nv_bfloat16 *>(a.dx) + row * a.cols + 8 * c, o);
+        if constexpr (SRQ) {
+          // the stored value (a bf16 dx stores the bf16-exact o unchanged)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) qv[i][j] = o[j];
+          float cs[8];
+          if (a.sq.col_scale != nullptr) ld8(a.sq.col_scale + 8 * c, cs);
+          sr_prepare_chunk(a.sq, row, c, qv[i], cs, amax);
+        }
       }
-      if (a.dx_add != nullptr) {  // the residual branch's gradient, summed as autograd would
-        float ad[8];
-        ld8(a.dx_add + row * a.cols + 8 * c, ad);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(ad[j], o[j]);
-      }
-      if (a.dx_dtype == RT_F32)
-        st8(static_cast<float *>(a.dx) + row * a.cols + 8 * c, o);
-      else
-        st8(static_cast<__nv_bfloat16 *>(a.dx) + row * a.cols + 8 * c, o);
+    }
+    if constexpr (SRQ) {
+      amax = row_max<RT>(amax, smx, sub, t);  // CTA-uniform trip count: its barriers are safe
+      if (live) sr_quant_store_row<RT, VPT>(a.sq, step, row, t, nch, qv, amax);
     }
   }
   if (a.dw != nullptr) {
@@ -1157,6 +1248,7 @@ __global__ void __launch_bounds__(CTA) rmsnorm_bwd_kernel(RmsBwdArgs a) {
       }
     }
   }
+  if constexpr (SRQ) sr_step_arrive(a.sq, step);
 }
 
 __global__ void __launch_bounds__(CTA)
@@ -1210,6 +1302,120 @@ __global__ void gelu_bwd_kernel(const void *gy, int gdt, const void *x, int xdt,
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     store_elem(dx, dxdt, i, gelu_tanh_grad(load_elem(x, xdt, i), load_elem(gy, gdt, i)));
+}
+
+// tanh-GELU backward fused with the stochastic-rounding quantisation of its result, the output
+// gradient of the expanding ratchet layer (int8_backward.py:53-89 followed by the layer's
+// ratchet.py:117-134 quantisation): dx is written once and quantised from registers.  Rows are
+// contiguous (a.sq.cols elements); grid-stride over row groups with a resident-sized grid.
+struct GeluBwdQArgs {
+  const void *gy;
+  const void *x;
+  void *dx;
+  QuantArgs sq;
+};
+template <typename T, int RT, int VPT>
+__global__ void __launch_bounds__(CTA, VPT <= 2 ? 4 : (VPT == 4 ? 2 : 1)) gelu_bwd_sr_kernel(GeluBwdQArgs a) {
+  constexpr int RPC = CTA / RT;
+  __shared__ float smx[RPC * 8];
+  const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
+  const int64_t nch = a.sq.cols / 8;
+  const int64_t groups = (a.sq.rows + RPC - 1) / RPC;
+  const uint32_t step = sr_step_read(a.sq);
+  float cs[VPT][8];
+  sr_load_col_scales<RT, VPT>(a.sq, t, nch, cs);
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t row = grp * RPC + sub;
+    const bool live = row < a.sq.rows;
+    const int64_t off = (live ? row : 0) * a.sq.cols;
+    const T *xr = static_cast<const T *>(a.x) + off;
+    const T *gr = static_cast<const T *>(a.gy) + off;
+    T *dr = static_cast<T *>(a.dx) + off;
+    float v[VPT][8];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      if (live && c < nch) {
+        float xv[8], g[8];
+        ld8(xr + 8 * c, xv);
+        ld8(gr + 8 * c, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = gelu_tanh_grad(xv[j], g[j]);
+        st8(dr + 8 * c, v[i]);  // bf16-exact values: a bf16 dx stores them unchanged
+        sr_prepare_chunk(a.sq, row, c, v[i], cs[i], amax);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+      }
+    }
+    amax = row_max<RT>(amax, smx, sub, t);
+    if (live) sr_quant_store_row<RT, VPT>(a.sq, step, row, t, nch, v, amax);
+  }
+  sr_step_arrive(a.sq, step);
+}
+
+// Gradients of the three [B, H, T, D] head views of a fused q|k|v projection output gathered
+// into its [B·T, 3·H·D] output gradient (the concatenation autograd forms for `.chunk(3)` of
+// model.py:61-70 and the head transposes), fused with the stochastic-rounding quantisation of
+// that gradient for the projection's int8 grad_input GEMM.  Part p of a row holds the channels
+// h·D + d of source p; every source needs unit stride along D and D % 8 == 0.
+struct HeadsQArgs {
+  const void *src[3];
+  int64_t sb[3], sh[3], ss[3];
+  int64_t seq, head_dim, width;  // width = H·D channels per part
+  void *out;
+  int64_t ldo;
+  QuantArgs sq;  // rows = B·T, cols = 3·width
+};
+template <typename T, int RT, int VPT>
+__global__ void __launch_bounds__(CTA, VPT <= 2 ? 4 : (VPT == 4 ? 2 : 1)) heads3_sr_kernel(HeadsQArgs a) {
+  constexpr int RPC = CTA / RT;
+  __shared__ float smx[RPC * 8];
+  const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
+  const int64_t nch = a.sq.cols / 8;
+  const int64_t groups = (a.sq.rows + RPC - 1) / RPC;
+  const uint32_t step = sr_step_read(a.sq);
+  float cs[VPT][8];
+  sr_load_col_scales<RT, VPT>(a.sq, t, nch, cs);
+  // this thread's chunks sit at the same (part, head, d) in every row
+  int part[VPT];
+  int64_t coff[VPT];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t ch = 8 * (t + static_cast<int64_t>(i) * RT);
+    const int64_t p = ch / a.width, w = ch - p * a.width;
+    const int64_t h = w / a.head_dim, d = w - h * a.head_dim;
+    part[i] = static_cast<int>(p < 3 ? p : 2);
+    coff[i] = h * (p == 0 ? a.sh[0] : (p == 1 ? a.sh[1] : a.sh[2])) + d;
+  }
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    const int64_t row = grp * RPC + sub;
+    const bool live = row < a.sq.rows;
+    const int64_t b = live ? row / a.seq : 0, s = live ? row - b * a.seq : 0;
+    const T *base0 = static_cast<const T *>(a.src[0]) + b * a.sb[0] + s * a.ss[0];
+    const T *base1 = static_cast<const T *>(a.src[1]) + b * a.sb[1] + s * a.ss[1];
+    const T *base2 = static_cast<const T *>(a.src[2]) + b * a.sb[2] + s * a.ss[2];
+    T *orow = static_cast<T *>(a.out) + (live ? row : 0) * a.ldo;
+    float v[VPT][8];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      if (live && c < nch) {
+        const T *src = part[i] == 0 ? base0 : (part[i] == 1 ? base1 : base2);
+        ld8(src + coff[i], v[i]);
+        st8(orow + 8 * c, v[i]);
+        sr_prepare_chunk(a.sq, row, c, v[i], cs[i], amax);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+      }
+    }
+    amax = row_max<RT>(amax, smx, sub, t);
+    if (live) sr_quant_store_row<RT, VPT>(a.sq, step, row, t, nch, v, amax);
+  }
+  sr_step_arrive(a.sq, step);
 }
 
 static inline unsigned grid_for(int64_t n, int threads) {
@@ -1430,6 +1636,51 @@ extern "C" int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, 
   return check_launch("rt_transpose_quantize");
 }
 
+static int rmsnorm_backward_launch(const RmsBwdArgs &a, int gy_dtype, int x_dtype, bool srq,
+                                   const char *who, cudaStream_t s) {
+  const bool vec = a.cols % 8 == 0 && aligned16(a.x) && aligned16(a.gy) && aligned16(a.dx) &&
+                   aligned16(a.w) && (a.dw == nullptr || aligned16(a.dw)) &&
+                   (a.dx_add == nullptr || aligned16(a.dx_add)) && (!srq || sr_outputs_vec(a.sq));
+  const RowCfg cfg = vec ? row_cfg_narrow(a.cols / 8) : RowCfg{0, 0};
+  if (cfg.rt == 0) {
+    if (srq) return fail(RT_ERR_UNSUPPORTED, "rt_rmsnorm_backward_sr: rows need 16-byte chunks");
+    rmsnorm_bwd_generic_kernel<<<static_cast<unsigned>(a.rows), CTA, 0, s>>>(a, gy_dtype, x_dtype);
+    return check_launch(who);
+  }
+  int sms = 0;
+  rt_sm_count(&sms);
+  const int64_t groups = (a.rows + (CTA / cfg.rt) - 1) / (CTA / cfg.rt);
+  const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 2;
+  const unsigned grid = static_cast<unsigned>(groups < cap ? groups : cap);
+  const size_t dsm = (a.dw != nullptr && cfg.rt < CTA) ? (CTA / cfg.rt) * a.cols * sizeof(float) : 0;
+  if (dsm > 48 * 1024) return fail(RT_ERR_UNSUPPORTED, "rt_rmsnorm_backward: row too long");
+  const int combo = (x_dtype == RT_F32 ? 0 : 2) + (gy_dtype == RT_F32 ? 0 : 1);
+#define RT_RMSB(X, G, Q)                                                                      \
+  switch (cfg.rt * 16 + cfg.vpt) {                                                            \
+    case 32 * 16 + 1: rmsnorm_bwd_kernel<X, G, 32, 1, Q><<<grid, CTA, dsm, s>>>(a); break;     \
+    case 32 * 16 + 2: rmsnorm_bwd_kernel<X, G, 32, 2, Q><<<grid, CTA, dsm, s>>>(a); break;     \
+    case 128 * 16 + 2: rmsnorm_bwd_kernel<X, G, 128, 2, Q><<<grid, CTA, dsm, s>>>(a); break;   \
+    default: rmsnorm_bwd_kernel<X, G, 256, 2, Q><<<grid, CTA, dsm, s>>>(a); break;             \
+  }
+  if (srq) {
+    switch (combo) {
+      case 0: RT_RMSB(float, float, true) break;
+      case 1: RT_RMSB(float, __nv_bfloat16, true) break;
+      case 2: RT_RMSB(__nv_bfloat16, float, true) break;
+      default: RT_RMSB(__nv_bfloat16, __nv_bfloat16, true) break;
+    }
+  } else {
+    switch (combo) {
+      case 0: RT_RMSB(float, float, false) break;
+      case 1: RT_RMSB(float, __nv_bfloat16, false) break;
+      case 2: RT_RMSB(__nv_bfloat16, float, false) break;
+      default: RT_RMSB(__nv_bfloat16, __nv_bfloat16, false) break;
+    }
+  }
+#undef RT_RMSB
+  return check_launch(who);
+}
+
 extern "C" int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
                                    const float *weight, double eps, int64_t rows, int64_t cols,
                                    void *dx, int dx_dtype, float *dw, const float *dx_add,
@@ -1438,39 +1689,31 @@ extern "C" int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void 
   if (rows == 0) return RT_OK;
   if (dx_add != nullptr && dx_dtype != RT_F32)
     return fail(RT_ERR_DTYPE, "rt_rmsnorm_backward: an added gradient needs a float32 dx");
-  cudaStream_t s = as_stream(stream);
-  RmsBwdArgs a{grad_y, x, weight, static_cast<float>(eps), rows, cols, dx, dx_dtype, dw, dx_add};
-  const bool vec = cols % 8 == 0 && aligned16(x) && aligned16(grad_y) && aligned16(dx) &&
-                   aligned16(weight) && (dw == nullptr || aligned16(dw)) &&
-                   (dx_add == nullptr || aligned16(dx_add));
-  const RowCfg cfg = vec ? row_cfg_narrow(cols / 8) : RowCfg{0, 0};
-  if (cfg.rt != 0) {
-    int sms = 0;
-    rt_sm_count(&sms);
-    const int64_t groups = (rows + (CTA / cfg.rt) - 1) / (CTA / cfg.rt);
-    const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 2;
-    const unsigned grid = static_cast<unsigned>(groups < cap ? groups : cap);
-    const size_t dsm = (dw != nullptr && cfg.rt < CTA) ? (CTA / cfg.rt) * cols * sizeof(float) : 0;
-    if (dsm > 48 * 1024) return fail(RT_ERR_UNSUPPORTED, "rt_rmsnorm_backward: row too long");
-    const int combo = (x_dtype == RT_F32 ? 0 : 2) + (gy_dtype == RT_F32 ? 0 : 1);
-#define RT_RMSB(X, G)                                                                        \
-  switch (cfg.rt * 16 + cfg.vpt) {                                                           \
-    case 32 * 16 + 1: rmsnorm_bwd_kernel<X, G, 32, 1><<<grid, CTA, dsm, s>>>(a); break;       \
-    case 32 * 16 + 2: rmsnorm_bwd_kernel<X, G, 32, 2><<<grid, CTA, dsm, s>>>(a); break;       \
-    case 128 * 16 + 2: rmsnorm_bwd_kernel<X, G, 128, 2><<<grid, CTA, dsm, s>>>(a); break;     \
-    default: rmsnorm_bwd_kernel<X, G, 256, 2><<<grid, CTA, dsm, s>>>(a); break;               \
-  }
-    switch (combo) {
-      case 0: RT_RMSB(float, float) break;
-      case 1: RT_RMSB(float, __nv_bfloat16) break;
-      case 2: RT_RMSB(__nv_bfloat16, float) break;
-      default: RT_RMSB(__nv_bfloat16, __nv_bfloat16) break;
-    }
-#undef RT_RMSB
-  } else {
-    rmsnorm_bwd_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a, gy_dtype, x_dtype);
-  }
-  return check_launch("rt_rmsnorm_backward");
+  RmsBwdArgs a{grad_y, x, weight, static_cast<float>(eps), rows, cols, dx, dx_dtype, dw, dx_add,
+               QuantArgs{}};
+  return rmsnorm_backward_launch(a, gy_dtype, x_dtype, false, "rt_rmsnorm_backward",
+                                 as_stream(stream));
+}
+
+extern "C" int rt_rmsnorm_backward_sr(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
+                                      const float *weight, double eps, int64_t rows, int64_t cols,
+                                      void *dx, int dx_dtype, float *dw, const float *dx_add,
+                                      const float *col_scale, int round_input_bf16, uint64_t seed,
+                                      uint32_t step, uint32_t layer, uint32_t *step_dev, int8_t *q,
+                                      int64_t ldq, float *row_scale, void *x_bf16_out,
+                                      int64_t ld_xbf16, void *stream) {
+  if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_rmsnorm_backward_sr: shape");
+  if (rows == 0) return RT_OK;
+  if (dx_add != nullptr && dx_dtype != RT_F32)
+    return fail(RT_ERR_DTYPE, "rt_rmsnorm_backward_sr: an added gradient needs a float32 dx");
+  if (q == nullptr || row_scale == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_rmsnorm_backward_sr: null pointer");
+  QuantArgs sq{dx, rows, cols, cols, 1, col_scale, 1,
+               dx_dtype == RT_F32 && round_input_bf16, seed, step, layer, step_dev, q, ldq,
+               row_scale, static_cast<unsigned short *>(x_bf16_out), ld_xbf16};
+  RmsBwdArgs a{grad_y, x, weight, static_cast<float>(eps), rows, cols, dx, dx_dtype, dw, dx_add, sq};
+  return rmsnorm_backward_launch(a, gy_dtype, x_dtype, true, "rt_rmsnorm_backward_sr",
+                                 as_stream(stream));
 }
 
 extern "C" int rt_gelu_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
@@ -1493,4 +1736,77 @@ extern "C" int rt_gelu_backward(const void *grad_y, int gy_dtype, const void *x,
     gelu_bwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(grad_y, gy_dtype, x, x_dtype, n, dx, dx_dtype);
   }
   return check_launch("rt_gelu_backward");
+}
+
+extern "C" int rt_gelu_backward_sr(const void *grad_y, const void *x, int dtype, int64_t rows,
+                                   int64_t cols, void *dx, const float *col_scale, uint64_t seed,
+                                   uint32_t step, uint32_t layer, uint32_t *step_dev, int8_t *q,
+                                   int64_t ldq, float *row_scale, void *x_bf16_out,
+                                   int64_t ld_xbf16, void *stream) {
+  if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_gelu_backward_sr: shape");
+  if (dtype != RT_F32 && dtype != RT_BF16) return fail(RT_ERR_DTYPE, "rt_gelu_backward_sr: dtype");
+  if (rows == 0) return RT_OK;
+  if (grad_y == nullptr || x == nullptr || dx == nullptr || q == nullptr || row_scale == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_gelu_backward_sr: null pointer");
+  QuantArgs sq{dx, rows, cols, cols, 1, col_scale, 1, 0, seed, step, layer, step_dev, q, ldq,
+               row_scale, static_cast<unsigned short *>(x_bf16_out), ld_xbf16};
+  GeluBwdQArgs a{grad_y, x, dx, sq};
+  const size_t es = dtype == RT_F32 ? 4 : 2;
+  const bool vec = cols % 8 == 0 && aligned16(grad_y) && aligned16(x) && aligned16(dx) &&
+                   (cols * es) % 16 == 0 && sr_outputs_vec(sq);
+  const RowCfg cfg = vec ? row_cfg(cols / 8, rows) : RowCfg{0, 0};
+  if (cfg.rt == 0) return fail(RT_ERR_UNSUPPORTED, "rt_gelu_backward_sr: rows need 16-byte chunks");
+  int sms = 0;
+  if (int rc = rt_sm_count(&sms)) return rc;
+  const unsigned resident = static_cast<unsigned>(sms) * 4;
+  const unsigned groups = row_grid(rows, cfg.rt);
+  const unsigned grid = groups < resident ? groups : resident;
+  cudaStream_t s = as_stream(stream);
+  if (dtype == RT_F32)
+    RT_DISPATCH_ROW(cfg, gelu_bwd_sr_kernel, float, grid, a);
+  else
+    RT_DISPATCH_ROW(cfg, gelu_bwd_sr_kernel, __nv_bfloat16, grid, a);
+  return check_launch("rt_gelu_backward_sr");
+}
+
+extern "C" int rt_heads_gather_sr(const void *const *src, const int64_t *strides, int dtype,
+                                  int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                                  void *out, int64_t ldo, const float *col_scale, uint64_t seed,
+                                  uint32_t step, uint32_t layer, uint32_t *step_dev, int8_t *q,
+                                  int64_t ldq, float *row_scale, void *x_bf16_out,
+                                  int64_t ld_xbf16, void *stream) {
+  if (batch < 0 || seq < 0 || heads <= 0 || head_dim <= 0)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_heads_gather_sr: shape");
+  if (dtype != RT_F32 && dtype != RT_BF16) return fail(RT_ERR_DTYPE, "rt_heads_gather_sr: dtype");
+  const int64_t rows = batch * seq;
+  if (rows == 0) return RT_OK;
+  if (src == nullptr || strides == nullptr || out == nullptr || q == nullptr ||
+      row_scale == nullptr || src[0] == nullptr || src[1] == nullptr || src[2] == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_heads_gather_sr: null pointer");
+  const int64_t width = heads * head_dim, cols = 3 * width;
+  QuantArgs sq{out, rows, cols, ldo, 1, col_scale, 1, 0, seed, step, layer, step_dev, q, ldq,
+               row_scale, static_cast<unsigned short *>(x_bf16_out), ld_xbf16};
+  HeadsQArgs a;
+  const int64_t es = dtype == RT_F32 ? 4 : 2;
+  bool vec = head_dim % 8 == 0 && aligned16(out) && (ldo * es) % 16 == 0 && sr_outputs_vec(sq);
+  for (int p = 0; p < 3; ++p) {
+    a.src[p] = src[p];
+    a.sb[p] = strides[4 * p], a.sh[p] = strides[4 * p + 1], a.ss[p] = strides[4 * p + 2];
+    vec = vec && strides[4 * p + 3] == 1 && aligned16(src[p]) && (a.sb[p] * es) % 16 == 0 &&
+          (a.sh[p] * es) % 16 == 0 && (a.ss[p] * es) % 16 == 0;
+  }
+  a.seq = seq, a.head_dim = head_dim, a.width = width, a.out = out, a.ldo = ldo, a.sq = sq;
+  const RowCfg cfg = vec ? row_cfg(cols / 8, rows) : RowCfg{0, 0};
+  if (cfg.rt == 0) return fail(RT_ERR_UNSUPPORTED, "rt_heads_gather_sr: heads need 16-byte chunks");
+  int sms = 0;
+  if (int rc = rt_sm_count(&sms)) return rc;
+  const unsigned resident = static_cast<unsigned>(sms) * 4;
+  const unsigned groups = row_grid(rows, cfg.rt);
+  const unsigned grid = groups < resident ? groups : resident;
+  cudaStream_t s = as_stream(stream);
+  if (dtype == RT_F32)
+    RT_DISPATCH_ROW(cfg, heads3_sr_kernel, float, grid, a);
+  else
+    RT_DISPATCH_ROW(cfg, heads3_sr_kernel, __nv_bfloat16, grid, a);
+  return check_launch("rt_heads_gather_sr");
 }

@@ -87,14 +87,18 @@ class FusedRMSNormQuantizeFn(torch.autograd.Function):
 
     residual_out=True also returns x itself as a fourth output, to be consumed as the residual
     of the block (`x + sublayer(norm(x))`): its gradient then arrives here and is added to the
-    RMSNorm input gradient by the same kernel, instead of autograd summing the two branches."""
+    RMSNorm input gradient by the same kernel, instead of autograd summing the two branches.
+
+    grad_plan: the GradientQuantPlan x carries when a ratchet layer produced it; the input
+    gradient computed here is then also quantised for that layer by the same kernel."""
 
     @staticmethod
     def forward(ctx, x: Tensor, weight: Tensor, eps: float = 1e-5, dummy_dtype=None,
-                residual_out: bool = False):
+                residual_out: bool = False, grad_plan=None):
         int8_out, scale_out = fused_rmsnorm_quantize(x, weight, eps)
         ctx.save_for_backward(x, weight)
         ctx.eps = eps
+        ctx.grad_plan = grad_plan
         dummy = torch.empty(x.shape, device=x.device, dtype=dummy_dtype or x.dtype)
         _no_zero_grads(ctx, int8_out, scale_out)
         if residual_out:
@@ -104,23 +108,27 @@ class FusedRMSNormQuantizeFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_int8, grad_scale, grad_dummy, grad_residual=None):
         if grad_dummy is None:
-            return grad_residual, None, None, None, None
+            return grad_residual, None, None, None, None, None
         x, weight = ctx.saved_tensors
         fuse = grad_residual is not None and x.dtype == torch.float32
+        plan = ctx.grad_plan if (fuse or grad_residual is None) else None
         grad_x, grad_w = rmsnorm_backward(grad_dummy, x, weight, ctx.eps,
-                                          residual_grad=grad_residual if fuse else None)
+                                          residual_grad=grad_residual if fuse else None,
+                                          quant_plan=plan)
         if grad_residual is not None and not fuse:
             grad_x = grad_x + grad_residual
-        return grad_x, grad_w, None, None, None
+        return grad_x, grad_w, None, None, None, None
 
 
 class FusedGELUQuantizeFn(torch.autograd.Function):
-    """(int8, scale, dummy) like the reference; `dummy_dtype` as in FusedRMSNormQuantizeFn."""
+    """(int8, scale, dummy) like the reference; `dummy_dtype` and `grad_plan` as in
+    FusedRMSNormQuantizeFn."""
 
     @staticmethod
-    def forward(ctx, x: Tensor, dummy_dtype=None):
+    def forward(ctx, x: Tensor, dummy_dtype=None, grad_plan=None):
         int8_out, scale_out = fused_gelu_quantize(x)
         ctx.save_for_backward(x)
+        ctx.grad_plan = grad_plan
         dummy = torch.empty(x.shape, device=x.device, dtype=dummy_dtype or x.dtype)
         _no_zero_grads(ctx, int8_out, scale_out)
         return int8_out, scale_out, dummy
@@ -128,9 +136,9 @@ class FusedGELUQuantizeFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_int8, grad_scale, grad_dummy):
         if grad_dummy is None:
-            return None, None
+            return None, None, None
         (x,) = ctx.saved_tensors
-        return gelu_backward(grad_dummy, x), None
+        return gelu_backward(grad_dummy, x, quant_plan=ctx.grad_plan), None, None
 
 
 class FusedTransposeQuantizeFn(torch.autograd.Function):
@@ -151,3 +159,69 @@ class FusedTransposeQuantizeFn(torch.autograd.Function):
         (attended,) = ctx.saved_tensors
         batch_size, n_head, seq_len, head_dim = attended.shape
         return grad_dummy.view(batch_size, seq_len, n_head, head_dim).transpose(1, 2)
+
+
+def heads_gather_quantize(grads: tuple[Tensor, Tensor, Tensor], plan) -> Tensor | None:
+    """[B, T, 3·H·D] gradient of a q|k|v projection output from the gradients of its three
+    [B, H, T, D] head views, quantised in the same kernel for the projection (GradientQuantPlan);
+    None when the layout does not allow 16-byte chunks (the caller concatenates instead)."""
+    from .int8_backward import _SrOutputs
+
+    g0 = grads[0]
+    b, h, t, d = g0.shape
+    if (d % 8 != 0 or g0.dtype not in (torch.float32, torch.bfloat16)
+            or any(g.dtype != g0.dtype or g.shape != g0.shape or g.stride(3) != 1
+                   or g.data_ptr() % 16 != 0 for g in grads)):
+        return None
+    es = g0.element_size()
+    if any((st * es) % 16 != 0 for g in grads for st in g.stride()[:3]):
+        return None
+    rows, cols = b * t, 3 * h * d
+    out = torch.empty((rows, cols), device=g0.device, dtype=g0.dtype)
+    sr = _SrOutputs(plan, rows, cols, out)
+    if not sr.usable():
+        return None
+    import ctypes
+
+    src = (ctypes.c_void_p * 3)(*[g.data_ptr() for g in grads])
+    strides = (ctypes.c_int64 * 12)(*[s for g in grads for s in g.stride()])
+    args = sr.args()
+    ev = _lib.prof_start(out)
+    _lib.check(_lib.lib().rt_heads_gather_sr(
+        ctypes.addressof(src), ctypes.addressof(strides), _lib.dtype_code(g0), b, h, t, d,
+        out.data_ptr(), out.stride(0), args[0], *args[2:], _lib.stream_of(out)))
+    _lib.prof_stop(ev, "heads_gather_sr", out, 0.0,
+                   rows * cols * (2 * es + 1 + (0 if sr.bf16_copy is None else 2)))
+    sr.deliver(out)
+    return out.view(b, t, cols)
+
+
+class QKVHeadsFn(torch.autograd.Function):
+    """(query, key, value) [B, H, T, D] head views of a q|k|v projection output [B, T, 3C]
+    (model.py:61-70: `.chunk(3, dim=-1)`, then view and transpose of each part).  Backward forms
+    the [B, T, 3C] gradient of the projection output from the three head gradients in one
+    kernel that also quantises it for the projection (`plan`, a GradientQuantPlan), instead of
+    autograd's concatenation followed by the projection's own quantisation pass."""
+
+    @staticmethod
+    def forward(ctx, qkv: Tensor, n_head: int, plan):
+        b, t, c3 = qkv.shape
+        c = c3 // 3
+        ctx.plan = plan
+        ctx.shape = qkv.shape
+        parts = qkv.chunk(3, dim=-1)
+        return tuple(p.view(b, t, n_head, c // n_head).transpose(1, 2) for p in parts)
+
+    @staticmethod
+    def backward(ctx, gq, gk, gv):
+        b, t, c3 = ctx.shape
+        grads = [g for g in (gq, gk, gv)]
+        if all(g is None for g in grads):
+            return None, None, None
+        if any(g is None for g in grads):
+            ref = next(g for g in grads if g is not None)
+            grads = [torch.zeros_like(ref) if g is None else g for g in grads]
+        out = heads_gather_quantize(tuple(grads), ctx.plan) if ctx.plan is not None else None
+        if out is None:
+            out = torch.cat([g.transpose(1, 2).reshape(b, t, c3 // 3) for g in grads], dim=-1)
+        return out, None, None

@@ -17,8 +17,9 @@ import torch.utils.checkpoint
 from torch import Tensor, nn
 from torch.nn import functional as F
 
-from .int8_fused import FusedGELUQuantizeFn, FusedRMSNormQuantizeFn, FusedTransposeQuantizeFn
-from .ratchet import DiscreteRatchetLinear, RatchetEmbedding, RatchetUpdateStats
+from .int8_fused import (FusedGELUQuantizeFn, FusedRMSNormQuantizeFn, FusedTransposeQuantizeFn,
+                         QKVHeadsFn)
+from .ratchet import DiscreteRatchetLinear, RatchetEmbedding, RatchetUpdateStats, grad_plan_of
 
 
 @dataclass(frozen=True)
@@ -52,6 +53,12 @@ class ModelConfig:
     # int8 mode: the residual adds of each block run in the epilogue of the sublayer's last GEMM
     # and in the RMSNorm backward kernel (TransformerBlock.forward); False keeps `x + f(x)`
     fused_residual: bool = True
+    # int8 backward: the backward kernel that produces a ratchet layer's output gradient (RMSNorm
+    # backward, GELU backward, the q|k|v head gather) also stochastic-rounds it for the layer's
+    # int8 grad_input GEMM (GradientQuantPlan).  Results are identical either way; off by default
+    # because on B200 the fused row passes (instruction-bound Philox rounding behind the
+    # producer's own row reduction) ran slower than the two separate passes
+    fused_grad_quant: bool = False
 
     def __post_init__(self) -> None:
         if min(self.vocab_size, self.block_size, self.n_layer, self.n_head, self.n_embd) <= 0:
@@ -105,6 +112,7 @@ class CausalSelfAttention(nn.Module):
         self.n_head = config.n_head
         self.head_size = config.n_embd // config.n_head
         self.dropout = config.dropout
+        self.fused_grad_quant = config.fused_grad_quant
 
     def forward(self, inputs: Tensor, *, inputs_int8: Tensor | None = None,
                 inputs_scale: Tensor | None = None, residual: Tensor | None = None) -> Tensor:
@@ -112,16 +120,23 @@ class CausalSelfAttention(nn.Module):
         GEMM epilogue."""
         batch_size, sequence_length, channels = inputs.shape
         if inputs_int8 is not None:
-            query, key, value = self.qkv(inputs, inputs_int8=inputs_int8,
-                                         inputs_scale=inputs_scale).chunk(3, dim=-1)
+            qkv = self.qkv(inputs, inputs_int8=inputs_int8, inputs_scale=inputs_scale)
         else:
-            query, key, value = self.qkv(inputs).chunk(3, dim=-1)
+            qkv = self.qkv(inputs)
+        plan = grad_plan_of(qkv) if self.fused_grad_quant else None
+        if plan is not None:
+            # the gradients of the three head views come back as the projection's quantised
+            # output gradient in one kernel
+            query, key, value = QKVHeadsFn.apply(qkv, self.n_head, plan)
+        else:
+            def heads(tensor: Tensor) -> Tensor:
+                return tensor.view(batch_size, sequence_length, self.n_head,
+                                   self.head_size).transpose(1, 2)
 
-        def heads(tensor: Tensor) -> Tensor:
-            return tensor.view(batch_size, sequence_length, self.n_head, self.head_size).transpose(1, 2)
+            query, key, value = (heads(t) for t in qkv.chunk(3, dim=-1))
 
         attended = F.scaled_dot_product_attention(
-            heads(query), heads(key), heads(value),
+            query, key, value,
             dropout_p=self.dropout if self.training else 0.0, is_causal=True,
         )
         if getattr(self.projection, "matmul_mode", "fp32") == "int8":
@@ -140,6 +155,7 @@ class FeedForward(nn.Module):
         self.expand = _linear(config, config.n_embd, hidden_size, max_code)
         self.contract = _linear(config, hidden_size, config.n_embd, max_code)
         self.dropout = config.dropout
+        self.fused_grad_quant = config.fused_grad_quant
         self.dummy_dtype = None
         if config.matmul_mode == "int8" and config.bf16_activations and max_code is not None:
             self.dummy_dtype = torch.bfloat16
@@ -155,7 +171,9 @@ class FeedForward(nn.Module):
             expanded = self.expand(inputs)
         fuse_residual = residual is not None and (self.dropout == 0.0 or not self.training)
         if getattr(self.contract, "matmul_mode", "fp32") == "int8":
-            gelu_int8, gelu_scale, dummy_gelu = FusedGELUQuantizeFn.apply(expanded, self.dummy_dtype)
+            plan = grad_plan_of(expanded) if self.fused_grad_quant else None
+            gelu_int8, gelu_scale, dummy_gelu = FusedGELUQuantizeFn.apply(expanded, self.dummy_dtype,
+                                                                          plan)
             contracted = self.contract(dummy_gelu, inputs_int8=gelu_int8, inputs_scale=gelu_scale,
                                        residual=residual if fuse_residual else None)
         else:
@@ -177,6 +195,7 @@ class TransformerBlock(nn.Module):
         self.dummy_dtype = (torch.bfloat16 if config.matmul_mode == "int8" and config.bf16_activations
                             and max_code is not None else None)
         self.fused_residual = config.fused_residual and max_code is not None
+        self.fused_grad_quant = config.fused_grad_quant
 
     def forward(self, inputs: Tensor) -> Tensor:
         # int8 path with fused residuals: the RMSNorm producer hands x on as the residual, the
@@ -185,8 +204,11 @@ class TransformerBlock(nn.Module):
         fused = self.fused_residual and inputs.dtype == torch.float32
         if getattr(self.attention.qkv, "matmul_mode", "fp32") == "int8":
             if fused:
+                # with the residual fused, this norm's input gradient is the whole gradient of
+                # `inputs`: quantise it for the ratchet layer that produced `inputs`, if any
+                plan = grad_plan_of(inputs) if self.fused_grad_quant else None
                 attn_int8, attn_scale, dummy_in, res = FusedRMSNormQuantizeFn.apply(
-                    inputs, self.attention_norm.weight, 1e-5, self.dummy_dtype, True)
+                    inputs, self.attention_norm.weight, 1e-5, self.dummy_dtype, True, plan)
                 inputs = self.attention(dummy_in, inputs_int8=attn_int8, inputs_scale=attn_scale,
                                         residual=res)
             else:
@@ -198,8 +220,9 @@ class TransformerBlock(nn.Module):
             inputs = inputs + self.attention(self.attention_norm(inputs))
         if getattr(self.feed_forward.expand, "matmul_mode", "fp32") == "int8":
             if fused:
+                plan = grad_plan_of(inputs) if self.fused_grad_quant else None
                 ffn_int8, ffn_scale, dummy_in, res = FusedRMSNormQuantizeFn.apply(
-                    inputs, self.feed_forward_norm.weight, 1e-5, self.dummy_dtype, True)
+                    inputs, self.feed_forward_norm.weight, 1e-5, self.dummy_dtype, True, plan)
                 inputs = self.feed_forward(dummy_in, inputs_int8=ffn_int8, inputs_scale=ffn_scale,
                                            residual=res)
             else:

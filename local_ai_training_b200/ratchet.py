@@ -153,11 +153,16 @@ class _RatchetMatmul(torch.autograd.Function):
                 grad_bf16 = torch.empty(flat_gradient.shape, device=flat_gradient.device,
                                         dtype=torch.bfloat16)
                 bf16_copy = grad_bf16
-            seed, step, layer, step_dev = _sr_key(ctx.gradient_sink)
-            gq, gs = _quantize_rows_fused(flat_gradient, scale.float(), stochastic=True, seed=seed,
-                                          step=step, layer=layer, bf16_copy=bf16_copy,
-                                          step_dev=step_dev,  # the call advances step_dev
-                                          round_input_bf16=round_grad_bf16)
+            pre = _take_prequantized(ctx.gradient_sink, flat_gradient, round_grad_bf16)
+            if pre is not None:  # quantised by the op that produced the gradient
+                gq, gs, grad_bf16 = pre
+            else:
+                seed, step, layer, step_dev = _sr_key(ctx.gradient_sink)
+                gq, gs = _quantize_rows_fused(flat_gradient, scale.float(), stochastic=True,
+                                              seed=seed, step=step, layer=layer,
+                                              bf16_copy=bf16_copy,
+                                              step_dev=step_dev,  # the call advances step_dev
+                                              round_input_bf16=round_grad_bf16)
             gi_dtype = ctx.input_dtype if ctx.input_dtype in (torch.float32, torch.bfloat16) else torch.bfloat16
             grad_input = torch.empty((gq.shape[0], in_features), device=gq.device, dtype=gi_dtype)
             _scaled_int8_mm_into(gq, code, gs, None, grad_input,
@@ -222,6 +227,60 @@ def _sr_key(sink) -> tuple[int | None, int, int, Tensor | None]:
     if isinstance(layer, DiscreteRatchetLinear):
         return layer._next_sr_key()
     return None, 0, 0, None
+
+
+class GradientQuantPlan:
+    """The int8-backward quantisation a ratchet layer will apply to its output gradient
+    (ratchet.py:117-134: fold the layer's row scales into the gradient, stochastic-round each
+    token row to int8), attached by the layer's forward to its output tensor as
+    `_ratchet_grad_plan`.  The op that consumes that output produces the gradient in its own
+    backward; it may quantise the gradient in the same pass (the same values, Philox stream and
+    step advance as the layer's own quantisation) and `deliver` the result, which the layer's
+    backward then uses instead of reading the gradient again.
+
+    round_if_fp32: an fp32 gradient is rounded to bf16 first (a bf16 layer output whose residual
+    sum is fp32)."""
+
+    __slots__ = ("layer", "round_if_fp32")
+
+    def __init__(self, layer: "DiscreteRatchetLinear", round_if_fp32: bool) -> None:
+        self.layer = layer
+        self.round_if_fp32 = round_if_fp32
+
+    def col_scale(self) -> Tensor:
+        return self.layer.scale.detach().float().contiguous()
+
+    def sr_key(self) -> tuple[int, int, int, Tensor | None]:
+        """(seed, step, layer id, step_dev) of the layer's next quantisation; a host-drawn seed
+        when the layer has none (int8_matmul.py:200)."""
+        seed, step, layer_id, step_dev = self.layer._next_sr_key()
+        if seed is None:
+            seed = int(torch.randint(0, 2**31 - 1, (1,)).item())
+        return seed, step, layer_id, step_dev
+
+    def deliver(self, gradient: Tensor, q: Tensor, row_scale: Tensor, grad_bf16: Tensor,
+                round_bf16: bool) -> None:
+        self.layer._prequant_grad = (gradient, q, row_scale, grad_bf16, round_bf16)
+
+
+def grad_plan_of(tensor: Tensor) -> GradientQuantPlan | None:
+    """The GradientQuantPlan a ratchet layer attached to its output tensor, if any."""
+    return getattr(tensor, "_ratchet_grad_plan", None)
+
+
+def _take_prequantized(sink, flat_gradient: Tensor, round_bf16: bool):
+    """(q, row_scale, grad_bf16) delivered for exactly this gradient tensor, else None."""
+    layer = getattr(sink, "__self__", None)
+    pre = getattr(layer, "_prequant_grad", None)
+    if pre is None:
+        return None
+    layer._prequant_grad = None
+    gradient, q, row_scale, grad_bf16, rounded = pre
+    if (gradient.data_ptr() != flat_gradient.data_ptr() or gradient.dtype != flat_gradient.dtype
+            or gradient.numel() != flat_gradient.numel() or not flat_gradient.is_contiguous()
+            or rounded != round_bf16 or q.shape != flat_gradient.shape):
+        return None
+    return q, row_scale, grad_bf16
 
 
 def pack_code_pressure(code: Tensor, pressure: Tensor, max_code: int) -> Tensor:
@@ -406,6 +465,8 @@ class DiscreteRatchetLinear(nn.Module):
         self.sr_layer: int = 0
         self._sr_step = 0
         self._sr_step_dev: Tensor | None = None
+        # output gradient already quantised by the op that produced it (GradientQuantPlan)
+        self._prequant_grad = None
         # data-parallel runtime this layer's gradient goes to (local_ai_training_b200.dist)
         self._dp = None
 
@@ -501,11 +562,20 @@ class DiscreteRatchetLinear(nn.Module):
         """residual (optional): returns residual + layer(inputs), the add fused into the int8
         GEMM epilogue when residual is fp32."""
         if self.matmul_mode != "fp32" or self.fuse_backward_update:
-            return _RatchetMatmul.apply(
+            output = _RatchetMatmul.apply(
                 inputs, inputs_int8, inputs_scale, self.code_int8(), self.scale, self.matmul_mode,
                 self.fuse_backward_update, self.int8_backward, self.tile_size,
                 self._capture_weight_gradient, residual,
             )
+            if (self.matmul_mode == "int8" and self.int8_backward and self.fuse_backward_update
+                    and inputs_int8 is not None and inputs_scale is not None
+                    and output.requires_grad):
+                # backward will stochastic-round this output's gradient: let the op that
+                # consumes the output quantise the gradient where it produces it
+                result_dtype = getattr(self, "output_dtype", None) or inputs.dtype
+                output._ratchet_grad_plan = GradientQuantPlan(
+                    self, residual is not None and result_dtype == torch.bfloat16)
+            return output
         _require_cuda(inputs, "the ratchet layer")
         effective = self.effective_weight().to(dtype=inputs.dtype)
         if self.training and torch.is_grad_enabled():

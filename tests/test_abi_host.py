@@ -148,3 +148,39 @@ def test_pack_unpack_and_bucket_helpers():
         cg, pg = torch.meshgrid(codes, pressures, indexing="ij")
         c2, p2 = unpack_code_pressure(pack_code_pressure(cg, pg, max_code), max_code)
         assert torch.equal(c2, cg) and torch.equal(p2, pg)
+
+
+def test_qkv_heads_fn_without_plan_matches_chunk_views():
+    """QKVHeadsFn (no quantisation plan): the views `.chunk(3)` + view + transpose give forward,
+    and the concatenated gradient backward."""
+    from local_ai_training_b200.int8_fused import QKVHeadsFn
+
+    torch.manual_seed(1)
+    qkv = torch.randn(2, 16, 3 * 32, requires_grad=True)
+    q, k, v = QKVHeadsFn.apply(qkv, 4, None)
+    q2, k2, v2 = (t.view(2, 16, 4, 8).transpose(1, 2) for t in qkv.chunk(3, dim=-1))
+    for a, b in zip((q, k, v), (q2, k2, v2)):
+        assert torch.equal(a, b) and a.stride() == b.stride()
+    w = [torch.randn_like(t) for t in (q, k, v)]
+    g1, = torch.autograd.grad(sum((a * c).sum() for a, c in zip((q, k, v), w)), qkv)
+    g2, = torch.autograd.grad(sum((a * c).sum() for a, c in zip((q2, k2, v2), w)), qkv)
+    assert torch.equal(g1, g2)
+
+
+def test_prequantized_gradient_is_taken_once_and_only_for_its_tensor():
+    from local_ai_training_b200.ratchet import (DiscreteRatchetLinear, GradientQuantPlan,
+                                                _take_prequantized)
+
+    layer = DiscreteRatchetLinear(16, 8, max_code=2, matmul_mode="int8", int8_backward=True)
+    plan = GradientQuantPlan(layer, round_if_fp32=True)
+    g = torch.zeros(4, 8)
+    q, s, gb = torch.zeros(4, 8, dtype=torch.int8), torch.ones(4), g.to(torch.bfloat16)
+    plan.deliver(g, q, s, gb, True)
+    assert _take_prequantized(layer._capture_weight_gradient, g.view(4, 8), False) is None
+    assert layer._prequant_grad is None  # a mismatch discards it
+    plan.deliver(g, q, s, gb, True)
+    assert _take_prequantized(layer._capture_weight_gradient, torch.zeros(4, 8), True) is None
+    plan.deliver(g, q, s, gb, True)
+    got = _take_prequantized(layer._capture_weight_gradient, g.view(4, 8), True)
+    assert got is not None and got[0] is q and got[1] is s and got[2] is gb
+    assert _take_prequantized(layer._capture_weight_gradient, g.view(4, 8), True) is None
