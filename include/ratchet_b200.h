@@ -178,19 +178,23 @@ int rt_ratchet_validate(const uint8_t *packed, int64_t ldp, int64_t rows, int64_
 
 /* ---------------------------------------------------------------------------------------------
  * Fused producers of pre-quantised layer inputs (int8_fused.py / int8_backward.py).
+ * dq_out (optional, rows x cols bf16, row stride ld_dq): also receives bf16(bf16(q) * bf16(s)),
+ * the grad_weight operand the layer's backward would otherwise dequantise from the saved int8
+ * rows (ratchet.py:73-76, rt_dequant_rows_bf16) -- written from registers by the producer.
  * ------------------------------------------------------------------------------------------- */
 /* y = x * rsqrt(mean(x^2) + eps) * w, then RN row quant (int8_fused.py:14-56). */
 int rt_rmsnorm_quantize(const void *x, int x_dtype, int64_t ldx, const float *weight, double eps,
                         int64_t rows, int64_t cols, int8_t *q, int64_t ldq, float *row_scale,
-                        void *stream);
+                        void *dq_out, int64_t ld_dq, void *stream);
 /* tanh-GELU then RN row quant (int8_fused.py:58-101). */
 int rt_gelu_quantize(const void *x, int x_dtype, int64_t ldx, int64_t rows, int64_t cols,
-                     int8_t *q, int64_t ldq, float *row_scale, void *stream);
+                     int8_t *q, int64_t ldq, float *row_scale, void *dq_out, int64_t ld_dq,
+                     void *stream);
 /* [B,H,T,D] (any strides) -> rows b*T+t of H*D channels, RN row quant (int8_fused.py:103-151). */
 int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, int64_t heads, int64_t seq,
                           int64_t head_dim, int64_t stride_b, int64_t stride_h, int64_t stride_s,
                           int64_t stride_d, int8_t *q, int64_t ldq, float *row_scale,
-                          void *stream);
+                          void *dq_out, int64_t ld_dq, void *stream);
 /* RMSNorm backward (int8_backward.py:7-51): dx written in dx_dtype (through bf16, as the
  * reference stores it); dw (optional, cols floats, accumulated) += sum over rows of gy*x*rsqrt.
  * dx_add (optional, fp32 dx only, may equal dx): the residual branch's gradient, added to dx the

@@ -56,10 +56,10 @@ _SIGNATURES = {
     "rt_ratchet_leak": ([_p, _i64, _i64, _i64, _i, _p], _i),
     "rt_unpack_code_pressure": ([_p, _i64, _i64, _i64, _i, _p, _i64, _p, _i64, _p], _i),
     "rt_ratchet_validate": ([_p, _i64, _i64, _i64, _i, _p, _p], _i),
-    "rt_rmsnorm_quantize": ([_p, _i, _i64, _p, _d, _i64, _i64, _p, _i64, _p, _p], _i),
-    "rt_gelu_quantize": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p], _i),
+    "rt_rmsnorm_quantize": ([_p, _i, _i64, _p, _d, _i64, _i64, _p, _i64, _p, _p, _i64, _p], _i),
+    "rt_gelu_quantize": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _p], _i),
     "rt_transpose_quantize": ([_p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64,
-                               _p, _p], _i),
+                               _p, _p, _i64, _p], _i),
     "rt_rmsnorm_backward": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p, _p, _p], _i),
     "rt_gelu_backward": ([_p, _i, _p, _i, _i64, _i64, _p, _i, _p], _i),
     "rt_rmsnorm_backward_sr": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p, _p, _p, _i, _u64,

@@ -1,5 +1,6 @@
 // rt_api.cu — library-wide entry points: ABI version, thread-local error text, the sticky device
 // status word and the cached SM count.
+#include <cstdlib>
 #include <mutex>
 
 #include "rt_common.cuh"
@@ -27,6 +28,14 @@ int check_launch(const char *what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(RT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return RT_OK;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("RT_PDL");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
 }
 
 }  // namespace rt

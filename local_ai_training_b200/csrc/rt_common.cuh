@@ -31,6 +31,38 @@ inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s
 inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // ------------------------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel of the library is launched with programmatic
+// stream serialisation, lets its dependents launch at once (pdl_trigger) and, before its first
+// access to global memory that an earlier kernel may still read or write, waits for the
+// preceding grid to complete and flush (pdl_wait).  The next kernel's launch, CTA placement and
+// set-up (barrier init, TMEM allocation, descriptor prefetch) then overlap the tail of the
+// current one instead of following its completion.  A grid that waits can only complete after
+// its predecessor, so ordering stays transitive along the stream; launched without the
+// attribute (or after a kernel that never triggers) both instructions are no-ops.
+// Setting RT_PDL=0 in the environment launches without the attribute.
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+bool pdl_enabled();
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                     Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);  // errors: check_launch
+}
+
+// ------------------------------------------------------------------------------------------
 // bf16 helpers (round-to-nearest-even, as torch's .to(torch.bfloat16)).
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ float bf16_round(float x) {

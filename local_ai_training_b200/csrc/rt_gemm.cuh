@@ -237,8 +237,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &p, int epi, int r
 // One 32-row group of 64 bf16 / 32 fp32 output columns through the warp's staging buffer:
 // 128-byte swizzled rows (conflict-free 16-byte shared stores), then one TMA store that clips
 // rows/columns outside the output.  `words` holds the 32 packed words of this lane's row.
-__device__ __forceinline__ void stage_and_store(const CUtensorMap *map, uint8_t *b, int lane,
-                                                const uint32_t (&words)[32], int x, int y) {
+__device__ __forceinline__ void stage_write(uint8_t *b, int lane, const uint32_t (&words)[32]) {
   if (lane == 0) bulk_wait_read_all();  // the warp's previous store has read the buffer
   __syncwarp();
 #pragma unroll
@@ -247,10 +246,18 @@ __device__ __forceinline__ void stage_and_store(const CUtensorMap *map, uint8_t 
         make_uint4(words[4 * c], words[4 * c + 1], words[4 * c + 2], words[4 * c + 3]);
   fence_proxy_async_smem();
   __syncwarp();
+}
+__device__ __forceinline__ void stage_issue(const CUtensorMap *map, uint8_t *b, int lane, int x,
+                                            int y) {
   if (lane == 0) {
     tma_store_2d(map, b, x, y);
     bulk_commit_group();
   }
+}
+__device__ __forceinline__ void stage_and_store(const CUtensorMap *map, uint8_t *b, int lane,
+                                                const uint32_t (&words)[32], int x, int y) {
+  stage_write(b, lane, words);
+  stage_issue(map, b, lane, x, y);
 }
 
 // Accumulator word -> fp32.  CONV 0: fp32 bits (kind::f16); 1: int32 known to lie in
@@ -272,22 +279,38 @@ __device__ __forceinline__ float cvt_acc(uint32_t b) {
 // rmap (fp32 output only, or null): the residual, whose tile of each group is TMA-loaded into
 // the staging buffer (completion on rbar, parity rphase) while the accumulators are read, then
 // added after the rounding.
+// The warp hands its accumulator columns back to the MMA warp (arrive on tempty_bar) as soon as
+// its last TMEM read has completed, not after its stores, so the next MMA into this accumulator
+// overlaps the conversion and stores: a bf16 group waits in the staging buffer, its TMA store
+// deferred, while the next group is read from TMEM.
+__device__ __forceinline__ void release_accumulator(uint64_t *tempty_bar, int lane) {
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(tempty_bar);
+}
+// Returns whether it arrived on tempty_bar (not when the warp's columns lie past the output).
 template <int CONV, int HALF>
-__device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *staging, int lane,
+__device__ __forceinline__ bool epilogue_tma(const CUtensorMap *map, uint8_t *staging, int lane,
                                              uint32_t t_row, int x0, int x_end, int y,
                                              bool bf16_out, bool scaled, float a_s,
                                              const float *bs, const CUtensorMap *rmap,
-                                             uint64_t *rbar, uint32_t &rphase) {
+                                             uint64_t *rbar, uint32_t &rphase,
+                                             uint64_t *tempty_bar) {
   if (bf16_out) {
+    if (x0 >= x_end) return false;
+    int pending = -1;  // column of the group staged but not yet stored
 #pragma unroll 1
     for (int g = 0; g < HALF / 64; ++g) {
       const int n0 = x0 + g * 64;
-      if (n0 >= x_end) break;
+      if (n0 >= x_end) break;  // warp-uniform
       uint32_t r0[32], r1[32];
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64), r0);
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64 + 32), r1);
       tmem_ld_wait_regs(r0);
       tmem_regs_after_wait(r1);
+      const bool last = g == HALF / 64 - 1 || n0 + 64 >= x_end;
+      if (last) release_accumulator(tempty_bar, lane);
+      if (pending >= 0) stage_issue(map, staging, lane, pending, y);
       uint32_t w[32];
       const float4 *bs4 = reinterpret_cast<const float4 *>(bs + g * 64);
 #pragma unroll
@@ -310,13 +333,20 @@ __device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *st
         w[16 + 2 * j] = pack_bf16x2(v[4], v[5]);
         w[16 + 2 * j + 1] = pack_bf16x2(v[6], v[7]);
       }
-      stage_and_store(map, staging, lane, w, n0, y);
+      stage_write(staging, lane, w);
+      if (last) {
+        stage_issue(map, staging, lane, n0, y);
+        pending = -1;
+      } else {
+        pending = n0;
+      }
     }
+    return true;
   } else {
+    const int groups = min(HALF / 32, (x_end - x0 + 31) / 32);
 #pragma unroll 1
-    for (int g = 0; g < HALF / 32; ++g) {
+    for (int g = 0; g < groups; ++g) {
       const int n0 = x0 + g * 32;
-      if (n0 >= x_end) break;
       if (rmap != nullptr && lane == 0) {
         bulk_wait_read_all();  // the previous store has read the staging buffer
         mbar_arrive_expect_tx(rbar, 4096);
@@ -325,6 +355,7 @@ __device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *st
       uint32_t r[32];
       tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 32), r);
       tmem_ld_wait_regs(r);
+      if (g == groups - 1) release_accumulator(tempty_bar, lane);
       uint32_t w[32];
       const float4 *bs4 = reinterpret_cast<const float4 *>(bs + g * 32);
       bool res_ok = true;
@@ -355,6 +386,7 @@ __device__ __forceinline__ void epilogue_tma(const CUtensorMap *map, uint8_t *st
       }
       stage_and_store(map, staging, lane, w, n0, y);
     }
+    return groups > 0;
   }
 }
 
@@ -381,6 +413,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
   __shared__ __align__(16) float s_bscale[BN];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();  // the next kernel may launch and set itself up while this one runs
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -405,18 +438,40 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // set-up above touches no global memory; operands, scales and outputs only after the
+  // preceding kernel has completed
+  pdl_wait();
 
   const int units = p.tiles_m * p.tiles_n * p.splits;
+  // Unit u -> (tile n, tile m, split) and the split's k-block range, in 32-bit unsigned
+  // arithmetic (split * kblocks stays far below 2^32): the single MMA-issuing thread runs this
+  // between tiles while the tensor pipe drains, so it must be short (64-bit divisions there
+  // left the tensor pipe idle ~0.9 us per tile).
+  const uint32_t tiles_n = static_cast<uint32_t>(p.tiles_n);
+  const uint32_t tiles_mn = static_cast<uint32_t>(p.tiles_m) * tiles_n;
+  const uint32_t kblocks = static_cast<uint32_t>(p.kblocks);
+  const uint32_t splits = static_cast<uint32_t>(p.splits);
+  auto k_range = [&](uint32_t uu, int &kb0, int &kb1) {
+    if (splits == 1) {
+      kb0 = 0, kb1 = static_cast<int>(kblocks);
+    } else {
+      const uint32_t split = uu / tiles_mn;
+      kb0 = static_cast<int>(split * kblocks / splits);
+      kb1 = static_cast<int>((split + 1) * kblocks / splits);
+    }
+  };
   if (warp == 0) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int tn = u % p.tiles_n, rest = u / p.tiles_n;
-        const int tm = rest % p.tiles_m, split = rest / p.tiles_m;
-        const int kb0 = static_cast<int>(static_cast<int64_t>(split) * p.kblocks / p.splits);
-        const int kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * p.kblocks / p.splits);
+        const uint32_t uu = static_cast<uint32_t>(u);
+        const uint32_t rest = uu / tiles_n;
+        const int tn = static_cast<int>(uu - rest * tiles_n);
+        const int tm = static_cast<int>(rest % static_cast<uint32_t>(p.tiles_m));
+        int kb0, kb1;
+        k_range(uu, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             ok = false;
@@ -439,10 +494,8 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
       bool ok = true;
       const uint32_t a_base = smem_u32(a_tiles), b_base = smem_u32(b_tiles);
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int rest = u / p.tiles_n;
-        const int split = rest / p.tiles_m;
-        const int kb0 = static_cast<int>(static_cast<int64_t>(split) * p.kblocks / p.splits);
-        const int kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * p.kblocks / p.splits);
+        int kb0, kb1;
+        k_range(static_cast<uint32_t>(u), kb0, kb1);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -484,8 +537,11 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     uint32_t acc_phase = 0;
     uint32_t rphase = 0;  // parity of this warp's residual barrier
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      const int tn = u % p.tiles_n, rest = u / p.tiles_n;
-      const int tm = rest % p.tiles_m, split = rest / p.tiles_m;
+      const uint32_t uu = static_cast<uint32_t>(u);
+      const uint32_t rest = uu / tiles_n;
+      const int tn = static_cast<int>(uu - rest * tiles_n);
+      const int tm = static_cast<int>(rest % static_cast<uint32_t>(p.tiles_m));
+      const int split = static_cast<int>(uu / tiles_mn);
       const int tile = tm * p.tiles_n + tn;
       const int trow = sub * 32 + lane;
       const int row = tm * C::BM + trow;
@@ -516,6 +572,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN + col0);
+      bool released = false;  // the epilogue has arrived on tempty[acc] itself
       if (p.tma_store) {
         // column scales of this tile in shared memory; the barrier above also guarantees that
         // every warp has finished reading the previous tile's (barrier 1: the epilogue warps)
@@ -538,14 +595,16 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
           // this warp's 32 rows lie past the output: nothing to store
         } else if constexpr (sizeof(T) == 1) {
           if (p.acc_small)
-            epilogue_tma<1, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out, scaled,
-                                  a_s, bs, rmap, rbar, rphase);
+            released = epilogue_tma<1, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y,
+                                             bf16_out, scaled, a_s, bs, rmap, rbar, rphase,
+                                             &tempty[acc]);
           else
-            epilogue_tma<2, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out, scaled,
-                                  a_s, bs, rmap, rbar, rphase);
+            released = epilogue_tma<2, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y,
+                                             bf16_out, scaled, a_s, bs, rmap, rbar, rphase,
+                                             &tempty[acc]);
         } else {
-          epilogue_tma<0, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out, scaled,
-                                a_s, bs, rmap, rbar, rphase);
+          released = epilogue_tma<0, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out,
+                                           scaled, a_s, bs, rmap, rbar, rphase, &tempty[acc]);
         }
       } else {
 #pragma unroll 1
@@ -558,9 +617,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
           epilogue_chunk<T>(p, p.epi, row, n0, r);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (!released) release_accumulator(&tempty[acc], lane);
       if (++acc == 2) acc = 0, acc_phase ^= 1;
     }
     if (p.tma_store && lane == 0) bulk_wait_all();  // staged stores done before the CTA exits
@@ -582,6 +639,8 @@ __global__ void simt_scaled_i8_kernel(const int8_t *lhs, int64_t slm, int64_t sl
                                       const float *ls, const float *rs, void *out, int out_dtype,
                                       int64_t ldo, int64_t M, int64_t N, int64_t K,
                                       const float *residual, int64_t ld_res) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t m = blockIdx.y * static_cast<int64_t>(blockDim.y) + threadIdx.y;
   if (m >= M || n >= N) return;
@@ -602,6 +661,8 @@ __global__ void simt_scaled_i8_kernel(const int8_t *lhs, int64_t slm, int64_t sl
 __global__ void simt_gradw_kernel(const uint16_t *g, int64_t ldg, const uint16_t *x, int64_t ldx,
                                   void *out, int out_dtype, int64_t ldo, int64_t Mt, int64_t N,
                                   int64_t K, int accumulate) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
   const int64_t n = blockIdx.y * static_cast<int64_t>(blockDim.y) + threadIdx.y;
   if (n >= N || k >= K) return;
@@ -741,7 +802,7 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
   }
   const int64_t units = static_cast<int64_t>(args.tiles_m) * args.tiles_n * args.splits;
   const int grid = static_cast<int>(units < sms ? units : sms);
-  kernel<<<grid, C::THREADS, C::SMEM_BYTES, s>>>(ma, mb, mc, mr, args);
+  launch_k(kernel, grid, C::THREADS, C::SMEM_BYTES, s, ma, mb, mc, mr, args);
   return check_launch("umma_gemm_kernel");
 }
 
@@ -807,7 +868,7 @@ extern "C" int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_
   }
   const dim3 block(32, 8);
   const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((M + 7) / 8));
-  simt_scaled_i8_kernel<<<grid, block, 0, s>>>(lhs, lhs_stride_m, lhs_stride_k, rhs, rhs_stride_k,
+  launch_k(simt_scaled_i8_kernel, grid, block, 0, s, lhs, lhs_stride_m, lhs_stride_k, rhs, rhs_stride_k,
                                                 rhs_stride_n, lhs_scale, rhs_scale, out, out_dtype,
                                                 ldo, M, N, K, residual, ld_residual);
   return check_launch("simt_scaled_i8_kernel");
@@ -825,6 +886,8 @@ __global__ void __launch_bounds__(256)
     splitk_reduce_kernel(const float *__restrict__ ws, int splits, int tiles_m, int tiles_n,
                          int rows, int cols, void *out, int out_dtype, int64_t ldo,
                          int accumulate, int vec_out) {
+  pdl_wait();
+  pdl_trigger();
   const int groups = (cols + 3) >> 2;
   const int64_t total = static_cast<int64_t>(rows) * groups;
   const int64_t split_stride = static_cast<int64_t>(tiles_m) * tiles_n * 128 * BN;
@@ -941,14 +1004,14 @@ extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, in
     if (blocks > static_cast<int64_t>(sms) * 8) blocks = static_cast<int64_t>(sms) * 8;
     const int tiles_m = static_cast<int>((N + 127) / 128);
     const int tiles_n = static_cast<int>((K + GW_BN - 1) / GW_BN);
-    splitk_reduce_kernel<GW_BN><<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+    launch_k(splitk_reduce_kernel<GW_BN>, static_cast<unsigned>(blocks), 256, 0, s, 
         static_cast<const float *>(workspace), splits, tiles_m, tiles_n, static_cast<int>(N),
         static_cast<int>(K), out, out_dtype, ldo, accumulate, args.vec_store);
     return check_launch("splitk_reduce_kernel");
   }
   const dim3 block(32, 8);
   const dim3 grid(static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>((N + 7) / 8));
-  simt_gradw_kernel<<<grid, block, 0, s>>>(static_cast<const uint16_t *>(g), ldg,
+  launch_k(simt_gradw_kernel, grid, block, 0, s, static_cast<const uint16_t *>(g), ldg,
                                             static_cast<const uint16_t *>(x), ldx, out, out_dtype,
                                             ldo, M_tok, N, K, accumulate);
   return check_launch("simt_gradw_kernel");

@@ -65,6 +65,8 @@ struct CeArgs {
 
 // Register-resident rows: fp32, cols % 4 == 0, cols <= CE_THREADS·4·CE_VEC, 16-byte rows.
 __global__ void __launch_bounds__(CE_THREADS) ce_fwd_vec_kernel(CeArgs a) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sm[CE_THREADS / 32];
   const int64_t row = blockIdx.x;
   const float *x = static_cast<const float *>(a.logits) + row * a.ld;
@@ -112,6 +114,8 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fwd_vec_kernel(CeArgs a) {
 // Any layout: two passes over the row in global memory.
 template <typename T>
 __global__ void __launch_bounds__(CE_THREADS) ce_fwd_generic_kernel(CeArgs a) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sm[CE_THREADS / 32];
   const int64_t row = blockIdx.x;
   const T *x = static_cast<const T *>(a.logits) + row * a.ld;
@@ -147,6 +151,8 @@ __device__ __forceinline__ float ce_grad(float xv, float m, float logsum, float 
 
 template <typename T>
 __global__ void __launch_bounds__(CE_THREADS) ce_bwd_kernel(CeArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const T *x = static_cast<const T *>(a.logits) + row * a.ld;
   uint16_t *o = a.out + row * a.ldo;
@@ -217,11 +223,11 @@ extern "C" int rt_cross_entropy_fwd(const void *logits, int dtype, int64_t ld, i
                    cols <= static_cast<int64_t>(CE_THREADS) * 4 * CE_VEC;
   const unsigned grid = static_cast<unsigned>(rows);
   if (vec)
-    ce_fwd_vec_kernel<<<grid, CE_THREADS, 0, s>>>(a);
+    launch_k(ce_fwd_vec_kernel, grid, CE_THREADS, 0, s, a);
   else if (dtype == RT_F32)
-    ce_fwd_generic_kernel<float><<<grid, CE_THREADS, 0, s>>>(a);
+    launch_k(ce_fwd_generic_kernel<float>, grid, CE_THREADS, 0, s, a);
   else
-    ce_fwd_generic_kernel<uint16_t><<<grid, CE_THREADS, 0, s>>>(a);
+    launch_k(ce_fwd_generic_kernel<uint16_t>, grid, CE_THREADS, 0, s, a);
   return check_launch("cross_entropy_fwd");
 }
 
@@ -248,8 +254,8 @@ extern "C" int rt_cross_entropy_bwd(const void *logits, int dtype, int64_t ld, i
   cudaStream_t s = as_stream(stream);
   const unsigned grid = static_cast<unsigned>(rows);
   if (dtype == RT_F32)
-    ce_bwd_kernel<float><<<grid, CE_THREADS, 0, s>>>(a);
+    launch_k(ce_bwd_kernel<float>, grid, CE_THREADS, 0, s, a);
   else
-    ce_bwd_kernel<uint16_t><<<grid, CE_THREADS, 0, s>>>(a);
+    launch_k(ce_bwd_kernel<uint16_t>, grid, CE_THREADS, 0, s, a);
   return check_launch("cross_entropy_bwd");
 }

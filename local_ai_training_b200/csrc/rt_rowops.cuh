@@ -178,6 +178,26 @@ __device__ __forceinline__ float row_scale_of(float amax) {
   return fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN);
 }
 
+// Round-to-nearest quant of eight values into one 8-byte int8 chunk; with dq, also the chunk of
+// bf16(bf16(q) · sb), sb = bf16(row scale): the grad_weight operand that the backward otherwise
+// dequantises from the saved int8 rows (ratchet.py:73-76), written here from registers.
+__device__ __forceinline__ void quant_rn_store8(int8_t *qp, unsigned short *dq, const float (&v)[8],
+                                                float scale, float rcp, float sb) {
+  int qi[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) qi[j] = quant_rn_i(v[j], scale, rcp);
+  uint2 o;
+  o.x = pack4_i8(qi[0], qi[1], qi[2], qi[3]);
+  o.y = pack4_i8(qi[4], qi[5], qi[6], qi[7]);
+  *reinterpret_cast<uint2 *>(qp) = o;
+  if (dq != nullptr) {
+    float d[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d[j] = __fmul_rn(static_cast<float>(qi[j]), sb);
+    st8(reinterpret_cast<__nv_bfloat16 *>(dq), d);
+  }
+}
+
 // Row-kernel configuration: threads per row and chunks per thread for a row of `nch` chunks.
 struct RowCfg {
   int rt, vpt;  // rt == 0: generic kernel
@@ -214,38 +234,38 @@ static inline unsigned row_grid(int64_t rows, int rt) {
 #define RT_DISPATCH_ROW(cfg, KERNEL, T, GRID, ...)                                 \
   do {                                                                               \
     switch ((cfg).rt * 16 + (cfg).vpt) {                                             \
-      case 32 * 16 + 1: KERNEL<T, 32, 1><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
-      case 32 * 16 + 2: KERNEL<T, 32, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
-      case 32 * 16 + 4: KERNEL<T, 32, 4><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
-      case 32 * 16 + 8: KERNEL<T, 32, 8><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
-      case 128 * 16 + 1: KERNEL<T, 128, 1><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
-      case 128 * 16 + 2: KERNEL<T, 128, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
-      case 128 * 16 + 4: KERNEL<T, 128, 4><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
-      case 128 * 16 + 8: KERNEL<T, 128, 8><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
-      case 256 * 16 + 1: KERNEL<T, 256, 1><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
-      case 256 * 16 + 2: KERNEL<T, 256, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
-      case 256 * 16 + 4: KERNEL<T, 256, 4><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
-      default: KERNEL<T, 256, 8><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;           \
+      case 32 * 16 + 1: launch_k(KERNEL<T, 32, 1>, GRID, CTA, 0, s, __VA_ARGS__); break;   \
+      case 32 * 16 + 2: launch_k(KERNEL<T, 32, 2>, GRID, CTA, 0, s, __VA_ARGS__); break;   \
+      case 32 * 16 + 4: launch_k(KERNEL<T, 32, 4>, GRID, CTA, 0, s, __VA_ARGS__); break;   \
+      case 32 * 16 + 8: launch_k(KERNEL<T, 32, 8>, GRID, CTA, 0, s, __VA_ARGS__); break;   \
+      case 128 * 16 + 1: launch_k(KERNEL<T, 128, 1>, GRID, CTA, 0, s, __VA_ARGS__); break; \
+      case 128 * 16 + 2: launch_k(KERNEL<T, 128, 2>, GRID, CTA, 0, s, __VA_ARGS__); break; \
+      case 128 * 16 + 4: launch_k(KERNEL<T, 128, 4>, GRID, CTA, 0, s, __VA_ARGS__); break; \
+      case 128 * 16 + 8: launch_k(KERNEL<T, 128, 8>, GRID, CTA, 0, s, __VA_ARGS__); break; \
+      case 256 * 16 + 1: launch_k(KERNEL<T, 256, 1>, GRID, CTA, 0, s, __VA_ARGS__); break; \
+      case 256 * 16 + 2: launch_k(KERNEL<T, 256, 2>, GRID, CTA, 0, s, __VA_ARGS__); break; \
+      case 256 * 16 + 4: launch_k(KERNEL<T, 256, 4>, GRID, CTA, 0, s, __VA_ARGS__); break; \
+      default: launch_k(KERNEL<T, 256, 8>, GRID, CTA, 0, s, __VA_ARGS__); break;           \
     }                                                                                \
   } while (0)
 
 #define RT_DISPATCH_ROW_NARROW(cfg, KERNEL, T, GRID, ...)                           \
   do {                                                                               \
     switch ((cfg).rt * 16 + (cfg).vpt) {                                             \
-      case 32 * 16 + 1: KERNEL<T, 32, 1><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
-      case 32 * 16 + 2: KERNEL<T, 32, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;   \
-      case 128 * 16 + 2: KERNEL<T, 128, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break; \
-      default: KERNEL<T, 256, 2><<<GRID, CTA, 0, s>>>(__VA_ARGS__); break;           \
+      case 32 * 16 + 1: launch_k(KERNEL<T, 32, 1>, GRID, CTA, 0, s, __VA_ARGS__); break;   \
+      case 32 * 16 + 2: launch_k(KERNEL<T, 32, 2>, GRID, CTA, 0, s, __VA_ARGS__); break;   \
+      case 128 * 16 + 2: launch_k(KERNEL<T, 128, 2>, GRID, CTA, 0, s, __VA_ARGS__); break; \
+      default: launch_k(KERNEL<T, 256, 2>, GRID, CTA, 0, s, __VA_ARGS__); break;           \
     }                                                                                \
   } while (0)
 
 #define RT_DISPATCH_ROW_NARROW_SMEM(cfg, KERNEL, T, GRID, SMEM, ...)                        \
   do {                                                                                        \
     switch ((cfg).rt * 16 + (cfg).vpt) {                                                      \
-      case 32 * 16 + 1: KERNEL<T, 32, 1><<<GRID, CTA, SMEM, s>>>(__VA_ARGS__); break;         \
-      case 32 * 16 + 2: KERNEL<T, 32, 2><<<GRID, CTA, SMEM, s>>>(__VA_ARGS__); break;         \
-      case 128 * 16 + 2: KERNEL<T, 128, 2><<<GRID, CTA, SMEM, s>>>(__VA_ARGS__); break;       \
-      default: KERNEL<T, 256, 2><<<GRID, CTA, SMEM, s>>>(__VA_ARGS__); break;                 \
+      case 32 * 16 + 1: launch_k(KERNEL<T, 32, 1>, GRID, CTA, SMEM, s, __VA_ARGS__); break;         \
+      case 32 * 16 + 2: launch_k(KERNEL<T, 32, 2>, GRID, CTA, SMEM, s, __VA_ARGS__); break;         \
+      case 128 * 16 + 2: launch_k(KERNEL<T, 128, 2>, GRID, CTA, SMEM, s, __VA_ARGS__); break;       \
+      default: launch_k(KERNEL<T, 256, 2>, GRID, CTA, SMEM, s, __VA_ARGS__); break;                 \
     }                                                                                         \
   } while (0)
 
@@ -292,6 +312,8 @@ __device__ __forceinline__ void sr_step_arrive(const QuantArgs &a, uint32_t step
 
 template <typename T, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
+  pdl_wait();
+  pdl_trigger();
   // grid-stride over groups of RPC rows: a resident-sized grid (few CTAs, so that the step
   // ticket of sr_step_arrive costs one atomic per resident CTA)
   constexpr int RPC = CTA / RT;
@@ -376,6 +398,8 @@ __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
 // Generic: any strides, one CTA per row, two passes (the second normally hits L2).
 template <typename T>
 __global__ void __launch_bounds__(CTA) quant_rows_generic_kernel(QuantArgs a) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float smx[8];
   const int64_t row = blockIdx.x;
   const T *xr = static_cast<const T *>(a.x) + row * a.stride_row;
@@ -495,7 +519,7 @@ static int quant_rows_dispatch(const QuantArgs &a, cudaStream_t s) {
     const unsigned groups = row_grid(a.rows, cfg.rt);
     RT_DISPATCH_ROW(cfg, quant_rows_kernel, T, groups < resident ? groups : resident, a);
   } else {
-    quant_rows_generic_kernel<T><<<static_cast<unsigned>(a.rows), CTA, 0, s>>>(a);
+    launch_k(quant_rows_generic_kernel<T>, static_cast<unsigned>(a.rows), CTA, 0, s, a);
   }
   return check_launch("rt_quantize_rows");
 }
@@ -596,6 +620,8 @@ __device__ __forceinline__ void publish_moves(Moves m, int (*redi)[4], const Upd
 
 template <typename G, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) ratchet_update_kernel(UpdateArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int RPC = CTA / RT, NT = CTA / RT;
   __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
   __shared__ float smb[RPC];
@@ -697,6 +723,8 @@ __global__ void __launch_bounds__(CTA) ratchet_update_kernel(UpdateArgs a) {
 
 // Generic update: any alignment and row length, one CTA per row, same arithmetic and order.
 __global__ void __launch_bounds__(CTA) ratchet_update_generic_kernel(UpdateArgs a) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sm[CTA];
   __shared__ float smb[1];
   __shared__ float smx[8];
@@ -750,6 +778,8 @@ __global__ void __launch_bounds__(CTA) ratchet_update_generic_kernel(UpdateArgs 
 // Small state kernels.
 // ===========================================================================================
 __global__ void leak_kernel(uint8_t *packed, int64_t ldp, int64_t rows, int64_t cols) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t n = rows * cols;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -764,6 +794,8 @@ __global__ void leak_kernel(uint8_t *packed, int64_t ldp, int64_t rows, int64_t 
 __global__ void unpack_kernel(const uint8_t *packed, int64_t ldp, int64_t rows, int64_t cols,
                               int max_code, int8_t *code, int64_t ldc, int8_t *pressure,
                               int64_t ldpr) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t n = rows * cols;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -777,6 +809,8 @@ __global__ void unpack_kernel(const uint8_t *packed, int64_t ldp, int64_t rows, 
 // Contiguous fast path of the unpack used to refresh the int8 code mirror (16 weights/thread).
 __global__ void unpack_codes_vec_kernel(const uint4 *packed, int64_t n16, int max_code,
                                         uint4 *code) {
+  pdl_wait();
+  pdl_trigger();
   const uint32_t bias = 0x01010101u * static_cast<uint32_t>(max_code);
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n16;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -792,6 +826,8 @@ __global__ void unpack_codes_vec_kernel(const uint4 *packed, int64_t n16, int ma
 
 __global__ void validate_kernel(const uint8_t *packed, int64_t ldp, int64_t rows, int64_t cols,
                                 int max_code, const float *scale) {
+  pdl_wait();
+  pdl_trigger();
   uint32_t bits = 0;
   const int64_t n = rows * cols;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -819,6 +855,8 @@ __global__ void validate_kernel(const uint8_t *packed, int64_t ldp, int64_t rows
 template <typename I>
 __global__ void dequant_vec_kernel(const int8_t *q, int64_t ldq, const float *s, __nv_bfloat16 *out,
                                    int64_t ldo, I rows, I cols8) {
+  pdl_wait();
+  pdl_trigger();
   const I n = rows * cols8;
   for (I i = blockIdx.x * static_cast<I>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<I>(gridDim.x) * blockDim.x) {
@@ -836,6 +874,8 @@ __global__ void dequant_vec_kernel(const int8_t *q, int64_t ldq, const float *s,
 }
 __global__ void dequant_kernel(const int8_t *q, int64_t ldq, const float *s, uint16_t *out,
                                int64_t ldo, int64_t rows, int64_t cols) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t n = rows * cols;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -877,11 +917,15 @@ struct ProdArgs {
   int8_t *q;
   int64_t ldq;
   float *row_scale;
+  unsigned short *xdq;  // optional bf16 dequantised copy (row stride ld_dq)
+  int64_t ld_dq;
 };
 
 // RMSNorm -> quant: y = (x · r) · w, r = 1 / sqrt(mean(x²) + eps) (IEEE sqrt and division).
 template <typename T, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) rmsnorm_quant_kernel(ProdArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int RPC = CTA / RT, NT = CTA / RT;
   __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
   __shared__ float smb[RPC];
@@ -928,22 +972,21 @@ __global__ void __launch_bounds__(CTA) rmsnorm_quant_kernel(ProdArgs a) {
   if (!live) return;
   const float scale = row_scale_of(amax);
   const float rcp = __frcp_rn(scale);
+  const float sb = bf16_round(scale);
   if (t == 0) a.row_scale[row] = scale;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     if (c >= nch) continue;
-    uint2 o;
-    o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
-                   quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
-    o.y = pack4_i8(quant_rn_i(v[i][4], scale, rcp), quant_rn_i(v[i][5], scale, rcp),
-                   quant_rn_i(v[i][6], scale, rcp), quant_rn_i(v[i][7], scale, rcp));
-    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = o;
+    quant_rn_store8(a.q + row * a.ldq + 8 * c, a.xdq == nullptr ? nullptr : a.xdq + row * a.ld_dq + 8 * c,
+                    v[i], scale, rcp, sb);
   }
 }
 
 template <typename T, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) gelu_quant_kernel(ProdArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int RPC = CTA / RT;
   __shared__ float smx[RPC * 8];
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
@@ -972,23 +1015,22 @@ __global__ void __launch_bounds__(CTA) gelu_quant_kernel(ProdArgs a) {
   if (!live) return;
   const float scale = row_scale_of(amax);
   const float rcp = __frcp_rn(scale);
+  const float sb = bf16_round(scale);
   if (t == 0) a.row_scale[row] = scale;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     if (c >= nch) continue;
-    uint2 o;
-    o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
-                   quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
-    o.y = pack4_i8(quant_rn_i(v[i][4], scale, rcp), quant_rn_i(v[i][5], scale, rcp),
-                   quant_rn_i(v[i][6], scale, rcp), quant_rn_i(v[i][7], scale, rcp));
-    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = o;
+    quant_rn_store8(a.q + row * a.ldq + 8 * c, a.xdq == nullptr ? nullptr : a.xdq + row * a.ld_dq + 8 * c,
+                    v[i], scale, rcp, sb);
   }
 }
 
 // Generic producers: one CTA per row, the row re-read from L2 between passes.
 __global__ void __launch_bounds__(CTA)
     rmsnorm_quant_generic_kernel(ProdArgs a, int dtype) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sm[CTA];
   __shared__ float smb[1];
   __shared__ float smx[8];
@@ -1012,14 +1054,20 @@ __global__ void __launch_bounds__(CTA)
   amax = cta_max(amax, smx);
   const float scale = row_scale_of(amax);
   const float rcp = __frcp_rn(scale);
+  const float sb = bf16_round(scale);
   if (threadIdx.x == 0) a.row_scale[row] = scale;
-  for (int64_t k = threadIdx.x; k < a.cols; k += CTA)
-    a.q[row * a.ldq + k] = quant_rn(
+  for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
+    const int8_t qv = quant_rn(
         __fmul_rn(__fmul_rn(load_elem(a.x, dtype, row * a.ldx + k), r), __ldg(a.w + k)), scale,
         rcp);
+    a.q[row * a.ldq + k] = qv;
+    if (a.xdq != nullptr) a.xdq[row * a.ld_dq + k] = bf16_bits(__fmul_rn(static_cast<float>(qv), sb));
+  }
 }
 
 __global__ void __launch_bounds__(CTA) gelu_quant_generic_kernel(ProdArgs a, int dtype) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float smx[8];
   const int64_t row = blockIdx.x;
   float amax = 0.0f;
@@ -1028,9 +1076,13 @@ __global__ void __launch_bounds__(CTA) gelu_quant_generic_kernel(ProdArgs a, int
   amax = cta_max(amax, smx);
   const float scale = row_scale_of(amax);
   const float rcp = __frcp_rn(scale);
+  const float sb = bf16_round(scale);
   if (threadIdx.x == 0) a.row_scale[row] = scale;
-  for (int64_t k = threadIdx.x; k < a.cols; k += CTA)
-    a.q[row * a.ldq + k] = quant_rn(gelu_tanh(load_elem(a.x, dtype, row * a.ldx + k)), scale, rcp);
+  for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
+    const int8_t qv = quant_rn(gelu_tanh(load_elem(a.x, dtype, row * a.ldx + k)), scale, rcp);
+    a.q[row * a.ldq + k] = qv;
+    if (a.xdq != nullptr) a.xdq[row * a.ld_dq + k] = bf16_bits(__fmul_rn(static_cast<float>(qv), sb));
+  }
 }
 
 // [B,H,T,D] heads -> rows b·T+t of H·D channels (int8_fused.py:103-131).
@@ -1040,9 +1092,13 @@ struct TransArgs {
   int8_t *q;
   int64_t ldq;
   float *row_scale;
+  unsigned short *xdq;  // optional bf16 dequantised copy (row stride ld_dq)
+  int64_t ld_dq;
 };
 template <typename T, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) transpose_quant_kernel(TransArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int RPC = CTA / RT;
   __shared__ float smx[RPC * 8];
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
@@ -1070,20 +1126,19 @@ __global__ void __launch_bounds__(CTA) transpose_quant_kernel(TransArgs a) {
   if (!live) return;
   const float scale = row_scale_of(amax);
   const float rcp = __frcp_rn(scale);
+  const float sb = bf16_round(scale);
   if (t == 0) a.row_scale[row] = scale;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     if (c >= nch) continue;
-    uint2 o;
-    o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
-                   quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
-    o.y = pack4_i8(quant_rn_i(v[i][4], scale, rcp), quant_rn_i(v[i][5], scale, rcp),
-                   quant_rn_i(v[i][6], scale, rcp), quant_rn_i(v[i][7], scale, rcp));
-    *reinterpret_cast<uint2 *>(a.q + row * a.ldq + 8 * c) = o;
+    quant_rn_store8(a.q + row * a.ldq + 8 * c, a.xdq == nullptr ? nullptr : a.xdq + row * a.ld_dq + 8 * c,
+                    v[i], scale, rcp, sb);
   }
 }
 __global__ void __launch_bounds__(CTA) transpose_quant_generic_kernel(TransArgs a, int dtype) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float smx[8];
   const int64_t row = blockIdx.x;
   const int64_t b = row / a.seq, s = row % a.seq;
@@ -1096,11 +1151,14 @@ __global__ void __launch_bounds__(CTA) transpose_quant_generic_kernel(TransArgs 
   amax = cta_max(amax, smx);
   const float scale = row_scale_of(amax);
   const float rcp = __frcp_rn(scale);
+  const float sbf = bf16_round(scale);
   if (threadIdx.x == 0) a.row_scale[row] = scale;
   for (int64_t c = threadIdx.x; c < channels; c += CTA) {
     const int64_t h = c / a.head_dim, d = c % a.head_dim;
-    a.q[row * a.ldq + c] =
+    const int8_t qv =
         quant_rn(load_elem(a.x, dtype, b * a.sb + h * a.sh + s * a.ss + d * a.sd), scale, rcp);
+    a.q[row * a.ldq + c] = qv;
+    if (a.xdq != nullptr) a.xdq[row * a.ld_dq + c] = bf16_bits(__fmul_rn(static_cast<float>(qv), sbf));
   }
 }
 
@@ -1124,6 +1182,8 @@ struct RmsBwdArgs {
 // row scales, bf16 copy), exactly as quant_rows_kernel would quantise the stored dx.
 template <typename X, typename G, int RT, int VPT, bool SRQ>
 __global__ void __launch_bounds__(CTA, 2) rmsnorm_bwd_kernel(RmsBwdArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int RPC = CTA / RT, NT = CTA / RT;
   __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
   __shared__ float smb[RPC];
@@ -1253,6 +1313,8 @@ __global__ void __launch_bounds__(CTA, 2) rmsnorm_bwd_kernel(RmsBwdArgs a) {
 
 __global__ void __launch_bounds__(CTA)
     rmsnorm_bwd_generic_kernel(RmsBwdArgs a, int gdt, int xdt) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sm[CTA];
   __shared__ float smb[1];
   const int64_t row = blockIdx.x;
@@ -1287,6 +1349,8 @@ __global__ void __launch_bounds__(CTA)
 
 template <typename T>
 __global__ void gelu_bwd_vec_kernel(const T *gy, const T *x, int64_t n8, T *dx) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     float xv[8], g[8], o[8];
@@ -1299,6 +1363,8 @@ __global__ void gelu_bwd_vec_kernel(const T *gy, const T *x, int64_t n8, T *dx) 
 }
 __global__ void gelu_bwd_kernel(const void *gy, int gdt, const void *x, int xdt, int64_t n,
                                 void *dx, int dxdt) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     store_elem(dx, dxdt, i, gelu_tanh_grad(load_elem(x, xdt, i), load_elem(gy, gdt, i)));
@@ -1316,6 +1382,8 @@ struct GeluBwdQArgs {
 };
 template <typename T, int RT, int VPT>
 __global__ void __launch_bounds__(CTA, VPT <= 2 ? 4 : (VPT == 4 ? 2 : 1)) gelu_bwd_sr_kernel(GeluBwdQArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int RPC = CTA / RT;
   __shared__ float smx[RPC * 8];
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
@@ -1370,6 +1438,8 @@ struct HeadsQArgs {
 };
 template <typename T, int RT, int VPT>
 __global__ void __launch_bounds__(CTA, VPT <= 2 ? 4 : (VPT == 4 ? 2 : 1)) heads3_sr_kernel(HeadsQArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int RPC = CTA / RT;
   __shared__ float smx[RPC * 8];
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
@@ -1465,13 +1535,13 @@ extern "C" int rt_dequant_rows_bf16(const int8_t *q, int64_t ldq, const float *r
     const int64_t n8 = rows * (cols / 8);
     auto *o = static_cast<__nv_bfloat16 *>(out);
     if (n8 < (int64_t(1) << 30) && rows * ldq < (int64_t(1) << 31) && rows * ldo < (int64_t(1) << 31))
-      dequant_vec_kernel<int32_t><<<grid_for(n8, 256), 256, 0, s>>>(
+      launch_k(dequant_vec_kernel<int32_t>, grid_for(n8, 256), 256, 0, s, 
           q, ldq, row_scale, o, ldo, static_cast<int32_t>(rows), static_cast<int32_t>(cols / 8));
     else
-      dequant_vec_kernel<int64_t><<<grid_for(n8, 256), 256, 0, s>>>(q, ldq, row_scale, o, ldo,
+      launch_k(dequant_vec_kernel<int64_t>, grid_for(n8, 256), 256, 0, s, q, ldq, row_scale, o, ldo,
                                                                     rows, cols / 8);
   } else {
-    dequant_kernel<<<grid_for(rows * cols, 256), 256, 0, s>>>(
+    launch_k(dequant_kernel, grid_for(rows * cols, 256), 256, 0, s, 
         q, ldq, row_scale, static_cast<uint16_t *>(out), ldo, rows, cols);
   }
   return check_launch("rt_dequant_rows_bf16");
@@ -1519,7 +1589,7 @@ extern "C" int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf1
     else
       RT_DISPATCH_ROW(cfg, ratchet_update_kernel, __nv_bfloat16, grid, a);
   } else {
-    ratchet_update_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a);
+    launch_k(ratchet_update_generic_kernel, static_cast<unsigned>(rows), CTA, 0, s, a);
   }
   return check_launch("rt_ratchet_update");
 }
@@ -1529,7 +1599,7 @@ extern "C" int rt_ratchet_leak(uint8_t *packed, int64_t ldp, int64_t rows, int64
   (void)max_code;
   if (rows < 0 || cols < 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_ratchet_leak: shape");
   if (rows * cols == 0) return RT_OK;
-  leak_kernel<<<grid_for(rows * cols, 256), 256, 0, as_stream(stream)>>>(packed, ldp, rows, cols);
+  launch_k(leak_kernel, grid_for(rows * cols, 256), 256, 0, as_stream(stream), packed, ldp, rows, cols);
   return check_launch("rt_ratchet_leak");
 }
 
@@ -1542,10 +1612,10 @@ extern "C" int rt_unpack_code_pressure(const uint8_t *packed, int64_t ldp, int64
   const int64_t n = rows * cols;
   if (pressure == nullptr && code != nullptr && ldp == cols && ldc == cols && n % 16 == 0 &&
       aligned16(packed) && aligned16(code)) {
-    unpack_codes_vec_kernel<<<grid_for(n / 16, 256), 256, 0, s>>>(
+    launch_k(unpack_codes_vec_kernel, grid_for(n / 16, 256), 256, 0, s, 
         reinterpret_cast<const uint4 *>(packed), n / 16, max_code, reinterpret_cast<uint4 *>(code));
   } else {
-    unpack_kernel<<<grid_for(n, 256), 256, 0, s>>>(packed, ldp, rows, cols, max_code, code, ldc,
+    launch_k(unpack_kernel, grid_for(n, 256), 256, 0, s, packed, ldp, rows, cols, max_code, code, ldc,
                                                    pressure, ldpr);
   }
   return check_launch("rt_unpack_code_pressure");
@@ -1555,22 +1625,24 @@ extern "C" int rt_ratchet_validate(const uint8_t *packed, int64_t ldp, int64_t r
                                    int max_code, const float *scale, void *stream) {
   if (rows < 0 || cols < 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_ratchet_validate: shape");
   if (rows * cols == 0) return RT_OK;
-  validate_kernel<<<grid_for(rows * cols, 256), 256, 0, as_stream(stream)>>>(packed, ldp, rows,
+  launch_k(validate_kernel, grid_for(rows * cols, 256), 256, 0, as_stream(stream), packed, ldp, rows,
                                                                              cols, max_code, scale);
   return check_launch("rt_ratchet_validate");
 }
 
 extern "C" int rt_rmsnorm_quantize(const void *x, int x_dtype, int64_t ldx, const float *weight,
                                    double eps, int64_t rows, int64_t cols, int8_t *q, int64_t ldq,
-                                   float *row_scale, void *stream) {
+                                   float *row_scale, void *dq_out, int64_t ld_dq, void *stream) {
   if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_rmsnorm_quantize: shape");
   if (x_dtype != RT_F32 && x_dtype != RT_BF16) return fail(RT_ERR_DTYPE, "rt_rmsnorm_quantize: dtype");
   if (rows == 0) return RT_OK;
   cudaStream_t s = as_stream(stream);
-  ProdArgs a{x, ldx, rows, cols, weight, static_cast<float>(eps), q, ldq, row_scale};
+  ProdArgs a{x, ldx, rows, cols, weight, static_cast<float>(eps), q, ldq, row_scale,
+             static_cast<unsigned short *>(dq_out), ld_dq};
   const size_t es = x_dtype == RT_F32 ? 4 : 2;
   const bool vec = cols % 8 == 0 && aligned16(x) && (ldx * es) % 16 == 0 && aligned16(weight) &&
-                   (reinterpret_cast<uintptr_t>(q) & 7) == 0 && ldq % 8 == 0;
+                   (reinterpret_cast<uintptr_t>(q) & 7) == 0 && ldq % 8 == 0 &&
+                   (dq_out == nullptr || (aligned16(dq_out) && ld_dq % 8 == 0));
   const RowCfg cfg = vec ? row_cfg(cols / 8) : RowCfg{0, 0};
   if (cfg.rt != 0) {
     if (x_dtype == RT_F32)
@@ -1578,22 +1650,24 @@ extern "C" int rt_rmsnorm_quantize(const void *x, int x_dtype, int64_t ldx, cons
     else
       RT_DISPATCH_ROW(cfg, rmsnorm_quant_kernel, __nv_bfloat16, row_grid(rows, cfg.rt), a);
   } else {
-    rmsnorm_quant_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a, x_dtype);
+    launch_k(rmsnorm_quant_generic_kernel, static_cast<unsigned>(rows), CTA, 0, s, a, x_dtype);
   }
   return check_launch("rt_rmsnorm_quantize");
 }
 
 extern "C" int rt_gelu_quantize(const void *x, int x_dtype, int64_t ldx, int64_t rows,
                                 int64_t cols, int8_t *q, int64_t ldq, float *row_scale,
-                                void *stream) {
+                                void *dq_out, int64_t ld_dq, void *stream) {
   if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_gelu_quantize: shape");
   if (x_dtype != RT_F32 && x_dtype != RT_BF16) return fail(RT_ERR_DTYPE, "rt_gelu_quantize: dtype");
   if (rows == 0) return RT_OK;
   cudaStream_t s = as_stream(stream);
-  ProdArgs a{x, ldx, rows, cols, nullptr, 0.0f, q, ldq, row_scale};
+  ProdArgs a{x, ldx, rows, cols, nullptr, 0.0f, q, ldq, row_scale,
+             static_cast<unsigned short *>(dq_out), ld_dq};
   const size_t es = x_dtype == RT_F32 ? 4 : 2;
   const bool vec = cols % 8 == 0 && aligned16(x) && (ldx * es) % 16 == 0 &&
-                   (reinterpret_cast<uintptr_t>(q) & 7) == 0 && ldq % 8 == 0;
+                   (reinterpret_cast<uintptr_t>(q) & 7) == 0 && ldq % 8 == 0 &&
+                   (dq_out == nullptr || (aligned16(dq_out) && ld_dq % 8 == 0));
   const RowCfg cfg = vec ? row_cfg(cols / 8) : RowCfg{0, 0};
   if (cfg.rt != 0) {
     if (x_dtype == RT_F32)
@@ -1601,7 +1675,7 @@ extern "C" int rt_gelu_quantize(const void *x, int x_dtype, int64_t ldx, int64_t
     else
       RT_DISPATCH_ROW(cfg, gelu_quant_kernel, __nv_bfloat16, row_grid(rows, cfg.rt), a);
   } else {
-    gelu_quant_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a, x_dtype);
+    launch_k(gelu_quant_generic_kernel, static_cast<unsigned>(rows), CTA, 0, s, a, x_dtype);
   }
   return check_launch("rt_gelu_quantize");
 }
@@ -1609,7 +1683,8 @@ extern "C" int rt_gelu_quantize(const void *x, int x_dtype, int64_t ldx, int64_t
 extern "C" int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, int64_t heads,
                                      int64_t seq, int64_t head_dim, int64_t stride_b,
                                      int64_t stride_h, int64_t stride_s, int64_t stride_d,
-                                     int8_t *q, int64_t ldq, float *row_scale, void *stream) {
+                                     int8_t *q, int64_t ldq, float *row_scale, void *dq_out,
+                                     int64_t ld_dq, void *stream) {
   if (batch < 0 || heads <= 0 || seq < 0 || head_dim <= 0)
     return fail(RT_ERR_INVALID_ARGUMENT, "rt_transpose_quantize: shape");
   if (x_dtype != RT_F32 && x_dtype != RT_BF16)
@@ -1617,12 +1692,12 @@ extern "C" int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, 
   if (batch * seq == 0) return RT_OK;
   cudaStream_t s = as_stream(stream);
   TransArgs a{x, batch, heads, seq, head_dim, stride_b, stride_h, stride_s, stride_d, q, ldq,
-              row_scale};
+              row_scale, static_cast<unsigned short *>(dq_out), ld_dq};
   const int64_t es = x_dtype == RT_F32 ? 4 : 2;
   const bool vec = stride_d == 1 && head_dim % 8 == 0 && aligned16(x) &&
                    (stride_b * es) % 16 == 0 && (stride_h * es) % 16 == 0 &&
                    (stride_s * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(q) & 7) == 0 &&
-                   ldq % 8 == 0;
+                   ldq % 8 == 0 && (dq_out == nullptr || (aligned16(dq_out) && ld_dq % 8 == 0));
   const RowCfg cfg = vec ? row_cfg(heads * head_dim / 8) : RowCfg{0, 0};
   const int64_t rows = batch * seq;
   if (cfg.rt != 0) {
@@ -1631,7 +1706,7 @@ extern "C" int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, 
     else
       RT_DISPATCH_ROW(cfg, transpose_quant_kernel, __nv_bfloat16, row_grid(rows, cfg.rt), a);
   } else {
-    transpose_quant_generic_kernel<<<static_cast<unsigned>(rows), CTA, 0, s>>>(a, x_dtype);
+    launch_k(transpose_quant_generic_kernel, static_cast<unsigned>(rows), CTA, 0, s, a, x_dtype);
   }
   return check_launch("rt_transpose_quantize");
 }
@@ -1644,7 +1719,7 @@ static int rmsnorm_backward_launch(const RmsBwdArgs &a, int gy_dtype, int x_dtyp
   const RowCfg cfg = vec ? row_cfg_narrow(a.cols / 8) : RowCfg{0, 0};
   if (cfg.rt == 0) {
     if (srq) return fail(RT_ERR_UNSUPPORTED, "rt_rmsnorm_backward_sr: rows need 16-byte chunks");
-    rmsnorm_bwd_generic_kernel<<<static_cast<unsigned>(a.rows), CTA, 0, s>>>(a, gy_dtype, x_dtype);
+    launch_k(rmsnorm_bwd_generic_kernel, static_cast<unsigned>(a.rows), CTA, 0, s, a, gy_dtype, x_dtype);
     return check_launch(who);
   }
   int sms = 0;
@@ -1657,10 +1732,10 @@ static int rmsnorm_backward_launch(const RmsBwdArgs &a, int gy_dtype, int x_dtyp
   const int combo = (x_dtype == RT_F32 ? 0 : 2) + (gy_dtype == RT_F32 ? 0 : 1);
 #define RT_RMSB(X, G, Q)                                                                      \
   switch (cfg.rt * 16 + cfg.vpt) {                                                            \
-    case 32 * 16 + 1: rmsnorm_bwd_kernel<X, G, 32, 1, Q><<<grid, CTA, dsm, s>>>(a); break;     \
-    case 32 * 16 + 2: rmsnorm_bwd_kernel<X, G, 32, 2, Q><<<grid, CTA, dsm, s>>>(a); break;     \
-    case 128 * 16 + 2: rmsnorm_bwd_kernel<X, G, 128, 2, Q><<<grid, CTA, dsm, s>>>(a); break;   \
-    default: rmsnorm_bwd_kernel<X, G, 256, 2, Q><<<grid, CTA, dsm, s>>>(a); break;             \
+    case 32 * 16 + 1: launch_k(rmsnorm_bwd_kernel<X, G, 32, 1, Q>, grid, CTA, dsm, s, a); break;     \
+    case 32 * 16 + 2: launch_k(rmsnorm_bwd_kernel<X, G, 32, 2, Q>, grid, CTA, dsm, s, a); break;     \
+    case 128 * 16 + 2: launch_k(rmsnorm_bwd_kernel<X, G, 128, 2, Q>, grid, CTA, dsm, s, a); break;   \
+    default: launch_k(rmsnorm_bwd_kernel<X, G, 256, 2, Q>, grid, CTA, dsm, s, a); break;             \
   }
   if (srq) {
     switch (combo) {
@@ -1725,15 +1800,15 @@ extern "C" int rt_gelu_backward(const void *grad_y, int gy_dtype, const void *x,
   if (gy_dtype == x_dtype && dx_dtype == x_dtype && n % 8 == 0 && aligned16(grad_y) &&
       aligned16(x) && aligned16(dx)) {
     if (x_dtype == RT_F32)
-      gelu_bwd_vec_kernel<float><<<grid_for(n / 8, 256), 256, 0, s>>>(
+      launch_k(gelu_bwd_vec_kernel<float>, grid_for(n / 8, 256), 256, 0, s, 
           static_cast<const float *>(grad_y), static_cast<const float *>(x), n / 8,
           static_cast<float *>(dx));
     else
-      gelu_bwd_vec_kernel<__nv_bfloat16><<<grid_for(n / 8, 256), 256, 0, s>>>(
+      launch_k(gelu_bwd_vec_kernel<__nv_bfloat16>, grid_for(n / 8, 256), 256, 0, s, 
           static_cast<const __nv_bfloat16 *>(grad_y), static_cast<const __nv_bfloat16 *>(x), n / 8,
           static_cast<__nv_bfloat16 *>(dx));
   } else {
-    gelu_bwd_kernel<<<grid_for(n, 256), 256, 0, s>>>(grad_y, gy_dtype, x, x_dtype, n, dx, dx_dtype);
+    launch_k(gelu_bwd_kernel, grid_for(n, 256), 256, 0, s, grad_y, gy_dtype, x, x_dtype, n, dx, dx_dtype);
   }
   return check_launch("rt_gelu_backward");
 }

@@ -23,41 +23,60 @@ def _rows(x: Tensor) -> Tensor:
     return flat
 
 
-def fused_rmsnorm_quantize(x: Tensor, weight: Tensor, eps: float = 1e-5) -> tuple[Tensor, Tensor]:
-    """RMSNorm -> per-token int8 (int8_fused.py:14-56)."""
+def _dequant_buffer(m: int, k: int, device, want: bool) -> Tensor | None:
+    return torch.empty((m, k), device=device, dtype=torch.bfloat16) if want else None
+
+
+def fused_rmsnorm_quantize(x: Tensor, weight: Tensor, eps: float = 1e-5, *,
+                           dequant_out: bool = False):
+    """RMSNorm -> per-token int8 (int8_fused.py:14-56).  dequant_out: also returns
+    bf16(bf16(q)·bf16(s)) [tokens, features], the layer's grad_weight operand (ratchet.py:73-76),
+    written by the same kernel."""
     if not x.is_cuda:
         raise RuntimeError("CUDA required")
     flat = _rows(x)
     m, k = flat.shape
     out = torch.empty((m, k), device=x.device, dtype=torch.int8)
     scale = torch.empty((m,), device=x.device, dtype=torch.float32)
+    dq = _dequant_buffer(m, k, x.device, dequant_out)
     w = weight.detach().float().contiguous()
     ev = _lib.prof_start(flat)
     _lib.check(_lib.lib().rt_rmsnorm_quantize(
         flat.data_ptr(), _lib.dtype_code(flat), flat.stride(0), w.data_ptr(), float(eps), m, k,
-        out.data_ptr(), out.stride(0), scale.data_ptr(), _lib.stream_of(flat)))
-    _lib.prof_stop(ev, "rmsnorm_quant", flat, 0.0, m * k * (flat.element_size() + 1) + 4 * m)
+        out.data_ptr(), out.stride(0), scale.data_ptr(), _lib.ptr(dq),
+        0 if dq is None else dq.stride(0), _lib.stream_of(flat)))
+    _lib.prof_stop(ev, "rmsnorm_quant", flat, 0.0,
+                   m * k * (flat.element_size() + 1 + (2 if dequant_out else 0)) + 4 * m)
+    if dequant_out:
+        return out.reshape(x.shape), scale.reshape(x.shape[:-1]), dq
     return out.reshape(x.shape), scale.reshape(x.shape[:-1])
 
 
-def fused_gelu_quantize(x: Tensor) -> tuple[Tensor, Tensor]:
-    """tanh-GELU -> per-token int8 (int8_fused.py:58-101)."""
+def fused_gelu_quantize(x: Tensor, *, dequant_out: bool = False):
+    """tanh-GELU -> per-token int8 (int8_fused.py:58-101); dequant_out as in
+    fused_rmsnorm_quantize."""
     if not x.is_cuda:
         raise RuntimeError("CUDA required")
     flat = _rows(x)
     m, k = flat.shape
     out = torch.empty((m, k), device=x.device, dtype=torch.int8)
     scale = torch.empty((m,), device=x.device, dtype=torch.float32)
+    dq = _dequant_buffer(m, k, x.device, dequant_out)
     ev = _lib.prof_start(flat)
     _lib.check(_lib.lib().rt_gelu_quantize(
         flat.data_ptr(), _lib.dtype_code(flat), flat.stride(0), m, k, out.data_ptr(),
-        out.stride(0), scale.data_ptr(), _lib.stream_of(flat)))
-    _lib.prof_stop(ev, "gelu_quant", flat, 0.0, m * k * (flat.element_size() + 1) + 4 * m)
+        out.stride(0), scale.data_ptr(), _lib.ptr(dq), 0 if dq is None else dq.stride(0),
+        _lib.stream_of(flat)))
+    _lib.prof_stop(ev, "gelu_quant", flat, 0.0,
+                   m * k * (flat.element_size() + 1 + (2 if dequant_out else 0)) + 4 * m)
+    if dequant_out:
+        return out.reshape(x.shape), scale.reshape(x.shape[:-1]), dq
     return out.reshape(x.shape), scale.reshape(x.shape[:-1])
 
 
-def fused_transpose_quantize(x: Tensor) -> tuple[Tensor, Tensor]:
-    """[B, H, T, D] heads -> (B*T, H*D) per-token int8 (int8_fused.py:103-151)."""
+def fused_transpose_quantize(x: Tensor, *, dequant_out: bool = False):
+    """[B, H, T, D] heads -> (B*T, H*D) per-token int8 (int8_fused.py:103-151); dequant_out as
+    in fused_rmsnorm_quantize."""
     if not x.is_cuda:
         raise RuntimeError("CUDA required")
     if x.dtype not in (torch.float32, torch.bfloat16):
@@ -65,19 +84,24 @@ def fused_transpose_quantize(x: Tensor) -> tuple[Tensor, Tensor]:
     b, h, t, d = x.shape
     out = torch.empty((b * t, h * d), device=x.device, dtype=torch.int8)
     scale = torch.empty((b * t,), device=x.device, dtype=torch.float32)
+    dq = _dequant_buffer(b * t, h * d, x.device, dequant_out)
     ev = _lib.prof_start(x)
     _lib.check(_lib.lib().rt_transpose_quantize(
         x.data_ptr(), _lib.dtype_code(x), b, h, t, d, x.stride(0), x.stride(1), x.stride(2),
-        x.stride(3), out.data_ptr(), out.stride(0), scale.data_ptr(), _lib.stream_of(x)))
-    _lib.prof_stop(ev, "transpose_quant", x, 0.0, b * h * t * d * (x.element_size() + 1) + 4 * b * t)
+        x.stride(3), out.data_ptr(), out.stride(0), scale.data_ptr(), _lib.ptr(dq),
+        0 if dq is None else dq.stride(0), _lib.stream_of(x)))
+    _lib.prof_stop(ev, "transpose_quant", x, 0.0,
+                   b * h * t * d * (x.element_size() + 1 + (2 if dequant_out else 0)) + 4 * b * t)
+    if dequant_out:
+        return out, scale, dq
     return out, scale
 
 
-def _no_zero_grads(ctx, int8_out: Tensor, scale_out: Tensor) -> None:
-    """The int8 codes and row scales carry no gradient: mark them so, and let backward see None
-    for gradients nobody produced instead of zero tensors autograd would fill (one fill kernel
-    per output per call)."""
-    ctx.mark_non_differentiable(int8_out, scale_out)
+def _no_zero_grads(ctx, *outputs: Tensor) -> None:
+    """The int8 codes, row scales (and dequantised copies) carry no gradient: mark them so, and
+    let backward see None for gradients nobody produced instead of zero tensors autograd would
+    fill (one fill kernel per output per call)."""
+    ctx.mark_non_differentiable(*outputs)
     ctx.set_materialize_grads(False)
 
 
@@ -90,25 +114,31 @@ class FusedRMSNormQuantizeFn(torch.autograd.Function):
     RMSNorm input gradient by the same kernel, instead of autograd summing the two branches.
 
     grad_plan: the GradientQuantPlan x carries when a ratchet layer produced it; the input
-    gradient computed here is then also quantised for that layer by the same kernel."""
+    gradient computed here is then also quantised for that layer by the same kernel.
+
+    dequant_out=True appends a last output: the bf16 dequantised rows for the consuming layer's
+    grad_weight (`inputs_dequant` of DiscreteRatchetLinear.forward)."""
 
     @staticmethod
     def forward(ctx, x: Tensor, weight: Tensor, eps: float = 1e-5, dummy_dtype=None,
-                residual_out: bool = False, grad_plan=None):
-        int8_out, scale_out = fused_rmsnorm_quantize(x, weight, eps)
+                residual_out: bool = False, grad_plan=None, dequant_out: bool = False):
+        produced = fused_rmsnorm_quantize(x, weight, eps, dequant_out=dequant_out)
+        int8_out, scale_out = produced[0], produced[1]
         ctx.save_for_backward(x, weight)
         ctx.eps = eps
         ctx.grad_plan = grad_plan
+        ctx.residual_out = residual_out
         dummy = torch.empty(x.shape, device=x.device, dtype=dummy_dtype or x.dtype)
-        _no_zero_grads(ctx, int8_out, scale_out)
-        if residual_out:
-            return int8_out, scale_out, dummy, x
-        return int8_out, scale_out, dummy
+        _no_zero_grads(ctx, int8_out, scale_out, *produced[2:])
+        outputs = (int8_out, scale_out, dummy) + ((x,) if residual_out else ()) + produced[2:]
+        return outputs
 
     @staticmethod
-    def backward(ctx, grad_int8, grad_scale, grad_dummy, grad_residual=None):
+    def backward(ctx, grad_int8, grad_scale, grad_dummy, *grad_rest):
+        # grad_rest: the residual output's gradient (residual_out), then the dequant copy's (None)
+        grad_residual = grad_rest[0] if ctx.residual_out else None
         if grad_dummy is None:
-            return grad_residual, None, None, None, None, None
+            return grad_residual, None, None, None, None, None, None
         x, weight = ctx.saved_tensors
         fuse = grad_residual is not None and x.dtype == torch.float32
         plan = ctx.grad_plan if (fuse or grad_residual is None) else None
@@ -117,7 +147,7 @@ class FusedRMSNormQuantizeFn(torch.autograd.Function):
                                           quant_plan=plan)
         if grad_residual is not None and not fuse:
             grad_x = grad_x + grad_residual
-        return grad_x, grad_w, None, None, None, None
+        return grad_x, grad_w, None, None, None, None, None
 
 
 class FusedGELUQuantizeFn(torch.autograd.Function):
@@ -125,40 +155,42 @@ class FusedGELUQuantizeFn(torch.autograd.Function):
     FusedRMSNormQuantizeFn."""
 
     @staticmethod
-    def forward(ctx, x: Tensor, dummy_dtype=None, grad_plan=None):
-        int8_out, scale_out = fused_gelu_quantize(x)
+    def forward(ctx, x: Tensor, dummy_dtype=None, grad_plan=None, dequant_out: bool = False):
+        produced = fused_gelu_quantize(x, dequant_out=dequant_out)
         ctx.save_for_backward(x)
         ctx.grad_plan = grad_plan
         dummy = torch.empty(x.shape, device=x.device, dtype=dummy_dtype or x.dtype)
-        _no_zero_grads(ctx, int8_out, scale_out)
-        return int8_out, scale_out, dummy
+        _no_zero_grads(ctx, *produced)
+        return (produced[0], produced[1], dummy) + produced[2:]
 
     @staticmethod
-    def backward(ctx, grad_int8, grad_scale, grad_dummy):
+    def backward(ctx, grad_int8, grad_scale, grad_dummy, grad_dq=None):
         if grad_dummy is None:
-            return None, None, None
+            return None, None, None, None
         (x,) = ctx.saved_tensors
-        return gelu_backward(grad_dummy, x, quant_plan=ctx.grad_plan), None, None
+        return gelu_backward(grad_dummy, x, quant_plan=ctx.grad_plan), None, None, None
 
 
 class FusedTransposeQuantizeFn(torch.autograd.Function):
+    """(int8, scale, dummy) like the reference; dequant_out as in FusedRMSNormQuantizeFn."""
+
     @staticmethod
-    def forward(ctx, attended: Tensor):
-        int8_out, scale_out = fused_transpose_quantize(attended)
+    def forward(ctx, attended: Tensor, dequant_out: bool = False):
+        produced = fused_transpose_quantize(attended, dequant_out=dequant_out)
         ctx.save_for_backward(attended)
         batch_size, n_head, seq_len, head_dim = attended.shape
         dummy = torch.empty((batch_size, seq_len, n_head * head_dim), device=attended.device,
                             dtype=attended.dtype)
-        _no_zero_grads(ctx, int8_out, scale_out)
-        return int8_out, scale_out, dummy
+        _no_zero_grads(ctx, *produced)
+        return (produced[0], produced[1], dummy) + produced[2:]
 
     @staticmethod
-    def backward(ctx, grad_int8, grad_scale, grad_dummy):
+    def backward(ctx, grad_int8, grad_scale, grad_dummy, grad_dq=None):
         if grad_dummy is None:
-            return None
+            return None, None
         (attended,) = ctx.saved_tensors
         batch_size, n_head, seq_len, head_dim = attended.shape
-        return grad_dummy.view(batch_size, seq_len, n_head, head_dim).transpose(1, 2)
+        return grad_dummy.view(batch_size, seq_len, n_head, head_dim).transpose(1, 2), None
 
 
 def heads_gather_quantize(grads: tuple[Tensor, Tensor, Tensor], plan) -> Tensor | None:

@@ -59,6 +59,11 @@ class ModelConfig:
     # because on B200 the fused row passes (instruction-bound Philox rounding behind the
     # producer's own row reduction) ran slower than the two separate passes
     fused_grad_quant: bool = False
+    # int8 mode: each fused producer (RMSNorm / GELU / head-transpose quantisers) also writes the
+    # bf16 dequantised rows its consuming layer's grad_weight GEMM uses, saved instead of the int8
+    # rows, so backward has no dequant pass (identical values; 2 instead of 1 byte per saved
+    # activation)
+    producer_dequant: bool = True
 
     def __post_init__(self) -> None:
         if min(self.vocab_size, self.block_size, self.n_layer, self.n_head, self.n_embd) <= 0:
@@ -113,14 +118,17 @@ class CausalSelfAttention(nn.Module):
         self.head_size = config.n_embd // config.n_head
         self.dropout = config.dropout
         self.fused_grad_quant = config.fused_grad_quant
+        self.producer_dequant = config.producer_dequant
 
     def forward(self, inputs: Tensor, *, inputs_int8: Tensor | None = None,
-                inputs_scale: Tensor | None = None, residual: Tensor | None = None) -> Tensor:
+                inputs_scale: Tensor | None = None, residual: Tensor | None = None,
+                inputs_dequant: Tensor | None = None) -> Tensor:
         """residual (int8 path): returns residual + attention(...), the add in the projection's
-        GEMM epilogue."""
+        GEMM epilogue.  inputs_dequant: the producer's bf16 dequantised rows (qkv grad_weight)."""
         batch_size, sequence_length, channels = inputs.shape
         if inputs_int8 is not None:
-            qkv = self.qkv(inputs, inputs_int8=inputs_int8, inputs_scale=inputs_scale)
+            qkv = self.qkv(inputs, inputs_int8=inputs_int8, inputs_scale=inputs_scale,
+                           inputs_dequant=inputs_dequant)
         else:
             qkv = self.qkv(inputs)
         plan = grad_plan_of(qkv) if self.fused_grad_quant else None
@@ -140,9 +148,10 @@ class CausalSelfAttention(nn.Module):
             dropout_p=self.dropout if self.training else 0.0, is_causal=True,
         )
         if getattr(self.projection, "matmul_mode", "fp32") == "int8":
-            attn_int8, attn_scale, dummy_joined = FusedTransposeQuantizeFn.apply(attended)
+            attn_int8, attn_scale, dummy_joined, *dq = FusedTransposeQuantizeFn.apply(
+                attended, self.producer_dequant)
             return self.projection(dummy_joined, inputs_int8=attn_int8, inputs_scale=attn_scale,
-                                   residual=residual)
+                                   residual=residual, inputs_dequant=dq[0] if dq else None)
         joined = attended.transpose(1, 2).contiguous().view(batch_size, sequence_length, channels)
         out = self.projection(joined)
         return out if residual is None else residual + out
@@ -156,26 +165,31 @@ class FeedForward(nn.Module):
         self.contract = _linear(config, hidden_size, config.n_embd, max_code)
         self.dropout = config.dropout
         self.fused_grad_quant = config.fused_grad_quant
+        self.producer_dequant = config.producer_dequant
         self.dummy_dtype = None
         if config.matmul_mode == "int8" and config.bf16_activations and max_code is not None:
             self.dummy_dtype = torch.bfloat16
             self.contract.output_dtype = torch.float32
 
     def forward(self, inputs: Tensor, *, inputs_int8: Tensor | None = None,
-                inputs_scale: Tensor | None = None, residual: Tensor | None = None) -> Tensor:
+                inputs_scale: Tensor | None = None, residual: Tensor | None = None,
+                inputs_dequant: Tensor | None = None) -> Tensor:
         """residual (int8 path, no active dropout): returns residual + feed_forward(...), the add
-        in the contraction's GEMM epilogue."""
+        in the contraction's GEMM epilogue.  inputs_dequant: the producer's bf16 dequantised rows
+        (expand grad_weight)."""
         if inputs_int8 is not None:
-            expanded = self.expand(inputs, inputs_int8=inputs_int8, inputs_scale=inputs_scale)
+            expanded = self.expand(inputs, inputs_int8=inputs_int8, inputs_scale=inputs_scale,
+                                   inputs_dequant=inputs_dequant)
         else:
             expanded = self.expand(inputs)
         fuse_residual = residual is not None and (self.dropout == 0.0 or not self.training)
         if getattr(self.contract, "matmul_mode", "fp32") == "int8":
             plan = grad_plan_of(expanded) if self.fused_grad_quant else None
-            gelu_int8, gelu_scale, dummy_gelu = FusedGELUQuantizeFn.apply(expanded, self.dummy_dtype,
-                                                                          plan)
+            gelu_int8, gelu_scale, dummy_gelu, *dq = FusedGELUQuantizeFn.apply(
+                expanded, self.dummy_dtype, plan, self.producer_dequant)
             contracted = self.contract(dummy_gelu, inputs_int8=gelu_int8, inputs_scale=gelu_scale,
-                                       residual=residual if fuse_residual else None)
+                                       residual=residual if fuse_residual else None,
+                                       inputs_dequant=dq[0] if dq else None)
         else:
             contracted = self.contract(F.gelu(expanded))
             fuse_residual = False
@@ -196,6 +210,7 @@ class TransformerBlock(nn.Module):
                             and max_code is not None else None)
         self.fused_residual = config.fused_residual and max_code is not None
         self.fused_grad_quant = config.fused_grad_quant
+        self.producer_dequant = config.producer_dequant
 
     def forward(self, inputs: Tensor) -> Tensor:
         # int8 path with fused residuals: the RMSNorm producer hands x on as the residual, the
@@ -207,29 +222,35 @@ class TransformerBlock(nn.Module):
                 # with the residual fused, this norm's input gradient is the whole gradient of
                 # `inputs`: quantise it for the ratchet layer that produced `inputs`, if any
                 plan = grad_plan_of(inputs) if self.fused_grad_quant else None
-                attn_int8, attn_scale, dummy_in, res = FusedRMSNormQuantizeFn.apply(
-                    inputs, self.attention_norm.weight, 1e-5, self.dummy_dtype, True, plan)
+                attn_int8, attn_scale, dummy_in, res, *dq = FusedRMSNormQuantizeFn.apply(
+                    inputs, self.attention_norm.weight, 1e-5, self.dummy_dtype, True, plan,
+                    self.producer_dequant)
                 inputs = self.attention(dummy_in, inputs_int8=attn_int8, inputs_scale=attn_scale,
-                                        residual=res)
+                                        residual=res, inputs_dequant=dq[0] if dq else None)
             else:
-                attn_int8, attn_scale, dummy_in = FusedRMSNormQuantizeFn.apply(
-                    inputs, self.attention_norm.weight, 1e-5, self.dummy_dtype)
+                attn_int8, attn_scale, dummy_in, *dq = FusedRMSNormQuantizeFn.apply(
+                    inputs, self.attention_norm.weight, 1e-5, self.dummy_dtype, False, None,
+                    self.producer_dequant)
                 inputs = inputs + self.attention(dummy_in, inputs_int8=attn_int8,
-                                                 inputs_scale=attn_scale)
+                                                 inputs_scale=attn_scale,
+                                                 inputs_dequant=dq[0] if dq else None)
         else:
             inputs = inputs + self.attention(self.attention_norm(inputs))
         if getattr(self.feed_forward.expand, "matmul_mode", "fp32") == "int8":
             if fused:
                 plan = grad_plan_of(inputs) if self.fused_grad_quant else None
-                ffn_int8, ffn_scale, dummy_in, res = FusedRMSNormQuantizeFn.apply(
-                    inputs, self.feed_forward_norm.weight, 1e-5, self.dummy_dtype, True, plan)
+                ffn_int8, ffn_scale, dummy_in, res, *dq = FusedRMSNormQuantizeFn.apply(
+                    inputs, self.feed_forward_norm.weight, 1e-5, self.dummy_dtype, True, plan,
+                    self.producer_dequant)
                 inputs = self.feed_forward(dummy_in, inputs_int8=ffn_int8, inputs_scale=ffn_scale,
-                                           residual=res)
+                                           residual=res, inputs_dequant=dq[0] if dq else None)
             else:
-                ffn_int8, ffn_scale, dummy_in = FusedRMSNormQuantizeFn.apply(
-                    inputs, self.feed_forward_norm.weight, 1e-5, self.dummy_dtype)
+                ffn_int8, ffn_scale, dummy_in, *dq = FusedRMSNormQuantizeFn.apply(
+                    inputs, self.feed_forward_norm.weight, 1e-5, self.dummy_dtype, False, None,
+                    self.producer_dequant)
                 inputs = inputs + self.feed_forward(dummy_in, inputs_int8=ffn_int8,
-                                                    inputs_scale=ffn_scale)
+                                                    inputs_scale=ffn_scale,
+                                                    inputs_dequant=dq[0] if dq else None)
         else:
             inputs = inputs + self.feed_forward(self.feed_forward_norm(inputs))
         return inputs

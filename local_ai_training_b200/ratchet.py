@@ -51,7 +51,7 @@ class _RatchetMatmul(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, inputs, inputs_int8, inputs_scale, code, scale, mode, fuse_backward_update,
-                int8_backward, tile_size, gradient_sink, residual=None):
+                int8_backward, tile_size, gradient_sink, residual=None, inputs_dequant=None):
         input_shape = inputs.shape
         flat_inputs = inputs.flatten(0, -2)
         out_features = code.shape[0]
@@ -72,10 +72,17 @@ class _RatchetMatmul(torch.autograd.Function):
         _require_cuda(code, "the ratchet matmul")
 
         if mode == "int8":
+            ctx.has_dequant = False
             if inputs_int8 is not None and inputs_scale is not None:
                 q = inputs_int8.flatten(0, -2)
                 s = inputs_scale.flatten(0, -1)
-                ctx.save_for_backward(q, s, code, scale)
+                if inputs_dequant is not None:
+                    # the producer also wrote bf16(bf16(q)·bf16(s)): keep it as the grad_weight
+                    # operand instead of the int8 rows (no dequant pass in backward)
+                    ctx.save_for_backward(inputs_dequant.flatten(0, -2), s, code, scale)
+                    ctx.has_dequant = True
+                else:
+                    ctx.save_for_backward(q, s, code, scale)
                 ctx.used_fused_int8 = True
             else:
                 if not inputs.is_cuda:
@@ -126,7 +133,8 @@ class _RatchetMatmul(torch.autograd.Function):
         if ctx.used_fused_int8:
             q, s, code, scale = ctx.saved_tensors
             flat_inputs = None
-            inputs_bf16 = dequant_rows_bf16(q, s)  # ratchet.py:73-76
+            # ratchet.py:73-76 (already done by the producer when it saved the bf16 rows)
+            inputs_bf16 = q if ctx.has_dequant else dequant_rows_bf16(q, s)
         else:
             flat_inputs, code, scale = ctx.saved_tensors
             inputs_bf16 = None if ctx.mode == "fp32" else flat_inputs.to(torch.bfloat16)
@@ -179,7 +187,7 @@ class _RatchetMatmul(torch.autograd.Function):
             ctx.gradient_sink, ctx.mode, ctx.fuse_backward_update, grad_bf16, inputs_bf16,
             flat_gradient, flat_inputs, code, bool(ctx.needs_input_grad[4]))
         return (grad_input.reshape(ctx.input_shape).to(ctx.input_dtype), None, None, None,
-                grad_scale, None, None, None, None, None, grad_residual)
+                grad_scale, None, None, None, None, None, grad_residual, None)
 
 
 def _deliver_weight_gradient(gradient_sink, mode: str, fuse_backward_update: bool,
@@ -558,14 +566,18 @@ class DiscreteRatchetLinear(nn.Module):
 
     # ------------------------------------------------------------------ forward
     def forward(self, inputs: Tensor, *, inputs_int8: Tensor | None = None,
-                inputs_scale: Tensor | None = None, residual: Tensor | None = None) -> Tensor:
+                inputs_scale: Tensor | None = None, residual: Tensor | None = None,
+                inputs_dequant: Tensor | None = None) -> Tensor:
         """residual (optional): returns residual + layer(inputs), the add fused into the int8
-        GEMM epilogue when residual is fp32."""
+        GEMM epilogue when residual is fp32.  inputs_dequant (with inputs_int8/inputs_scale):
+        bf16(bf16(inputs_int8)·bf16(inputs_scale)) written by the producer, saved for the
+        grad_weight GEMM instead of the int8 rows."""
         if self.matmul_mode != "fp32" or self.fuse_backward_update:
             output = _RatchetMatmul.apply(
                 inputs, inputs_int8, inputs_scale, self.code_int8(), self.scale, self.matmul_mode,
                 self.fuse_backward_update, self.int8_backward, self.tile_size,
                 self._capture_weight_gradient, residual,
+                inputs_dequant if self.matmul_mode == "int8" else None,
             )
             if (self.matmul_mode == "int8" and self.int8_backward and self.fuse_backward_update
                     and inputs_int8 is not None and inputs_scale is not None

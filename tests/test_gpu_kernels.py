@@ -425,6 +425,36 @@ def test_transpose_quantize_matches_oracle(cuda_device):
     np.testing.assert_array_equal(_np(s), so)
 
 
+@pytest.mark.parametrize("kind", ["rmsnorm", "gelu", "transpose"])
+@pytest.mark.parametrize("width", [512, 2048, 100])  # 100: the generic one-CTA-per-row kernels
+def test_producer_dequant_copy_equals_dequant_pass(cuda_device, kind, width):
+    """The bf16 rows a producer writes beside its int8 output are exactly what the backward's
+    dequant pass makes of them: bf16(bf16(q) * bf16(s))."""
+    from local_ai_training_b200.int8_fused import (fused_gelu_quantize, fused_rmsnorm_quantize,
+                                                   fused_transpose_quantize)
+    from local_ai_training_b200.int8_matmul import dequant_rows_bf16
+
+    torch.manual_seed(width)
+    if kind == "rmsnorm":
+        x = torch.randn(333, width, device=cuda_device)
+        w = torch.rand(width, device=cuda_device) + 0.5
+        q, s, dq = fused_rmsnorm_quantize(x, w, 1e-5, dequant_out=True)
+        q2, s2 = fused_rmsnorm_quantize(x, w, 1e-5)
+    elif kind == "gelu":
+        x = (torch.randn(333, width, device=cuda_device) * 2).to(torch.bfloat16)
+        q, s, dq = fused_gelu_quantize(x, dequant_out=True)
+        q2, s2 = fused_gelu_quantize(x)
+    else:
+        heads = 4 if width % 4 == 0 else 2
+        x = torch.randn(3, heads, 111, width // heads, device=cuda_device, dtype=torch.bfloat16)
+        q, s, dq = fused_transpose_quantize(x, dequant_out=True)
+        q2, s2 = fused_transpose_quantize(x)
+    assert torch.equal(q, q2) and torch.equal(s, s2)
+    q = q.reshape(-1, q.shape[-1])
+    assert dq.dtype == torch.bfloat16 and dq.shape == q.shape
+    assert torch.equal(dq, dequant_rows_bf16(q, s.reshape(-1)))
+
+
 def test_producer_backwards_match_oracle(cuda_device):
     from local_ai_training_b200.int8_backward import gelu_backward, rmsnorm_backward
 

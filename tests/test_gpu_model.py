@@ -127,17 +127,19 @@ def test_bf16_activation_plumbing_matches_reference_plumbing(cuda_device):
             torch.testing.assert_close(pa.grad, pb.grad, rtol=1e-5, atol=1e-7, msg=na)
 
 
+@pytest.mark.parametrize("flag", ["fused_residual", "producer_dequant"])
 @pytest.mark.parametrize("int8_backward", [False, True])
-def test_fused_residual_adds_match_unfused_bit_exact(cuda_device, int8_backward):
-    """The residual adds in the GEMM epilogues and in the RMSNorm backward kernel compute the
-    same fp32 values as `x + f(x)` with autograd's gradient sum: loss, logits, every ratchet
-    state and the embedding gradient are bit-identical over two steps."""
+def test_fusions_match_unfused_bit_exact(cuda_device, int8_backward, flag):
+    """fused_residual: the residual adds in the GEMM epilogues and in the RMSNorm backward kernel
+    compute the same fp32 values as `x + f(x)` with autograd's gradient sum.  producer_dequant:
+    the producers' bf16 rows equal the backward's dequant of the saved int8 rows.  Loss, logits,
+    every ratchet state and the embedding gradient are bit-identical over two steps."""
     from local_ai_training_b200 import ModelConfig, build_seeded_model
 
     def run(fused):
         cfg = ModelConfig(vocab_size=256, block_size=32, n_layer=2, n_head=2, n_embd=64,
                           dropout=0.0, pressure_threshold=2, matmul_mode="int8",
-                          int8_backward=int8_backward, fused_residual=fused)
+                          int8_backward=int8_backward, **{flag: fused})
         model = build_seeded_model(cfg, max_code=2, seed=4).to(cuda_device).train()
         for layer in model.ratchet_layers():
             layer.sr_seed = 9
