@@ -118,6 +118,23 @@ int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, int64_t ldx, 
 /* Workspace bytes rt_grad_weight_bf16 can use for this shape on the current device (0: none). */
 int64_t rt_grad_weight_workspace_bytes(int64_t M_tok, int64_t N, int64_t K);
 
+/* grad_weight GEMM and ratchet update in one call: the fused-update path of ratchet.py:148-163
+ * (per-tile bf16 GEMM, `.float()` of its bf16 result) -> _capture_weight_gradient -> the update of
+ * rt_ratchet_update(normalize=1, round_bf16=1) with grad[n,k] = sum_m g[m,n] * x[m,k].  grad_W is
+ * never stored: the GEMM leaves fp32 partial tiles in `workspace` (at least
+ * rt_grad_weight_update_workspace_bytes, 256-byte aligned) and the update sums them in split order
+ * as it reads each row, giving the values rt_grad_weight_bf16 + rt_ratchet_update would use.
+ * g (M_tok, rows) and x (M_tok, cols) bf16 with 16-byte rows, cols % 8 == 0, else
+ * RT_ERR_UNSUPPORTED.  Remaining arguments as rt_ratchet_update. */
+int rt_grad_weight_ratchet_update(const void *g, int64_t ldg, const void *x, int64_t ldx,
+                                  int64_t M_tok, int64_t rows, int64_t cols, void *workspace,
+                                  int64_t workspace_bytes, uint8_t *packed, int64_t ldp,
+                                  int8_t *code_out, int64_t ldc, float *rms_ema, double ema_beta,
+                                  int max_code, int threshold, double bucket_low,
+                                  double bucket_high, double eps, int64_t *counts, float *row_rms,
+                                  float *rms_sum, float *grad_scale, void *stream);
+int64_t rt_grad_weight_update_workspace_bytes(int64_t M_tok, int64_t rows, int64_t cols);
+
 /* rt_grad_weight_bf16 that allocates nothing and takes no workspace (no counterpart in the
  * reference, whose grad_weight GEMM is a cuBLAS call).  For callers that bind the C ABI without
  * a device allocator of their own (an FFI host with no caching allocator, where cudaMalloc would

@@ -48,6 +48,10 @@ _SIGNATURES = {
     "rt_grad_weight_bf16": ([_p, _i64, _p, _i64, _p, _i, _i64, _i64, _i64, _i64, _i, _p, _i64, _p],
                             _i),
     "rt_grad_weight_workspace_bytes": ([_i64, _i64, _i64], _i64),
+    "rt_grad_weight_ratchet_update": ([_p, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _i64,
+                                       _p, _i64, _p, _d, _i, _i, _d, _d, _d, _p, _p, _p, _p, _p],
+                                      _i),
+    "rt_grad_weight_update_workspace_bytes": ([_i64, _i64, _i64], _i64),
     "rt_grad_weight_bf16_noalloc": ([_p, _i64, _p, _i64, _p, _i, _i64, _i64, _i64, _i64, _i, _p],
                                     _i),
     "rt_dequant_rows_bf16": ([_p, _i64, _p, _p, _i64, _i64, _i64, _p], _i),

@@ -1017,6 +1017,62 @@ extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, in
   return check_launch("simt_gradw_kernel");
 }
 
+extern "C" int64_t rt_grad_weight_update_workspace_bytes(int64_t M_tok, int64_t N, int64_t K) {
+  int sms = 0;
+  if (rt_sm_count(&sms) != RT_OK || M_tok <= 0 || N <= 0 || K <= 0) return 0;
+  const int s = gw_splits(M_tok, N, K, sms, INT64_MAX / 4);
+  return static_cast<int64_t>(s < 1 ? 1 : s) * gw_tiles(N, K) * GW_TILE_BYTES;
+}
+
+// grad_W = gᵀ·x (bf16 operands, fp32 accumulation) straight into the ratchet update: the GEMM
+// writes its fp32 partial tiles (one split or more) to the workspace and the update kernel sums
+// them in split order as it reads each row -- the values the split-K reduce would store, without
+// storing them, and without its launch.
+extern "C" int rt_grad_weight_ratchet_update(
+    const void *g, int64_t ldg, const void *x, int64_t ldx, int64_t M_tok, int64_t rows,
+    int64_t cols, void *workspace, int64_t workspace_bytes, uint8_t *packed, int64_t ldp,
+    int8_t *code_out, int64_t ldc, float *rms_ema, double ema_beta, int max_code, int threshold,
+    double bucket_low, double bucket_high, double eps, int64_t *counts, float *row_rms,
+    float *rms_sum, float *grad_scale, void *stream) {
+  if (int rc = ratchet_update_check(rows, cols, max_code, threshold, bucket_low, bucket_high))
+    return rc;
+  if (M_tok < 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_grad_weight_ratchet_update: shape");
+  if (rows == 0) return RT_OK;
+  if (g == nullptr || x == nullptr || packed == nullptr || workspace == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_grad_weight_ratchet_update: null pointer");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(RT_ERR_ALIGNMENT, "rt_grad_weight_ratchet_update: workspace must be 256-byte aligned");
+  const bool tma_ok = M_tok > 0 && aligned16(g) && aligned16(x) && (ldg * 2) % 16 == 0 &&
+                      (ldx * 2) % 16 == 0 && rows <= INT32_MAX / 2 && cols <= INT32_MAX / 2 &&
+                      M_tok <= INT32_MAX / 2 && cols % 8 == 0;
+  if (!tma_ok)
+    return fail(RT_ERR_UNSUPPORTED, "rt_grad_weight_ratchet_update: operands need 16-byte rows");
+  int sms = 0;
+  if (int rc = rt_sm_count(&sms)) return rc;
+  int splits = gw_splits(M_tok, rows, cols, sms, workspace_bytes);
+  if (splits < 1) splits = 1;
+  const int64_t tiles = gw_tiles(rows, cols);
+  if (workspace_bytes < splits * tiles * GW_TILE_BYTES)
+    return fail(RT_ERR_UNSUPPORTED, "rt_grad_weight_ratchet_update: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  GemmArgs args{};
+  args.M = static_cast<int>(rows), args.N = static_cast<int>(cols), args.K = static_cast<int>(M_tok);
+  args.out_dtype = RT_F32, args.splits = splits, args.epi = EPI_SPLIT;
+  args.workspace = static_cast<float *>(workspace);
+  Operand A{g, true, ldg, rows, M_tok};
+  Operand B{x, true, ldx, cols, M_tok};
+  if (int rc = launch_umma<__nv_bfloat16, true, true, GW_BN, 4>(A, B, args, s)) return rc;
+  UpdateArgs a = update_args(nullptr, RT_F32, 1, 0, rows, cols, packed, ldp, code_out, ldc, 1,
+                             rms_ema, ema_beta, max_code, threshold, bucket_low, bucket_high, eps,
+                             counts, row_rms, rms_sum, grad_scale);
+  a.ws = static_cast<const float *>(workspace);
+  a.ws_splits = static_cast<int>(splits > (M_tok + 63) / 64 ? (M_tok + 63) / 64 : splits);
+  a.ws_tiles_n = static_cast<int>((cols + GW_BN - 1) / GW_BN);
+  a.ws_bn = GW_BN;
+  a.ws_split_stride = tiles * 128 * GW_BN;
+  return ratchet_update_launch(a, s);
+}
+
 // ---------------------------------------------------------------------------------------------
 // rt_grad_weight_bf16 without a caller-provided workspace: the split-K partial tiles live in a
 // fixed device array of this library.  Nothing is allocated per call.

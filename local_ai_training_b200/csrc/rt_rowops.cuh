@@ -542,6 +542,12 @@ struct UpdateArgs {
   float low, high, eps;
   unsigned long long *counts;
   float *row_rms, *rms_sum, *grad_scale;
+  // grad_W as split-K partial tiles of the grad_weight GEMM instead of `grad`: element (n, k) is
+  // the sum, in split order, of ws[s·ws_split_stride + ((n/128)·ws_tiles_n + k/ws_bn)·128·ws_bn
+  // + (n%128)·ws_bn + k%ws_bn] (the order of the split-K reduce)
+  const float *ws;
+  int ws_splits, ws_tiles_n, ws_bn;
+  int64_t ws_split_stride;
 };
 
 struct Moves {
@@ -601,7 +607,10 @@ __device__ __forceinline__ float row_denominator(const UpdateArgs &a, int64_t ro
   return __fadd_rn(rms, a.eps);
 }
 
-__device__ __forceinline__ void publish_moves(Moves m, int (*redi)[4], const UpdateArgs &a) {
+// The CTA's move counts (and, with rrs, the sum of its rows' gradient rms: RPC values) go to
+// the global counters with one atomic each per CTA.
+__device__ __forceinline__ void publish_moves(Moves m, int (*redi)[4], const UpdateArgs &a,
+                                              const float *rrs = nullptr, int nrr = 0) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   m.pos = warp_isum(m.pos), m.neg = warp_isum(m.neg);
   m.bpos = warp_isum(m.bpos), m.bneg = warp_isum(m.bneg);
@@ -616,17 +625,42 @@ __device__ __forceinline__ void publish_moves(Moves m, int (*redi)[4], const Upd
     for (int w = 0; w < CTA / 32; ++w) sum += redi[w][threadIdx.x];
     if (sum != 0) atomicAdd(a.counts + threadIdx.x, static_cast<unsigned long long>(sum));
   }
+  if (threadIdx.x == 32 && rrs != nullptr && a.rms_sum != nullptr) {
+    float sum = 0.0f;
+    for (int r = 0; r < nrr; ++r) sum = __fadd_rn(sum, rrs[r]);
+    atomicAdd(a.rms_sum, sum);
+  }
 }
 
-template <typename G, int RT, int VPT>
-__global__ void __launch_bounds__(CTA) ratchet_update_kernel(UpdateArgs a) {
-  pdl_wait();
-  pdl_trigger();
+// Eight gradient values of row `row`, chunk c: from `grad`, or (WS) summed over the split-K
+// partial tiles in split order.
+template <typename G, bool WS>
+__device__ __forceinline__ void load_grad8(const UpdateArgs &a, const G *gr, int64_t row,
+                                           int64_t c, float (&v)[8]) {
+  if constexpr (WS) {
+    const int64_t k0 = 8 * c;
+    const int64_t tile = (row >> 7) * a.ws_tiles_n + k0 / a.ws_bn;
+    const float *src = a.ws + (tile * 128 + (row & 127)) * a.ws_bn + k0 % a.ws_bn;
+    ld8(src, v);
+    for (int sp = 1; sp < a.ws_splits; ++sp) {
+      float f[8];
+      ld8(src + sp * a.ws_split_stride, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], f[j]);
+    }
+  } else {
+    ld8(gr + 8 * c, v);
+  }
+}
+
+template <typename G, int RT, int VPT, bool WS>
+__device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a) {
   constexpr int RPC = CTA / RT, NT = CTA / RT;
   __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
   __shared__ float smb[RPC];
   __shared__ float smx[RPC * 8];
   __shared__ int redi[CTA / 32][4];
+  __shared__ float rrs[RPC];  // the rows' gradient rms, summed once per CTA
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * RPC + sub;
   const bool live = row < a.rows;
@@ -642,7 +676,7 @@ __global__ void __launch_bounds__(CTA) ratchet_update_kernel(UpdateArgs a) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     pk[i] = make_uint2(0, 0);
     if (live && c < nch) {
-      ld8(gr + 8 * c, g[i]);
+      load_grad8<G, WS>(a, gr, row, c, g[i]);
       if (a.round_bf16) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) g[i][j] = bf16_round(g[i][j]);
@@ -680,10 +714,11 @@ __global__ void __launch_bounds__(CTA) ratchet_update_kernel(UpdateArgs a) {
   if (RT == 32) __syncwarp();
   const float denom = row_denominator(a, row, ms, ema_old, bad, live && t == 0);
   const float rcp = __frcp_rn(denom);
+  if (t == 0) rrs[sub] = 0.0f;
   if (live && t == 0) {
     const float rr = __fsqrt_rn(ms);
     if (a.row_rms != nullptr) a.row_rms[row] = rr;
-    if (a.rms_sum != nullptr) atomicAdd(a.rms_sum, rr);
+    rrs[sub] = rr;
     if (a.grad_scale != nullptr) a.grad_scale[row] = gsum;
     if (bad) raise_status(RT_STATUS_NONFINITE_GRADIENT);
   }
@@ -718,7 +753,19 @@ __global__ void __launch_bounds__(CTA) ratchet_update_kernel(UpdateArgs a) {
       *reinterpret_cast<uint2 *>(a.code_out + row * a.ldc + 8 * c) = make_uint2(cw[0], cw[1]);
     }
   }
-  publish_moves(m, redi, a);
+  publish_moves(m, redi, a, rrs, RPC);
+}
+template <typename G, int RT, int VPT>
+__global__ void __launch_bounds__(CTA) ratchet_update_kernel(UpdateArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  ratchet_update_body<G, RT, VPT, false>(a);
+}
+template <typename G, int RT, int VPT>
+__global__ void __launch_bounds__(CTA) ratchet_update_ws_kernel(UpdateArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  ratchet_update_body<G, RT, VPT, true>(a);
 }
 
 // Generic update: any alignment and row length, one CTA per row, same arithmetic and order.
@@ -1547,25 +1594,25 @@ extern "C" int rt_dequant_rows_bf16(const int8_t *q, int64_t ldq, const float *r
   return check_launch("rt_dequant_rows_bf16");
 }
 
-extern "C" int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf16, int64_t ldg,
-                                 int64_t rows, int64_t cols, uint8_t *packed, int64_t ldp,
-                                 int8_t *code_out, int64_t ldc, int normalize, float *rms_ema,
-                                 double ema_beta, int max_code, int threshold, double bucket_low,
-                                 double bucket_high, double eps, int64_t *counts, float *row_rms,
-                                 float *rms_sum, float *grad_scale, void *stream) {
+static int ratchet_update_check(int64_t rows, int64_t cols, int max_code, int threshold,
+                                double bucket_low, double bucket_high) {
   if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_ratchet_update: shape");
-  if (rows == 0) return RT_OK;
-  if (grad == nullptr || packed == nullptr)
-    return fail(RT_ERR_INVALID_ARGUMENT, "rt_ratchet_update: null pointer");
-  if (grad_dtype != RT_F32 && grad_dtype != RT_BF16)
-    return fail(RT_ERR_DTYPE, "rt_ratchet_update: gradient must be float32 or bfloat16");
   if (max_code < 1 || max_code > 7)
     return fail(RT_ERR_INVALID_ARGUMENT, "max_code must be in 1..7 (3..15 states)");
   if (threshold <= 0 || threshold > 127)
     return fail(RT_ERR_INVALID_ARGUMENT, "pressure_threshold must be in [1, 127]");
   if (!(0.0 <= bucket_low && bucket_low < bucket_high))
     return fail(RT_ERR_INVALID_ARGUMENT, "bucket thresholds must satisfy 0 <= low < high");
-  UpdateArgs a;
+  return RT_OK;
+}
+
+static UpdateArgs update_args(const void *grad, int grad_dtype, int round_bf16, int64_t ldg,
+                              int64_t rows, int64_t cols, uint8_t *packed, int64_t ldp,
+                              int8_t *code_out, int64_t ldc, int normalize, float *rms_ema,
+                              double ema_beta, int max_code, int threshold, double bucket_low,
+                              double bucket_high, double eps, int64_t *counts, float *row_rms,
+                              float *rms_sum, float *grad_scale) {
+  UpdateArgs a{};
   a.grad = grad, a.grad_dtype = grad_dtype, a.round_bf16 = round_bf16, a.ldg = ldg;
   a.rows = rows, a.cols = cols, a.packed = packed, a.ldp = ldp, a.code_out = code_out;
   a.ldc = ldc, a.normalize = normalize, a.rms_ema = (ema_beta > 0.0) ? rms_ema : nullptr;
@@ -1576,15 +1623,29 @@ extern "C" int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf1
   a.eps = static_cast<float>(eps);
   a.counts = reinterpret_cast<unsigned long long *>(counts);
   a.row_rms = row_rms, a.rms_sum = rms_sum, a.grad_scale = grad_scale;
-  cudaStream_t s = as_stream(stream);
-  const bool vec = cols % 8 == 0 && ldg % 8 == 0 && ldp % 8 == 0 && aligned16(grad) &&
-                   (reinterpret_cast<uintptr_t>(packed) & 7) == 0 &&
-                   (code_out == nullptr ||
-                    ((reinterpret_cast<uintptr_t>(code_out) & 7) == 0 && ldc % 8 == 0));
-  const RowCfg cfg = vec ? row_cfg(cols / 8, rows) : RowCfg{0, 0};
-  if (cfg.rt != 0) {
+  return a;
+}
+
+// Launch of the update over a.rows rows (a.ws set: from split-K partial tiles).
+static int ratchet_update_launch(const UpdateArgs &a, cudaStream_t s) {
+  const int64_t rows = a.rows, cols = a.cols;
+  const bool ws_ok = a.ws == nullptr || (aligned16(a.ws) && a.ws_bn % 8 == 0);
+  const bool vec = cols % 8 == 0 && (a.ws != nullptr || (a.ldg % 8 == 0 && aligned16(a.grad))) &&
+                   a.ldp % 8 == 0 && ws_ok && (reinterpret_cast<uintptr_t>(a.packed) & 7) == 0 &&
+                   (a.code_out == nullptr ||
+                    ((reinterpret_cast<uintptr_t>(a.code_out) & 7) == 0 && a.ldc % 8 == 0));
+  // a warp per row up to four chunks a lane: the row's reductions are shuffles only (the
+  // update's layers have few rows, so its time is the latency of one row's chain, and a CTA per
+  // row pair spent it in barriers)
+  RowCfg cfg = vec ? row_cfg(cols / 8, rows) : RowCfg{0, 0};
+  if (cfg.rt != 0 && cols / 8 <= 32 * 4) cfg = RowCfg{32, pow2_at_least((cols / 8 + 31) / 32)};
+  if (a.ws != nullptr) {
+    if (cfg.rt == 0)
+      return fail(RT_ERR_UNSUPPORTED, "rt_grad_weight_ratchet_update: rows need 8-element chunks");
+    RT_DISPATCH_ROW(cfg, ratchet_update_ws_kernel, float, row_grid(rows, cfg.rt), a);
+  } else if (cfg.rt != 0) {
     const unsigned grid = row_grid(rows, cfg.rt);
-    if (grad_dtype == RT_F32)
+    if (a.grad_dtype == RT_F32)
       RT_DISPATCH_ROW(cfg, ratchet_update_kernel, float, grid, a);
     else
       RT_DISPATCH_ROW(cfg, ratchet_update_kernel, __nv_bfloat16, grid, a);
@@ -1592,6 +1653,26 @@ extern "C" int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf1
     launch_k(ratchet_update_generic_kernel, static_cast<unsigned>(rows), CTA, 0, s, a);
   }
   return check_launch("rt_ratchet_update");
+}
+
+extern "C" int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf16, int64_t ldg,
+                                 int64_t rows, int64_t cols, uint8_t *packed, int64_t ldp,
+                                 int8_t *code_out, int64_t ldc, int normalize, float *rms_ema,
+                                 double ema_beta, int max_code, int threshold, double bucket_low,
+                                 double bucket_high, double eps, int64_t *counts, float *row_rms,
+                                 float *rms_sum, float *grad_scale, void *stream) {
+  if (int rc = ratchet_update_check(rows, cols, max_code, threshold, bucket_low, bucket_high))
+    return rc;
+  if (rows == 0) return RT_OK;
+  if (grad == nullptr || packed == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_ratchet_update: null pointer");
+  if (grad_dtype != RT_F32 && grad_dtype != RT_BF16)
+    return fail(RT_ERR_DTYPE, "rt_ratchet_update: gradient must be float32 or bfloat16");
+  const UpdateArgs a = update_args(grad, grad_dtype, round_bf16, ldg, rows, cols, packed, ldp,
+                                   code_out, ldc, normalize, rms_ema, ema_beta, max_code,
+                                   threshold, bucket_low, bucket_high, eps, counts, row_rms,
+                                   rms_sum, grad_scale);
+  return ratchet_update_launch(a, as_stream(stream));
 }
 
 extern "C" int rt_ratchet_leak(uint8_t *packed, int64_t ldp, int64_t rows, int64_t cols,

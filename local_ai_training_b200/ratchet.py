@@ -212,6 +212,12 @@ def _deliver_weight_gradient(gradient_sink, mode: str, fuse_backward_update: boo
         grad_weight = flat_gradient.to(torch.float32).t() @ flat_inputs.to(torch.float32)
         round_bf16 = False
     else:
+        layer = getattr(gradient_sink, "__self__", None)
+        if (fuse_backward_update and isinstance(layer, DiscreteRatchetLinear)
+                and layer.fused_gradw_update):
+            done, grad_scale = layer._grad_weight_update(grad_bf16, inputs_bf16, want_scale)
+            if done:
+                return grad_scale
         grad_weight = grad_weight_bf16(grad_bf16, inputs_bf16)
         round_bf16 = True
     if fuse_backward_update:
@@ -378,6 +384,12 @@ def bucket_pressure(z: Tensor, *, low: float = 0.5, high: float = 1.5) -> Tensor
 
 class DiscreteRatchetLinear(nn.Module):
     """Linear layer with integer codes and pressure, but no master weight parameter."""
+
+    # fused update: grad_W goes from the GEMM's split-K partial tiles straight into the update
+    # kernel (never stored; identical results).  Off by default: summing up to ~18 partials per
+    # element inside the row-wise update ran slower on B200 than the all-SM split-K reduce it
+    # replaces followed by the update
+    fused_gradw_update: bool = False
 
     def __init__(
         self,
@@ -636,6 +648,54 @@ class DiscreteRatchetLinear(nn.Module):
                            rows * self.in_features * (gradient.element_size() + 3) + 4 * rows)
         return grad_scale
 
+    def _pending_stat_slots(self, device) -> None:
+        if self._pending_counts is None:
+            # one buffer for the four move counters and the rms sum (bit pattern of a float)
+            self._pending_buf = (self._stats_slot if self._stats_slot is not None else
+                                 torch.zeros(5, device=device, dtype=torch.int64))
+            self._pending_counts = self._pending_buf[:4]
+            self._pending_rms = self._pending_buf[4:].view(torch.float32)[:1]
+
+    def _grad_weight_update(self, grad_bf16: Tensor, inputs_bf16: Tensor,
+                            want_grad_scale: bool) -> tuple[bool, Tensor | None]:
+        """The fused update of grad_W = grad_bf16ᵀ·inputs_bf16 (ratchet.py:148-163 then
+        _capture_weight_gradient) without storing grad_W: one GEMM writing split-K partial tiles
+        and the update reading them (rt_grad_weight_ratchet_update).  Returns (False, None) when
+        the operands' layout does not allow it (the caller then takes the two-step path)."""
+        pk = self.packed
+        mt, out_features = grad_bf16.shape
+        if (not pk.is_cuda or grad_bf16.dtype != torch.bfloat16
+                or inputs_bf16.dtype != torch.bfloat16 or inputs_bf16.shape[0] != mt
+                or out_features != self.out_features or inputs_bf16.shape[1] != self.in_features
+                or self.in_features % 8 != 0 or mt == 0):
+            return False, None
+        for t in (grad_bf16, inputs_bf16):
+            if t.stride(1) != 1 or (t.stride(0) * 2) % 16 != 0 or t.data_ptr() % 16 != 0:
+                return False, None
+        self._pending_stat_slots(pk.device)
+        mirror = self.code_int8()
+        ema = self.rms_ema if self.rms_ema_beta > 0.0 else None
+        grad_scale = (torch.empty(out_features, device=pk.device, dtype=torch.float32)
+                      if want_grad_scale else None)
+        need = _lib.lib().rt_grad_weight_update_workspace_bytes(mt, out_features, self.in_features)
+        ws = _lib.workspace(pk.device, need)
+        ev = _lib.prof_start(pk)
+        _lib.check(_lib.lib().rt_grad_weight_ratchet_update(
+            grad_bf16.data_ptr(), grad_bf16.stride(0), inputs_bf16.data_ptr(),
+            inputs_bf16.stride(0), mt, out_features, self.in_features, _lib.ptr(ws), need,
+            pk.data_ptr(), pk.stride(0), mirror.data_ptr(), mirror.stride(0), _lib.ptr(ema),
+            float(self.rms_ema_beta), self.max_code, self.pressure_threshold,
+            float(self.bucket_low), float(self.bucket_high), float(self.eps),
+            self._pending_counts.data_ptr(), None, self._pending_rms.data_ptr(),
+            _lib.ptr(grad_scale), _lib.stream_of(pk)))
+        if ev is not None:
+            n, k = out_features, self.in_features
+            _lib.prof_stop(ev, "gemm_gradw_update", pk, 2.0 * mt * n * k,
+                           2 * mt * (n + k) + 3 * n * k + 4 * n)
+        self._pending_stats_total_weights += out_features * self.in_features
+        self._pending_stats_rms_sum = self._pending_rms[0]
+        return True, grad_scale
+
     def _capture_weight_gradient(self, gradient: Tensor, tile_start: int | None,
                                  tile_end: int | None, *, round_bf16: bool = False,
                                  want_grad_scale: bool = False) -> Tensor | None:
@@ -650,12 +710,7 @@ class DiscreteRatchetLinear(nn.Module):
         assert tile_start is not None and tile_end is not None
         if gradient.shape != (tile_end - tile_start, self.in_features):
             raise ValueError("fused tile gradient shape mismatch")
-        if self._pending_counts is None:
-            # one buffer for the four move counters and the rms sum (bit pattern of a float)
-            self._pending_buf = (self._stats_slot if self._stats_slot is not None else
-                                 torch.zeros(5, device=gradient.device, dtype=torch.int64))
-            self._pending_counts = self._pending_buf[:4]
-            self._pending_rms = self._pending_buf[4:].view(torch.float32)[:1]
+        self._pending_stat_slots(gradient.device)
         grad_scale = self._run_update(gradient, tile_start, tile_end, normalize=True,
                                       round_bf16=round_bf16, counts=self._pending_counts,
                                       want_grad_scale=want_grad_scale, rms_sum=self._pending_rms)

@@ -290,6 +290,53 @@ def _update_gpu(grad, packed, *, max_code, threshold=8, low=0.5, high=1.5, eps=1
                 rms_sum=rms_sum)
 
 
+@pytest.mark.parametrize("m,rows,cols", [(16384, 512, 512), (16384, 1536, 512), (4096, 8192, 512),
+                                          (300, 200, 136), (16384, 512, 2048)])
+@pytest.mark.parametrize("ema", [False, True])
+def test_grad_weight_update_equals_gemm_then_update(cuda_device, m, rows, cols, ema):
+    """rt_grad_weight_ratchet_update (grad_W from split-K partial tiles, never stored) gives the
+    update that rt_grad_weight_bf16 followed by rt_ratchet_update(round_bf16=1) gives."""
+    from local_ai_training_b200 import _lib
+    from local_ai_training_b200.int8_matmul import grad_weight_bf16
+
+    torch.manual_seed(m + rows + cols)
+    max_code = 2
+    g = (torch.randn(m, rows, device=cuda_device) * 1e-3).to(torch.bfloat16)
+    x = torch.randn(m, cols, device=cuda_device).to(torch.bfloat16)
+    code = torch.randint(-max_code, max_code + 1, (rows, cols))
+    pressure = torch.randint(-7, 8, (rows, cols))
+    packed = torch.from_numpy(O.pack_code_pressure(code.numpy(), pressure.numpy(), max_code))
+    packed = packed.to(cuda_device)
+    ema0 = torch.rand(rows, device=cuda_device) * 1e-6 if ema else None
+    beta = 0.9 if ema else 0.0
+    gw = grad_weight_bf16(g, x)
+    ref = _update_gpu(gw, packed, max_code=max_code, round_bf16=True, ema=ema0, beta=beta,
+                      want_gs=True)
+    pk = packed.clone()
+    mirror = torch.empty_like(pk, dtype=torch.int8)
+    counts = torch.zeros(4, device=cuda_device, dtype=torch.int64)
+    rms_sum = torch.zeros(1, device=cuda_device)
+    row_rms = torch.empty(rows, device=cuda_device)
+    gs = torch.empty(rows, device=cuda_device)
+    ema_t = None if ema0 is None else ema0.clone()
+    need = _lib.lib().rt_grad_weight_update_workspace_bytes(m, rows, cols)
+    ws = torch.empty(need, device=cuda_device, dtype=torch.uint8)
+    _lib.check(_lib.lib().rt_grad_weight_ratchet_update(
+        g.data_ptr(), g.stride(0), x.data_ptr(), x.stride(0), m, rows, cols, ws.data_ptr(), need,
+        pk.data_ptr(), pk.stride(0), mirror.data_ptr(), mirror.stride(0),
+        None if ema_t is None else ema_t.data_ptr(), beta, max_code, 8, 0.5, 1.5, 1e-8,
+        counts.data_ptr(), row_rms.data_ptr(), rms_sum.data_ptr(), gs.data_ptr(),
+        _lib.stream_of(g)))
+    assert torch.equal(pk, ref["packed"])
+    assert torch.equal(mirror, ref["code"])
+    assert torch.equal(counts, ref["counts"])
+    assert torch.equal(row_rms, ref["row_rms"])
+    assert torch.equal(gs, ref["grad_scale"])
+    if ema:
+        assert torch.equal(ema_t, ref["rms_ema"])
+    torch.testing.assert_close(rms_sum, ref["rms_sum"], rtol=1e-5, atol=0)
+
+
 @pytest.mark.parametrize("idx", range(7))
 def test_update_matches_oracle_bit_exact(cuda_device, idx):
     g = load_golden("update_random.npz")

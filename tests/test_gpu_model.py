@@ -127,7 +127,7 @@ def test_bf16_activation_plumbing_matches_reference_plumbing(cuda_device):
             torch.testing.assert_close(pa.grad, pb.grad, rtol=1e-5, atol=1e-7, msg=na)
 
 
-@pytest.mark.parametrize("flag", ["fused_residual", "producer_dequant"])
+@pytest.mark.parametrize("flag", ["fused_residual", "producer_dequant", "fused_gradw_update"])
 @pytest.mark.parametrize("int8_backward", [False, True])
 def test_fusions_match_unfused_bit_exact(cuda_device, int8_backward, flag):
     """fused_residual: the residual adds in the GEMM epilogues and in the RMSNorm backward kernel
@@ -137,12 +137,15 @@ def test_fusions_match_unfused_bit_exact(cuda_device, int8_backward, flag):
     from local_ai_training_b200 import ModelConfig, build_seeded_model
 
     def run(fused):
+        kw = {} if flag == "fused_gradw_update" else {flag: fused}
         cfg = ModelConfig(vocab_size=256, block_size=32, n_layer=2, n_head=2, n_embd=64,
                           dropout=0.0, pressure_threshold=2, matmul_mode="int8",
-                          int8_backward=int8_backward, **{flag: fused})
+                          int8_backward=int8_backward, **kw)
         model = build_seeded_model(cfg, max_code=2, seed=4).to(cuda_device).train()
         for layer in model.ratchet_layers():
             layer.sr_seed = 9
+            if flag == "fused_gradw_update":
+                layer.fused_gradw_update = fused
         gen = torch.Generator().manual_seed(2)
         out = []
         for _ in range(2):
