@@ -136,13 +136,14 @@ __host__ __device__ __forceinline__ Philox4 sr_block(uint64_t seed, uint32_t ste
                        0x52415443u, static_cast<uint32_t>(seed),
                        static_cast<uint32_t>(seed >> 32) ^ layer);
 }
-// u of the low / high 16 bits of a word, built in the mantissa of a float in [1, 2) (exact,
-// no int->float conversion): 1 + h * 2^-16 + 2^-17, minus 1.
-__device__ __forceinline__ float sr_u_lo(uint32_t word) {
-  return __uint_as_float(((word << 7) & 0x007FFF80u) | 0x3F800040u) - 1.0f;
+// u - 1/2 of the low / high 16 bits of a word, built in the mantissa of a float in [1, 2)
+// (exact, no int->float conversion): 1 + h * 2^-16 + 2^-17, minus 3/2 (u itself is this + 1/2,
+// also exact).  The quantiser adds u - 1/2 to the scaled value in one fused multiply-add.
+__device__ __forceinline__ float sr_um_lo(uint32_t word) {
+  return __uint_as_float(((word << 7) & 0x007FFF80u) | 0x3F800040u) - 1.5f;
 }
-__device__ __forceinline__ float sr_u_hi(uint32_t word) {
-  return __uint_as_float(((word >> 9) & 0x007FFF80u) | 0x3F800040u) - 1.0f;
+__device__ __forceinline__ float sr_um_hi(uint32_t word) {
+  return __uint_as_float(((word >> 9) & 0x007FFF80u) | 0x3F800040u) - 1.5f;
 }
 __host__ __device__ __forceinline__ uint32_t philox_word(const Philox4 &p, int j) {
   return j == 0 ? p.x : (j == 1 ? p.y : (j == 2 ? p.z : p.w));

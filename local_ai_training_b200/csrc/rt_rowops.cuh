@@ -148,16 +148,17 @@ __device__ __forceinline__ int quant_rn_i(float v, float scale, float rcp) {
     return static_cast<int>(rintf(fminf(fmaxf(__fdiv_rn(v, scale), -127.0f), 127.0f)));
   return __float_as_int(t) - 0x4B400000;
 }
-// Stochastic rounding floor(RN(RN(v / scale) + u)), as an int in [-127, 127].  With
-// t = v·rcp + u, floor(t) is taken as RN(t - 1/2) through the rounding magic (t - 1/2 is exact:
-// |t| < 2^8 and t is a multiple of 2^-17), which equals floor(t) unless t lies within the
-// window of an integer; those elements go to the IEEE division, floor and clamp.  Outside the
+// Stochastic rounding floor(RN(RN(v / scale) + u)), as an int in [-127, 127], given um = u - 1/2.
+// th = fma(v, rcp, um) lies within 2^-15 of RN(v / scale) + u - 1/2 (the reciprocal estimate,
+// the division's and the fma's roundings), so RN(th), taken through the rounding magic, is
+// floor(RN(RN(v / scale) + u)) unless th lies within the window of a half-integer; those
+// elements go to the IEEE division, the reference's two roundings, floor and clamp.  Outside the
 // window the estimate stays within (-128, 128), so the fast path needs no clamp.
-__device__ __forceinline__ int quant_sr_i(float v, float scale, float rcp, float u) {
-  const float th = __fsub_rn(__fadd_rn(__fmul_rn(v, rcp), u), 0.5f);
+__device__ __forceinline__ int quant_sr_i(float v, float scale, float rcp, float um) {
+  const float th = __fmaf_rn(v, rcp, um);
   const float z = __fadd_rn(th, kRoundMagic);
   if (fabsf(__fsub_rn(th, __fsub_rn(z, kRoundMagic))) >= 0.5f - kBoundaryWindow) {
-    const float t = __fadd_rn(__fdiv_rn(v, scale), u);
+    const float t = __fadd_rn(__fdiv_rn(v, scale), __fadd_rn(um, 0.5f));  // u exact
     return min(max(__float2int_rd(t), -127), 127);
   }
   return __float_as_int(z) - 0x4B400000;
@@ -165,8 +166,8 @@ __device__ __forceinline__ int quant_sr_i(float v, float scale, float rcp, float
 __device__ __forceinline__ int8_t quant_rn(float v, float scale, float rcp) {
   return static_cast<int8_t>(quant_rn_i(v, scale, rcp));
 }
-__device__ __forceinline__ int8_t quant_sr(float v, float scale, float rcp, float u) {
-  return static_cast<int8_t>(quant_sr_i(v, scale, rcp, u));
+__device__ __forceinline__ int8_t quant_sr(float v, float scale, float rcp, float um) {
+  return static_cast<int8_t>(quant_sr_i(v, scale, rcp, um));
 }
 // Four ints in [-128, 127] -> one word of int8 bytes (two byte permutes and a merge).
 __device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
@@ -375,14 +376,14 @@ __global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
       if (a.stochastic) {
         const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;  // multiple of 8
         const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
-        o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_u_lo(p.x)),
-                       quant_sr_i(v[i][1], scale, rcp, sr_u_hi(p.x)),
-                       quant_sr_i(v[i][2], scale, rcp, sr_u_lo(p.y)),
-                       quant_sr_i(v[i][3], scale, rcp, sr_u_hi(p.y)));
-        o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_u_lo(p.z)),
-                       quant_sr_i(v[i][5], scale, rcp, sr_u_hi(p.z)),
-                       quant_sr_i(v[i][6], scale, rcp, sr_u_lo(p.w)),
-                       quant_sr_i(v[i][7], scale, rcp, sr_u_hi(p.w)));
+        o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_um_lo(p.x)),
+                       quant_sr_i(v[i][1], scale, rcp, sr_um_hi(p.x)),
+                       quant_sr_i(v[i][2], scale, rcp, sr_um_lo(p.y)),
+                       quant_sr_i(v[i][3], scale, rcp, sr_um_hi(p.y)));
+        o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_um_lo(p.z)),
+                       quant_sr_i(v[i][5], scale, rcp, sr_um_hi(p.z)),
+                       quant_sr_i(v[i][6], scale, rcp, sr_um_lo(p.w)),
+                       quant_sr_i(v[i][7], scale, rcp, sr_um_hi(p.w)));
       } else {
         o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
                        quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
@@ -425,7 +426,7 @@ __global__ void __launch_bounds__(CTA) quant_rows_generic_kernel(QuantArgs a) {
       const uint64_t e = static_cast<uint64_t>(row) * a.cols + k;
       const Philox4 p = sr_block(a.seed, step, a.layer, e >> 3);
       const uint32_t w = philox_word(p, static_cast<int>((e & 7) >> 1));
-      o = quant_sr(v, scale, rcp, (e & 1) ? sr_u_hi(w) : sr_u_lo(w));
+      o = quant_sr(v, scale, rcp, (e & 1) ? sr_um_hi(w) : sr_um_lo(w));
     } else {
       o = quant_rn(v, scale, rcp);
     }
@@ -485,14 +486,14 @@ __device__ __forceinline__ void sr_quant_store_row(const QuantArgs &a, uint32_t 
     const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;
     const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
     uint2 o;
-    o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_u_lo(p.x)),
-                   quant_sr_i(v[i][1], scale, rcp, sr_u_hi(p.x)),
-                   quant_sr_i(v[i][2], scale, rcp, sr_u_lo(p.y)),
-                   quant_sr_i(v[i][3], scale, rcp, sr_u_hi(p.y)));
-    o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_u_lo(p.z)),
-                   quant_sr_i(v[i][5], scale, rcp, sr_u_hi(p.z)),
-                   quant_sr_i(v[i][6], scale, rcp, sr_u_lo(p.w)),
-                   quant_sr_i(v[i][7], scale, rcp, sr_u_hi(p.w)));
+    o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_um_lo(p.x)),
+                   quant_sr_i(v[i][1], scale, rcp, sr_um_hi(p.x)),
+                   quant_sr_i(v[i][2], scale, rcp, sr_um_lo(p.y)),
+                   quant_sr_i(v[i][3], scale, rcp, sr_um_hi(p.y)));
+    o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_um_lo(p.z)),
+                   quant_sr_i(v[i][5], scale, rcp, sr_um_hi(p.z)),
+                   quant_sr_i(v[i][6], scale, rcp, sr_um_lo(p.w)),
+                   quant_sr_i(v[i][7], scale, rcp, sr_um_hi(p.w)));
     *reinterpret_cast<uint2 *>(qr + 8 * c) = o;
   }
 }
