@@ -1254,6 +1254,9 @@ __global__ void __launch_bounds__(CTA, 2) rmsnorm_bwd_kernel(RmsBwdArgs a) {
   }
   // column scales are re-read per row (L1 hits) rather than held: two CTAs per SM stay resident
   const uint32_t step = SRQ ? sr_step_read(a.sq) : 0u;
+  // x / cols as a multiply when cols is a power of two (then exact, the same value)
+  const bool cols_pow2 = (a.cols & (a.cols - 1)) == 0;
+  const float inv_cols = 1.0f / static_cast<float>(a.cols);
   // rows are visited in groups of RPC by a grid-stride loop (uniform across the CTA), so each
   // thread accumulates the weight gradient of its own columns over many rows
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
@@ -1261,7 +1264,7 @@ __global__ void __launch_bounds__(CTA, 2) rmsnorm_bwd_kernel(RmsBwdArgs a) {
     const bool live = row < a.rows;
     const X *xr = static_cast<const X *>(a.x) + (live ? row : 0) * a.cols;
     const G *gr = static_cast<const G *>(a.gy) + (live ? row : 0) * a.cols;
-    float xv[VPT][8], gv[VPT][8];
+    float xv[VPT][8], gv[VPT][8], ad[VPT][8];
     float ss[NT], dot[NT];
 #pragma unroll
     for (int k = 0; k < NT; ++k) ss[k] = 0.0f, dot[k] = 0.0f;
@@ -1271,6 +1274,9 @@ __global__ void __launch_bounds__(CTA, 2) rmsnorm_bwd_kernel(RmsBwdArgs a) {
       if (live && c < nch) {
         ld8(xr + 8 * c, xv[i]);
         ld8(gr + 8 * c, gv[i]);
+        // the residual branch's gradient, requested with the row (it may alias dx: each element
+        // is read before this thread stores it)
+        if (a.dx_add != nullptr) ld8(a.dx_add + row * a.cols + 8 * c, ad[i]);
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j) xv[i][j] = 0.0f, gv[i][j] = 0.0f;
@@ -1298,16 +1304,15 @@ __global__ void __launch_bounds__(CTA, 2) rmsnorm_bwd_kernel(RmsBwdArgs a) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const float dh = __fmul_rn(gv[i][j], wv[i][j]);
-          o[j] = bf16_round(__fadd_rn(__fmul_rn(dh, r),
-                                      __fdiv_rn(__fmul_rn(__fmul_rn(dvar, 2.0f), xv[i][j]),
-                                                static_cast<float>(a.cols))));
+          const float num = __fmul_rn(__fmul_rn(dvar, 2.0f), xv[i][j]);
+          const float q = cols_pow2 ? __fmul_rn(num, inv_cols)
+                                    : __fdiv_rn(num, static_cast<float>(a.cols));
+          o[j] = bf16_round(__fadd_rn(__fmul_rn(dh, r), q));
           dwp[i][j] = __fadd_rn(dwp[i][j], __fmul_rn(__fmul_rn(gv[i][j], xv[i][j]), r));
         }
-        if (a.dx_add != nullptr) {  // the residual branch's gradient, summed as autograd would
-          float ad[8];
-          ld8(a.dx_add + row * a.cols + 8 * c, ad);
+        if (a.dx_add != nullptr) {  // summed as autograd sums the two branches
 #pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(ad[j], o[j]);
+          for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(ad[i][j], o[j]);
         }
         if (a.dx_dtype == RT_F32)
           st8(static_cast<float *>(a.dx) + row * a.cols + 8 * c, o);

@@ -183,15 +183,16 @@ def bench_producers(m, k, reps, flush, peaks, dtype=torch.float32):
     x = torch.randn(m, k, device=dev).to(dtype)
     w = torch.rand(k, device=dev) + 0.5
     es = x.element_size()
-    t = _time(lambda: fused_rmsnorm_quantize(x, w), reps, flush)
-    _report(f"rmsnorm_quant_{str(dtype).split('.')[-1]}", [m, k], t, m * k * (es + 1), 0, 0, peaks)
-    xg = torch.randn(m, 4 * k, device=dev).to(dtype)
-    t = _time(lambda: fused_gelu_quantize(xg), reps, flush)
-    _report(f"gelu_quant_{str(dtype).split('.')[-1]}", [m, 4 * k], t, m * 4 * k * (es + 1), 0, 0, peaks)
+    # as the train step calls them: int8 rows, scales and the bf16 dequantised copy
+    t = _time(lambda: fused_rmsnorm_quantize(x, w, dequant_out=True), reps, flush)
+    _report(f"rmsnorm_quant_{str(dtype).split('.')[-1]}", [m, k], t, m * k * (es + 3), 0, 0, peaks)
+    xg = torch.randn(m, 4 * k, device=dev).to(torch.bfloat16)
+    t = _time(lambda: fused_gelu_quantize(xg, dequant_out=True), reps, flush)
+    _report("gelu_quant_bfloat16", [m, 4 * k], t, m * 4 * k * (2 + 3), 0, 0, peaks)
     heads = k // 64
     xt = torch.randn(m // 512, heads, 512, 64, device=dev, dtype=torch.bfloat16)
-    t = _time(lambda: fused_transpose_quantize(xt), reps, flush)
-    _report("transpose_quant_bfloat16", list(xt.shape), t, xt.numel() * 3, 0, 0, peaks)
+    t = _time(lambda: fused_transpose_quantize(xt, dequant_out=True), reps, flush)
+    _report("transpose_quant_bfloat16", list(xt.shape), t, xt.numel() * 5, 0, 0, peaks)
 
 
 def main() -> None:
