@@ -1152,7 +1152,13 @@ __global__ void __launch_bounds__(CTA) transpose_quant_kernel(TransArgs a) {
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * RPC + sub;
   const bool live = row < a.batch * a.seq;
-  const int64_t b = live ? row / a.seq : 0, s = live ? row % a.seq : 0;
+  // row -> (b, s) and chunk -> (head, d) in 32-bit unsigned arithmetic (the launch checks that
+  // rows and channels fit), a shift when head_dim is a power of two
+  const uint32_t seq = static_cast<uint32_t>(a.seq), hd = static_cast<uint32_t>(a.head_dim);
+  const uint32_t r32 = live ? static_cast<uint32_t>(row) : 0u;
+  const uint32_t b = r32 / seq, s = r32 - b * seq;
+  const bool hd_pow2 = (hd & (hd - 1)) == 0;
+  const int hd_shift = __ffs(static_cast<int>(hd)) - 1;
   const int64_t nch = a.heads * a.head_dim / 8;
   const T *base = static_cast<const T *>(a.x) + b * a.sb + s * a.ss;
   float v[VPT][8];
@@ -1161,7 +1167,8 @@ __global__ void __launch_bounds__(CTA) transpose_quant_kernel(TransArgs a) {
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     if (live && c < nch) {
-      const int64_t ch = 8 * c, h = ch / a.head_dim, d = ch % a.head_dim;
+      const uint32_t ch = 8u * static_cast<uint32_t>(c);
+      const uint32_t h = hd_pow2 ? ch >> hd_shift : ch / hd, d = ch - h * hd;
       ld8(base + h * a.sh + d, v[i]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
@@ -1515,7 +1522,8 @@ __global__ void __launch_bounds__(CTA, VPT <= 2 ? 4 : (VPT == 4 ? 2 : 1)) heads3
   for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
     const int64_t row = grp * RPC + sub;
     const bool live = row < a.sq.rows;
-    const int64_t b = live ? row / a.seq : 0, s = live ? row - b * a.seq : 0;
+    const uint32_t r32 = live ? static_cast<uint32_t>(row) : 0u;  // rows < 2^31 (launch)
+    const int64_t b = r32 / static_cast<uint32_t>(a.seq), s = r32 - b * a.seq;
     const T *base0 = static_cast<const T *>(a.src[0]) + b * a.sb[0] + s * a.ss[0];
     const T *base1 = static_cast<const T *>(a.src[1]) + b * a.sb[1] + s * a.ss[1];
     const T *base2 = static_cast<const T *>(a.src[2]) + b * a.sb[2] + s * a.ss[2];
@@ -1785,8 +1793,9 @@ extern "C" int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, 
                    (stride_b * es) % 16 == 0 && (stride_h * es) % 16 == 0 &&
                    (stride_s * es) % 16 == 0 && (reinterpret_cast<uintptr_t>(q) & 7) == 0 &&
                    ldq % 8 == 0 && (dq_out == nullptr || (aligned16(dq_out) && ld_dq % 8 == 0));
-  const RowCfg cfg = vec ? row_cfg(heads * head_dim / 8) : RowCfg{0, 0};
   const int64_t rows = batch * seq;
+  const bool fits32 = rows < (int64_t(1) << 31) && heads * head_dim < (int64_t(1) << 31);
+  const RowCfg cfg = vec && fits32 ? row_cfg(heads * head_dim / 8) : RowCfg{0, 0};
   if (cfg.rt != 0) {
     if (x_dtype == RT_F32)
       RT_DISPATCH_ROW(cfg, transpose_quant_kernel, float, row_grid(rows, cfg.rt), a);
@@ -1958,7 +1967,7 @@ extern "C" int rt_heads_gather_sr(const void *const *src, const int64_t *strides
           (a.sh[p] * es) % 16 == 0 && (a.ss[p] * es) % 16 == 0;
   }
   a.seq = seq, a.head_dim = head_dim, a.width = width, a.out = out, a.ldo = ldo, a.sq = sq;
-  const RowCfg cfg = vec ? row_cfg(cols / 8, rows) : RowCfg{0, 0};
+  const RowCfg cfg = vec && rows < (int64_t(1) << 31) ? row_cfg(cols / 8, rows) : RowCfg{0, 0};
   if (cfg.rt == 0) return fail(RT_ERR_UNSUPPORTED, "rt_heads_gather_sr: heads need 16-byte chunks");
   int sms = 0;
   if (int rc = rt_sm_count(&sms)) return rc;
