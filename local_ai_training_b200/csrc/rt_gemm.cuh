@@ -891,9 +891,13 @@ __global__ void __launch_bounds__(256)
   const int groups = (cols + 3) >> 2;
   const int64_t total = static_cast<int64_t>(rows) * groups;
   const int64_t split_stride = static_cast<int64_t>(tiles_m) * tiles_n * 128 * BN;
+  const bool idx32 = total <= static_cast<int64_t>(UINT32_MAX);
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int row = static_cast<int>(i / groups);
+    // element group -> (row, col): a 32-bit division whenever the index fits (a 64-bit one is a
+    // long instruction sequence per four elements)
+    const int row = idx32 ? static_cast<int>(static_cast<uint32_t>(i) / static_cast<uint32_t>(groups))
+                          : static_cast<int>(i / groups);
     const int col = static_cast<int>(i - static_cast<int64_t>(row) * groups) * 4;
     const int tile = (row >> 7) * tiles_n + col / BN;
     const float *src = ws + (static_cast<int64_t>(tile) * 128 + (row & 127)) * BN + col % BN;

@@ -216,7 +216,8 @@ static inline RowCfg row_cfg(int64_t nch, int64_t rows = INT64_MAX) {
   const int64_t want_threads = 148 * 2048;
   if (nch > 256 * 8) return {0, 0};
   int rt = nch <= 32 * 2 ? 32 : (nch <= 128 * 2 ? 128 : 256);
-  while (rt < 256 && rows * rt < want_threads && nch > rt) rt = rt == 32 ? 128 : 256;
+  // (rows < want / rt, not rows * rt < want: the default row count would overflow the product)
+  while (rt < 256 && rows < want_threads / rt && nch > rt) rt = rt == 32 ? 128 : 256;
   return {rt, pow2_at_least((nch + rt - 1) / rt)};
 }
 // Kernels holding four row arrays per chunk (RMSNorm backward) keep at most 2 chunks per thread.
