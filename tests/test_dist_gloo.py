@@ -10,7 +10,6 @@ process applying the update to the whole matrix with the averaged gradient.
 from __future__ import annotations
 
 import os
-import socket
 
 import numpy as np
 import pytest
@@ -95,10 +94,14 @@ def _local_grad(rank: int, n: int, shape) -> torch.Tensor:
     return (torch.randn(shape[0], shape[1], generator=g) * 1e-2).to(torch.bfloat16)
 
 
-def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+def _init(rank: int, world: int, out_dir: str) -> None:
+    # file rendezvous in the test's own directory: no TCP port to race for
+    dist.init_process_group("gloo", init_method=f"file://{os.path.join(out_dir, 'store')}",
+                            rank=rank, world_size=world)
+
+
+def _worker(rank: int, world: int, out_dir: str) -> None:
+    _init(rank, world, out_dir)
     from local_ai_training_b200.dist import RatchetDataParallel
 
     model = _StubModel()
@@ -122,15 +125,9 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
     dist.destroy_process_group()
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
 def test_row_owner_update_equals_single_process_update(tmp_path):
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+    mp.start_processes(_worker, args=(world, str(tmp_path)), nprocs=world,
                        start_method="spawn")
     res = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
     # replicated state: identical on both ranks
@@ -168,17 +165,14 @@ def test_row_owner_update_equals_single_process_update(tmp_path):
 
 def test_rejects_rows_not_divisible_by_ranks(tmp_path):
     world = 2
-    port = _free_port()
-    mp.start_processes(_reject_worker, args=(world, port, str(tmp_path)), nprocs=world,
+    mp.start_processes(_reject_worker, args=(world, str(tmp_path)), nprocs=world,
                        start_method="spawn")
     for r in range(world):
         assert (tmp_path / f"ok{r}").read_text() == "ValueError"
 
 
-def _reject_worker(rank: int, world: int, port: int, out_dir: str) -> None:
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+def _reject_worker(rank: int, world: int, out_dir: str) -> None:
+    _init(rank, world, out_dir)
     from local_ai_training_b200.dist import RatchetDataParallel
 
     model = _StubModel()
