@@ -163,6 +163,18 @@ __device__ __forceinline__ int quant_sr_i(float v, float scale, float rcp, float
   }
   return __float_as_int(z) - 0x4B400000;
 }
+// quant_rn_i that also returns the rounded value as a float (exact: a small integer), which the
+// rounding magic has produced already -- no int-to-float conversion for the dequantised copy.
+__device__ __forceinline__ int quant_rn_if(float v, float scale, float rcp, float &qf) {
+  const float y = fminf(fmaxf(__fmul_rn(v, rcp), -127.0f), 127.0f);
+  const float t = __fadd_rn(y, kRoundMagic);
+  qf = __fsub_rn(t, kRoundMagic);
+  if (fabsf(__fsub_rn(y, qf)) >= 0.5f - kBoundaryWindow) {
+    qf = rintf(fminf(fmaxf(__fdiv_rn(v, scale), -127.0f), 127.0f));
+    return static_cast<int>(qf);
+  }
+  return __float_as_int(t) - 0x4B400000;
+}
 __device__ __forceinline__ int8_t quant_rn(float v, float scale, float rcp) {
   return static_cast<int8_t>(quant_rn_i(v, scale, rcp));
 }
@@ -185,8 +197,9 @@ __device__ __forceinline__ float row_scale_of(float amax) {
 __device__ __forceinline__ void quant_rn_store8(int8_t *qp, unsigned short *dq, const float (&v)[8],
                                                 float scale, float rcp, float sb) {
   int qi[8];
+  float qf[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) qi[j] = quant_rn_i(v[j], scale, rcp);
+  for (int j = 0; j < 8; ++j) qi[j] = quant_rn_if(v[j], scale, rcp, qf[j]);
   uint2 o;
   o.x = pack4_i8(qi[0], qi[1], qi[2], qi[3]);
   o.y = pack4_i8(qi[4], qi[5], qi[6], qi[7]);
@@ -194,7 +207,7 @@ __device__ __forceinline__ void quant_rn_store8(int8_t *qp, unsigned short *dq, 
   if (dq != nullptr) {
     float d[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) d[j] = __fmul_rn(static_cast<float>(qi[j]), sb);
+    for (int j = 0; j < 8; ++j) d[j] = __fmul_rn(qf[j], sb);
     st8(reinterpret_cast<__nv_bfloat16 *>(dq), d);
   }
 }
