@@ -59,7 +59,7 @@ struct KindOf<__nv_bfloat16> {
   static constexpr uint32_t abfmt = 1; // BF16
 };
 
-template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
+template <typename T, bool A_MN, bool B_MN, int BN, int STAGES, int EPI = 8>
 struct GemmCfg {
   static constexpr int BM = 128;
   static constexpr int ES = sizeof(T);
@@ -69,8 +69,10 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  // eight epilogue warps: two per TMEM lane quarter, each taking half of the tile's columns
-  static constexpr int EPI_WARPS = 8;
+  // EPI epilogue warps (8 or 16): EPI/4 per TMEM lane quarter, each taking BN/(EPI/4) columns
+  static constexpr int EPI_WARPS = EPI;
+  static constexpr int COLW = BN / (EPI / 4);
+  static_assert(EPI == 8 || EPI == 16, "EPI");
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   // per epilogue warp: one 32-row x 128-byte staging buffer for TMA stores
   static constexpr int EPI_BYTES = EPI_WARPS * 4096;
@@ -303,35 +305,33 @@ __device__ __forceinline__ bool epilogue_tma(const CUtensorMap *map, uint8_t *st
     for (int g = 0; g < HALF / 64; ++g) {
       const int n0 = x0 + g * 64;
       if (n0 >= x_end) break;  // warp-uniform
-      uint32_t r0[32], r1[32];
-      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64), r0);
-      tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64 + 32), r1);
-      tmem_ld_wait_regs(r0);
-      tmem_regs_after_wait(r1);
+      // the group's two 32-column halves, each read, converted and packed before the next is
+      // read (32 accumulator registers live, not 64)
       const bool last = g == HALF / 64 - 1 || n0 + 64 >= x_end;
-      if (last) release_accumulator(tempty_bar, lane);
-      if (pending >= 0) stage_issue(map, staging, lane, pending, y);
       uint32_t w[32];
       const float4 *bs4 = reinterpret_cast<const float4 *>(bs + g * 64);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {  // columns 4j..4j+3 of r0 and 32+4j..32+4j+3 of r1
-        float v[8];
+      for (int h = 0; h < 2; ++h) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + static_cast<uint32_t>(g * 64 + 32 * h), r);
+        tmem_ld_wait_regs(r);
+        if (h == 1) {
+          if (last) release_accumulator(tempty_bar, lane);
+          if (pending >= 0) stage_issue(map, staging, lane, pending, y);
+        }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          v[e] = cvt_acc<CONV>(r0[4 * j + e]);
-          v[4 + e] = cvt_acc<CONV>(r1[4 * j + e]);
+        for (int j = 0; j < 8; ++j) {  // columns 32h + 4j .. 32h + 4j + 3
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] = cvt_acc<CONV>(r[4 * j + e]);
+          if (scaled) {
+            const float4 sc = bs4[8 * h + j];  // 16-byte broadcast read
+            v[0] = __fmul_rn(__fmul_rn(v[0], a_s), sc.x), v[1] = __fmul_rn(__fmul_rn(v[1], a_s), sc.y);
+            v[2] = __fmul_rn(__fmul_rn(v[2], a_s), sc.z), v[3] = __fmul_rn(__fmul_rn(v[3], a_s), sc.w);
+          }
+          w[16 * h + 2 * j] = pack_bf16x2(v[0], v[1]);
+          w[16 * h + 2 * j + 1] = pack_bf16x2(v[2], v[3]);
         }
-        if (scaled) {
-          const float4 sa = bs4[j], sb = bs4[8 + j];  // 16-byte broadcast reads
-          v[0] = __fmul_rn(__fmul_rn(v[0], a_s), sa.x), v[1] = __fmul_rn(__fmul_rn(v[1], a_s), sa.y);
-          v[2] = __fmul_rn(__fmul_rn(v[2], a_s), sa.z), v[3] = __fmul_rn(__fmul_rn(v[3], a_s), sa.w);
-          v[4] = __fmul_rn(__fmul_rn(v[4], a_s), sb.x), v[5] = __fmul_rn(__fmul_rn(v[5], a_s), sb.y);
-          v[6] = __fmul_rn(__fmul_rn(v[6], a_s), sb.z), v[7] = __fmul_rn(__fmul_rn(v[7], a_s), sb.w);
-        }
-        w[2 * j] = pack_bf16x2(v[0], v[1]);
-        w[2 * j + 1] = pack_bf16x2(v[2], v[3]);
-        w[16 + 2 * j] = pack_bf16x2(v[4], v[5]);
-        w[16 + 2 * j + 1] = pack_bf16x2(v[6], v[7]);
       }
       stage_write(staging, lane, w);
       if (last) {
@@ -390,13 +390,13 @@ __device__ __forceinline__ bool epilogue_tma(const CUtensorMap *map, uint8_t *st
   }
 }
 
-template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
-__global__ void __launch_bounds__(64 + 32 * 8, 1)
+template <typename T, bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(64 + 32 * EPI, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_c,
                      const __grid_constant__ CUtensorMap tma_r, GemmArgs p) {
-  using C = GemmCfg<T, A_MN, B_MN, BN, STAGES>;
+  using C = GemmCfg<T, A_MN, B_MN, BN, STAGES, EPI>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -526,8 +526,8 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     }
   } else {
     // epilogue warps 2..9: TMEM lane quarter (warp % 4) holds accumulator rows 32·(warp%4)..+31;
-    // warps 2..5 take the tile's first BN/2 columns, warps 6..9 the second half
-    constexpr int HALF = BN / 2;
+    // warps 2..5 take the tile's first COLW columns, warps 6..9 the next COLW, and so on
+    constexpr int HALF = C::COLW;  // columns of this warp
     const int sub = warp & 3;
     const int col0 = ((warp - 2) >> 2) * HALF;  // first tile column of this warp
     const int ep_tid = threadIdx.x - 64;        // 0..255 across the epilogue warps
@@ -737,9 +737,9 @@ static int operand_map(CUtensorMap *map, const Operand &o, int tile_rows) {
     return make_map(map, dt, o.ptr, o.extent_k, o.rows_mn, o.ld * sizeof(T), Cfg::KE, tile_rows);
 }
 
-template <typename T, bool A_MN, bool B_MN, int BN, int STAGES>
+template <typename T, bool A_MN, bool B_MN, int BN, int STAGES, int EPI = 8>
 static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaStream_t s) {
-  using C = GemmCfg<T, A_MN, B_MN, BN, STAGES>;
+  using C = GemmCfg<T, A_MN, B_MN, BN, STAGES, EPI>;
   CUtensorMap ma, mb, mc, mr;
   memset(&mr, 0, sizeof(mr));
   memset(&mc, 0, sizeof(mc));
@@ -789,7 +789,7 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
   if ((rc = rt_sm_count(&sms)) != RT_OK) return rc;
   static std::mutex mu;
   static bool configured[64] = {false};
-  auto kernel = umma_gemm_kernel<T, A_MN, B_MN, BN, STAGES>;
+  auto kernel = umma_gemm_kernel<T, A_MN, B_MN, BN, STAGES, EPI>;
   {
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -857,9 +857,13 @@ extern "C" int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_
     Operand A{lhs, a_mn, a_k ? lhs_stride_m : lhs_stride_k, M, K};
     Operand B{rhs, b_mn, b_k ? rhs_stride_n : rhs_stride_k, N, K};
     const bool narrow = N <= 128;
+    // fp32 outputs (twice the bytes per tile, and the residual tiles) run sixteen epilogue warps
+    // over three stages; bf16 outputs eight warps over four stages (measured faster each way)
+    const bool wide_epi = out_dtype == RT_F32;
 #define RT_GO(AMN, BMN)                                                              \
   return narrow ? launch_umma<int8_t, AMN, BMN, 128, 6>(A, B, args, s)               \
-                : launch_umma<int8_t, AMN, BMN, 256, 4>(A, B, args, s)
+                : (wide_epi ? launch_umma<int8_t, AMN, BMN, 256, 3, 16>(A, B, args, s) \
+                            : launch_umma<int8_t, AMN, BMN, 256, 4>(A, B, args, s))
     if (!a_mn && !b_mn) RT_GO(false, false);
     if (!a_mn && b_mn) RT_GO(false, true);
     if (a_mn && !b_mn) RT_GO(true, false);
