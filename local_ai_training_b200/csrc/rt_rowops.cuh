@@ -241,6 +241,9 @@ static inline RowCfg row_cfg_narrow(int64_t nch) {
   if (nch <= 512) return {256, 2};
   return {0, 0};
 }
+// Resident 256-thread CTAs per SM of the grid-striding row kernels, whose launch bounds give
+// four at up to two chunks a thread, two at four, one at eight.
+static inline unsigned resident_ctas(int vpt) { return vpt <= 2 ? 4u : (vpt == 4 ? 2u : 1u); }
 static inline unsigned row_grid(int64_t rows, int rt) {
   const int64_t rpc = CTA / rt;
   return static_cast<unsigned>((rows + rpc - 1) / rpc);
@@ -325,8 +328,11 @@ __device__ __forceinline__ void sr_step_arrive(const QuantArgs &a, uint32_t step
   }
 }
 
+// (launch bounds as resident_ctas: the resident-sized grid of the dispatch counts on them; at
+// four CTAs, 64 registers, the bf16 2048-wide case ran 61 instead of 80 us at 92 registers)
 template <typename T, int RT, int VPT>
-__global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
+__global__ void __launch_bounds__(CTA, VPT <= 2 ? 4 : (VPT == 4 ? 2 : 1))
+    quant_rows_kernel(QuantArgs a) {
   pdl_wait();
   pdl_trigger();
   // grid-stride over groups of RPC rows: a resident-sized grid (few CTAs, so that the step
@@ -529,8 +535,8 @@ static int quant_rows_dispatch(const QuantArgs &a, cudaStream_t s) {
   if (cfg.rt != 0) {
     int sms = 0;
     if (int rc = rt_sm_count(&sms)) return rc;
-    // four CTAs per SM are resident for every configuration up to two chunks per thread
-    const unsigned resident = static_cast<unsigned>(sms) * 4;
+    // CTAs per SM that stay resident (the kernels' launch bounds: 4 up to two chunks a thread)
+    const unsigned resident = static_cast<unsigned>(sms) * resident_ctas(cfg.vpt);
     const unsigned groups = row_grid(a.rows, cfg.rt);
     RT_DISPATCH_ROW(cfg, quant_rows_kernel, T, groups < resident ? groups : resident, a);
   } else {
@@ -1943,7 +1949,7 @@ extern "C" int rt_gelu_backward_sr(const void *grad_y, const void *x, int dtype,
   if (cfg.rt == 0) return fail(RT_ERR_UNSUPPORTED, "rt_gelu_backward_sr: rows need 16-byte chunks");
   int sms = 0;
   if (int rc = rt_sm_count(&sms)) return rc;
-  const unsigned resident = static_cast<unsigned>(sms) * 4;
+  const unsigned resident = static_cast<unsigned>(sms) * resident_ctas(cfg.vpt);
   const unsigned groups = row_grid(rows, cfg.rt);
   const unsigned grid = groups < resident ? groups : resident;
   cudaStream_t s = as_stream(stream);
@@ -1985,7 +1991,7 @@ extern "C" int rt_heads_gather_sr(const void *const *src, const int64_t *strides
   if (cfg.rt == 0) return fail(RT_ERR_UNSUPPORTED, "rt_heads_gather_sr: heads need 16-byte chunks");
   int sms = 0;
   if (int rc = rt_sm_count(&sms)) return rc;
-  const unsigned resident = static_cast<unsigned>(sms) * 4;
+  const unsigned resident = static_cast<unsigned>(sms) * resident_ctas(cfg.vpt);
   const unsigned groups = row_grid(rows, cfg.rt);
   const unsigned grid = groups < resident ? groups : resident;
   cudaStream_t s = as_stream(stream);
