@@ -328,13 +328,27 @@ __device__ __forceinline__ void sr_step_arrive(const QuantArgs &a, uint32_t step
   }
 }
 
-// (launch bounds as resident_ctas: the resident-sized grid of the dispatch counts on them; at
-// four CTAs, 64 registers, the bf16 2048-wide case ran 61 instead of 80 us at 92 registers)
+// Two entry points over one body.  The resident-sized grid of the dispatch counts on four CTAs
+// per SM at up to two chunks a thread: the bf16 variants compile to 64 registers unforced, the
+// fp32 ones (70 registers unforced) are held to it by their launch bounds.  Forcing the bf16
+// variants too cost 11 % (more instructions at the same register count); leaving them unbounded
+// under an explicit minimum of one CTA gave 92 registers and 80 instead of 55 us (2048 wide).
 template <typename T, int RT, int VPT>
-__global__ void __launch_bounds__(CTA, VPT <= 2 ? 4 : (VPT == 4 ? 2 : 1))
-    quant_rows_kernel(QuantArgs a) {
+__device__ __forceinline__ void quant_rows_body(const QuantArgs &a);
+template <typename T, int RT, int VPT>
+__global__ void __launch_bounds__(CTA) quant_rows_kernel(QuantArgs a) {
   pdl_wait();
   pdl_trigger();
+  quant_rows_body<T, RT, VPT>(a);
+}
+template <typename T, int RT, int VPT>
+__global__ void __launch_bounds__(CTA, 4) quant_rows_f32_kernel(QuantArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  quant_rows_body<T, RT, VPT>(a);
+}
+template <typename T, int RT, int VPT>
+__device__ __forceinline__ void quant_rows_body(const QuantArgs &a) {
   // grid-stride over groups of RPC rows: a resident-sized grid (few CTAs, so that the step
   // ticket of sr_step_arrive costs one atomic per resident CTA)
   constexpr int RPC = CTA / RT;
@@ -538,7 +552,11 @@ static int quant_rows_dispatch(const QuantArgs &a, cudaStream_t s) {
     // CTAs per SM that stay resident (the kernels' launch bounds: 4 up to two chunks a thread)
     const unsigned resident = static_cast<unsigned>(sms) * resident_ctas(cfg.vpt);
     const unsigned groups = row_grid(a.rows, cfg.rt);
-    RT_DISPATCH_ROW(cfg, quant_rows_kernel, T, groups < resident ? groups : resident, a);
+    const unsigned grid = groups < resident ? groups : resident;
+    if (sizeof(T) == 4 && cfg.vpt <= 2)
+      RT_DISPATCH_ROW(cfg, quant_rows_f32_kernel, T, grid, a);
+    else
+      RT_DISPATCH_ROW(cfg, quant_rows_kernel, T, grid, a);
   } else {
     launch_k(quant_rows_generic_kernel<T>, static_cast<unsigned>(a.rows), CTA, 0, s, a);
   }
