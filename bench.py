@@ -3,7 +3,7 @@
 
     python bench.py --gpus N --steps K --warmup W [--impl ours|reference] [--workload 25m]
 
-Prints ONE JSON line (rank 0).  Workloads (BASELINE configs):
+Prints ONE JSON line (rank 0).  Workloads:
   25m  ratchet decoder d512 L8 H8 MLP2048 vocab 8192 block 512 batch 32 (16,384 tokens/step),
        quinary codes, matmul_mode=int8, int8_backward; embeddings/RMSNorm fp32 with AdamW.
 Synthetic data: uint16 token ids uniform in [0, 8192) from a fixed seed, random-init weights.

@@ -1,4 +1,4 @@
-"""Kernel microbenchmarks of the ratchet-linear hot path (BASELINE configs 2 and 3).
+"""Kernel microbenchmarks of the ratchet-linear hot path (the 25M model's layer shapes).
 
     python -m local_ai_training_b200.kernel_bench all              # every kernel, three shapes
     python -m local_ai_training_b200.kernel_bench gradw --m 16384 --n 1536 --k 512 --reps 3
@@ -25,7 +25,7 @@ from .int8_matmul import (
     grad_weight_bf16,
 )
 
-SHAPES = [(512, 512), (512, 2048), (2048, 512)]  # (K in, N out) of BASELINE configs 2/3
+SHAPES = [(512, 512), (512, 2048), (2048, 512)]  # (K in, N out) of the 25M model's ratchet layers
 
 
 def _peaks() -> dict:

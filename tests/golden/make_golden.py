@@ -13,7 +13,7 @@ Fixtures (npz):
                        tests/test_ratchet.py:196-208 (seed 1234, 6x8, 60 steps, max_code 2/3/4)
   update_random.npz    _normalize + _ratchet_update_core (ratchet.py:265-301, 539-556) on random
                        states and gradients, several shapes / max_code / thresholds / EMA
-  config1.npz          BASELINE config 1: one 256x256 quinary fused-backward layer, fp32, 10 steps
+  config1.npz          single-layer case: one 256x256 quinary fused-backward layer, fp32, 10 steps
   model_tiny.npz       RatchetGPT (model.py) fp32 tiny config, one train step
 """
 
@@ -143,7 +143,7 @@ def update_random(ref) -> None:
 
 
 def config1(ref) -> None:
-    """X[512,256] ~N(0,1); quinary codes uniform {-2..2} [256,256]; scales
+    """Single-layer case: X[512,256] ~N(0,1); quinary codes uniform {-2..2} [256,256]; scales
     U(0.01,0.05); pressure 0; grad_out [512,256] ~N(0,1e-2); seed 1337; 10 update steps."""
     rt = ref["ratchet"]
     torch.manual_seed(1337)

@@ -2,7 +2,7 @@
 
 Bars: bit-exact for integer/byte outputs, quantised values, row scales and bf16-rounded GEMM
 outputs; grad_weight (fp32 accumulation in tensor-core order) within 1e-5 relative Frobenius of a
-double-precision sum (the north-star gate is 1e-2).  Full BASELINE sizes are checked through exact
+double-precision sum (the north-star gate is 1e-2).  Full benchmark sizes are checked through exact
 integer arithmetic on the device (int32 sums of int8 products are exact in fp32 below 2^24).
 """
 
@@ -201,7 +201,7 @@ def test_scaled_int8_mm_residual_epilogue(cuda_device, m, k, n, pad, inplace):
 @pytest.mark.parametrize("bound", [0, 7])
 @pytest.mark.parametrize("k,n", [(512, 512), (512, 2048), (2048, 512), (4096, 256)])
 def test_scaled_int8_mm_full_size_exact(cuda_device, k, n, bound):
-    """BASELINE config 2 shapes, M = 16384: exact integer sums on the device as the checker;
+    """The 25M model's layer shapes, M = 16384: exact integer sums on the device as the checker;
     bound = 7 (the codes' bound) takes the 2-op accumulator conversion up to K·128·7 < 2^22."""
     from local_ai_training_b200.int8_matmul import _scaled_int8_mm_into, quantize_rows
 

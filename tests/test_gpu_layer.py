@@ -195,7 +195,7 @@ def test_zero_gradient_stays_finite_and_nonfinite_raises(cuda_device):
 
 
 def test_config1_layer_step_matches_reference_trajectory(cuda_device):
-    """BASELINE config 1 on the GPU layer (fp32 mode, fused backward, 10 steps): the packed state
+    """The single-layer case on the GPU layer (fp32 mode, fused backward, 10 steps): the packed state
     after every step equals the reference's up to reduction-order boundary flips."""
     from local_ai_training_b200 import DiscreteRatchetLinear, pack_code_pressure
 

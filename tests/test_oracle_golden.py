@@ -160,7 +160,7 @@ def test_normalised_update_matches_reference(idx):
 
 
 def test_config1_trajectory_counts_match_reference():
-    """BASELINE config 1 (fp32 layer, 10 fused steps): the oracle's update fed with the fp32
+    """The single-layer case (fp32 layer, 10 fused steps): the oracle's update fed with the fp32
     grad_weight of each step reproduces the reference's packed trajectory."""
     g = load_golden("config1.npz")
     x, grad_out, scale = g["x"], g["grad_out"], g["scale"]
