@@ -1,12 +1,19 @@
 #!/usr/bin/env python
 """Throughput benchmark of the ratchet train step on B200 (one process per GPU).
 
-    python bench.py --gpus N --steps K --warmup W [--impl ours|reference] [--workload 25m]
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference] [--workload 1b|25m]
 
-Prints ONE JSON line (rank 0).  Workloads:
-  25m  ratchet decoder d512 L8 H8 MLP2048 vocab 8192 block 512 batch 32 (16,384 tokens/step),
-       quinary codes, matmul_mode=int8, int8_backward; embeddings/RMSNorm fp32 with AdamW.
-Synthetic data: uint16 token ids uniform in [0, 8192) from a fixed seed, random-init weights.
+Prints ONE JSON line (rank 0).  Workloads (synthetic uint16 token ids, uniform in [0, 8192),
+from a fixed seed; random-init weights of the architecture):
+  1b   (default) ratchet decoder d2048 L20 H16 MLP8192 vocab 8192 block 1024, septenary codes,
+       GLOBAL batch 256 sequences (262,144 tokens) at every N: each of the N ranks takes 256/N
+       sequences as micro-batches of 16 whose grad_W accumulate, then one update per step --
+       bf16 grad_W reduce-scattered by output-row ownership, rank-local update, all-gather of
+       the int8 code|pressure bytes.  Fixed global batch: strong scaling.
+  25m  ratchet decoder d512 L8 H8 MLP2048 vocab 8192 block 512, batch 32 sequences per rank
+       (16,384 tokens), quinary codes (weak scaling).  At N = 1 the 1b line also carries this
+       workload's measurement under "workloads".
+Both: matmul_mode=int8, int8_backward; embeddings/RMSNorm fp32 with AdamW.
 
 value  tokens/s with the token batch resident on the device, timed with CUDA events between a
        barrier + synchronize on both sides, max over ranks.
@@ -14,6 +21,7 @@ e2e    the same step through the public API with the batch copied every step fro
        memory and the loss copied back to pinned host memory.
 roofline  the library kernel family with the largest share of device time in the timed region:
        algorithmic bytes (or flops) per launch / mean launch time (CUDA events on its stream).
+collectives  (N > 1) time the compute stream waited per step for each collective group.
 cpu_baseline  the CPU restatement of the reference's fp32 eager step (oracle/model_fp32.py) on
        this host's cores over a bounded token sample (rank 0, N = 1).
 --impl reference  times that same CPU step as the reference arm.
@@ -24,6 +32,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -35,10 +44,22 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 WORKLOADS = {
+    "1b": dict(name="ratchet-decoder-1b", n_embd=2048, n_layer=20, n_head=16, vocab=8192,
+               block=1024, global_batch=256, micro_batch=16, max_code=3, seed=1338,
+               ref_batch=1, ref_seq=256),
     "25m": dict(name="ratchet-decoder-25m", n_embd=512, n_layer=8, n_head=8, vocab=8192, block=512,
-                batch=32, max_code=2, seed=1337, ref_batch=2),
+                batch_per_rank=32, micro_batch=32, max_code=2, seed=1337, ref_batch=2,
+                ref_seq=512),
 }
 METRIC = "ratchet train-step tokens/s"
+
+
+def sequences_per_rank(wl: dict, world: int) -> int:
+    if "global_batch" in wl:
+        if wl["global_batch"] % world:
+            raise SystemExit(f"global batch {wl['global_batch']} is not divisible by {world} ranks")
+        return wl["global_batch"] // world
+    return wl["batch_per_rank"]
 
 
 # DRAM bytes (read + write) that ncu measured for one launch of a family's kernel, and that
@@ -47,15 +68,18 @@ METRIC = "ratchet train-step tokens/s"
 # this ratio times the family's mean algorithmic bytes per launch (traffic grows in proportion
 # with the rows processed).  Below 1: outputs still resident in L2 when the kernel ends.
 NCU_TRAFFIC = {
-    "gemm_i8": ((9.59e6 + 9.11e6), 76.6e6, "profiles/gemm_i8_fwd_16384x512x2048.md"),
-    "quant_rows_sr": ((67.15e6 + 7.62e6), 100.7e6, "profiles/quant_rows_sr_bf16_16384x2048.md"),
+    ("gemm_i8", "ratchet-decoder-25m"): ((9.59e6 + 9.11e6), 76.6e6,
+                                         "profiles/gemm_i8_fwd_16384x512x2048.md"),
+    ("quant_rows_sr", "ratchet-decoder-25m"): ((67.15e6 + 7.62e6), 100.7e6,
+                                               "profiles/quant_rows_sr_bf16_16384x2048.md"),
 }
 
 
-def _traffic(family: str, bytes_per_launch: float) -> tuple[float | None, str | None]:
-    if family not in NCU_TRAFFIC:
+def _traffic(family: str, workload: str, bytes_per_launch: float) -> tuple[float | None, str | None]:
+    key = (family, workload)
+    if key not in NCU_TRAFFIC:
         return None, None
-    measured, algorithmic, source = NCU_TRAFFIC[family]
+    measured, algorithmic, source = NCU_TRAFFIC[key]
     return round(measured / algorithmic * bytes_per_launch), source
 
 
@@ -134,8 +158,20 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU baseline
-def cpu_reference_steps(wl: dict, batch: int, steps: int, warmup: int) -> dict:
-    """Times the CPU fp32 restatement of the reference step (oracle/model_fp32.py)."""
+def cpu_model_name() -> str:
+    """The host CPU's model name (lscpu / /proc/cpuinfo)."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor() or "unknown"
+
+
+def cpu_reference_steps(wl: dict, steps: int, warmup: int) -> dict:
+    """Times the CPU fp32 restatement of the reference step (oracle/model_fp32.py) on a sample
+    of ref_batch x ref_seq tokens of the workload's model."""
     import torch
 
     from oracle.model_fp32 import Config, build_seeded, train_step
@@ -147,33 +183,41 @@ def cpu_reference_steps(wl: dict, batch: int, steps: int, warmup: int) -> dict:
     model = build_seeded(cfg, wl["seed"]).train()
     opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.0)
     gen = torch.Generator().manual_seed(wl["seed"])
-    tokens = torch.randint(0, wl["vocab"], (batch, wl["block"] + 1), generator=gen)
+    batch, seq = wl["ref_batch"], wl["ref_seq"]
+    tokens = torch.randint(0, wl["vocab"], (batch, seq + 1), generator=gen)
     for _ in range(warmup):
         train_step(model, opt, tokens)
     t0 = time.perf_counter()
     for _ in range(steps):
         train_step(model, opt, tokens)
     dt = time.perf_counter() - t0
-    tokens_per_step = batch * wl["block"]
+    tokens_per_step = batch * seq
     return {"value": tokens_per_step * steps / dt, "unit": "tokens/s", "cores": threads,
-            "seconds_per_step": dt / steps, "tokens_per_step": tokens_per_step}
+            "seconds_per_step": dt / steps, "tokens_per_step": tokens_per_step,
+            "cpu_model": cpu_model_name()}
 
 
-def run_reference(args, wl: dict, rank: int) -> None:
+def _sample_text(wl: dict, steps: int) -> str:
+    return (f"{wl['ref_batch']} x {wl['ref_seq']} tokens per step of the {wl['name']} model "
+            f"(fp32 eager restatement of the reference step: fused ratchet update of every "
+            f"layer, AdamW), {steps} timed steps")
+
+
+def run_reference(args, wl: dict, rank: int, world: int) -> None:
     if rank != 0:
         return
-    res = cpu_reference_steps(wl, wl["ref_batch"], args.steps, args.warmup)
-    sample = (f"{wl['ref_batch']} x {wl['block']} tokens per step of the {wl['name']} config "
-              f"(fp32 eager, fused ratchet update, AdamW), {args.steps} timed steps")
+    res = cpu_reference_steps(wl, args.steps, args.warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": res["value"], "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": res["seconds_per_step"] * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong" if "global_batch" in wl else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
         "config": {"workload": wl["name"], "tokens_per_step": res["tokens_per_step"],
-                   "sample_of": f"batch {wl['batch']} x {wl['block']}"},
+                   "sample_of": f"{sequences_per_rank(wl, world) * world} x {wl['block']} tokens"},
         "cpu_baseline": {"value": res["value"], "unit": "tokens/s", "cores": res["cores"],
-                         "kind": "port", "sample": sample},
+                         "cpu_model": res["cpu_model"], "kind": "port",
+                         "sample": _sample_text(wl, args.steps)},
         "e2e": {"value": res["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -229,57 +273,57 @@ def summarize_profile(profile: dict, steps: int) -> dict:
     return fams
 
 
-def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
+def measure(args, wl: dict, rank: int, local_rank: int, world: int, *, steps: int,
+            profile_steps: int, sample_clocks: bool) -> dict:
+    """Builds the workload's model on this rank's GPU and times its train step: resident
+    tokens (`value`), end to end from pinned host memory (`e2e`), and per library call (profile
+    pass).  Returns the raw measurements; rank 0 formats them."""
     import torch
     import torch.distributed as dist
 
     from local_ai_training_b200 import ModelConfig, _lib, build_seeded_model
+    from local_ai_training_b200.dist import RatchetDataParallel
 
-    torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
-    if world > 1:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     config = ModelConfig(vocab_size=wl["vocab"], block_size=wl["block"], n_layer=wl["n_layer"],
                          n_head=wl["n_head"], n_embd=wl["n_embd"], dropout=0.0,
                          matmul_mode="int8", int8_backward=True)
     model = build_seeded_model(config, max_code=wl["max_code"], seed=wl["seed"]).to(device).train()
     for layer in model.ratchet_layers():
-        layer.sr_seed = wl["seed"] + 7 * (rank + 1)
+        layer.sr_seed = wl["seed"] + 7
     opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.0, fused=True,
                             capturable=True)
+    seqs = sequences_per_rank(wl, world)
+    mb = min(wl["micro_batch"], seqs)
+    if seqs % mb:
+        raise SystemExit(f"{seqs} sequences per rank are not a multiple of micro-batch {mb}")
+    micro = seqs // mb
+    # deferred grouped updates after backward, grad_W accumulated over the micro-batches, and
+    # (N > 1) reduce-scatter by owned rows, owner update, all-gather of the packed bytes
+    ddp = RatchetDataParallel(model, bucket_layers=args.dp_bucket_layers, accumulation_steps=micro)
     gen = torch.Generator().manual_seed(wl["seed"] + rank)
-    batch, block = wl["batch"], wl["block"]
-    host_tokens = torch.randint(0, wl["vocab"], (batch, block + 1), generator=gen,
+    block = wl["block"]
+    host_tokens = torch.randint(0, wl["vocab"], (seqs, block + 1), generator=gen,
                                 dtype=torch.int64).to(torch.int16).pin_memory()
     dev_tokens16 = torch.empty(host_tokens.shape, device=device, dtype=torch.int16)
     dev_tokens16.copy_(host_tokens)
-    tokens_resident = dev_tokens16.long()
     loss_host = torch.zeros(1, dtype=torch.float32).pin_memory()
 
-    ddp = None
-    if world > 1:
-        # data parallel: reduce-scatter of bf16 grad_W by owned rows during backward, rank-local
-        # update, all-gather of the owned packed rows, averaged support gradients
-        from local_ai_training_b200.dist import RatchetDataParallel
+    def step():
+        tokens = dev_tokens16.long()  # uint16 ids widened on the device
+        losses = []
+        for i in range(micro):
+            chunk = tokens[i * mb:(i + 1) * mb]
+            with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+                _, loss = model(chunk[:, :-1], chunk[:, 1:])
+            loss.backward()
+            losses.append(loss.detach())
+        ddp.step(opt)  # support sync, owned-row updates, AdamW, re-replication
+        return losses[0] if micro == 1 else torch.stack(losses).mean()
 
-        ddp = RatchetDataParallel(model, bucket_layers=args.dp_bucket_layers)
-
-    def step(tokens):
-        with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
-            _, loss = model(tokens[:, :-1], tokens[:, 1:])
-        loss.backward()
-        if ddp is None:
-            model.ratchet_update(validate=False)
-            opt.step()
-        else:
-            ddp.step(opt)  # support all-reduce, owned-row updates, AdamW, re-replication
-        return loss
-
-    def eager_step(tokens):
+    def eager_step():
         opt.zero_grad(set_to_none=True)
-        return step(tokens)
+        return step()
 
     def barrier():
         if world > 1:
@@ -287,21 +331,21 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
         torch.cuda.synchronize()
 
     # warm-up (eager, on a side stream as graph capture requires), then capture one whole step:
-    # token widening, forward, backward with the fused ratchet updates, AdamW.
+    # token widening, every micro-batch's forward and backward, the updates, AdamW, collectives
     side = torch.cuda.Stream(device)
     side.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(side):
         for _ in range(args.warmup):
-            eager_step(tokens_resident)
+            eager_step()
     torch.cuda.current_stream(device).wait_stream(side)
     barrier()
-    graph, graph_error = None, None
+    graph, graph_error, static_loss = None, None, None
     if not args.no_graph:
         try:
             opt.zero_grad(set_to_none=True)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                static_loss = step(dev_tokens16.long())
+                static_loss = step()
             for _ in range(2):
                 graph.replay()
             barrier()
@@ -315,13 +359,13 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
         if graph is not None:
             graph.replay()
             return static_loss
-        return eager_step(dev_tokens16.long())
+        return eager_step()
 
-    def timed(fn) -> float:
+    def timed(fn, n) -> float:
         barrier()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-        for _ in range(args.steps):
+        for _ in range(n):
             fn()
         end.record()
         barrier()
@@ -331,10 +375,10 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
         return float(el.item())
 
     # ---- A: batch resident in HBM
-    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    sampler = ClockSampler(list(range(world))) if (rank == 0 and sample_clocks) else None
     if sampler:
         sampler.start()
-    elapsed = timed(run_step)
+    elapsed = timed(run_step, steps)
     clocks = sampler.stop() if sampler else None
 
     # ---- B: end to end, batch copied from pinned host memory, loss copied back every step
@@ -343,7 +387,7 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
         loss = run_step()
         loss_host.copy_(loss.detach().float().reshape(1), non_blocking=True)
 
-    e_elapsed = timed(e2e_step)
+    e_elapsed = timed(e2e_step, steps)
 
     # ---- C: CUDA events around every library call.  Preferred: a second captured graph whose
     # event-record nodes re-time each call on every replay (no launch gaps); otherwise eager steps.
@@ -355,12 +399,12 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
         _lib.PROFILE, _lib.PROFILE_EXTERNAL = {}, True
         pgraph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(pgraph, pool=graph.pool()):
-            step(dev_tokens16.long())
+            step()
         template, _lib.PROFILE = _lib.PROFILE, None
         barrier()
         pstart, pend = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         p_elapsed = 0.0
-        for _ in range(args.steps):
+        for _ in range(profile_steps):
             pstart.record()
             pgraph.replay()
             pend.record()
@@ -374,115 +418,185 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
         profile_mode = f"eager ({type(exc).__name__})"
         fams_acc = {}
         _lib.PROFILE, _lib.PROFILE_EXTERNAL = {}, False
-        p_elapsed = timed(lambda: eager_step(tokens_resident))
+        p_elapsed = timed(eager_step, profile_steps)
         for name, entries in _lib.PROFILE.items():
             fams_acc[name] = [(st.elapsed_time(en) / 1e3, fl, nb) for st, en, fl, nb in entries]
         _lib.PROFILE = None
     _lib.PROFILE_EXTERNAL = False
     status |= _lib.device_status(device, clear=True)
 
-    tokens_per_step = batch * block * world
-    fams = summarize_profile(fams_acc, args.steps)
-    gpu_launches = sum(f["launches"] for f in fams.values())  # library kernels per K steps
-
-    peak_info = int8_peak_probe(torch, device) if rank == 0 and not args.no_peak_probe else {}
+    replicas = None
+    if world > 1:  # the replicated state must agree on every rank after the timed steps
+        ck = ddp.state_checksum()
+        lo, hi = ck.clone(), ck.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        replicas = bool(torch.equal(lo, hi))
+    peak_mem = torch.cuda.max_memory_allocated(device)
     used_graph = graph is not None
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
-        graph = None  # a graph holding NCCL work is released before the group goes
-        torch.cuda.synchronize()
-        dist.destroy_process_group()
-    if rank != 0:
-        return
+    graph = None  # a graph holding NCCL work is released before the process group goes
+    del model, opt, ddp
+    torch.cuda.synchronize()
+    return {
+        "elapsed": elapsed, "e_elapsed": e_elapsed, "p_elapsed": p_elapsed, "steps": steps,
+        "profile_steps": profile_steps, "profile_mode": profile_mode,
+        "fams": summarize_profile(fams_acc, profile_steps), "clocks": clocks,
+        "status": status, "graph": used_graph, "graph_error": graph_error,
+        "tokens_per_step": seqs * block * world, "sequences_per_rank": seqs,
+        "micro_batch": mb, "micro_batches": micro,
+        "h2d": host_tokens.numel() * host_tokens.element_size(), "replicas_agree": replicas,
+        "peak_mem_gb": round(peak_mem / 1e9, 2),
+    }
 
-    peaks = _load_peaks()
+
+def kernel_report(res: dict, workload: str, peaks: dict, int8_peak: float,
+                  int8_peak_source: str) -> dict:
+    """Per-family table, the dominant family's roofline and the collectives' waits."""
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
     bf16_peak = peaks.get("bf16_tflops", 1590.0)
-    int8_peak = max(v for v in (peak_info.get("ours_tops"), peak_info.get("cublas_int_mm_tops"), 0.0)
-                    if v is not None)
-    int8_peak_source = "measured in this run (int8 GEMM probe)"
-    if not int8_peak:  # probe skipped: nominal dense int8 of the part
-        int8_peak, int8_peak_source = 4500.0, "nominal dense int8 (probe skipped)"
-    dominant = max(fams, key=lambda k: fams[k]["total_s"])
+    steps = res["profile_steps"]
+    fams = {k: v for k, v in res["fams"].items() if not k.startswith("comm_")}
+    comm = {k[len("comm_"):]: v for k, v in res["fams"].items() if k.startswith("comm_")}
     kernels = {}
     for name, f in sorted(fams.items(), key=lambda kv: -kv[1]["total_s"]):
         mean_s = f["mean_us"] / 1e6
         gbs = f["bytes_per_launch"] / mean_s / 1e9
+        t_mem = f["bytes_per_launch"] / (hbm_peak * 1e9)
         entry = {"launches_per_step": f["launches_per_step"], "mean_us": round(f["mean_us"], 2),
-                 "share_of_step": round(f["total_s"] / p_elapsed, 4),
+                 "share_of_step": round(f["total_s"] / res["p_elapsed"], 4),
                  "GB_per_s": round(gbs, 1), "hbm_frac": round(gbs / hbm_peak, 3)}
+        t_bound = t_mem
         if f["flops_per_launch"] > 0:
             tf = f["flops_per_launch"] / mean_s / 1e12
+            peak = int8_peak if name == "gemm_i8" else bf16_peak
+            t_bound = max(t_mem, f["flops_per_launch"] / (peak * 1e12))
             entry["TFLOP_per_s"] = round(tf, 1)
             if name == "gemm_i8":
                 entry["int8_frac_datasheet_4500"] = round(tf / 4500.0, 3)
                 entry["int8_frac_measured"] = round(tf / int8_peak, 3) if int8_peak else None
             else:
                 entry["bf16_frac_measured"] = round(tf / bf16_peak, 3)
+        # the fraction of the binding roofline: max(flops / tensor peak, bytes / HBM) over time
+        entry["binding_frac"] = round(t_bound / mean_s, 3)
         kernels[name] = entry
+    dominant = max(fams, key=lambda k: fams[k]["total_s"])
     d = fams[dominant]
     mean_s = d["mean_us"] / 1e6
-    # The bound of the dominant family: its arithmetic intensity against the ridge point.
+    traffic, source = _traffic(dominant, workload, d["bytes_per_launch"])
+    tensor = False
     if d["flops_per_launch"] > 0:
         tensor_peak = int8_peak if dominant == "gemm_i8" else bf16_peak
-        t_compute = d["flops_per_launch"] / (tensor_peak * 1e12)
-        t_memory = d["bytes_per_launch"] / (hbm_peak * 1e9)
-        if t_compute >= t_memory:
-            achieved = d["flops_per_launch"] / mean_s / 1e12
-            roofline = {"kernel": dominant, "bound": "tensor", "achieved": round(achieved, 1),
-                        "peak": round(tensor_peak, 1), "unit": "TFLOP/s",
-                        "frac": round(achieved / tensor_peak, 3),
-                        "traffic": _traffic(dominant, d["bytes_per_launch"])[0],
-                        "traffic_source": _traffic(dominant, d["bytes_per_launch"])[1],
-                        "peak_source": int8_peak_source if dominant == "gemm_i8"
-                        else "MEASURED_PEAKS.json bf16_tflops"}
-        else:
-            achieved = d["bytes_per_launch"] / mean_s / 1e9
-            roofline = {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 1),
-                        "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 3),
-                        "traffic": _traffic(dominant, d["bytes_per_launch"])[0],
-                        "traffic_source": _traffic(dominant, d["bytes_per_launch"])[1],
-                        "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
+        tensor = d["flops_per_launch"] / (tensor_peak * 1e12) >= d["bytes_per_launch"] / (hbm_peak * 1e9)
+    if tensor:
+        achieved = d["flops_per_launch"] / mean_s / 1e12
+        roofline = {"kernel": dominant, "bound": "tensor", "achieved": round(achieved, 1),
+                    "peak": round(tensor_peak, 1), "unit": "TFLOP/s",
+                    "frac": round(achieved / tensor_peak, 3),
+                    "peak_source": int8_peak_source if dominant == "gemm_i8"
+                    else "MEASURED_PEAKS.json bf16_tflops (of measured)"}
     else:
         achieved = d["bytes_per_launch"] / mean_s / 1e9
         roofline = {"kernel": dominant, "bound": "hbm", "achieved": round(achieved, 1),
                     "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 3),
-                    "traffic": _traffic(dominant, d["bytes_per_launch"])[0],
-                    "traffic_source": _traffic(dominant, d["bytes_per_launch"])[1],
-                    "peak_source": "MEASURED_PEAKS.json hbm_gbs"}
+                    "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"}
+    roofline.update({"traffic": traffic, "traffic_source": source,
+                     "algorithmic_bytes_per_launch": round(d["bytes_per_launch"]),
+                     "algorithmic_flops_per_launch": d["flops_per_launch"],
+                     "mean_launch_us": round(d["mean_us"], 2)})
+    collectives = {name: {"waits_per_step": c["launches_per_step"],
+                          "exposed_ms_per_step": round(c["total_s"] / steps * 1e3, 3)}
+                   for name, c in comm.items()}
+    launches = sum(f["launches"] for f in fams.values()) / steps
+    return {"kernels": kernels, "roofline": roofline, "collectives": collectives,
+            "launches_per_step": launches}
+
+
+def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    big = wl["name"] == WORKLOADS["1b"]["name"]
+    res = measure(args, wl, rank, local_rank, world, steps=args.steps,
+                  profile_steps=min(args.steps, 3) if big else args.steps, sample_clocks=True)
+    secondary = None
+    if world == 1 and big and not args.no_secondary:
+        torch.cuda.empty_cache()
+        secondary = measure(args, WORKLOADS["25m"], rank, local_rank, world, steps=args.steps,
+                            profile_steps=args.steps, sample_clocks=False)
+    peak_info = int8_peak_probe(torch, device) if rank == 0 and not args.no_peak_probe else {}
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks = _load_peaks()
+    int8_peak = max([v for v in (peak_info.get("ours_tops"), peak_info.get("cublas_int_mm_tops"))
+                     if v is not None] or [0.0])
+    int8_peak_source = "measured in this run (best 8192^3 int8 GEMM: ours or torch._int_mm)"
+    if not int8_peak:  # probe skipped: nominal dense int8 of the part
+        int8_peak, int8_peak_source = 4500.0, "nominal dense int8 (probe skipped)"
+    rep = kernel_report(res, wl["name"], peaks, int8_peak, int8_peak_source)
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        res = cpu_reference_steps(wl, wl["ref_batch"], steps=2, warmup=1)
-        cpu = {"value": res["value"], "unit": "tokens/s", "cores": res["cores"], "kind": "port",
-               "sample": (f"{wl['ref_batch']} x {wl['block']} tokens per step, 2 timed steps of the "
-                          f"same config, fp32 eager CPU restatement of the reference step")}
-    value = tokens_per_step * args.steps / elapsed
-    h2d = host_tokens.numel() * host_tokens.element_size()
+        c = cpu_reference_steps(wl, steps=2, warmup=1)
+        cpu = {"value": c["value"], "unit": "tokens/s", "cores": c["cores"],
+               "cpu_model": c["cpu_model"], "kind": "port", "sample": _sample_text(wl, 2)}
+    tokens = res["tokens_per_step"]
     line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "metric": METRIC, "value": tokens * args.steps / res["elapsed"], "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": res["elapsed"] / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong" if "global_batch" in wl else "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic (uniform uint16 token ids, random-init weights)",
         "config": {"workload": wl["name"], "n_embd": wl["n_embd"], "n_layer": wl["n_layer"],
-                   "n_head": wl["n_head"], "vocab": wl["vocab"], "seq_len": block,
-                   "global_batch": batch * world, "codes": 2 * wl["max_code"] + 1,
-                   "matmul_mode": "int8", "int8_backward": True,
+                   "n_head": wl["n_head"], "vocab": wl["vocab"], "seq_len": wl["block"],
+                   "global_batch": res["sequences_per_rank"] * world,
+                   "micro_batch": res["micro_batch"], "micro_batches_per_rank": res["micro_batches"],
+                   "codes": 2 * wl["max_code"] + 1, "matmul_mode": "int8", "int8_backward": True,
                    "parallelism": f"dp{world}" if world > 1 else "single",
-                   "l2": "working set (activations, logits) far above the 126 MB L2"},
-        "e2e": {"value": tokens_per_step * args.steps / e_elapsed, "unit": "tokens/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
-        "roofline": roofline,
+                   "l2": "inputs larger than L2: working set (activations, logits) of many GB"},
+        "e2e": {"value": tokens * args.steps / res["e_elapsed"], "unit": "tokens/s",
+                "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": 4},
+        "roofline": rep["roofline"],
         "cpu_baseline": cpu,
-        "gpu_launches": gpu_launches,
-        "cuda_graph": used_graph,
-        "cuda_graph_error": graph_error,
-        "profile_pass": profile_mode,
-        "profile_ms_per_step": p_elapsed / args.steps * 1e3,
-        "clocks": clocks,
-        "int8_peak_probe_tops": {k: (round(v, 1) if isinstance(v, float) else v) for k, v in peak_info.items()},
-        "kernels": kernels,
-        "device_status": status,
+        "gpu_launches": int(round(rep["launches_per_step"] * args.steps)),
+        "cuda_graph": res["graph"],
+        "cuda_graph_error": res["graph_error"],
+        "profile_pass": res["profile_mode"],
+        "profile_ms_per_step": res["p_elapsed"] / res["profile_steps"] * 1e3,
+        "clocks": res["clocks"],
+        "int8_peak_probe_tops": {k: (round(v, 1) if isinstance(v, float) else v)
+                                 for k, v in peak_info.items()},
+        "kernels": rep["kernels"],
+        "collectives": rep["collectives"],
+        "replicas_agree": res["replicas_agree"],
+        "peak_mem_gb": res["peak_mem_gb"],
+        "device_status": res["status"],
     }
+    if secondary is not None:
+        srep = kernel_report(secondary, WORKLOADS["25m"]["name"], peaks, int8_peak,
+                             int8_peak_source)
+        sw = WORKLOADS["25m"]
+        line["workloads"] = {sw["name"]: {
+            "value": secondary["tokens_per_step"] * args.steps / secondary["elapsed"],
+            "unit": "tokens/s", "ms_per_step": secondary["elapsed"] / args.steps * 1e3,
+            "e2e": {"value": secondary["tokens_per_step"] * args.steps / secondary["e_elapsed"],
+                    "unit": "tokens/s", "h2d_bytes_per_step": secondary["h2d"],
+                    "d2h_bytes_per_step": 4},
+            "global_batch": secondary["sequences_per_rank"], "seq_len": sw["block"],
+            "codes": 2 * sw["max_code"] + 1, "cuda_graph": secondary["graph"],
+            "roofline": srep["roofline"], "kernels": srep["kernels"],
+            "gpu_launches_per_step": srep["launches_per_step"],
+            "device_status": secondary["status"]}}
     print(json.dumps(line), flush=True)
 
 
@@ -492,7 +606,9 @@ def main() -> None:
     parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="25m")
+    parser.add_argument("--workload", choices=sorted(WORKLOADS), default="1b")
+    parser.add_argument("--no-secondary", action="store_true",
+                        help="N = 1, workload 1b: skip the 25m measurement carried in the line")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-graph", action="store_true", help="time eager steps (no CUDA graph)")
     parser.add_argument("--dp-bucket-layers", type=int, default=4,
@@ -507,7 +623,7 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
-        run_reference(args, wl, rank)
+        run_reference(args, wl, rank, world)
         return
     run_ours(args, wl, rank, local_rank, world)
 

@@ -141,14 +141,30 @@ int64_t rt_grad_weight_update_workspace_bytes(int64_t M_tok, int64_t rows, int64
  * synchronise the device in the middle of a step) or that have budgeted all HBM to resident
  * state.  The split-K partial tiles live in a 20 MiB device array of this library (one copy per
  * device); shapes whose workspace (rt_grad_weight_workspace_bytes) exceeds it fail with
- * RT_ERR_UNSUPPORTED.  The first call on each device looks up that array's address with the
- * device current; make it before any stream capture.  Nothing in the array needs to start at
- * zero (every partial tile is written before it is read, within a call).  All calls on one device share the array: calls that overlap on the GPU
+ * RT_ERR_UNSUPPORTED (on B200, 148 SMs, no shape needs more than 18.5 MiB, so this only happens on
+ * parts with more than 160 SMs).  The array's address belongs to one CUDA context: the first call
+ * in each context (a device's primary context, a context created after cudaDeviceReset, or any
+ * other context the host makes current) looks it up with that context current and caches it
+ * under the context's unique id; make that first call before any stream capture.  Nothing in the
+ * array needs to start at zero (every partial tile is written before it is read, within a call).
+ * All calls on one device share the array: calls that overlap on the GPU
  * (different streams, no ordering between them) race and give wrong results.  Results equal
  * rt_grad_weight_bf16 with a workspace of rt_grad_weight_workspace_bytes bytes. */
 int rt_grad_weight_bf16_noalloc(const void *g, int64_t ldg, const void *x, int64_t ldx, void *out,
                                 int out_dtype, int64_t ldo, int64_t M_tok, int64_t N, int64_t K,
                                 int accumulate, void *stream);
+
+/* rt_grad_weight_bf16 adding a float32 matrix: out[n,k] = round(addend[n,k] + sum_m g[m,n]*x[m,k])
+ * in out_dtype (float32 or bfloat16), addend row stride ld_addend; addend may be `out` itself
+ * when out is float32.  For gradient accumulation over micro-batches (no counterpart in the
+ * reference, which takes one batch per update): earlier micro-batches accumulate their grad_W
+ * in float32, and the last one writes the bf16-rounded total straight into the buffer that is
+ * reduce-scattered or updated -- the reference's bf16 rounding of the GEMM output
+ * (ratchet.py:162-163) then happens once, on the accumulated sum. */
+int rt_grad_weight_bf16_add(const void *g, int64_t ldg, const void *x, int64_t ldx,
+                            const float *addend, int64_t ld_addend, void *out, int out_dtype,
+                            int64_t ldo, int64_t M_tok, int64_t N, int64_t K, void *workspace,
+                            int64_t workspace_bytes, void *stream);
 
 /* Dequantises saved int8 activations: out[m,k] = bf16(bf16(q[m,k]) * bf16(s[m]))
  * (ratchet.py:73-76). */
@@ -177,6 +193,34 @@ int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf16, int64_t 
                       int normalize, float *rms_ema, double ema_beta, int max_code, int threshold,
                       double bucket_low, double bucket_high, double eps, int64_t *counts,
                       float *row_rms, float *rms_sum, float *grad_scale, void *stream);
+
+/* One layer of a grouped update (rt_ratchet_update_grouped). */
+typedef struct rt_update_layer {
+  const void *grad;   /* (rows, cols) gradient in the group's dtype, row stride ldg elements */
+  int64_t ldg;
+  int64_t rows;
+  uint8_t *packed;    /* updated in place, row stride ldp */
+  int64_t ldp;
+  int8_t *code_out;   /* optional: receives the new int8 codes, row stride ldc */
+  int64_t ldc;
+  float *rms_ema;     /* optional (rows), used when ema_beta > 0 */
+  int64_t *counts;    /* int64[4] move counters of the layer, accumulated */
+  float *rms_sum;     /* optional: += sum of the layer's row rms values */
+  float grad_mul;     /* gradient multiplier applied after the optional bf16 rounding (1: none) */
+} rt_update_layer;
+
+/* rt_ratchet_update over many layers in as few launches as possible (one per 64 layers).
+ * Replaces the reference's per-layer update inside backward (ratchet.py:_capture_weight_gradient
+ * 487-537 called once per 256-row tile from _RatchetMatmul.backward, ratchet.py:150-169) after
+ * the whole backward: rows are independent, so updating every layer after backward gives the
+ * same state as updating each inside its own backward (each layer's grad_input has already
+ * read its codes).  All layers share cols, dtype and the ratchet parameters; per layer the
+ * result equals rt_ratchet_update on grad * grad_mul (normalize, round_bf16 as there; row_rms and
+ * grad_scale are not produced).  `layers` is host memory, read during the call. */
+int rt_ratchet_update_grouped(const rt_update_layer *layers, int n_layers, int grad_dtype,
+                              int round_bf16, int64_t cols, int normalize, double ema_beta,
+                              int max_code, int threshold, double bucket_low, double bucket_high,
+                              double eps, void *stream);
 
 /* Pressure leak: every nonzero pressure moves one unit toward zero (ratchet.py:613-625).
  * code_out, when given, is refreshed with the (unchanged) codes. */

@@ -52,6 +52,9 @@ _SIGNATURES = {
                                        _p, _i64, _p, _d, _i, _i, _d, _d, _d, _p, _p, _p, _p, _p],
                                       _i),
     "rt_grad_weight_update_workspace_bytes": ([_i64, _i64, _i64], _i64),
+    "rt_grad_weight_bf16_add": ([_p, _i64, _p, _i64, _p, _i64, _p, _i, _i64, _i64, _i64, _i64, _p,
+                                 _i64, _p], _i),
+    "rt_ratchet_update_grouped": ([_p, _i, _i, _i, _i64, _i, _d, _i, _i, _d, _d, _d, _p], _i),
     "rt_grad_weight_bf16_noalloc": ([_p, _i64, _p, _i64, _p, _i, _i64, _i64, _i64, _i64, _i, _p],
                                     _i),
     "rt_dequant_rows_bf16": ([_p, _i64, _p, _p, _i64, _i64, _i64, _p], _i),
@@ -76,6 +79,14 @@ _SIGNATURES = {
     "rt_cross_entropy_bwd": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _p,
                               _i64, _p], _i),
 }
+
+
+class UpdateLayer(ctypes.Structure):
+    """struct rt_update_layer of include/ratchet_b200.h (one layer of a grouped update)."""
+
+    _fields_ = [("grad", _p), ("ldg", _i64), ("rows", _i64), ("packed", _p), ("ldp", _i64),
+                ("code_out", _p), ("ldc", _i64), ("rms_ema", _p), ("counts", _p),
+                ("rms_sum", _p), ("grad_mul", ctypes.c_float)]
 
 
 def exported_symbols() -> list[str]:

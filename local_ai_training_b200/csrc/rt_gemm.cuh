@@ -44,6 +44,9 @@ struct GemmArgs {
   int tma_store;   // epilogue stages 32-row groups in shared memory and stores them with TMA
   int acc_small;   // int8: every |accumulator| < 2^22 (K·127·max|rhs| below it), 2-op conversion
   float *workspace;  // EPI_SPLIT: [splits][tiles][BM][BN] fp32 partial tiles
+  // EPI_F32_STORE / EPI_BF16_STORE: out = round(addend + result) (M x N fp32, ld_add), or null
+  const float *addend;
+  int64_t ld_add;
 };
 
 template <typename T>
@@ -192,6 +195,25 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &p, int epi, int r
         for (int j = 0; j < 32; ++j)
           if (n0 + j < p.N) o[j] = v[j];
       }
+    }
+    return;
+  }
+  if (p.addend != nullptr) {  // out = round(addend + result), fp32 or bf16
+    const float *ad = p.addend + static_cast<int64_t>(row) * p.ld_add + n0;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      v[j] = (n0 + j < p.N) ? __fadd_rn(__ldg(ad + j), acc_to_float<T>(r[j])) : 0.0f;
+    if (epi == EPI_BF16_STORE) {
+      uint16_t *o = static_cast<uint16_t *>(p.out) + static_cast<int64_t>(row) * p.ldo + n0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) o[j] = bf16_bits(v[j]);
+    } else {
+      float *o = static_cast<float *>(p.out) + static_cast<int64_t>(row) * p.ldo + n0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < p.N) o[j] = v[j];
     }
     return;
   }
@@ -660,7 +682,7 @@ __global__ void simt_scaled_i8_kernel(const int8_t *lhs, int64_t slm, int64_t sl
 
 __global__ void simt_gradw_kernel(const uint16_t *g, int64_t ldg, const uint16_t *x, int64_t ldx,
                                   void *out, int out_dtype, int64_t ldo, int64_t Mt, int64_t N,
-                                  int64_t K, int accumulate) {
+                                  int64_t K, int accumulate, const float *addend, int64_t ld_add) {
   pdl_wait();
   pdl_trigger();
   const int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
@@ -669,6 +691,7 @@ __global__ void simt_gradw_kernel(const uint16_t *g, int64_t ldg, const uint16_t
   float acc = 0.0f;
   for (int64_t m = 0; m < Mt; ++m)
     acc = __fadd_rn(acc, __fmul_rn(bf16_from_bits(g[m * ldg + n]), bf16_from_bits(x[m * ldx + k])));
+  if (addend != nullptr) acc = __fadd_rn(addend[n * ld_add + k], acc);
   if (out_dtype == RT_F32) {
     float *o = static_cast<float *>(out) + n * ldo + k;
     *o = accumulate ? __fadd_rn(*o, acc) : acc;
@@ -762,8 +785,9 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
                   static_cast<uint64_t>(BN) * 4, 32, 32);
     if (rc) return rc;
   } else {
-    args.tma_store = args.vec_store && (args.epi == EPI_SCALED || args.epi == EPI_BF16_STORE ||
-                                        (args.epi == EPI_F32_STORE && !args.accumulate));
+    args.tma_store = args.vec_store && args.addend == nullptr &&
+                     (args.epi == EPI_SCALED || args.epi == EPI_BF16_STORE ||
+                      (args.epi == EPI_F32_STORE && !args.accumulate));
   }
   if (args.tma_store && args.epi != EPI_SPLIT) {
     const size_t es = out_bf16 ? 2 : 4;
@@ -889,7 +913,7 @@ template <int BN>
 __global__ void __launch_bounds__(256)
     splitk_reduce_kernel(const float *__restrict__ ws, int splits, int tiles_m, int tiles_n,
                          int rows, int cols, void *out, int out_dtype, int64_t ldo,
-                         int accumulate, int vec_out) {
+                         int accumulate, int vec_out, const float *addend, int64_t ld_add) {
   pdl_wait();
   pdl_trigger();
   const int groups = (cols + 3) >> 2;
@@ -905,12 +929,20 @@ __global__ void __launch_bounds__(256)
     const int col = static_cast<int>(i - static_cast<int64_t>(row) * groups) * 4;
     const int tile = (row >> 7) * tiles_n + col / BN;
     const float *src = ws + (static_cast<int64_t>(tile) * 128 + (row & 127)) * BN + col % BN;
-    float4 v = __ldcs(reinterpret_cast<const float4 *>(src));
+    float4 v = splits > 0 ? __ldcs(reinterpret_cast<const float4 *>(src))
+                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll 4
     for (int sp = 1; sp < splits; ++sp) {
       const float4 f = __ldcs(reinterpret_cast<const float4 *>(src + sp * split_stride));
       v.x = __fadd_rn(v.x, f.x), v.y = __fadd_rn(v.y, f.y);
       v.z = __fadd_rn(v.z, f.z), v.w = __fadd_rn(v.w, f.w);
+    }
+    if (addend != nullptr) {  // out = round(addend + sum), the order of `accumulate`
+      const float *ad = addend + static_cast<int64_t>(row) * ld_add + col;
+      v.x = __fadd_rn(ad[0], v.x);
+      if (col + 1 < cols) v.y = __fadd_rn(ad[1], v.y);
+      if (col + 2 < cols) v.z = __fadd_rn(ad[2], v.z);
+      if (col + 3 < cols) v.w = __fadd_rn(ad[3], v.w);
     }
     const float r[4] = {v.x, v.y, v.z, v.w};
     if (out_dtype == RT_F32) {
@@ -961,11 +993,14 @@ extern "C" int64_t rt_grad_weight_workspace_bytes(int64_t M_tok, int64_t N, int6
   return static_cast<int64_t>(s) * tiles * GW_TILE_BYTES;
 }
 
-extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, int64_t ldx,
-                                   void *out, int out_dtype, int64_t ldo, int64_t M_tok, int64_t N,
-                                   int64_t K, int accumulate, void *workspace,
-                                   int64_t workspace_bytes, void *stream) {
+namespace rt {
+static int grad_weight_impl(const void *g, int64_t ldg, const void *x, int64_t ldx, void *out,
+                            int out_dtype, int64_t ldo, int64_t M_tok, int64_t N, int64_t K,
+                            int accumulate, const float *addend, int64_t ld_add, void *workspace,
+                            int64_t workspace_bytes, void *stream) {
   if (M_tok < 0 || N < 0 || K < 0) return fail(RT_ERR_INVALID_ARGUMENT, "grad_weight: shape");
+  if (addend != nullptr && accumulate)
+    return fail(RT_ERR_INVALID_ARGUMENT, "grad_weight: accumulate and an addend exclude each other");
   if (out_dtype != RT_F32 && out_dtype != RT_BF16)
     return fail(RT_ERR_DTYPE, "grad_weight: output must be float32 or bfloat16");
   if (out_dtype == RT_BF16 && accumulate)
@@ -977,6 +1012,13 @@ extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, in
     return fail(RT_ERR_ALIGNMENT, "grad_weight: workspace must be 256-byte aligned");
   cudaStream_t s = as_stream(stream);
   const size_t osz = out_dtype == RT_BF16 ? 2 : 4;
+  if (M_tok == 0 && addend != nullptr) {
+    // nothing to add: out = round(addend), through the split-K reduce with no splits read
+    launch_k(splitk_reduce_kernel<GW_BN>, 1u, 256, 0, s, static_cast<const float *>(nullptr), 0,
+             0, 0, static_cast<int>(N), static_cast<int>(K), out, out_dtype, ldo, 0, 0, addend,
+             ld_add);
+    return check_launch("splitk_reduce_kernel");
+  }
   if (M_tok == 0) {
     if (accumulate) return RT_OK;
     cudaError_t e = cudaMemset2DAsync(out, ldo * osz, 0, K * osz, N, s);
@@ -991,6 +1033,7 @@ extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, in
     GemmArgs args{};
     args.M = static_cast<int>(N), args.N = static_cast<int>(K), args.K = static_cast<int>(M_tok);
     args.out = out, args.ldo = ldo, args.out_dtype = out_dtype, args.accumulate = accumulate;
+    args.addend = addend, args.ld_add = ld_add;
     args.vec_store = aligned16(out) && (ldo * static_cast<int64_t>(osz)) % 16 == 0;
     const int splits =
         workspace == nullptr ? 1 : gw_splits(M_tok, N, K, sms, workspace_bytes);
@@ -1014,15 +1057,35 @@ extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, in
     const int tiles_n = static_cast<int>((K + GW_BN - 1) / GW_BN);
     launch_k(splitk_reduce_kernel<GW_BN>, static_cast<unsigned>(blocks), 256, 0, s, 
         static_cast<const float *>(workspace), splits, tiles_m, tiles_n, static_cast<int>(N),
-        static_cast<int>(K), out, out_dtype, ldo, accumulate, args.vec_store);
+        static_cast<int>(K), out, out_dtype, ldo, accumulate, args.vec_store, addend, ld_add);
     return check_launch("splitk_reduce_kernel");
   }
   const dim3 block(32, 8);
   const dim3 grid(static_cast<unsigned>((K + 31) / 32), static_cast<unsigned>((N + 7) / 8));
   launch_k(simt_gradw_kernel, grid, block, 0, s, static_cast<const uint16_t *>(g), ldg,
-                                            static_cast<const uint16_t *>(x), ldx, out, out_dtype,
-                                            ldo, M_tok, N, K, accumulate);
+           static_cast<const uint16_t *>(x), ldx, out, out_dtype, ldo, M_tok, N, K, accumulate,
+           addend, ld_add);
   return check_launch("simt_gradw_kernel");
+}
+}  // namespace rt
+
+extern "C" int rt_grad_weight_bf16(const void *g, int64_t ldg, const void *x, int64_t ldx,
+                                   void *out, int out_dtype, int64_t ldo, int64_t M_tok, int64_t N,
+                                   int64_t K, int accumulate, void *workspace,
+                                   int64_t workspace_bytes, void *stream) {
+  return grad_weight_impl(g, ldg, x, ldx, out, out_dtype, ldo, M_tok, N, K, accumulate, nullptr, 0,
+                          workspace, workspace_bytes, stream);
+}
+
+extern "C" int rt_grad_weight_bf16_add(const void *g, int64_t ldg, const void *x, int64_t ldx,
+                                       const float *addend, int64_t ld_addend, void *out,
+                                       int out_dtype, int64_t ldo, int64_t M_tok, int64_t N,
+                                       int64_t K, void *workspace, int64_t workspace_bytes,
+                                       void *stream) {
+  if (addend == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "grad_weight_add: null addend");
+  return grad_weight_impl(g, ldg, x, ldx, out, out_dtype, ldo, M_tok, N, K, 0, addend, ld_addend,
+                          workspace, workspace_bytes, stream);
 }
 
 extern "C" int64_t rt_grad_weight_update_workspace_bytes(int64_t M_tok, int64_t N, int64_t K) {
@@ -1085,27 +1148,76 @@ extern "C" int rt_grad_weight_ratchet_update(
 // rt_grad_weight_bf16 without a caller-provided workspace: the split-K partial tiles live in a
 // fixed device array of this library.  Nothing is allocated per call.
 namespace rt {
-constexpr int64_t kGwScratchBytes = int64_t(20) << 20;  // >= SMs x 128 KiB partial tiles
-constexpr int kGwScratchDevices = 64;
+// Split-K never needs more than SMs x 128 KiB of partial tiles (gw_splits caps splits x tiles at
+// the SM count): 20 MiB covers every part with up to 160 SMs (B200: 148 -> 18.5 MiB at most),
+// so the size check in rt_grad_weight_bf16_noalloc only rejects shapes on larger parts.
+constexpr int64_t kGwScratchBytes = int64_t(20) << 20;
+static_assert(kGwScratchBytes >= int64_t(148) * GW_TILE_BYTES, "scratch below B200's split-K need");
 static __device__ __align__(256) uint8_t g_gw_scratch[kGwScratchBytes];
 
-// Address of this device's copy of g_gw_scratch, looked up once per device.
-static int gw_scratch_address(int dev, void **out) {
-  static std::mutex mu;
-  static void *addr[kGwScratchDevices] = {};
-  if (dev < 0 || dev >= kGwScratchDevices)
-    return fail(RT_ERR_UNSUPPORTED, "grad_weight_noalloc: device ordinal %d beyond %d", dev,
-                kGwScratchDevices);
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+
+// Unique id of the CUDA context current on this thread (0 when none is current).  Ids are never
+// reused within a process, so a context created after a cudaDeviceReset, or another context an
+// FFI host makes current on the same device, gets a fresh one.
+static int current_context_id(unsigned long long *id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void *p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_gw_scratch);
-    if (e != cudaSuccess || p == nullptr)
-      return fail(RT_ERR_CUDA, "grad_weight_noalloc: scratch address lookup failed: %s",
-                  cudaGetErrorString(e));
-    addr[dev] = p;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (get_current == nullptr || get_id == nullptr)
+    return fail(RT_ERR_CUDA, "grad_weight_noalloc: cuCtxGetCurrent/cuCtxGetId are unavailable");
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS)
+    return fail(RT_ERR_CUDA, "grad_weight_noalloc: cuCtxGetCurrent failed");
+  *id = 0;
+  if (ctx != nullptr && get_id(ctx, id) != CUDA_SUCCESS)
+    return fail(RT_ERR_CUDA, "grad_weight_noalloc: cuCtxGetId failed");
+  return RT_OK;
+}
+
+// Address of g_gw_scratch in the context current on this thread.  The symbol's address belongs
+// to one context (the module is loaded once per context), so it is looked up once per context
+// -- the first call with that context current -- and cached under the context's unique id.
+static int gw_scratch_address(void **out) {
+  constexpr int kEntries = 64;
+  static std::mutex mu;
+  static unsigned long long ids[kEntries] = {};
+  static void *addrs[kEntries] = {};
+  static int next = 0;
+  unsigned long long id = 0;
+  if (int rc = current_context_id(&id)) return rc;
+  std::lock_guard<std::mutex> lock(mu);
+  if (id != 0)
+    for (int i = 0; i < kEntries; ++i)
+      if (ids[i] == id) {
+        *out = addrs[i];
+        return RT_OK;
+      }
+  void *p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_gw_scratch);  // initialises the context if needed
+  if (e != cudaSuccess || p == nullptr)
+    return fail(RT_ERR_CUDA, "grad_weight_noalloc: scratch address lookup failed: %s",
+                cudaGetErrorString(e));
+  if (id == 0 && (current_context_id(&id) != RT_OK || id == 0)) {
+    *out = p;  // no id to key it under: use it for this call only
+    return RT_OK;
   }
-  *out = addr[dev];
+  ids[next] = id;
+  addrs[next] = p;
+  next = (next + 1) % kEntries;
+  *out = p;
   return RT_OK;
 }
 }  // namespace rt
@@ -1124,10 +1236,7 @@ extern "C" int rt_grad_weight_bf16_noalloc(const void *g, int64_t ldg, const voi
                 static_cast<long long>(need), static_cast<long long>(kGwScratchBytes));
   void *scratch = nullptr;
   if (need > 0) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return fail(RT_ERR_CUDA, "grad_weight_noalloc: %s", cudaGetErrorString(e));
-    int rc = gw_scratch_address(dev, &scratch);
+    int rc = gw_scratch_address(&scratch);
     if (rc) return rc;
     // nothing in the scratch needs to start at zero: every partial tile is written before it
     // is read, within the call

@@ -587,6 +587,9 @@ struct UpdateArgs {
   const float *ws;
   int ws_splits, ws_tiles_n, ws_bn;
   int64_t ws_split_stride;
+  // the gradient is multiplied by grad_mul after the optional bf16 rounding (1: untouched); the
+  // mean over ranks / micro-batches of summed gradients, exact for powers of two
+  float grad_mul;
 };
 
 struct Moves {
@@ -693,7 +696,7 @@ __device__ __forceinline__ void load_grad8(const UpdateArgs &a, const G *gr, int
 }
 
 template <typename G, int RT, int VPT, bool WS>
-__device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a) {
+__device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a, int64_t block) {
   constexpr int RPC = CTA / RT, NT = CTA / RT;
   __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
   __shared__ float smb[RPC];
@@ -701,7 +704,7 @@ __device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a) {
   __shared__ int redi[CTA / 32][4];
   __shared__ float rrs[RPC];  // the rows' gradient rms, summed once per CTA
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * RPC + sub;
+  const int64_t row = block * RPC + sub;
   const bool live = row < a.rows;
   const int64_t nch = a.cols / 8;
   const G *gr = static_cast<const G *>(a.grad) + (live ? row : 0) * a.ldg;
@@ -719,6 +722,10 @@ __device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a) {
       if (a.round_bf16) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) g[i][j] = bf16_round(g[i][j]);
+      }
+      if (a.grad_mul != 1.0f) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) g[i][j] = __fmul_rn(g[i][j], a.grad_mul);
       }
       pk[i] = *reinterpret_cast<const uint2 *>(pr + 8 * c);
 #pragma unroll
@@ -798,13 +805,52 @@ template <typename G, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) ratchet_update_kernel(UpdateArgs a) {
   pdl_wait();
   pdl_trigger();
-  ratchet_update_body<G, RT, VPT, false>(a);
+  ratchet_update_body<G, RT, VPT, false>(a, blockIdx.x);
 }
 template <typename G, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) ratchet_update_ws_kernel(UpdateArgs a) {
   pdl_wait();
   pdl_trigger();
-  ratchet_update_body<G, RT, VPT, true>(a);
+  ratchet_update_body<G, RT, VPT, true>(a, blockIdx.x);
+}
+
+// Grouped update: the rows of up to kUpdateGroup layers (same row length, dtype and ratchet
+// parameters) in one launch.  Layer l owns blocks [block0[l], block0[l+1]); each block runs the
+// single-layer body on that layer's rows, so the arithmetic is the per-layer kernel's.
+constexpr int kUpdateGroup = 64;
+struct GroupLayer {
+  const void *grad;
+  int64_t ldg, rows;
+  uint8_t *packed;
+  int64_t ldp;
+  int8_t *code_out;
+  int64_t ldc;
+  float *rms_ema;
+  unsigned long long *counts;
+  float *rms_sum;
+  float grad_mul;
+  int block0;
+};
+struct GroupArgs {
+  UpdateArgs common;  // row length, dtype and ratchet parameters shared by the group
+  int n;
+  int blocks;  // total blocks of the group (block0 of a virtual layer n)
+  GroupLayer L[kUpdateGroup];
+};
+template <typename G, int RT, int VPT>
+__global__ void __launch_bounds__(CTA) ratchet_update_grouped_kernel(const __grid_constant__ GroupArgs g) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = static_cast<int>(blockIdx.x);
+  int l = 0;
+  while (l + 1 < g.n && g.L[l + 1].block0 <= b) ++l;
+  const GroupLayer &L = g.L[l];
+  UpdateArgs a = g.common;
+  a.grad = L.grad, a.ldg = L.ldg, a.rows = L.rows, a.packed = L.packed, a.ldp = L.ldp;
+  a.code_out = L.code_out, a.ldc = L.ldc, a.rms_ema = L.rms_ema, a.counts = L.counts;
+  a.rms_sum = L.rms_sum, a.grad_mul = L.grad_mul;
+  a.row_rms = nullptr, a.grad_scale = nullptr, a.ws = nullptr;
+  ratchet_update_body<G, RT, VPT, false>(a, b - L.block0);
 }
 
 // Generic update: any alignment and row length, one CTA per row, same arithmetic and order.
@@ -826,6 +872,7 @@ __global__ void __launch_bounds__(CTA) ratchet_update_generic_kernel(UpdateArgs 
       if (k >= a.cols) break;
       float gv = load_elem(a.grad, a.grad_dtype, row * a.ldg + k);
       if (a.round_bf16) gv = bf16_round(gv);
+      if (a.grad_mul != 1.0f) gv = __fmul_rn(gv, a.grad_mul);
       bad |= !isfinite(gv);
       ss = __fadd_rn(ss, __fmul_rn(gv, gv));
       if (a.grad_scale != nullptr)
@@ -852,6 +899,7 @@ __global__ void __launch_bounds__(CTA) ratchet_update_generic_kernel(UpdateArgs 
     if (!bad) {
       float gv = load_elem(a.grad, a.grad_dtype, row * a.ldg + k);
       if (a.round_bf16) gv = bf16_round(gv);
+      if (a.grad_mul != 1.0f) gv = __fmul_rn(gv, a.grad_mul);
       v = ratchet_one(v, pressure_increment(gv, denom, rcp, a.normalize, a.low, a.high), a, m);
       a.packed[row * a.ldp + k] = v;
     }
@@ -1675,6 +1723,7 @@ static UpdateArgs update_args(const void *grad, int grad_dtype, int round_bf16, 
   a.eps = static_cast<float>(eps);
   a.counts = reinterpret_cast<unsigned long long *>(counts);
   a.row_rms = row_rms, a.rms_sum = rms_sum, a.grad_scale = grad_scale;
+  a.grad_mul = 1.0f;
   return a;
 }
 
@@ -1725,6 +1774,88 @@ extern "C" int rt_ratchet_update(const void *grad, int grad_dtype, int round_bf1
                                    threshold, bucket_low, bucket_high, eps, counts, row_rms,
                                    rms_sum, grad_scale);
   return ratchet_update_launch(a, as_stream(stream));
+}
+
+extern "C" int rt_ratchet_update_grouped(const rt_update_layer *layers, int n_layers,
+                                         int grad_dtype, int round_bf16, int64_t cols,
+                                         int normalize, double ema_beta, int max_code,
+                                         int threshold, double bucket_low, double bucket_high,
+                                         double eps, void *stream) {
+  if (n_layers < 0 || (n_layers > 0 && layers == nullptr))
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_ratchet_update_grouped: layer list");
+  if (int rc = ratchet_update_check(0, cols, max_code, threshold, bucket_low, bucket_high))
+    return rc;
+  if (grad_dtype != RT_F32 && grad_dtype != RT_BF16)
+    return fail(RT_ERR_DTYPE, "rt_ratchet_update_grouped: gradient must be float32 or bfloat16");
+  cudaStream_t s = as_stream(stream);
+  const size_t es = grad_dtype == RT_F32 ? 4 : 2;
+  UpdateArgs common = update_args(nullptr, grad_dtype, round_bf16, 0, 0, cols, nullptr, 0, nullptr,
+                                  0, normalize, nullptr, ema_beta, max_code, threshold, bucket_low,
+                                  bucket_high, eps, nullptr, nullptr, nullptr, nullptr);
+  // every layer must take the vectorised path (8-element chunks, 16-byte gradient rows, 8-byte
+  // packed and code rows); otherwise the layers run one launch each
+  bool vec = cols % 8 == 0 && cols / 8 <= 256 * 8;
+  for (int i = 0; i < n_layers && vec; ++i) {
+    const rt_update_layer &L = layers[i];
+    if (L.rows < 0 || L.rows > INT32_MAX / 2)
+      return fail(RT_ERR_INVALID_ARGUMENT, "rt_ratchet_update_grouped: layer %d rows", i);
+    if (L.rows > 0 && (L.grad == nullptr || L.packed == nullptr))
+      return fail(RT_ERR_INVALID_ARGUMENT, "rt_ratchet_update_grouped: layer %d null pointer", i);
+    vec = vec && (L.rows == 0 || (aligned16(L.grad) && (L.ldg * es) % 16 == 0 &&
+                                  (reinterpret_cast<uintptr_t>(L.packed) & 7) == 0 &&
+                                  L.ldp % 8 == 0 &&
+                                  (L.code_out == nullptr ||
+                                   ((reinterpret_cast<uintptr_t>(L.code_out) & 7) == 0 &&
+                                    L.ldc % 8 == 0))));
+  }
+  if (!vec) {
+    for (int i = 0; i < n_layers; ++i) {
+      const rt_update_layer &L = layers[i];
+      if (L.rows == 0) continue;
+      UpdateArgs a = common;
+      a.grad = L.grad, a.ldg = L.ldg, a.rows = L.rows, a.packed = L.packed, a.ldp = L.ldp;
+      a.code_out = L.code_out, a.ldc = L.ldc;
+      a.rms_ema = ema_beta > 0.0 ? L.rms_ema : nullptr;
+      a.counts = reinterpret_cast<unsigned long long *>(L.counts);
+      a.rms_sum = L.rms_sum, a.grad_mul = L.grad_mul;
+      if (int rc = ratchet_update_launch(a, s)) return rc;
+    }
+    return RT_OK;
+  }
+  // one configuration for the whole group: a warp per row up to four chunks a lane (as the
+  // single-layer launch), else the row configuration of the group's total row count
+  int64_t total_rows = 0;
+  for (int i = 0; i < n_layers; ++i) total_rows += layers[i].rows;
+  RowCfg cfg = row_cfg(cols / 8, total_rows);
+  if (cols / 8 <= 32 * 4) cfg = RowCfg{32, pow2_at_least((cols / 8 + 31) / 32)};
+  const int rpc = CTA / cfg.rt;
+  for (int first = 0; first < n_layers;) {
+    GroupArgs g;
+    g.common = common;
+    g.n = 0;
+    int blocks = 0;
+    for (; first < n_layers && g.n < kUpdateGroup; ++first) {
+      const rt_update_layer &L = layers[first];
+      if (L.rows == 0) continue;
+      GroupLayer &d = g.L[g.n++];
+      d.grad = L.grad, d.ldg = L.ldg, d.rows = L.rows, d.packed = L.packed, d.ldp = L.ldp;
+      d.code_out = L.code_out, d.ldc = L.ldc;
+      d.rms_ema = ema_beta > 0.0 ? L.rms_ema : nullptr;
+      d.counts = reinterpret_cast<unsigned long long *>(L.counts);
+      d.rms_sum = L.rms_sum, d.grad_mul = L.grad_mul;
+      d.block0 = blocks;
+      blocks += static_cast<int>((L.rows + rpc - 1) / rpc);
+    }
+    g.blocks = blocks;
+    if (g.n == 0) continue;
+    if (grad_dtype == RT_F32)
+      RT_DISPATCH_ROW(cfg, ratchet_update_grouped_kernel, float, static_cast<unsigned>(blocks), g);
+    else
+      RT_DISPATCH_ROW(cfg, ratchet_update_grouped_kernel, __nv_bfloat16,
+                      static_cast<unsigned>(blocks), g);
+    if (int rc = check_launch("rt_ratchet_update_grouped")) return rc;
+  }
+  return RT_OK;
 }
 
 extern "C" int rt_ratchet_leak(uint8_t *packed, int64_t ldp, int64_t rows, int64_t cols,

@@ -129,8 +129,10 @@ def _scaled_int8_mm_into(
         )
     )
     if ev is not None:
+        # operands, scales, the output and (fused residual add) the fp32 residual tile reads
         _lib.prof_stop(ev, "gemm_i8", lhs, 2.0 * m * n * k,
-                       m * k + n * k + 4 * (m + n) + m * n * out.element_size())
+                       m * k + n * k + 4 * (m + n) + m * n * out.element_size()
+                       + (4 * m * n if residual is not None else 0))
     return out
 
 
@@ -164,9 +166,12 @@ def scaled_int8_mm(lhs: Tensor, rhs: Tensor, lhs_scale: Tensor, rhs_scale: Tenso
 
 
 def grad_weight_bf16(grad: Tensor, inputs: Tensor, out: Tensor | None = None, *,
-                     accumulate: bool = False) -> Tensor:
+                     accumulate: bool = False, addend: Tensor | None = None) -> Tensor:
     """gw[n, k] (+)= sum_m grad[m, n] * inputs[m, k]: bf16 operands, fp32 accumulation/output
-    (the per-tile grad_weight GEMM of ratchet.py:148-163 as one tcgen05 launch)."""
+    (the per-tile grad_weight GEMM of ratchet.py:148-163 as one tcgen05 launch).
+
+    addend (fp32 [n, k], optional): out = round(addend + gw) in out's dtype -- the last
+    micro-batch of an accumulated step writing the bf16 total."""
     if grad.dtype != torch.bfloat16 or inputs.dtype != torch.bfloat16:
         raise TypeError("grad_weight_bf16 operands must be bfloat16")
     if grad.stride(1) != 1:
@@ -183,15 +188,29 @@ def grad_weight_bf16(grad: Tensor, inputs: Tensor, out: Tensor | None = None, *,
     need = _lib.lib().rt_grad_weight_workspace_bytes(mt, n, k)
     ws = _lib.workspace(grad.device, need)
     ev = _lib.prof_start(grad)
-    _lib.check(
-        _lib.lib().rt_grad_weight_bf16(
-            grad.data_ptr(), grad.stride(0), inputs.data_ptr(), inputs.stride(0), out.data_ptr(),
-            _lib.dtype_code(out), out.stride(0), mt, n, k, int(accumulate), _lib.ptr(ws),
-            0 if ws is None else ws.numel(), _lib.stream_of(grad),
+    if addend is not None:
+        if addend.dtype != torch.float32 or addend.shape != (n, k) or addend.stride(1) != 1:
+            raise TypeError("grad_weight_bf16 addend must be a float32 [out, in] row-major matrix")
+        _lib.check(
+            _lib.lib().rt_grad_weight_bf16_add(
+                grad.data_ptr(), grad.stride(0), inputs.data_ptr(), inputs.stride(0),
+                addend.data_ptr(), addend.stride(0), out.data_ptr(), _lib.dtype_code(out),
+                out.stride(0), mt, n, k, _lib.ptr(ws), 0 if ws is None else ws.numel(),
+                _lib.stream_of(grad),
+            )
         )
-    )
+    else:
+        _lib.check(
+            _lib.lib().rt_grad_weight_bf16(
+                grad.data_ptr(), grad.stride(0), inputs.data_ptr(), inputs.stride(0),
+                out.data_ptr(), _lib.dtype_code(out), out.stride(0), mt, n, k, int(accumulate),
+                _lib.ptr(ws), 0 if ws is None else ws.numel(), _lib.stream_of(grad),
+            )
+        )
     if ev is not None:
-        _lib.prof_stop(ev, "gemm_gradw_bf16", grad, 2.0 * mt * n * k, 2 * mt * (n + k) + 4 * n * k)
+        extra = 4 * n * k if (accumulate or addend is not None) else 0  # the fp32 read
+        _lib.prof_stop(ev, "gemm_gradw_bf16", grad, 2.0 * mt * n * k,
+                       2 * mt * (n + k) + out.element_size() * n * k + extra)
     return out
 
 

@@ -2,8 +2,9 @@
 
 Same configuration fields, module tree, parameter names and initialisation order as the reference
 (so seeded models and state_dicts match); the int8 path routes through the fused producers and
-the ratchet layers of this package.  Attention (SDPA), RMSNorm weights, embeddings and the loss
-stay PyTorch ops.
+the ratchet layers of this package.  The lm_head and the token cross-entropy run as fused CUDA
+kernels of this library (cross_entropy.py); attention (SDPA), the embedding lookup and the
+optimizer stay PyTorch ops.
 """
 
 from __future__ import annotations

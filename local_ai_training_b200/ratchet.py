@@ -203,9 +203,15 @@ def _deliver_weight_gradient(gradient_sink, mode: str, fuse_backward_update: boo
         # data-parallel: the bf16-rounded grad_W goes to the layer's reduce-scatter buffer and
         # the update runs later on the owned rows of the summed gradient
         layer = gradient_sink.__self__
-        target = dp.grad_buffer(layer)
-        grad_weight_bf16(grad_bf16, inputs_bf16, out=target)
-        grad_scale = (target.float() * code.float()).sum(dim=1) if want_scale else None
+        target = dp.grad_target(layer)
+        grad_weight_bf16(grad_bf16, inputs_bf16, out=target.out, accumulate=target.accumulate,
+                         addend=target.addend)
+        grad_scale = None
+        if want_scale:
+            # the trainable-scale gradient is linear in grad_W: the micro-batch that completes
+            # the step's total returns it for the whole step, the earlier ones zero
+            grad_scale = ((target.out.float() * code.float()).sum(dim=1) if target.last else
+                          torch.zeros(out_features, device=code.device, dtype=torch.float32))
         dp.grad_ready(layer)
         return grad_scale
     if mode == "fp32":
@@ -227,6 +233,67 @@ def _deliver_weight_gradient(gradient_sink, mode: str, fuse_backward_update: boo
         grad_weight = grad_weight.to(torch.bfloat16).float()
     gradient_sink(grad_weight, None, None)
     return (grad_weight * code.float()).sum(dim=1) if want_scale else None
+
+
+def ratchet_update_grouped(entries: list[tuple["DiscreteRatchetLinear", Tensor, int, int, float]],
+                           *, stats_weights: dict | None = None) -> None:
+    """The fused update (normalise, bucket, pressure/code step; ratchet.py:487-556, 265-301) of
+    many layers after backward, in as few launches as possible (rt_ratchet_update_grouped).
+
+    entries: (layer, gradient rows, row_start, row_end, grad_mul) -- `gradient` holds rows
+    [row_start, row_end) of the layer's effective-weight gradient (fp32 or bf16, unit column
+    stride), multiplied by grad_mul inside the kernel.  Per layer the result is that of
+    `_capture_weight_gradient` on gradient * grad_mul; the layer's move counters and rms sum
+    accumulate in its pending statistics.  stats_weights (optional): layer -> the weight count
+    to record for the layer's statistics instead of its updated rows (data-parallel owners
+    report the whole matrix)."""
+    groups: dict[tuple, list] = {}
+    for layer, grad, row_start, row_end, grad_mul in entries:
+        pk = layer.packed
+        _require_cuda(pk, "the ratchet update")
+        if grad.dtype not in (torch.float32, torch.bfloat16):
+            grad = grad.float()
+        if grad.stride(-1) != 1:
+            grad = grad.contiguous()
+        if grad.shape != (row_end - row_start, layer.in_features):
+            raise ValueError("grouped update: gradient rows do not match the row range")
+        key = (pk.device, grad.dtype, layer.in_features, layer.max_code,
+               layer.pressure_threshold, float(layer.bucket_low), float(layer.bucket_high),
+               float(layer.eps), float(layer.rms_ema_beta))
+        groups.setdefault(key, []).append((layer, grad, row_start, row_end, grad_mul))
+    for key, items in groups.items():
+        device, dtype, cols, max_code, threshold, low, high, eps, beta = key
+        descs = (_lib.UpdateLayer * len(items))()
+        for d, (layer, grad, row_start, row_end, grad_mul) in zip(descs, items):
+            layer._pending_stat_slots(device)
+            mirror = layer.code_int8()
+            pk = layer.packed
+            d.grad = grad.data_ptr()
+            d.ldg = grad.stride(0)
+            d.rows = row_end - row_start
+            d.packed = pk[row_start:row_end].data_ptr()
+            d.ldp = pk.stride(0)
+            d.code_out = mirror[row_start:row_end].data_ptr()
+            d.ldc = mirror.stride(0)
+            d.rms_ema = (layer.rms_ema[row_start:row_end].data_ptr()
+                         if beta > 0.0 else None)
+            d.counts = layer._pending_counts.data_ptr()
+            d.rms_sum = layer._pending_rms.data_ptr()
+            d.grad_mul = float(grad_mul)
+        first = items[0][1]
+        ev = _lib.prof_start(first)
+        _lib.check(_lib.lib().rt_ratchet_update_grouped(
+            descs, len(items), _lib.dtype_code(first), 0, cols, 1, beta, max_code, threshold,
+            low, high, eps, _lib.stream_of(first)))
+        if ev is not None:
+            rows = sum(r1 - r0 for _, _, r0, r1, _ in items)
+            _lib.prof_stop(ev, "ratchet_update", first, 0.0,
+                           rows * cols * (first.element_size() + 3) + 4 * rows)
+        for layer, grad, row_start, row_end, grad_mul in items:
+            weights = (stats_weights or {}).get(layer)
+            layer._pending_stats_total_weights += (
+                weights if weights is not None else (row_end - row_start) * layer.in_features)
+            layer._pending_stats_rms_sum = layer._pending_rms[0]
 
 
 def _code_bound(sink) -> int:
@@ -554,9 +621,12 @@ class DiscreteRatchetLinear(nn.Module):
             self.code_int8()
             return
         rows, cols = pk.shape
+        ev = _lib.prof_start(pk)
         _lib.check(_lib.lib().rt_unpack_code_pressure(
             pk.data_ptr(), pk.stride(0), rows, cols, self.max_code, self._code_mirror.data_ptr(),
             self._code_mirror.stride(0), None, 0, _lib.stream_of(pk)))
+        if ev is not None:
+            _lib.prof_stop(ev, "unpack_codes", pk, 0.0, 2 * rows * cols)
         self._code_mirror_key = key
 
     def code_int8(self) -> Tensor:

@@ -20,6 +20,7 @@ Fixtures (npz):
 from __future__ import annotations
 
 import argparse
+import os
 import sys
 from pathlib import Path
 
@@ -205,9 +206,12 @@ def model_tiny(ref) -> None:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference/src",
-                        help="directory containing the reference package local_ai_training")
+    parser.add_argument("--reference", default=os.environ.get("RATCHET_REFERENCE_SRC"),
+                        help="directory containing the reference package local_ai_training "
+                             "(default: $RATCHET_REFERENCE_SRC)")
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("give --reference or set RATCHET_REFERENCE_SRC")
     sys.path.insert(0, args.reference)
     import importlib
 

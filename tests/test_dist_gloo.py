@@ -202,3 +202,103 @@ def _reject_worker(rank: int, world: int, out_dir: str) -> None:
     with open(os.path.join(out_dir, f"ok{rank}"), "w") as f:
         f.write(result)
     dist.destroy_process_group()
+
+
+MICRO = 2
+
+
+def _apply_target(target, g: torch.Tensor) -> None:
+    """What the grad_weight GEMM does with a GradTarget (fp32 arithmetic, one rounding)."""
+    if target.addend is not None:
+        target.out.copy_((target.addend + g.float()).to(target.out.dtype))
+    elif target.accumulate:
+        target.out.add_(g.float())
+    else:
+        target.out.copy_(g.to(target.out.dtype))
+
+
+def _micro_grad(rank: int, micro: int, n: int, shape) -> torch.Tensor:
+    g = torch.Generator().manual_seed(5000 + 100 * rank + 10 * micro + n)
+    return torch.randn(shape[0], shape[1], generator=g) * 1e-2
+
+
+def _accum_worker(rank: int, world: int, out_dir: str) -> None:
+    _init(rank, world, out_dir)
+    from local_ai_training_b200.dist import RatchetDataParallel
+
+    model = _StubModel()
+    ddp = RatchetDataParallel(model, accumulation_steps=MICRO)
+    for micro in range(MICRO):
+        for n in reversed(range(len(SHAPES))):
+            layer = model.layers[n]
+            target = ddp.grad_target(layer)
+            assert target.last == (micro == MICRO - 1)
+            _apply_target(target, _micro_grad(rank, micro, n, SHAPES[n][:2]))
+            ddp.grad_ready(layer)
+        # the support gradient accumulates over micro-batches as autograd does
+        g = torch.full((6,), float(rank + 1 + micro))
+        model.norm.grad = g if model.norm.grad is None else model.norm.grad + g
+    extra = "none"
+    try:  # a third micro-batch before the update is refused
+        ddp.grad_target(model.layers[0])
+    except RuntimeError:
+        extra = "RuntimeError"
+    stats = ddp.step(torch.optim.SGD([model.norm], lr=1.0))
+    torch.save({"packed": [l.packed.clone() for l in model.layers],
+                "norm_grad": model.norm.grad.clone(), "extra": extra,
+                "stats": [int(stats.positive_moves), int(stats.negative_moves),
+                          int(stats.total_weights)]},
+               os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_accumulated_micro_batches_equal_one_update_of_the_mean(tmp_path):
+    """Two ranks x two micro-batches: each rank's bf16 total round(g0 + g1), summed across ranks
+    (bf16), divided by 4, then one update -- identical on both ranks."""
+    world = 2
+    tmp_path = _run_ranks(_accum_worker, world, tmp_path)
+    res = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
+    assert res[0]["extra"] == res[1]["extra"] == "RuntimeError"
+    for a, b in zip(res[0]["packed"], res[1]["packed"]):
+        assert torch.equal(a, b)
+    # support: mean over ranks and micro-batches of (rank + 1 + micro)
+    assert torch.equal(res[0]["norm_grad"], torch.full((6,), 2.0))
+    fresh = _StubModel()
+    counts = np.zeros(4, np.int64)
+    for n, (o, i, beta) in enumerate(SHAPES):
+        totals = [(_micro_grad(r, 0, n, (o, i)) + _micro_grad(r, 1, n, (o, i))).to(torch.bfloat16)
+                  for r in range(world)]
+        g = (totals[0].float() + totals[1].float()).to(torch.bfloat16).float() * 0.25
+        ema = np.zeros(o, np.float32) if beta > 0 else None
+        out = O.ratchet_update(g.numpy(), fresh.layers[n].packed.numpy(), max_code=MAX_CODE,
+                               threshold=THRESHOLD, rms_ema=ema, beta=beta)
+        np.testing.assert_array_equal(res[0]["packed"][n].numpy(), out["packed"])
+        counts += out["counts"]
+    assert res[0]["stats"][:2] == counts[:2].tolist()
+    assert res[0]["stats"][2] == sum(o * i for o, i, _ in SHAPES)
+
+
+def test_single_process_accumulation_without_distributed():
+    """No process group: world 1, the micro-batch gradients accumulate and one update runs."""
+    from local_ai_training_b200.dist import RatchetDataParallel
+
+    assert not dist.is_initialized()
+    model = _StubModel()
+    ddp = RatchetDataParallel(model, accumulation_steps=MICRO)
+    assert ddp.world == 1 and ddp.rank == 0
+    for micro in range(MICRO):
+        for n in reversed(range(len(SHAPES))):
+            layer = model.layers[n]
+            _apply_target(ddp.grad_target(layer), _micro_grad(0, micro, n, SHAPES[n][:2]))
+            ddp.grad_ready(layer)
+    model.norm.grad = torch.full((6,), 3.0)
+    ddp.step(torch.optim.SGD([model.norm], lr=1.0))
+    assert torch.equal(model.norm.grad, torch.full((6,), 1.5))
+    fresh = _StubModel()
+    for n, (o, i, beta) in enumerate(SHAPES):
+        g = (_micro_grad(0, 0, n, (o, i)) + _micro_grad(0, 1, n, (o, i))).to(torch.bfloat16)
+        g = g.float() * 0.5
+        ema = np.zeros(o, np.float32) if beta > 0 else None
+        out = O.ratchet_update(g.numpy(), fresh.layers[n].packed.numpy(), max_code=MAX_CODE,
+                               threshold=THRESHOLD, rms_ema=ema, beta=beta)
+        np.testing.assert_array_equal(model.layers[n].packed.numpy(), out["packed"])

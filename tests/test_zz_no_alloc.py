@@ -44,7 +44,7 @@ def test_noalloc_matches_workspace_entry(cuda_device, shape, out_dtype):
     x = torch.randn((mt, k), device=cuda_device, generator=gen).to(torch.bfloat16)
     want = torch.empty((n, k), device=cuda_device, dtype=out_dtype)
     grad_weight_bf16(g, x, want)
-    for _ in range(2):  # two calls in a row: the tickets must be left (or made) zero
+    for _ in range(2):  # two calls in a row: scratch left by the first must not change the second
         got = torch.full((n, k), float("nan"), device=cuda_device, dtype=out_dtype)
         _noalloc(g, x, got, False)
         torch.cuda.synchronize()
@@ -73,7 +73,7 @@ def test_noalloc_takes_no_device_memory(cuda_device):
     g = torch.randn((mt, n), device=cuda_device).to(torch.bfloat16)
     x = torch.randn((mt, k), device=cuda_device).to(torch.bfloat16)
     out = torch.empty((n, k), device=cuda_device)
-    _noalloc(g, x, out, False)  # first call on the device: scratch address set-up
+    _noalloc(g, x, out, False)  # first call in this context: scratch address set-up
     torch.cuda.synchronize()
     free_before, _ = torch.cuda.mem_get_info()
     reserved_before = torch.cuda.memory_reserved()
