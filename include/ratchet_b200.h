@@ -154,6 +154,13 @@ int rt_grad_weight_bf16_noalloc(const void *g, int64_t ldg, const void *x, int64
                                 int out_dtype, int64_t ldo, int64_t M_tok, int64_t N, int64_t K,
                                 int accumulate, void *stream);
 
+/* out[M,N] = A[M,K] @ B[K,N]: bf16 operands, row-major (row strides lda / ldb elements, 16-byte
+ * aligned rows), fp32 accumulation, bf16 (RN) or float32 output.  Replaces the bf16 grad_input
+ * matmul of ratchet.py:135-141 (`grad_output.to(bf16) @ (code.to(bf16) * scale.to(bf16))`, the
+ * non-int8-backward branch and the self-quantising lm_head) with the tcgen05 kind::f16 GEMM. */
+int rt_matmul_bf16(const void *a, int64_t lda, const void *b, int64_t ldb, void *out,
+                   int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K, void *stream);
+
 /* rt_grad_weight_bf16 adding a float32 matrix: out[n,k] = round(addend[n,k] + sum_m g[m,n]*x[m,k])
  * in out_dtype (float32 or bfloat16), addend row stride ld_addend; addend may be `out` itself
  * when out is float32.  For gradient accumulation over micro-batches (no counterpart in the

@@ -54,6 +54,7 @@ _SIGNATURES = {
     "rt_grad_weight_update_workspace_bytes": ([_i64, _i64, _i64], _i64),
     "rt_grad_weight_bf16_add": ([_p, _i64, _p, _i64, _p, _i64, _p, _i, _i64, _i64, _i64, _i64, _p,
                                  _i64, _p], _i),
+    "rt_matmul_bf16": ([_p, _i64, _p, _i64, _p, _i, _i64, _i64, _i64, _i64, _p], _i),
     "rt_ratchet_update_grouped": ([_p, _i, _i, _i, _i64, _i, _d, _i, _i, _d, _d, _d, _p], _i),
     "rt_grad_weight_bf16_noalloc": ([_p, _i64, _p, _i64, _p, _i, _i64, _i64, _i64, _i64, _i, _p],
                                     _i),

@@ -18,7 +18,7 @@ import torch
 from torch import Tensor
 
 from . import _lib
-from .int8_matmul import _scaled_int8_mm_into, quantize_rows
+from .int8_matmul import _scaled_int8_mm_into, dequant_rows_bf16, matmul_bf16, quantize_rows
 from .ratchet import DiscreteRatchetLinear, _code_bound, _deliver_weight_gradient, _require_cuda
 
 IGNORE_INDEX = -100
@@ -103,8 +103,9 @@ class _LMHeadCrossEntropy(torch.autograd.Function):
         extra = None if grad_logits is None else grad_logits.reshape(logits.shape)
         grad_bf16 = cross_entropy_grad_bf16(logits, flat_targets, row_max, row_logsum, grad_loss,
                                             count, extra, ctx.ignore_index)
-        effective = code.to(torch.bfloat16) * scale.to(torch.bfloat16)[:, None]
-        grad_input = grad_bf16 @ effective
+        # bf16 grad_input against bf16(code)·bf16(scale) (ratchet.py:135-141) on the tcgen05 GEMM
+        effective = dequant_rows_bf16(code, scale.float().contiguous())
+        grad_input = matmul_bf16(grad_bf16, effective)
         grad_scale = _deliver_weight_gradient(
             ctx.gradient_sink, "int8", ctx.fuse_backward_update, grad_bf16,
             flat_inputs.to(torch.bfloat16), None, flat_inputs, code, bool(ctx.needs_input_grad[3]))

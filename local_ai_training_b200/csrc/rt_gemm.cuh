@@ -902,6 +902,38 @@ extern "C" int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_
   return check_launch("simt_scaled_i8_kernel");
 }
 
+extern "C" int rt_matmul_bf16(const void *a, int64_t lda, const void *b, int64_t ldb, void *out,
+                              int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                              void *stream) {
+  if (M < 0 || N < 0 || K < 0) return fail(RT_ERR_INVALID_ARGUMENT, "matmul_bf16: negative shape");
+  if (out_dtype != RT_BF16 && out_dtype != RT_F32)
+    return fail(RT_ERR_DTYPE, "matmul_bf16: output must be bfloat16 or float32");
+  if (M == 0 || N == 0) return RT_OK;
+  if (a == nullptr || b == nullptr || out == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "matmul_bf16: null pointer");
+  if (M > INT32_MAX / 2 || N > INT32_MAX / 2 || K > INT32_MAX / 2)
+    return fail(RT_ERR_UNSUPPORTED, "matmul_bf16: dimension too large");
+  cudaStream_t s = as_stream(stream);
+  const size_t osz = out_dtype == RT_BF16 ? 2 : 4;
+  if (K == 0) {
+    cudaError_t e = cudaMemset2DAsync(out, ldo * osz, 0, N * osz, M, s);
+    return e == cudaSuccess ? RT_OK : fail(RT_ERR_CUDA, "matmul_bf16 memset: %s", cudaGetErrorString(e));
+  }
+  // A (M x K) row-major is K-major; B (K x N) row-major is MN-major: the tcgen05 kind::f16 GEMM
+  // reads both in place (no transposed or padded copies)
+  if (!aligned16(a) || !aligned16(b) || (lda * 2) % 16 != 0 || (ldb * 2) % 16 != 0)
+    return fail(RT_ERR_ALIGNMENT, "matmul_bf16: operands need 16-byte aligned rows");
+  GemmArgs args{};
+  args.M = static_cast<int>(M), args.N = static_cast<int>(N), args.K = static_cast<int>(K);
+  args.out = out, args.ldo = ldo, args.out_dtype = out_dtype, args.splits = 1;
+  args.epi = out_dtype == RT_F32 ? EPI_F32_STORE : EPI_BF16_STORE;
+  args.vec_store = aligned16(out) && (ldo * static_cast<int64_t>(osz)) % 16 == 0;
+  Operand A{a, false, lda, M, K};
+  Operand B{b, true, ldb, N, K};
+  if (N <= 128) return launch_umma<__nv_bfloat16, false, true, 128, 6>(A, B, args, s);
+  return launch_umma<__nv_bfloat16, false, true, 256, 4>(A, B, args, s);
+}
+
 namespace rt {
 constexpr int GW_BN = 256;
 constexpr int64_t GW_TILE_BYTES = 128 * GW_BN * 4;

@@ -214,6 +214,35 @@ def grad_weight_bf16(grad: Tensor, inputs: Tensor, out: Tensor | None = None, *,
     return out
 
 
+def matmul_bf16(a: Tensor, b: Tensor, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+    """a[M, K] @ b[K, N] with bf16 operands and fp32 accumulation on the tcgen05 GEMM (the bf16
+    grad_input matmul of ratchet.py:135-141); output bf16 (RN) or float32."""
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("matmul_bf16 operands must be bfloat16")
+    if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0]:
+        raise ValueError("matmul_bf16 needs a[M, K] and b[K, N]")
+    _require = [t for t in (a, b) if not t.is_cuda]
+    if _require:
+        raise RuntimeError("matmul_bf16 requires CUDA operands")
+    if a.stride(1) != 1 or (a.stride(0) * 2) % 16 or a.data_ptr() % 16:
+        a = a.contiguous()
+    if b.stride(1) != 1 or (b.stride(0) * 2) % 16 or b.data_ptr() % 16:
+        b = b.contiguous()
+    m, k = a.shape
+    n = b.shape[1]
+    out = torch.empty((m, n), device=a.device, dtype=out_dtype)
+    if out.numel() == 0:
+        return out
+    ev = _lib.prof_start(a)
+    _lib.check(_lib.lib().rt_matmul_bf16(
+        a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0), out.data_ptr(),
+        _lib.dtype_code(out), out.stride(0), m, n, k, _lib.stream_of(a)))
+    if ev is not None:
+        _lib.prof_stop(ev, "gemm_bf16", a, 2.0 * m * n * k,
+                       2 * (m * k + k * n) + out.element_size() * m * n)
+    return out
+
+
 def dequant_rows_bf16(q: Tensor, scale: Tensor) -> Tensor:
     """bf16(bf16(q) * bf16(scale[:, None])) (ratchet.py:73-76)."""
     if q.stride(1) != 1:

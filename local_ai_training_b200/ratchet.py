@@ -31,6 +31,7 @@ from .int8_matmul import (
     _scaled_int8_mm_into,
     dequant_rows_bf16,
     grad_weight_bf16,
+    matmul_bf16,
     quantize_rows,
 )
 
@@ -176,9 +177,10 @@ class _RatchetMatmul(torch.autograd.Function):
             _scaled_int8_mm_into(gq, code, gs, None, grad_input,
                                  rhs_abs_max=_code_bound(ctx.gradient_sink))
         else:
+            # ratchet.py:135-141: bf16 gradient against bf16(code)·bf16(scale), on the tcgen05 GEMM
             grad_bf16 = flat_gradient.to(torch.bfloat16)
-            effective = code.to(torch.bfloat16) * scale.to(torch.bfloat16)[:, None]
-            grad_input = grad_bf16 @ effective
+            effective = dequant_rows_bf16(code, scale.float().contiguous())
+            grad_input = matmul_bf16(grad_bf16, effective)
 
         # ---- grad_weight (ratchet.py:148-163)
         if ctx.mode != "fp32" and grad_bf16 is None:
