@@ -19,7 +19,7 @@
 extern "C" {
 #endif
 
-#define RT_ABI_VERSION 1
+#define RT_ABI_VERSION 2
 
 /* status codes */
 #define RT_OK 0
@@ -264,12 +264,17 @@ int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, int64_t hea
                           int64_t stride_d, int8_t *q, int64_t ldq, float *row_scale,
                           void *dq_out, int64_t ld_dq, void *stream);
 /* RMSNorm backward (int8_backward.py:7-51): dx written in dx_dtype (through bf16, as the
- * reference stores it); dw (optional, cols floats, accumulated) += sum over rows of gy*x*rsqrt.
- * dx_add (optional, fp32 dx only, may equal dx): the residual branch's gradient, added to dx the
- * way autograd accumulates the two branches of the residual stream. */
+ * reference stores it); dw (optional, cols floats, accumulated) += sum over rows of gy*x*rsqrt,
+ * summed in a fixed order (per-CTA partial rows, then the partials in CTA order), so the result
+ * is the same on every call, as the reference's torch reduction is.  dw_work: with dw, a device
+ * workspace of rt_rmsnorm_backward_workspace_bytes(rows, cols) bytes (16-byte aligned), used
+ * within the call.  dx_add (optional, fp32 dx only, may equal dx): the residual branch's
+ * gradient, added to dx the way autograd accumulates the two branches of the residual stream. */
 int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
                         const float *weight, double eps, int64_t rows, int64_t cols, void *dx,
-                        int dx_dtype, float *dw, const float *dx_add, void *stream);
+                        int dx_dtype, float *dw, const float *dx_add, float *dw_work,
+                        int64_t dw_work_bytes, void *stream);
+int64_t rt_rmsnorm_backward_workspace_bytes(int64_t rows, int64_t cols);
 /* tanh-GELU backward (int8_backward.py:53-89); dx written in dx_dtype. */
 int rt_gelu_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype, int64_t rows,
                      int64_t cols, void *dx, int dx_dtype, void *stream);
@@ -298,7 +303,8 @@ int rt_rmsnorm_backward_sr(const void *grad_y, int gy_dtype, const void *x, int 
                            int dx_dtype, float *dw, const float *dx_add, const float *col_scale,
                            int round_input_bf16, uint64_t seed, uint32_t step, uint32_t layer,
                            uint32_t *step_dev, int8_t *q, int64_t ldq, float *row_scale,
-                           void *x_bf16_out, int64_t ld_xbf16, void *stream);
+                           void *x_bf16_out, int64_t ld_xbf16, float *dw_work,
+                           int64_t dw_work_bytes, void *stream);
 int rt_gelu_backward_sr(const void *grad_y, const void *x, int dtype, int64_t rows, int64_t cols,
                         void *dx, const float *col_scale, uint64_t seed, uint32_t step,
                         uint32_t layer, uint32_t *step_dev, int8_t *q, int64_t ldq,

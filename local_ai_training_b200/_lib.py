@@ -24,7 +24,7 @@ STATUS_PRESSURE_RANGE = 0x8
 STATUS_SCALE_INVALID = 0x10
 
 _ERR_INVALID, _ERR_DTYPE, _ERR_ALIGN = 1, 2, 3
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _LOCK = threading.Lock()
 _LIB: ctypes.CDLL | None = None
@@ -68,10 +68,12 @@ _SIGNATURES = {
     "rt_gelu_quantize": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _p], _i),
     "rt_transpose_quantize": ([_p, _i, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p, _i64,
                                _p, _p, _i64, _p], _i),
-    "rt_rmsnorm_backward": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p, _p, _p], _i),
+    "rt_rmsnorm_backward": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p, _p, _p, _i64, _p],
+                            _i),
+    "rt_rmsnorm_backward_workspace_bytes": ([_i64, _i64], _i64),
     "rt_gelu_backward": ([_p, _i, _p, _i, _i64, _i64, _p, _i, _p], _i),
     "rt_rmsnorm_backward_sr": ([_p, _i, _p, _i, _p, _d, _i64, _i64, _p, _i, _p, _p, _p, _i, _u64,
-                                _u32, _u32, _p, _p, _i64, _p, _p, _i64, _p], _i),
+                                _u32, _u32, _p, _p, _i64, _p, _p, _i64, _p, _i64, _p], _i),
     "rt_gelu_backward_sr": ([_p, _p, _i, _i64, _i64, _p, _p, _u64, _u32, _u32, _p, _p, _i64, _p,
                              _p, _i64, _p], _i),
     "rt_heads_gather_sr": ([_p, _p, _i, _i64, _i64, _i64, _i64, _p, _i64, _p, _u64, _u32, _u32,

@@ -38,6 +38,14 @@ bool pdl_enabled() {
   return on;
 }
 
+bool pair_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("RT_GEMM_PAIR");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
 }  // namespace rt
 
 using namespace rt;

@@ -62,14 +62,18 @@ struct KindOf<__nv_bfloat16> {
   static constexpr uint32_t abfmt = 1; // BF16
 };
 
-template <typename T, bool A_MN, bool B_MN, int BN, int STAGES, int EPI = 8>
+template <typename T, bool A_MN, bool B_MN, int BN, int STAGES, int EPI = 8, int CG = 1>
 struct GemmCfg {
+  // CG = 2: a CTA pair (cluster of two) computes one (2·BM) x BN tile; each CTA holds BM rows of
+  // A, BN/2 rows of B and BM accumulator rows x BN columns in its tensor memory
   static constexpr int BM = 128;
+  static constexpr int TILE_M = BM * CG;
   static constexpr int ES = sizeof(T);
   static constexpr int KE = 128 / ES;  // K elements per stage
   static constexpr int UK = 32 / ES;   // K elements per tcgen05.mma
+  static constexpr int B_ROWS = BN / CG;  // B rows (N) this CTA loads
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int B_BYTES = B_ROWS * 128;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
   // EPI epilogue warps (8 or 16): EPI/4 per TMEM lane quarter, each taking BN/(EPI/4) columns
@@ -85,8 +89,10 @@ struct GemmCfg {
                                     (KindOf<T>::abfmt << 10) | ((A_MN ? 1u : 0u) << 15) |
                                     ((B_MN ? 1u : 0u) << 16) |
                                     (static_cast<uint32_t>(BN >> 3) << 17) |
-                                    (static_cast<uint32_t>(BM >> 4) << 24);
+                                    (static_cast<uint32_t>(TILE_M >> 4) << 24);
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+  static_assert(CG == 1 || CG == 2, "CG");
+  static_assert(B_ROWS % (128 / ES) == 0 || !B_MN, "MN-major B half: whole 128-byte boxes");
   static_assert(TMEM_COLS <= 512, "TMEM");
 };
 
@@ -113,6 +119,21 @@ __device__ __forceinline__ void load_operand(const CUtensorMap *map, uint64_t *b
       tma_load_2d(map, bar, dst + j * (KE * 128), row0 + j * PER_BOX, k0);
   } else {
     tma_load_2d(map, bar, dst, k0, row0);
+  }
+}
+
+// The same loads for a CTA pair: into this CTA's shared memory, completion counted on the
+// barrier at cluster-window address bar0 (rank 0's).
+template <bool MN, int ROWS, int KE, int ES>
+__device__ __forceinline__ void load_operand_pair(const CUtensorMap *map, uint32_t bar0,
+                                                  uint8_t *dst, int row0, int k0) {
+  if constexpr (MN) {
+    constexpr int PER_BOX = 128 / ES;
+#pragma unroll
+    for (int j = 0; j < ROWS / PER_BOX; ++j)
+      tma_load_2d_pair(map, bar0, dst + j * (KE * 128), row0 + j * PER_BOX, k0);
+  } else {
+    tma_load_2d_pair(map, bar0, dst, k0, row0);
   }
 }
 
@@ -307,10 +328,12 @@ __device__ __forceinline__ float cvt_acc(uint32_t b) {
 // its last TMEM read has completed, not after its stores, so the next MMA into this accumulator
 // overlaps the conversion and stores: a bf16 group waits in the staging buffer, its TMA store
 // deferred, while the next group is read from TMEM.
-__device__ __forceinline__ void release_accumulator(uint64_t *tempty_bar, int lane) {
+// tempty_addr: the barrier's address in the cluster shared window (this CTA's own barrier, or
+// rank 0's when a CTA pair shares the accumulator-free barrier).
+__device__ __forceinline__ void release_accumulator(uint32_t tempty_addr, int lane) {
   tc_fence_before();
   __syncwarp();
-  if (lane == 0) mbar_arrive(tempty_bar);
+  if (lane == 0) mbar_arrive_cluster(tempty_addr);
 }
 // Returns whether it arrived on tempty_bar (not when the warp's columns lie past the output).
 template <int CONV, int HALF>
@@ -319,7 +342,7 @@ __device__ __forceinline__ bool epilogue_tma(const CUtensorMap *map, uint8_t *st
                                              bool bf16_out, bool scaled, float a_s,
                                              const float *bs, const CUtensorMap *rmap,
                                              uint64_t *rbar, uint32_t &rphase,
-                                             uint64_t *tempty_bar) {
+                                             uint32_t tempty_bar) {
   if (bf16_out) {
     if (x0 >= x_end) return false;
     int pending = -1;  // column of the group staged but not yet stored
@@ -412,13 +435,13 @@ __device__ __forceinline__ bool epilogue_tma(const CUtensorMap *map, uint8_t *st
   }
 }
 
-template <typename T, bool A_MN, bool B_MN, int BN, int STAGES, int EPI>
+template <typename T, bool A_MN, bool B_MN, int BN, int STAGES, int EPI, int CG>
 __global__ void __launch_bounds__(64 + 32 * EPI, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                      const __grid_constant__ CUtensorMap tma_b,
                      const __grid_constant__ CUtensorMap tma_c,
                      const __grid_constant__ CUtensorMap tma_r, GemmArgs p) {
-  using C = GemmCfg<T, A_MN, B_MN, BN, STAGES, EPI>;
+  using C = GemmCfg<T, A_MN, B_MN, BN, STAGES, EPI, CG>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -435,6 +458,10 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
   __shared__ __align__(16) float s_bscale[BN];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // CTA pair: rank 0 issues the MMAs of the pair; both ranks load and run the epilogue
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const int group = CG == 2 ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int groups = CG == 2 ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   pdl_trigger();  // the next kernel may launch and set itself up while this one runs
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -443,7 +470,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], C::EPI_WARPS);
+      // rank 0's barrier collects the epilogue warps of both CTAs of a pair
+      mbar_init(&tempty[b], C::EPI_WARPS * CG);
     }
     for (int w = 0; w < C::EPI_WARPS; ++w) mbar_init(&rfull[w], 1);
     fence_barrier_init();
@@ -453,11 +481,19 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
     if (p.residual != nullptr && p.tma_store) tma_prefetch_desc(&tma_r);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync();  // both CTAs' barriers exist before either signals the other's
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   // set-up above touches no global memory; operands, scales and outputs only after the
@@ -487,35 +523,57 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int u = group; u < units && ok; u += groups) {
         const uint32_t uu = static_cast<uint32_t>(u);
         const uint32_t rest = uu / tiles_n;
         const int tn = static_cast<int>(uu - rest * tiles_n);
         const int tm = static_cast<int>(rest % static_cast<uint32_t>(p.tiles_m));
         int kb0, kb1;
         k_range(uu, kb0, kb1);
+        const int a_row = tm * C::TILE_M + static_cast<int>(rank) * C::BM;
+        const int b_row = tn * BN + static_cast<int>(rank) * C::B_ROWS;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          load_operand<A_MN, C::BM, C::KE, C::ES>(&tma_a, &full[stage],
-                                                  a_tiles + stage * C::A_BYTES, tm * C::BM,
-                                                  kb * C::KE);
-          load_operand<B_MN, BN, C::KE, C::ES>(&tma_b, &full[stage],
-                                               b_tiles + stage * C::B_BYTES, tn * BN, kb * C::KE);
+          if constexpr (CG == 2) {
+            // both CTAs' loads complete on rank 0's full barrier, which expects the bytes of both
+            const uint32_t bar0 = mapa_shared(smem_u32(&full[stage]), 0);
+            if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+            load_operand_pair<A_MN, C::BM, C::KE, C::ES>(&tma_a, bar0,
+                                                         a_tiles + stage * C::A_BYTES, a_row,
+                                                         kb * C::KE);
+            load_operand_pair<B_MN, C::B_ROWS, C::KE, C::ES>(&tma_b, bar0,
+                                                             b_tiles + stage * C::B_BYTES, b_row,
+                                                             kb * C::KE);
+          } else {
+            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            load_operand<A_MN, C::BM, C::KE, C::ES>(&tma_a, &full[stage],
+                                                    a_tiles + stage * C::A_BYTES, a_row,
+                                                    kb * C::KE);
+            load_operand<B_MN, BN, C::KE, C::ES>(&tma_b, &full[stage],
+                                                 b_tiles + stage * C::B_BYTES, b_row, kb * C::KE);
+          }
+          if (++stage == STAGES) stage = 0, phase ^= 1;
+        }
+      }
+      if constexpr (CG == 2) {
+        // producer tail: every stage this CTA filled has been released (rank 0's MMA commits
+        // arrive on this CTA's barriers) before the CTA can leave
+        for (int i = 0; i < STAGES && ok; ++i) {
+          ok = mbar_wait(&empty[stage], phase ^ 1);
           if (++stage == STAGES) stage = 0, phase ^= 1;
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       int stage = 0, acc = 0;
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true;
       const uint32_t a_base = smem_u32(a_tiles), b_base = smem_u32(b_tiles);
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      for (int u = group; u < units && ok; u += groups) {
         int kb0, kb1;
         k_range(static_cast<uint32_t>(u), kb0, kb1);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1)) break;
@@ -534,15 +592,28 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
             const uint64_t ad = operand_desc<A_MN, C::KE, C::UK>(a_addr, j);
             const uint64_t bd = operand_desc<B_MN, C::KE, C::UK>(b_addr, j);
             const uint32_t accumulate = (kb > kb0 || j > 0) ? 1u : 0u;
-            if constexpr (sizeof(T) == 1)
+            if constexpr (CG == 2) {
+              if constexpr (sizeof(T) == 1)
+                umma_i8_pair(d_tmem, ad, bd, C::IDESC, accumulate);
+              else
+                umma_f16_pair(d_tmem, ad, bd, C::IDESC, accumulate);
+            } else if constexpr (sizeof(T) == 1) {
               umma_i8(d_tmem, ad, bd, C::IDESC, accumulate);
-            else
+            } else {
               umma_f16(d_tmem, ad, bd, C::IDESC, accumulate);
+            }
           }
-          umma_commit(&empty[stage]);
+          // the stage is free in both CTAs once these MMAs have read it
+          if constexpr (CG == 2)
+            umma_commit_pair(&empty[stage]);
+          else
+            umma_commit(&empty[stage]);
           if (++stage == STAGES) stage = 0, phase ^= 1;
         }
-        umma_commit(&tfull[acc]);
+        if constexpr (CG == 2)
+          umma_commit_pair(&tfull[acc]);
+        else
+          umma_commit(&tfull[acc]);
         if (++acc == 2) acc = 0, acc_phase ^= 1;
       }
     }
@@ -558,7 +629,10 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     uint32_t rphase = 0;  // parity of this warp's residual barrier
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+    // the accumulator-free barriers live in rank 0 (its MMA thread waits on them)
+    const uint32_t tempty0 = CG == 2 ? mapa_shared(smem_u32(&tempty[0]), 0) : smem_u32(&tempty[0]);
+    const uint32_t tempty1 = CG == 2 ? mapa_shared(smem_u32(&tempty[1]), 0) : smem_u32(&tempty[1]);
+    for (int u = group; u < units; u += groups) {
       const uint32_t uu = static_cast<uint32_t>(u);
       const uint32_t rest = uu / tiles_n;
       const int tn = static_cast<int>(uu - rest * tiles_n);
@@ -566,7 +640,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
       const int split = static_cast<int>(uu / tiles_mn);
       const int tile = tm * p.tiles_n + tn;
       const int trow = sub * 32 + lane;
-      const int row = tm * C::BM + trow;
+      const int row = tm * C::TILE_M + static_cast<int>(rank) * C::BM + trow;
       // this tile's scales, requested before the wait so that their latency overlaps the MMA
       const bool scaled = p.epi == EPI_SCALED && p.tma_store;
       static_assert(BN <= 32 * C::EPI_WARPS, "one column scale per epilogue thread");
@@ -595,6 +669,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(sub * 32) << 16) +
                              static_cast<uint32_t>(acc * BN + col0);
       bool released = false;  // the epilogue has arrived on tempty[acc] itself
+      const uint32_t tempty_addr = acc == 0 ? tempty0 : tempty1;
       if (p.tma_store) {
         // column scales of this tile in shared memory; the barrier above also guarantees that
         // every warp has finished reading the previous tile's (barrier 1: the epilogue warps)
@@ -606,8 +681,9 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
             !split_mode && (p.out_dtype == RT_BF16 || p.epi == EPI_BF16_STORE);
         // split mode: the fp32 partial tile goes to its own 128 x BN block of the workspace
         const int y = split_mode
-                          ? (split * p.tiles_m * p.tiles_n + tile) * C::BM + sub * 32
-                          : tm * C::BM + sub * 32;
+                          ? (split * p.tiles_m * p.tiles_n + tile) * C::TILE_M +
+                                static_cast<int>(rank) * C::BM + sub * 32
+                          : tm * C::TILE_M + static_cast<int>(rank) * C::BM + sub * 32;
         const int x0 = (split_mode ? 0 : tn * BN) + col0;
         const int x_end = split_mode ? BN : p.N;
         const float *bs = s_bscale + col0;
@@ -619,14 +695,14 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
           if (p.acc_small)
             released = epilogue_tma<1, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y,
                                              bf16_out, scaled, a_s, bs, rmap, rbar, rphase,
-                                             &tempty[acc]);
+                                             tempty_addr);
           else
             released = epilogue_tma<2, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y,
                                              bf16_out, scaled, a_s, bs, rmap, rbar, rphase,
-                                             &tempty[acc]);
+                                             tempty_addr);
         } else {
           released = epilogue_tma<0, HALF>(&tma_c, staging, lane, t_row, x0, x_end, y, bf16_out,
-                                           scaled, a_s, bs, rmap, rbar, rphase, &tempty[acc]);
+                                           scaled, a_s, bs, rmap, rbar, rphase, tempty_addr);
         }
       } else {
 #pragma unroll 1
@@ -639,17 +715,26 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1)
           epilogue_chunk<T>(p, p.epi, row, n0, r);
         }
       }
-      if (!released) release_accumulator(&tempty[acc], lane);
+      if (!released) release_accumulator(tempty_addr, lane);
       if (++acc == 2) acc = 0, acc_phase ^= 1;
     }
     if (p.tma_store && lane == 0) bulk_wait_all();  // staged stores done before the CTA exits
   }
   __syncwarp();
   tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  if constexpr (CG == 2) {
+    // neither CTA leaves while the other may still signal its barriers or read its tiles
+    cluster_sync();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+    }
+  } else {
+    __syncthreads();
+    if (warp == 1) {
+      tc_fence_after();
+      tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
   }
 }
 
@@ -698,6 +783,23 @@ __global__ void simt_gradw_kernel(const uint16_t *g, int64_t ldg, const uint16_t
   } else {
     static_cast<uint16_t *>(out)[n * ldo + k] = bf16_bits(acc);
   }
+}
+
+__global__ void simt_matmul_bf16_kernel(const uint16_t *a, int64_t lda, const uint16_t *b,
+                                        int64_t ldb, void *out, int out_dtype, int64_t ldo,
+                                        int64_t M, int64_t N, int64_t K) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t n = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t m = blockIdx.y * static_cast<int64_t>(blockDim.y) + threadIdx.y;
+  if (m >= M || n >= N) return;
+  float acc = 0.0f;
+  for (int64_t k = 0; k < K; ++k)
+    acc = __fadd_rn(acc, __fmul_rn(bf16_from_bits(a[m * lda + k]), bf16_from_bits(b[k * ldb + n])));
+  if (out_dtype == RT_F32)
+    static_cast<float *>(out)[m * ldo + n] = acc;
+  else
+    static_cast<uint16_t *>(out)[m * ldo + n] = bf16_bits(acc);
 }
 
 // -------------------------------------------------------------------------------------------
@@ -760,17 +862,19 @@ static int operand_map(CUtensorMap *map, const Operand &o, int tile_rows) {
     return make_map(map, dt, o.ptr, o.extent_k, o.rows_mn, o.ld * sizeof(T), Cfg::KE, tile_rows);
 }
 
-template <typename T, bool A_MN, bool B_MN, int BN, int STAGES, int EPI = 8>
+template <typename T, bool A_MN, bool B_MN, int BN, int STAGES, int EPI = 8, int CG = 1>
 static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaStream_t s) {
-  using C = GemmCfg<T, A_MN, B_MN, BN, STAGES, EPI>;
+  using C = GemmCfg<T, A_MN, B_MN, BN, STAGES, EPI, CG>;
   CUtensorMap ma, mb, mc, mr;
   memset(&mr, 0, sizeof(mr));
   memset(&mc, 0, sizeof(mc));
   int rc = operand_map<T, A_MN>(&ma, a, C::BM);
   if (rc) return rc;
-  rc = operand_map<T, B_MN>(&mb, b, BN);
+  rc = operand_map<T, B_MN>(&mb, b, C::B_ROWS);
   if (rc) return rc;
-  args.tiles_m = static_cast<int>((args.M + C::BM - 1) / C::BM);
+  if (CG == 2 && args.splits > 1)
+    return fail(RT_ERR_UNSUPPORTED, "umma_gemm: CTA-pair tiles take no split-K");
+  args.tiles_m = static_cast<int>((args.M + C::TILE_M - 1) / C::TILE_M);
   args.tiles_n = static_cast<int>((args.N + BN - 1) / BN);
   args.kblocks = static_cast<int>((args.K + C::KE - 1) / C::KE);
   if (args.splits < 1) args.splits = 1;
@@ -813,7 +917,8 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
   if ((rc = rt_sm_count(&sms)) != RT_OK) return rc;
   static std::mutex mu;
   static bool configured[64] = {false};
-  auto kernel = umma_gemm_kernel<T, A_MN, B_MN, BN, STAGES, EPI>;
+  static int pair_slots[64] = {0};  // co-resident CTA pairs of this kernel per device
+  auto kernel = umma_gemm_kernel<T, A_MN, B_MN, BN, STAGES, EPI, CG>;
   {
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
@@ -821,12 +926,34 @@ static int launch_umma(const Operand &a, const Operand &b, GemmArgs args, cudaSt
           cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
       if (e != cudaSuccess)
         return fail(RT_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      if constexpr (CG == 2) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1));
+        cfg.blockDim = dim3(C::THREADS);
+        cfg.dynamicSmemBytes = C::SMEM_BYTES;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2, attr[0].val.clusterDim.y = 1, attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr, cfg.numAttrs = 1;
+        int clusters = 0;
+        e = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg);
+        if (e != cudaSuccess || clusters < 1)
+          return fail(RT_ERR_CUDA, "cudaOccupancyMaxActiveClusters: %s (%d)",
+                      cudaGetErrorString(e), clusters);
+        pair_slots[dev] = clusters;
+      }
       configured[dev] = true;
     }
   }
   const int64_t units = static_cast<int64_t>(args.tiles_m) * args.tiles_n * args.splits;
-  const int grid = static_cast<int>(units < sms ? units : sms);
-  launch_k(kernel, grid, C::THREADS, C::SMEM_BYTES, s, ma, mb, mc, mr, args);
+  if constexpr (CG == 2) {
+    const int64_t slots = dev >= 0 && dev < 64 ? pair_slots[dev] : sms / 2;
+    const int pairs = static_cast<int>(units < slots ? units : slots);
+    launch_k_cluster2(kernel, 2 * pairs, C::THREADS, C::SMEM_BYTES, s, ma, mb, mc, mr, args);
+  } else {
+    const int grid = static_cast<int>(units < sms ? units : sms);
+    launch_k(kernel, grid, C::THREADS, C::SMEM_BYTES, s, ma, mb, mc, mr, args);
+  }
   return check_launch("umma_gemm_kernel");
 }
 
@@ -881,16 +1008,28 @@ extern "C" int rt_scaled_int8_mm(const int8_t *lhs, int64_t lhs_stride_m, int64_
     Operand A{lhs, a_mn, a_k ? lhs_stride_m : lhs_stride_k, M, K};
     Operand B{rhs, b_mn, b_k ? rhs_stride_n : rhs_stride_k, N, K};
     const bool narrow = N <= 128;
-    // fp32 outputs (twice the bytes per tile, and the residual tiles) run sixteen epilogue warps
-    // over three stages; bf16 outputs eight warps over four stages (measured faster each way)
+    // fp32 outputs (twice the bytes per tile, and the residual tiles) run sixteen epilogue warps;
+    // bf16 outputs eight (measured faster each way).  Wide tiles run on CTA pairs: 256 x 256
+    // per pair, each SM loading 128 rows of A and 128 of B per stage instead of 128 + 256
+#define RT_GO(AMN, BMN)                                                                     \
+  if (narrow) return launch_umma<int8_t, AMN, BMN, 128, 6>(A, B, args, s);                  \
+  if (pair) return wide_epi ? launch_umma<int8_t, AMN, BMN, 256, 5, 16, 2>(A, B, args, s)   \
+                            : launch_umma<int8_t, AMN, BMN, 256, 6, 8, 2>(A, B, args, s);   \
+  return wide_epi ? launch_umma<int8_t, AMN, BMN, 256, 3, 16>(A, B, args, s)                \
+                  : launch_umma<int8_t, AMN, BMN, 256, 4>(A, B, args, s)
     const bool wide_epi = out_dtype == RT_F32;
-#define RT_GO(AMN, BMN)                                                              \
-  return narrow ? launch_umma<int8_t, AMN, BMN, 128, 6>(A, B, args, s)               \
-                : (wide_epi ? launch_umma<int8_t, AMN, BMN, 256, 3, 16>(A, B, args, s) \
-                            : launch_umma<int8_t, AMN, BMN, 256, 4>(A, B, args, s))
-    if (!a_mn && !b_mn) RT_GO(false, false);
-    if (!a_mn && b_mn) RT_GO(false, true);
-    if (a_mn && !b_mn) RT_GO(true, false);
+    // pairs pay off where the MMA sets the pace (long contractions); at K = 512 the tile period
+    // is the epilogue's and the pair's cluster set-up only adds to it (measured both ways)
+    const bool pair = pair_enabled() && M > 128 && K >= 1024;
+    if (!a_mn && !b_mn) {
+      RT_GO(false, false);
+    }
+    if (!a_mn && b_mn) {
+      RT_GO(false, true);
+    }
+    if (a_mn && !b_mn) {
+      RT_GO(true, false);
+    }
     RT_GO(true, true);
 #undef RT_GO
   }
@@ -920,9 +1059,15 @@ extern "C" int rt_matmul_bf16(const void *a, int64_t lda, const void *b, int64_t
     return e == cudaSuccess ? RT_OK : fail(RT_ERR_CUDA, "matmul_bf16 memset: %s", cudaGetErrorString(e));
   }
   // A (M x K) row-major is K-major; B (K x N) row-major is MN-major: the tcgen05 kind::f16 GEMM
-  // reads both in place (no transposed or padded copies)
-  if (!aligned16(a) || !aligned16(b) || (lda * 2) % 16 != 0 || (ldb * 2) % 16 != 0)
-    return fail(RT_ERR_ALIGNMENT, "matmul_bf16: operands need 16-byte aligned rows");
+  // reads both in place (no transposed or padded copies).  Rows TMA cannot address (not 16-byte
+  // aligned) take a SIMT kernel with fp32 accumulation.
+  if (!aligned16(a) || !aligned16(b) || (lda * 2) % 16 != 0 || (ldb * 2) % 16 != 0) {
+    const dim3 block(32, 8);
+    const dim3 grid(static_cast<unsigned>((N + 31) / 32), static_cast<unsigned>((M + 7) / 8));
+    launch_k(simt_matmul_bf16_kernel, grid, block, 0, s, static_cast<const uint16_t *>(a), lda,
+             static_cast<const uint16_t *>(b), ldb, out, out_dtype, ldo, M, N, K);
+    return check_launch("simt_matmul_bf16_kernel");
+  }
   GemmArgs args{};
   args.M = static_cast<int>(M), args.N = static_cast<int>(N), args.K = static_cast<int>(K);
   args.out = out, args.ldo = ldo, args.out_dtype = out_dtype, args.splits = 1;
@@ -931,6 +1076,8 @@ extern "C" int rt_matmul_bf16(const void *a, int64_t lda, const void *b, int64_t
   Operand A{a, false, lda, M, K};
   Operand B{b, true, ldb, N, K};
   if (N <= 128) return launch_umma<__nv_bfloat16, false, true, 128, 6>(A, B, args, s);
+  if (pair_enabled() && M > 128 && K >= 1024)
+    return launch_umma<__nv_bfloat16, false, true, 256, 6, 8, 2>(A, B, args, s);
   return launch_umma<__nv_bfloat16, false, true, 256, 4>(A, B, args, s);
 }
 
@@ -1038,7 +1185,7 @@ static int grad_weight_impl(const void *g, int64_t ldg, const void *x, int64_t l
   if (out_dtype == RT_BF16 && accumulate)
     return fail(RT_ERR_UNSUPPORTED, "grad_weight: accumulate needs a float32 output");
   if (N == 0 || K == 0) return RT_OK;
-  if (g == nullptr || x == nullptr || out == nullptr)
+  if (out == nullptr || (M_tok > 0 && (g == nullptr || x == nullptr)))
     return fail(RT_ERR_INVALID_ARGUMENT, "grad_weight: null pointer");
   if (workspace != nullptr && (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
     return fail(RT_ERR_ALIGNMENT, "grad_weight: workspace must be 256-byte aligned");
@@ -1079,6 +1226,8 @@ static int grad_weight_impl(const void *g, int64_t ldg, const void *x, int64_t l
     // A = gᵀ: (N × M_tok) with N contiguous (MN-major); B = x: (K × M_tok) with K contiguous.
     Operand A{g, true, ldg, N, M_tok};
     Operand B{x, true, ldx, K, M_tok};
+    if (splits == 1 && pair_enabled() && N > 128 && M_tok >= 1024)
+      return launch_umma<__nv_bfloat16, true, true, 256, 6, 8, 2>(A, B, args, s);
     rc = launch_umma<__nv_bfloat16, true, true, GW_BN, 4>(A, B, args, s);
     if (rc || splits == 1) return rc;
     // the partial tiles, summed in split order into the output

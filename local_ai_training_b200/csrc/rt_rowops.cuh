@@ -1316,6 +1316,9 @@ struct RmsBwdArgs {
   float *dw;
   const float *dx_add;  // optional fp32 gradient added to dx (the residual branch), may be dx
   QuantArgs sq;         // SRQ: stochastic-rounding quantisation of dx for the layer it feeds
+  // dw != null: per-CTA partial rows of dw (vectorised kernel, [gridDim.x][cols]) or per-row
+  // rsqrt values (generic kernel, [rows]); a second kernel sums them in a fixed order into dw
+  float *dw_work;
 };
 // X: input dtype, G: incoming-gradient dtype (fp32 or bf16 each).  SRQ: dx (the output gradient
 // of the ratchet layer whose output is this norm's input) is also quantised with stochastic
@@ -1427,8 +1430,10 @@ __global__ void __launch_bounds__(CTA, 2) rmsnorm_bwd_kernel(RmsBwdArgs a) {
     }
   }
   if (a.dw != nullptr) {
-    // sum the RPC row-partials of the CTA in shared memory, then one reduction per column per
-    // CTA (the grid is about one CTA per SM, so the tiny dw buffer sees few atomics)
+    // the CTA's partial row of dw: its RPC sub-row partials summed in shared memory in sub
+    // order, stored to this CTA's row of the workspace; dw_partials_reduce_kernel then adds the
+    // CTA rows in index order (deterministic, unlike one atomic per column per CTA)
+    float *part = a.dw_work + static_cast<int64_t>(blockIdx.x) * a.cols;
     extern __shared__ float dws[];  // [RPC][cols] when RPC > 1
     if constexpr (RPC > 1) {
 #pragma unroll
@@ -1442,15 +1447,14 @@ __global__ void __launch_bounds__(CTA, 2) rmsnorm_bwd_kernel(RmsBwdArgs a) {
       for (int64_t k = threadIdx.x; k < a.cols; k += CTA) {
         float acc = dws[k];
         for (int r2 = 1; r2 < RPC; ++r2) acc = __fadd_rn(acc, dws[r2 * a.cols + k]);
-        atomicAdd(a.dw + k, acc);
+        part[k] = acc;
       }
     } else {
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int64_t c = t + static_cast<int64_t>(i) * RT;
         if (c >= nch) continue;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) atomicAdd(a.dw + 8 * c + j, dwp[i][j]);
+        st8(part + 8 * c, dwp[i]);
       }
     }
   }
@@ -1489,8 +1493,35 @@ __global__ void __launch_bounds__(CTA)
     float o = bf16_round(v);
     if (a.dx_add != nullptr) o = __fadd_rn(a.dx_add[row * a.cols + k], o);
     store_elem(a.dx, a.dx_dtype, row * a.cols + k, o);
-    if (a.dw != nullptr) atomicAdd(a.dw + k, __fmul_rn(__fmul_rn(g, xv), r));
   }
+  if (a.dw != nullptr && threadIdx.x == 0) a.dw_work[row] = r;  // dw_rows_reduce_kernel's input
+}
+
+// dw[k] += sum over partial rows p = 0..parts-1 (in order) of part[p][k]: the fixed-order
+// reduction of the vectorised RMSNorm backward's per-CTA partials.
+__global__ void __launch_bounds__(256)
+    dw_partials_reduce_kernel(const float *__restrict__ part, int parts, int64_t cols, float *dw) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (k >= cols) return;
+  float acc = part[k];
+  for (int p = 1; p < parts; ++p) acc = __fadd_rn(acc, part[static_cast<int64_t>(p) * cols + k]);
+  dw[k] = __fadd_rn(dw[k], acc);
+}
+// dw[k] += sum over rows (in order) of (gy·x)·r[row]: the generic kernel's weight gradient.
+__global__ void __launch_bounds__(256)
+    dw_rows_reduce_kernel(const void *gy, int gdt, const void *x, int xdt, const float *r,
+                          int64_t rows, int64_t cols, float *dw) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (k >= cols) return;
+  float acc = 0.0f;
+  for (int64_t row = 0; row < rows; ++row)
+    acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(load_elem(gy, gdt, row * cols + k),
+                                             load_elem(x, xdt, row * cols + k)), r[row]));
+  dw[k] = __fadd_rn(dw[k], acc);
 }
 
 template <typename T>
@@ -1976,22 +2007,46 @@ extern "C" int rt_transpose_quantize(const void *x, int x_dtype, int64_t batch, 
   return check_launch("rt_transpose_quantize");
 }
 
-static int rmsnorm_backward_launch(const RmsBwdArgs &a, int gy_dtype, int x_dtype, bool srq,
-                                   const char *who, cudaStream_t s) {
+// Launch shape of the RMSNorm backward: cfg.rt == 0 for the generic kernel (one CTA per row).
+static RowCfg rmsnorm_bwd_cfg(const RmsBwdArgs &a, bool srq) {
   const bool vec = a.cols % 8 == 0 && aligned16(a.x) && aligned16(a.gy) && aligned16(a.dx) &&
                    aligned16(a.w) && (a.dw == nullptr || aligned16(a.dw)) &&
-                   (a.dx_add == nullptr || aligned16(a.dx_add)) && (!srq || sr_outputs_vec(a.sq));
-  const RowCfg cfg = vec ? row_cfg_narrow(a.cols / 8) : RowCfg{0, 0};
+                   (a.dx_add == nullptr || aligned16(a.dx_add)) && (!srq || sr_outputs_vec(a.sq)) &&
+                   (a.dw == nullptr || aligned16(a.dw_work));
+  return vec ? row_cfg_narrow(a.cols / 8) : RowCfg{0, 0};
+}
+static int64_t rmsnorm_bwd_grid(int64_t rows, const RowCfg &cfg) {
+  if (cfg.rt == 0) return rows;
+  int sms = 0;
+  rt_sm_count(&sms);
+  const int64_t groups = (rows + (CTA / cfg.rt) - 1) / (CTA / cfg.rt);
+  const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 2;
+  return groups < cap ? groups : cap;
+}
+// Workspace of the weight gradient: per-CTA partial rows (vectorised) or per-row rsqrt (generic);
+// the larger of the two, so that it does not depend on the operands' alignment.
+static int64_t rmsnorm_bwd_work_bytes(int64_t rows, int64_t cols) {
+  const RowCfg cfg = row_cfg_narrow(cols / 8);
+  const int64_t vec = cfg.rt == 0 || cols % 8 ? 0 : rmsnorm_bwd_grid(rows, cfg) * cols * 4;
+  const int64_t gen = rows * 4;
+  return vec > gen ? vec : gen;
+}
+
+static int rmsnorm_backward_launch(const RmsBwdArgs &a, int gy_dtype, int x_dtype, bool srq,
+                                   const char *who, cudaStream_t s) {
+  const RowCfg cfg = rmsnorm_bwd_cfg(a, srq);
   if (cfg.rt == 0) {
     if (srq) return fail(RT_ERR_UNSUPPORTED, "rt_rmsnorm_backward_sr: rows need 16-byte chunks");
     launch_k(rmsnorm_bwd_generic_kernel, static_cast<unsigned>(a.rows), CTA, 0, s, a, gy_dtype, x_dtype);
-    return check_launch(who);
+    if (int rc = check_launch(who)) return rc;
+    if (a.dw != nullptr) {
+      launch_k(dw_rows_reduce_kernel, static_cast<unsigned>((a.cols + 255) / 256), 256, 0, s, a.gy,
+               gy_dtype, a.x, x_dtype, static_cast<const float *>(a.dw_work), a.rows, a.cols, a.dw);
+      return check_launch(who);
+    }
+    return RT_OK;
   }
-  int sms = 0;
-  rt_sm_count(&sms);
-  const int64_t groups = (a.rows + (CTA / cfg.rt) - 1) / (CTA / cfg.rt);
-  const int64_t cap = static_cast<int64_t>(sms > 0 ? sms : 148) * 2;
-  const unsigned grid = static_cast<unsigned>(groups < cap ? groups : cap);
+  const unsigned grid = static_cast<unsigned>(rmsnorm_bwd_grid(a.rows, cfg));
   const size_t dsm = (a.dw != nullptr && cfg.rt < CTA) ? (CTA / cfg.rt) * a.cols * sizeof(float) : 0;
   if (dsm > 48 * 1024) return fail(RT_ERR_UNSUPPORTED, "rt_rmsnorm_backward: row too long");
   const int combo = (x_dtype == RT_F32 ? 0 : 2) + (gy_dtype == RT_F32 ? 0 : 1);
@@ -2018,19 +2073,41 @@ static int rmsnorm_backward_launch(const RmsBwdArgs &a, int gy_dtype, int x_dtyp
     }
   }
 #undef RT_RMSB
-  return check_launch(who);
+  if (int rc = check_launch(who)) return rc;
+  if (a.dw != nullptr) {
+    launch_k(dw_partials_reduce_kernel, static_cast<unsigned>((a.cols + 255) / 256), 256, 0, s,
+             static_cast<const float *>(a.dw_work), static_cast<int>(grid), a.cols, a.dw);
+    return check_launch(who);
+  }
+  return RT_OK;
+}
+
+extern "C" int64_t rt_rmsnorm_backward_workspace_bytes(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return rmsnorm_bwd_work_bytes(rows, cols);
+}
+
+static int rmsnorm_dw_work_check(float *dw, float *work, int64_t work_bytes, int64_t rows,
+                                 int64_t cols, const char *who) {
+  if (dw != nullptr && (work == nullptr || work_bytes < rmsnorm_bwd_work_bytes(rows, cols)))
+    return fail(RT_ERR_INVALID_ARGUMENT,
+                "%s: the weight gradient needs a workspace of rt_rmsnorm_backward_workspace_bytes",
+                who);
+  return RT_OK;
 }
 
 extern "C" int rt_rmsnorm_backward(const void *grad_y, int gy_dtype, const void *x, int x_dtype,
                                    const float *weight, double eps, int64_t rows, int64_t cols,
                                    void *dx, int dx_dtype, float *dw, const float *dx_add,
-                                   void *stream) {
+                                   float *dw_work, int64_t dw_work_bytes, void *stream) {
   if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_rmsnorm_backward: shape");
   if (rows == 0) return RT_OK;
   if (dx_add != nullptr && dx_dtype != RT_F32)
     return fail(RT_ERR_DTYPE, "rt_rmsnorm_backward: an added gradient needs a float32 dx");
+  if (int rc = rmsnorm_dw_work_check(dw, dw_work, dw_work_bytes, rows, cols, "rt_rmsnorm_backward"))
+    return rc;
   RmsBwdArgs a{grad_y, x, weight, static_cast<float>(eps), rows, cols, dx, dx_dtype, dw, dx_add,
-               QuantArgs{}};
+               QuantArgs{}, dw_work};
   return rmsnorm_backward_launch(a, gy_dtype, x_dtype, false, "rt_rmsnorm_backward",
                                  as_stream(stream));
 }
@@ -2041,9 +2118,13 @@ extern "C" int rt_rmsnorm_backward_sr(const void *grad_y, int gy_dtype, const vo
                                       const float *col_scale, int round_input_bf16, uint64_t seed,
                                       uint32_t step, uint32_t layer, uint32_t *step_dev, int8_t *q,
                                       int64_t ldq, float *row_scale, void *x_bf16_out,
-                                      int64_t ld_xbf16, void *stream) {
+                                      int64_t ld_xbf16, float *dw_work, int64_t dw_work_bytes,
+                                      void *stream) {
   if (rows < 0 || cols <= 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_rmsnorm_backward_sr: shape");
   if (rows == 0) return RT_OK;
+  if (int rc = rmsnorm_dw_work_check(dw, dw_work, dw_work_bytes, rows, cols,
+                                     "rt_rmsnorm_backward_sr"))
+    return rc;
   if (dx_add != nullptr && dx_dtype != RT_F32)
     return fail(RT_ERR_DTYPE, "rt_rmsnorm_backward_sr: an added gradient needs a float32 dx");
   if (q == nullptr || row_scale == nullptr)
@@ -2051,7 +2132,8 @@ extern "C" int rt_rmsnorm_backward_sr(const void *grad_y, int gy_dtype, const vo
   QuantArgs sq{dx, rows, cols, cols, 1, col_scale, 1,
                dx_dtype == RT_F32 && round_input_bf16, seed, step, layer, step_dev, q, ldq,
                row_scale, static_cast<unsigned short *>(x_bf16_out), ld_xbf16};
-  RmsBwdArgs a{grad_y, x, weight, static_cast<float>(eps), rows, cols, dx, dx_dtype, dw, dx_add, sq};
+  RmsBwdArgs a{grad_y, x, weight, static_cast<float>(eps), rows, cols, dx, dx_dtype, dw, dx_add, sq,
+               dw_work};
   return rmsnorm_backward_launch(a, gy_dtype, x_dtype, true, "rt_rmsnorm_backward_sr",
                                  as_stream(stream));
 }

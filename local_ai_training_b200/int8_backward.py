@@ -77,19 +77,23 @@ def rmsnorm_backward(grad_y: Tensor, x: Tensor, w: Tensor, eps: float = 1e-5, *,
         sr = _SrOutputs(quant_plan, m, k, grad_x)
         if not sr.usable():
             sr = None
+    # the weight gradient's per-CTA partial rows, summed in a fixed order by the library
+    need = _lib.lib().rt_rmsnorm_backward_workspace_bytes(m, k)
+    work = _lib.workspace(x.device, need)
     ev = _lib.prof_start(x_flat)
     if sr is not None:
         _lib.check(_lib.lib().rt_rmsnorm_backward_sr(
             gy_flat.data_ptr(), _lib.dtype_code(gy_flat), x_flat.data_ptr(),
             _lib.dtype_code(x_flat), wf.data_ptr(), float(eps), m, k, grad_x.data_ptr(),
             _lib.dtype_code(grad_x), grad_w.data_ptr(), _lib.ptr(add), *sr.args(),
-            _lib.stream_of(x_flat)))
+            _lib.ptr(work), need, _lib.stream_of(x_flat)))
         sr.deliver(grad_x)
     else:
         _lib.check(_lib.lib().rt_rmsnorm_backward(
             gy_flat.data_ptr(), _lib.dtype_code(gy_flat), x_flat.data_ptr(),
             _lib.dtype_code(x_flat), wf.data_ptr(), float(eps), m, k, grad_x.data_ptr(),
-            _lib.dtype_code(grad_x), grad_w.data_ptr(), _lib.ptr(add), _lib.stream_of(x_flat)))
+            _lib.dtype_code(grad_x), grad_w.data_ptr(), _lib.ptr(add), _lib.ptr(work), need,
+            _lib.stream_of(x_flat)))
     _lib.prof_stop(ev, "rmsnorm_bwd" if sr is None else "rmsnorm_bwd_sr", x_flat, 0.0,
                    m * k * (gy_flat.element_size() + x_flat.element_size() + grad_x.element_size()
                             + (0 if add is None else 4)

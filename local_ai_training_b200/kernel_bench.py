@@ -26,6 +26,7 @@ from .int8_matmul import (
 )
 
 SHAPES = [(512, 512), (512, 2048), (2048, 512)]  # (K in, N out) of the 25M model's ratchet layers
+SHAPES_1B = [(2048, 6144), (2048, 2048), (2048, 8192), (8192, 2048)]  # the ~1B model's layers
 
 
 def _peaks() -> dict:
@@ -144,6 +145,50 @@ def bench_dequant(m, k, reps, flush, peaks):
     return _report("dequant", [m, k], t, 3 * m * k + 4 * m, 0, 0, peaks)
 
 
+def bench_update_grouped(shapes, reps, flush, peaks, name):
+    """One grouped update launch per row length over the layers `shapes` ((rows, cols) each,
+    bf16 gradients), as the train step runs it after backward."""
+    dev = torch.device("cuda")
+    groups: dict = {}
+    keep = []
+    for rows, cols in shapes:
+        grad = (torch.randn(rows, cols, device=dev) * 1e-3).to(torch.bfloat16)
+        packed = (torch.randint(0, 7, (rows, cols), device=dev, dtype=torch.uint8)
+                  | (torch.randint(0, 15, (rows, cols), device=dev, dtype=torch.uint8) << 4))
+        code = torch.empty((rows, cols), device=dev, dtype=torch.int8)
+        counts = torch.zeros(4, device=dev, dtype=torch.int64)
+        rms = torch.zeros(1, device=dev)
+        keep.append((grad, packed, code, counts, rms))
+        groups.setdefault(cols, []).append(len(keep) - 1)
+    descs = {}
+    for cols, idx in groups.items():
+        arr = (_lib.UpdateLayer * len(idx))()
+        for d, i in zip(arr, idx):
+            grad, packed, code, counts, rms = keep[i]
+            d.grad, d.ldg, d.rows = grad.data_ptr(), cols, grad.shape[0]
+            d.packed, d.ldp, d.code_out, d.ldc = packed.data_ptr(), cols, code.data_ptr(), cols
+            d.rms_ema, d.counts, d.rms_sum, d.grad_mul = None, counts.data_ptr(), rms.data_ptr(), 1.0
+        descs[cols] = arr
+    stream = _lib.stream_of(keep[0][0])
+
+    def run():
+        for cols, arr in descs.items():
+            _lib.check(_lib.lib().rt_ratchet_update_grouped(
+                arr, len(arr), _lib.BF16, 0, cols, 1, 0.0, 3, 8, 0.5, 1.5, 1e-8, stream))
+
+    t = _time(run, reps, flush)
+    weights = sum(r * c for r, c in shapes)
+    rows = sum(r for r, _ in shapes)
+    return _report(name, [len(shapes), weights], t, weights * 5 + 4 * rows, 0, 0, peaks)
+
+
+def model_layer_shapes(d: int, layers: int, vocab: int) -> list[tuple[int, int]]:
+    """(rows, cols) of every ratchet matrix of the decoder: qkv, projection, expand, contract per
+    block and the lm_head."""
+    block = [(3 * d, d), (d, d), (4 * d, d), (d, 4 * d)]
+    return block * layers + [(vocab, d)]
+
+
 def bench_update(rows, cols, reps, flush, peaks, grad_dtype=torch.float32):
     dev = torch.device("cuda")
     grad = (torch.randn(rows, cols, device=dev) * 1e-3).to(grad_dtype)
@@ -197,12 +242,14 @@ def bench_producers(m, k, reps, flush, peaks, dtype=torch.float32):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("kernel", choices=["all", "fwd", "grad_input", "gradw", "quant_sr", "quant_rn",
-                                           "dequant", "update", "rmsnorm_bwd", "producers"])
+    parser.add_argument("kernel", choices=["all", "all1b", "fwd", "grad_input", "gradw", "quant_sr",
+                                           "quant_rn", "dequant", "update", "update_grouped",
+                                           "rmsnorm_bwd", "producers"])
     parser.add_argument("--m", type=int, default=16384)
     parser.add_argument("--k", type=int, default=512)
     parser.add_argument("--n", type=int, default=2048)
     parser.add_argument("--reps", type=int, default=20)
+    parser.add_argument("--layers", type=int, default=20, help="update_grouped: decoder blocks")
     parser.add_argument("--no-flush", action="store_true")
     parser.add_argument("--dtype", choices=["f32", "bf16"], default="f32",
                         help="input dtype of quant_sr / quant_rn")
@@ -223,8 +270,24 @@ def main() -> None:
             bench_dequant(m, k, args.reps, flush, peaks)
             bench_update(n, k, args.reps, flush, peaks)
         bench_update(8192, 2048, args.reps, flush, peaks)
+        bench_update(8192, 2048, args.reps, flush, peaks, torch.bfloat16)
+        bench_update_grouped(model_layer_shapes(512, 8, 8192), args.reps, flush, peaks,
+                             "ratchet_update_grouped_25m")
+        bench_update_grouped(model_layer_shapes(2048, 20, 8192), args.reps, flush, peaks,
+                             "ratchet_update_grouped_1b")
         bench_rmsnorm_bwd(m, 512, args.reps, flush, peaks)
         bench_producers(m, 512, args.reps, flush, peaks)
+        return
+    if args.kernel == "all1b":  # the ~1B decoder's layer shapes, M = 16384 tokens
+        for k, n in SHAPES_1B:
+            bench_gemm_fwd(m, k, n, args.reps, flush, peaks, args.int8_peak)
+            bench_gemm_grad_input(m, k, n, args.reps, flush, peaks, args.int8_peak)
+            bench_gradw(m, k, n, args.reps, flush, peaks)
+            bench_quant_sr(m, n, args.reps, flush, peaks, torch.bfloat16)
+        bench_update(8192, 2048, args.reps, flush, peaks, torch.bfloat16)
+        bench_update_grouped(model_layer_shapes(2048, 20, 8192), args.reps, flush, peaks,
+                             "ratchet_update_grouped_1b")
+        bench_rmsnorm_bwd(m, 2048, args.reps, flush, peaks)
         return
     if args.kernel == "fwd":
         bench_gemm_fwd(m, args.k, args.n, args.reps, flush, peaks, args.int8_peak)
@@ -241,7 +304,11 @@ def main() -> None:
     elif args.kernel == "dequant":
         bench_dequant(m, args.k, args.reps, flush, peaks)
     elif args.kernel == "update":
-        bench_update(args.n, args.k, args.reps, flush, peaks)
+        bench_update(args.n, args.k, args.reps, flush, peaks,
+                     torch.bfloat16 if args.dtype == "bf16" else torch.float32)
+    elif args.kernel == "update_grouped":
+        bench_update_grouped(model_layer_shapes(args.k, args.layers, 8192), args.reps, flush,
+                             peaks, f"ratchet_update_grouped_d{args.k}")
     elif args.kernel == "rmsnorm_bwd":
         bench_rmsnorm_bwd(m, args.k, args.reps, flush, peaks)
     elif args.kernel == "producers":

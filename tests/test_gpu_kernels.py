@@ -516,3 +516,22 @@ def test_producer_backwards_match_oracle(cuda_device):
     torch.testing.assert_close(dw.double(), ref_dw, rtol=1e-4, atol=1e-6)
     dg = gelu_backward(gy, x)
     np.testing.assert_allclose(_np(dg), O.gelu_backward(_np(gy), _np(x)), rtol=1e-2, atol=1e-6)
+
+
+@pytest.mark.parametrize("rows,cols,dtype", [(16384, 512, torch.float32), (16384, 2048, torch.float32),
+                                             (16384, 512, torch.bfloat16), (300, 100, torch.float32)])
+def test_rmsnorm_weight_gradient_is_deterministic(cuda_device, rows, cols, dtype):
+    """dw sums per-CTA partial rows in a fixed order (the 100-wide rows take the generic kernel's
+    per-column sum over rows): repeated calls give the same bits, close to a double sum."""
+    from local_ai_training_b200.int8_backward import rmsnorm_backward
+
+    torch.manual_seed(rows + cols)
+    x = torch.randn(rows, cols, device=cuda_device).to(dtype)
+    gy = (torch.randn(rows, cols, device=cuda_device) * 1e-2).to(dtype)
+    w = torch.rand(cols, device=cuda_device) + 0.5
+    dws = [rmsnorm_backward(gy, x, w, 1e-5)[1] for _ in range(3)]
+    for other in dws[1:]:
+        assert torch.equal(dws[0], other)
+    xd, gd = x.double(), gy.double()
+    ref = (gd * xd * torch.rsqrt((xd ** 2).mean(1, keepdim=True) + 1e-5)).sum(0)
+    torch.testing.assert_close(dws[0].double(), ref, rtol=1e-4, atol=1e-5)
