@@ -244,6 +244,13 @@ static inline RowCfg row_cfg_narrow(int64_t nch) {
 // Resident 256-thread CTAs per SM of the grid-striding row kernels, whose launch bounds give
 // four at up to two chunks a thread, two at four, one at eight.
 static inline unsigned resident_ctas(int vpt) { return vpt <= 2 ? 4u : (vpt == 4 ? 2u : 1u); }
+// Grid of the persistent update kernels: the row blocks, at most the CTAs resident at once.
+static inline unsigned update_grid(unsigned blocks, int vpt) {
+  int sms = 0;
+  if (rt_sm_count(&sms) != RT_OK || sms <= 0) sms = 148;
+  const unsigned cap = static_cast<unsigned>(sms) * resident_ctas(vpt);
+  return blocks < cap ? blocks : cap;
+}
 static inline unsigned row_grid(int64_t rows, int rt) {
   const int64_t rpc = CTA / rt;
   return static_cast<unsigned>((rows + rpc - 1) / rpc);
@@ -634,6 +641,43 @@ __device__ __forceinline__ int8_t code_of(uint8_t packed, int max_code) {
   return static_cast<int8_t>(static_cast<int>(packed & 0x0F) - max_code);
 }
 
+// The whole code/pressure step of one weight as a table lookup.  Entry (old << 3 | bucket << 1
+// | negative) for a packed byte `old`, a bucket in {0, 1, 2} and the gradient's sign holds what
+// ratchet_one computes for the increment -sign(g)·bucket: bits 0-15 the four move counts as
+// 4-bit fields (positive, negative, blocked positive, blocked negative), bits 16-23 the new
+// packed byte, bits 24-31 its int8 code.  Built by each CTA from ratchet_one itself, so the
+// lookup and the direct computation agree by construction.
+constexpr int kUpdateLut = 256 * 8;
+__device__ __forceinline__ void build_update_lut(uint32_t *lut, const UpdateArgs &a) {
+  for (int e = threadIdx.x; e < kUpdateLut; e += blockDim.x) {
+    const int old = e >> 3, bucket = (e >> 1) & 3, negative = e & 1;
+    uint32_t v = 0;
+    if (bucket <= 2) {
+      Moves m = {0, 0, 0, 0};
+      const uint8_t nb = ratchet_one(static_cast<uint8_t>(old), negative ? bucket : -bucket, a, m);
+      v = static_cast<uint32_t>(m.pos) | (static_cast<uint32_t>(m.neg) << 4) |
+          (static_cast<uint32_t>(m.bpos) << 8) | (static_cast<uint32_t>(m.bneg) << 12) |
+          (static_cast<uint32_t>(nb) << 16) |
+          (static_cast<uint32_t>(static_cast<uint8_t>(code_of(nb, a.max_code))) << 24);
+    }
+    lut[e] = v;
+  }
+  __syncthreads();
+}
+// Table index of one weight: the bucket of |z| (z = g / denom, formed as in pressure_increment)
+// and the sign of g; g == 0 moves nothing (bucket 0).
+__device__ __forceinline__ uint32_t lut_index(uint32_t old, float g, float denom, float rcp,
+                                              int normalize, float low, float high) {
+  float mag = normalize ? fabsf(__fmul_rn(g, rcp)) : fabsf(g);
+  if (normalize) {
+    const float win = __fmul_rn(mag, 9.5367431640625e-07f);  // 2^-20
+    if (fabsf(__fsub_rn(mag, high)) <= win || fabsf(__fsub_rn(mag, low)) <= win)
+      mag = fabsf(__fdiv_rn(g, denom));
+  }
+  const uint32_t bucket = g == 0.0f ? 0u : static_cast<uint32_t>(mag >= high) + static_cast<uint32_t>(mag >= low);
+  return (old << 3) | (bucket << 1) | static_cast<uint32_t>(g < 0.0f);
+}
+
 // Per-row normaliser (ratchet.py:539-556); returns rms + eps.  Only `writer` stores rms_ema.
 __device__ __forceinline__ float row_denominator(const UpdateArgs &a, int64_t row, float ms,
                                                  float ema_old, bool bad, bool writer) {
@@ -696,13 +740,17 @@ __device__ __forceinline__ void load_grad8(const UpdateArgs &a, const G *gr, int
 }
 
 template <typename G, int RT, int VPT, bool WS>
-__device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a, int64_t block) {
+__device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a, int64_t block,
+                                                    const uint32_t *lut) {
   constexpr int RPC = CTA / RT, NT = CTA / RT;
   __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
   __shared__ float smb[RPC];
   __shared__ float smx[RPC * 8];
   __shared__ int redi[CTA / 32][4];
   __shared__ float rrs[RPC];  // the rows' gradient rms, summed once per CTA
+  // a CTA runs this once per row block: the shared arrays of the previous block are read
+  // by every thread before any thread writes them again
+  __syncthreads();
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
   const int64_t row = block * RPC + sub;
   const bool live = row < a.rows;
@@ -774,24 +822,34 @@ __device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a, int64_t
   for (int i = 0; i < VPT; ++i) {
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     if (!live || c >= nch) continue;
-    uint2 out = pk[i];
     if (!bad) {
-      uint32_t w[2] = {0, 0};
+      // eight table lookups; the new packed and code bytes are gathered from the entries with
+      // byte permutes, the move counts summed as 4-bit fields (at most 8 per chunk)
+      uint32_t e[8];
+      uint32_t counts = 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint32_t word = j < 4 ? pk[i].x : pk[i].y;
-        const uint8_t old = static_cast<uint8_t>(word >> (8 * (j & 3)));
-        const int inc = pressure_increment(g[i][j], denom, rcp, a.normalize, a.low, a.high);
-        w[j >> 2] |= static_cast<uint32_t>(ratchet_one(old, inc, a, m)) << (8 * (j & 3));
+        const uint32_t old = (word >> (8 * (j & 3))) & 0xFFu;
+        e[j] = lut[lut_index(old, g[i][j], denom, rcp, a.normalize, a.low, a.high)];
+        counts += e[j];
       }
-      out = make_uint2(w[0], w[1]);
+      const uint32_t t01 = __byte_perm(e[0], e[1], 0x7362), t23 = __byte_perm(e[2], e[3], 0x7362);
+      const uint32_t t45 = __byte_perm(e[4], e[5], 0x7362), t67 = __byte_perm(e[6], e[7], 0x7362);
+      const uint2 out = make_uint2(__byte_perm(t01, t23, 0x5410), __byte_perm(t45, t67, 0x5410));
       *reinterpret_cast<uint2 *>(a.packed + row * a.ldp + 8 * c) = out;
-    }
-    if (a.code_out != nullptr) {
+      if (a.code_out != nullptr)
+        *reinterpret_cast<uint2 *>(a.code_out + row * a.ldc + 8 * c) =
+            make_uint2(__byte_perm(t01, t23, 0x7632), __byte_perm(t45, t67, 0x7632));
+      m.pos += counts & 0xF;
+      m.neg += (counts >> 4) & 0xF;
+      m.bpos += (counts >> 8) & 0xF;
+      m.bneg += (counts >> 12) & 0xF;
+    } else if (a.code_out != nullptr) {
       uint32_t cw[2] = {0, 0};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const uint32_t word = j < 4 ? out.x : out.y;
+        const uint32_t word = j < 4 ? pk[i].x : pk[i].y;
         cw[j >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(
                           code_of(static_cast<uint8_t>(word >> (8 * (j & 3))), a.max_code)))
                       << (8 * (j & 3));
@@ -801,17 +859,27 @@ __device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a, int64_t
   }
   publish_moves(m, redi, a, rrs, RPC);
 }
+// The vectorised update kernels stride a resident-sized grid over row blocks (each CTA builds
+// the lookup table once and then serves many rows).
 template <typename G, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) ratchet_update_kernel(UpdateArgs a) {
-  pdl_wait();
+  __shared__ uint32_t lut[kUpdateLut];
   pdl_trigger();
-  ratchet_update_body<G, RT, VPT, false>(a, blockIdx.x);
+  build_update_lut(lut, a);  // from the launch arguments only: overlaps the previous kernel
+  pdl_wait();
+  const int64_t blocks = (a.rows + (CTA / RT) - 1) / (CTA / RT);
+  for (int64_t b = blockIdx.x; b < blocks; b += gridDim.x)
+    ratchet_update_body<G, RT, VPT, false>(a, b, lut);
 }
 template <typename G, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) ratchet_update_ws_kernel(UpdateArgs a) {
-  pdl_wait();
+  __shared__ uint32_t lut[kUpdateLut];
   pdl_trigger();
-  ratchet_update_body<G, RT, VPT, true>(a, blockIdx.x);
+  build_update_lut(lut, a);
+  pdl_wait();
+  const int64_t blocks = (a.rows + (CTA / RT) - 1) / (CTA / RT);
+  for (int64_t b = blockIdx.x; b < blocks; b += gridDim.x)
+    ratchet_update_body<G, RT, VPT, true>(a, b, lut);
 }
 
 // Grouped update: the rows of up to kUpdateGroup layers (same row length, dtype and ratchet
@@ -839,18 +907,21 @@ struct GroupArgs {
 };
 template <typename G, int RT, int VPT>
 __global__ void __launch_bounds__(CTA) ratchet_update_grouped_kernel(const __grid_constant__ GroupArgs g) {
-  pdl_wait();
+  __shared__ uint32_t lut[kUpdateLut];
   pdl_trigger();
-  const int b = static_cast<int>(blockIdx.x);
+  build_update_lut(lut, g.common);
+  pdl_wait();
   int l = 0;
-  while (l + 1 < g.n && g.L[l + 1].block0 <= b) ++l;
-  const GroupLayer &L = g.L[l];
-  UpdateArgs a = g.common;
-  a.grad = L.grad, a.ldg = L.ldg, a.rows = L.rows, a.packed = L.packed, a.ldp = L.ldp;
-  a.code_out = L.code_out, a.ldc = L.ldc, a.rms_ema = L.rms_ema, a.counts = L.counts;
-  a.rms_sum = L.rms_sum, a.grad_mul = L.grad_mul;
-  a.row_rms = nullptr, a.grad_scale = nullptr, a.ws = nullptr;
-  ratchet_update_body<G, RT, VPT, false>(a, b - L.block0);
+  for (int b = static_cast<int>(blockIdx.x); b < g.blocks; b += static_cast<int>(gridDim.x)) {
+    while (l + 1 < g.n && g.L[l + 1].block0 <= b) ++l;  // blocks only grow: resume the search
+    const GroupLayer &L = g.L[l];
+    UpdateArgs a = g.common;
+    a.grad = L.grad, a.ldg = L.ldg, a.rows = L.rows, a.packed = L.packed, a.ldp = L.ldp;
+    a.code_out = L.code_out, a.ldc = L.ldc, a.rms_ema = L.rms_ema, a.counts = L.counts;
+    a.rms_sum = L.rms_sum, a.grad_mul = L.grad_mul;
+    a.row_rms = nullptr, a.grad_scale = nullptr, a.ws = nullptr;
+    ratchet_update_body<G, RT, VPT, false>(a, b - L.block0, lut);
+  }
 }
 
 // Generic update: any alignment and row length, one CTA per row, same arithmetic and order.
@@ -1497,17 +1568,37 @@ __global__ void __launch_bounds__(CTA)
   if (a.dw != nullptr && threadIdx.x == 0) a.dw_work[row] = r;  // dw_rows_reduce_kernel's input
 }
 
-// dw[k] += sum over partial rows p = 0..parts-1 (in order) of part[p][k]: the fixed-order
-// reduction of the vectorised RMSNorm backward's per-CTA partials.
+// dw[k] += the fixed-order sum of part[0..parts-1][k], the vectorised RMSNorm backward's per-CTA
+// partial rows.  A CTA covers 32 columns with 8 lanes groups: group g sums the partials
+// p = g, g + 8, g + 16, ... in order (loads issued eight at a time), then the eight group sums
+// are added in g order -- the same tree on every call.
 __global__ void __launch_bounds__(256)
     dw_partials_reduce_kernel(const float *__restrict__ part, int parts, int64_t cols, float *dw) {
   pdl_wait();
   pdl_trigger();
-  const int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (k >= cols) return;
-  float acc = part[k];
-  for (int p = 1; p < parts; ++p) acc = __fadd_rn(acc, part[static_cast<int64_t>(p) * cols + k]);
-  dw[k] = __fadd_rn(dw[k], acc);
+  __shared__ float sums[8][33];
+  const int lane = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int64_t k = blockIdx.x * 32ll + lane;
+  float acc = 0.0f;
+  if (k < cols) {
+    int p = g;
+    for (; p + 56 < parts; p += 64) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __ldg(part + static_cast<int64_t>(p + 8 * j) * cols + k);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v[j]);
+    }
+    for (; p < parts; p += 8) acc = __fadd_rn(acc, __ldg(part + static_cast<int64_t>(p) * cols + k));
+  }
+  sums[g][lane] = acc;
+  __syncthreads();
+  if (g == 0 && k < cols) {
+    float t = sums[0][lane];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) t = __fadd_rn(t, sums[j][lane]);
+    dw[k] = __fadd_rn(dw[k], t);
+  }
 }
 // dw[k] += sum over rows (in order) of (gy·x)·r[row]: the generic kernel's weight gradient.
 __global__ void __launch_bounds__(256)
@@ -1774,9 +1865,9 @@ static int ratchet_update_launch(const UpdateArgs &a, cudaStream_t s) {
   if (a.ws != nullptr) {
     if (cfg.rt == 0)
       return fail(RT_ERR_UNSUPPORTED, "rt_grad_weight_ratchet_update: rows need 8-element chunks");
-    RT_DISPATCH_ROW(cfg, ratchet_update_ws_kernel, float, row_grid(rows, cfg.rt), a);
+    RT_DISPATCH_ROW(cfg, ratchet_update_ws_kernel, float, update_grid(row_grid(rows, cfg.rt), cfg.vpt), a);
   } else if (cfg.rt != 0) {
-    const unsigned grid = row_grid(rows, cfg.rt);
+    const unsigned grid = update_grid(row_grid(rows, cfg.rt), cfg.vpt);
     if (a.grad_dtype == RT_F32)
       RT_DISPATCH_ROW(cfg, ratchet_update_kernel, float, grid, a);
     else
@@ -1879,11 +1970,11 @@ extern "C" int rt_ratchet_update_grouped(const rt_update_layer *layers, int n_la
     }
     g.blocks = blocks;
     if (g.n == 0) continue;
+    const unsigned grid = update_grid(static_cast<unsigned>(blocks), cfg.vpt);
     if (grad_dtype == RT_F32)
-      RT_DISPATCH_ROW(cfg, ratchet_update_grouped_kernel, float, static_cast<unsigned>(blocks), g);
+      RT_DISPATCH_ROW(cfg, ratchet_update_grouped_kernel, float, grid, g);
     else
-      RT_DISPATCH_ROW(cfg, ratchet_update_grouped_kernel, __nv_bfloat16,
-                      static_cast<unsigned>(blocks), g);
+      RT_DISPATCH_ROW(cfg, ratchet_update_grouped_kernel, __nv_bfloat16, grid, g);
     if (int rc = check_launch("rt_ratchet_update_grouped")) return rc;
   }
   return RT_OK;
@@ -2075,7 +2166,7 @@ static int rmsnorm_backward_launch(const RmsBwdArgs &a, int gy_dtype, int x_dtyp
 #undef RT_RMSB
   if (int rc = check_launch(who)) return rc;
   if (a.dw != nullptr) {
-    launch_k(dw_partials_reduce_kernel, static_cast<unsigned>((a.cols + 255) / 256), 256, 0, s,
+    launch_k(dw_partials_reduce_kernel, static_cast<unsigned>((a.cols + 31) / 32), 256, 0, s,
              static_cast<const float *>(a.dw_work), static_cast<int>(grid), a.cols, a.dw);
     return check_launch(who);
   }
