@@ -141,20 +141,11 @@ constexpr float kRoundMagic = 12582912.0f;            // 1.5 * 2^23
 // Round-to-nearest-even quant of one value, as an int in [-127, 127].  The estimate is clamped
 // first (clamping commutes with rounding at the integer bounds) and rounded by adding 1.5·2^23,
 // whose low mantissa bits then hold the integer.
-// The IEEE-division paths of the two quantisers, out of line: a boundary case is rare, and as
-// separate calls they cannot be turned into predicated instructions that every element issues.
-__device__ __noinline__ int quant_rn_exact(float v, float scale) {
-  return static_cast<int>(rintf(fminf(fmaxf(__fdiv_rn(v, scale), -127.0f), 127.0f)));
-}
-__device__ __noinline__ int quant_sr_exact(float v, float scale, float um) {
-  const float t = __fadd_rn(__fdiv_rn(v, scale), __fadd_rn(um, 0.5f));  // u exact
-  return min(max(__float2int_rd(t), -127), 127);
-}
 __device__ __forceinline__ int quant_rn_i(float v, float scale, float rcp) {
   const float y = fminf(fmaxf(__fmul_rn(v, rcp), -127.0f), 127.0f);
   const float t = __fadd_rn(y, kRoundMagic);
-  if (__builtin_expect(fabsf(__fsub_rn(y, __fsub_rn(t, kRoundMagic))) >= 0.5f - kBoundaryWindow, 0))
-    return quant_rn_exact(v, scale);
+  if (fabsf(__fsub_rn(y, __fsub_rn(t, kRoundMagic))) >= 0.5f - kBoundaryWindow)
+    return static_cast<int>(rintf(fminf(fmaxf(__fdiv_rn(v, scale), -127.0f), 127.0f)));
   return __float_as_int(t) - 0x4B400000;
 }
 // Stochastic rounding floor(RN(RN(v / scale) + u)), as an int in [-127, 127], given um = u - 1/2.
@@ -166,38 +157,11 @@ __device__ __forceinline__ int quant_rn_i(float v, float scale, float rcp) {
 __device__ __forceinline__ int quant_sr_i(float v, float scale, float rcp, float um) {
   const float th = __fmaf_rn(v, rcp, um);
   const float z = __fadd_rn(th, kRoundMagic);
-  if (__builtin_expect(fabsf(__fsub_rn(th, __fsub_rn(z, kRoundMagic))) >= 0.5f - kBoundaryWindow, 0))
-    return quant_sr_exact(v, scale, um);
+  if (fabsf(__fsub_rn(th, __fsub_rn(z, kRoundMagic))) >= 0.5f - kBoundaryWindow) {
+    const float t = __fadd_rn(__fdiv_rn(v, scale), __fadd_rn(um, 0.5f));  // u exact
+    return min(max(__float2int_rd(t), -127), 127);
+  }
   return __float_as_int(z) - 0x4B400000;
-}
-__device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
-  const uint32_t lo = __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040);
-  const uint32_t hi = __byte_perm(static_cast<uint32_t>(c), static_cast<uint32_t>(d), 0x0040);
-  return __byte_perm(lo, hi, 0x5410);
-}
-// Eight consecutive elements (one Philox block p): the fast estimates of all eight and one
-// branch, taken only when some estimate lies in the boundary window, to the exact path.
-__device__ __forceinline__ uint2 quant_sr_chunk(const float (&v)[8], float scale, float rcp,
-                                                const Philox4 &p) {
-  const uint32_t w[4] = {p.x, p.y, p.z, p.w};
-  int q[8];
-  bool near = false;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float um = (j & 1) ? sr_um_hi(w[j >> 1]) : sr_um_lo(w[j >> 1]);
-    const float th = __fmaf_rn(v[j], rcp, um);
-    const float z = __fadd_rn(th, kRoundMagic);
-    near |= fabsf(__fsub_rn(th, __fsub_rn(z, kRoundMagic))) >= 0.5f - kBoundaryWindow;
-    q[j] = __float_as_int(z) - 0x4B400000;
-  }
-  if (__builtin_expect(near, 0)) {
-#pragma unroll 1
-    for (int j = 0; j < 8; ++j) {
-      const float um = (j & 1) ? sr_um_hi(w[j >> 1]) : sr_um_lo(w[j >> 1]);
-      q[j] = quant_sr_i(v[j], scale, rcp, um);
-    }
-  }
-  return make_uint2(pack4_i8(q[0], q[1], q[2], q[3]), pack4_i8(q[4], q[5], q[6], q[7]));
 }
 // quant_rn_i that also returns the rounded value as a float (exact: a small integer), which the
 // rounding magic has produced already -- no int-to-float conversion for the dequantised copy.
@@ -205,10 +169,9 @@ __device__ __forceinline__ int quant_rn_if(float v, float scale, float rcp, floa
   const float y = fminf(fmaxf(__fmul_rn(v, rcp), -127.0f), 127.0f);
   const float t = __fadd_rn(y, kRoundMagic);
   qf = __fsub_rn(t, kRoundMagic);
-  if (__builtin_expect(fabsf(__fsub_rn(y, qf)) >= 0.5f - kBoundaryWindow, 0)) {
-    const int q = quant_rn_exact(v, scale);
-    qf = static_cast<float>(q);
-    return q;
+  if (fabsf(__fsub_rn(y, qf)) >= 0.5f - kBoundaryWindow) {
+    qf = rintf(fminf(fmaxf(__fdiv_rn(v, scale), -127.0f), 127.0f));
+    return static_cast<int>(qf);
   }
   return __float_as_int(t) - 0x4B400000;
 }
@@ -219,6 +182,11 @@ __device__ __forceinline__ int8_t quant_sr(float v, float scale, float rcp, floa
   return static_cast<int8_t>(quant_sr_i(v, scale, rcp, um));
 }
 // Four ints in [-128, 127] -> one word of int8 bytes (two byte permutes and a merge).
+__device__ __forceinline__ uint32_t pack4_i8(int a, int b, int c, int d) {
+  const uint32_t lo = __byte_perm(static_cast<uint32_t>(a), static_cast<uint32_t>(b), 0x0040);
+  const uint32_t hi = __byte_perm(static_cast<uint32_t>(c), static_cast<uint32_t>(d), 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
+}
 __device__ __forceinline__ float row_scale_of(float amax) {
   return fmaxf(__fdiv_rn(amax, 127.0f), FLT_MIN);
 }
@@ -449,7 +417,14 @@ __device__ __forceinline__ void quant_rows_body(const QuantArgs &a) {
       if (a.stochastic) {
         const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;  // multiple of 8
         const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
-        o = quant_sr_chunk(v[i], scale, rcp, p);
+        o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_um_lo(p.x)),
+                       quant_sr_i(v[i][1], scale, rcp, sr_um_hi(p.x)),
+                       quant_sr_i(v[i][2], scale, rcp, sr_um_lo(p.y)),
+                       quant_sr_i(v[i][3], scale, rcp, sr_um_hi(p.y)));
+        o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_um_lo(p.z)),
+                       quant_sr_i(v[i][5], scale, rcp, sr_um_hi(p.z)),
+                       quant_sr_i(v[i][6], scale, rcp, sr_um_lo(p.w)),
+                       quant_sr_i(v[i][7], scale, rcp, sr_um_hi(p.w)));
       } else {
         o.x = pack4_i8(quant_rn_i(v[i][0], scale, rcp), quant_rn_i(v[i][1], scale, rcp),
                        quant_rn_i(v[i][2], scale, rcp), quant_rn_i(v[i][3], scale, rcp));
@@ -552,7 +527,14 @@ __device__ __forceinline__ void sr_quant_store_row(const QuantArgs &a, uint32_t 
     const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;
     const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
     uint2 o;
-    o = quant_sr_chunk(v[i], scale, rcp, p);
+    o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_um_lo(p.x)),
+                   quant_sr_i(v[i][1], scale, rcp, sr_um_hi(p.x)),
+                   quant_sr_i(v[i][2], scale, rcp, sr_um_lo(p.y)),
+                   quant_sr_i(v[i][3], scale, rcp, sr_um_hi(p.y)));
+    o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_um_lo(p.z)),
+                   quant_sr_i(v[i][5], scale, rcp, sr_um_hi(p.z)),
+                   quant_sr_i(v[i][6], scale, rcp, sr_um_lo(p.w)),
+                   quant_sr_i(v[i][7], scale, rcp, sr_um_hi(p.w)));
     *reinterpret_cast<uint2 *>(qr + 8 * c) = o;
   }
 }
@@ -625,16 +607,13 @@ struct Moves {
 // z = RN(g / denom).  Only the two threshold comparisons depend on the quotient, so it is formed
 // as g · RN(1/denom) (relative error below 2^-22) and the IEEE division is taken only when that
 // estimate lies within a relative 2^-20 of a threshold.  sign(z) = sign(g) since denom > 0.
-__device__ __noinline__ float abs_quotient(float g, float denom) {
-  return fabsf(__fdiv_rn(g, denom));
-}
 __device__ __forceinline__ int pressure_increment(float g, float denom, float rcp, int normalize,
                                                   float low, float high) {
   float mag = normalize ? fabsf(__fmul_rn(g, rcp)) : fabsf(g);
   if (normalize) {
     const float win = __fmul_rn(mag, 9.5367431640625e-07f);  // 2^-20
-    if (__builtin_expect(fabsf(__fsub_rn(mag, high)) <= win || fabsf(__fsub_rn(mag, low)) <= win, 0))
-      mag = abs_quotient(g, denom);
+    if (fabsf(__fsub_rn(mag, high)) <= win || fabsf(__fsub_rn(mag, low)) <= win)
+      mag = fabsf(__fdiv_rn(g, denom));
   }
   const int bucket = mag >= high ? 2 : (mag >= low ? 1 : 0);
   const int sgn = (g > 0.0f) - (g < 0.0f);
@@ -685,28 +664,18 @@ __device__ __forceinline__ void build_update_lut(uint32_t *lut, const UpdateArgs
   }
   __syncthreads();
 }
-// Table index of one weight from the bucket of |z| and the sign of g (g == 0 moves nothing:
-// bucket 0).  |z| = |g / denom| is estimated as |g · rcp| (relative error below 2^-22); `near`
-// reports an estimate within a relative 2^-20 of a bucket threshold, where only the IEEE
-// quotient decides (lut_index_exact, out of line: the common path stays a few instructions).
-__device__ __forceinline__ uint32_t lut_bucket_index(uint32_t old, float g, float mag, float low,
-                                                     float high) {
-  const uint32_t bucket =
-      g == 0.0f ? 0u : static_cast<uint32_t>(mag >= high) + static_cast<uint32_t>(mag >= low);
-  return (old << 3) | (bucket << 1) | static_cast<uint32_t>(g < 0.0f);
-}
-__device__ __forceinline__ uint32_t lut_index(uint32_t old, float g, float rcp, int normalize,
-                                              float low, float high, bool &near) {
-  const float mag = normalize ? fabsf(__fmul_rn(g, rcp)) : fabsf(g);
+// Table index of one weight: the bucket of |z| (z = g / denom, formed as in pressure_increment)
+// and the sign of g; g == 0 moves nothing (bucket 0).
+__device__ __forceinline__ uint32_t lut_index(uint32_t old, float g, float denom, float rcp,
+                                              int normalize, float low, float high) {
+  float mag = normalize ? fabsf(__fmul_rn(g, rcp)) : fabsf(g);
   if (normalize) {
     const float win = __fmul_rn(mag, 9.5367431640625e-07f);  // 2^-20
-    near |= fabsf(__fsub_rn(mag, high)) <= win || fabsf(__fsub_rn(mag, low)) <= win;
+    if (fabsf(__fsub_rn(mag, high)) <= win || fabsf(__fsub_rn(mag, low)) <= win)
+      mag = fabsf(__fdiv_rn(g, denom));
   }
-  return lut_bucket_index(old, g, mag, low, high);
-}
-__device__ __noinline__ uint32_t lut_index_exact(uint32_t old, float g, float denom, float low,
-                                                 float high) {
-  return lut_bucket_index(old, g, fabsf(__fdiv_rn(g, denom)), low, high);
+  const uint32_t bucket = g == 0.0f ? 0u : static_cast<uint32_t>(mag >= high) + static_cast<uint32_t>(mag >= low);
+  return (old << 3) | (bucket << 1) | static_cast<uint32_t>(g < 0.0f);
 }
 
 // Per-row normaliser (ratchet.py:539-556); returns rms + eps.  Only `writer` stores rms_ema.
@@ -807,12 +776,15 @@ __device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a, int64_t
         for (int j = 0; j < 8; ++j) g[i][j] = __fmul_rn(g[i][j], a.grad_mul);
       }
       pk[i] = *reinterpret_cast<const uint2 *>(pr + 8 * c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bad |= !isfinite(g[i][j]);
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) g[i][j] = 0.0f;
     }
   }
   const float ema_old = (a.rms_ema != nullptr && live) ? a.rms_ema[row] : 0.0f;
+  bad = row_max<RT>(bad ? 1.0f : 0.0f, smx, sub, t) > 0.0f;
 
   float ss[NT], gsa[NT];
 #pragma unroll
@@ -832,19 +804,6 @@ __device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a, int64_t
   }
   const float total = row_sum<RT>(ss, sm, smb, sub, t);
   const float gsum = a.grad_scale != nullptr ? row_sum<RT>(gsa, sm, smb, sub, t) : 0.0f;
-  // A NaN or infinite gradient makes the sum of squares non-finite (so does a finite one whose
-  // square overflows); only then are the row's values checked one by one.  The test is uniform
-  // over the threads that share the row-max barriers (the warp, or the CTA).
-  const bool suspect = live && !isfinite(total);
-  const bool any_suspect = RT == 32 ? __any_sync(0xffffffffu, suspect) : __syncthreads_or(suspect);
-  if (any_suspect) {
-    bool mine = false;
-#pragma unroll
-    for (int i = 0; i < VPT; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) mine |= !isfinite(g[i][j]);
-    bad = row_max<RT>(mine ? 1.0f : 0.0f, smx, sub, t) > 0.0f;
-  }
   const float ms = __fdiv_rn(total, static_cast<float>(a.cols));
   if (RT == 32) __syncwarp();
   const float denom = row_denominator(a, row, ms, ema_old, bad, live && t == 0);
@@ -868,25 +827,11 @@ __device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a, int64_t
       // byte permutes, the move counts summed as 4-bit fields (at most 8 per chunk)
       uint32_t e[8];
       uint32_t counts = 0;
-      uint32_t idx[8];
-      bool near = false;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const uint32_t word = j < 4 ? pk[i].x : pk[i].y;
-        idx[j] = lut_index((word >> (8 * (j & 3))) & 0xFFu, g[i][j], rcp, a.normalize, a.low,
-                           a.high, near);
-      }
-      if (__builtin_expect(near, 0)) {  // rare: some estimate lies at a bucket threshold
-#pragma unroll 1
-        for (int j = 0; j < 8; ++j) {
-          const uint32_t word = j < 4 ? pk[i].x : pk[i].y;
-          idx[j] = lut_index_exact((word >> (8 * (j & 3))) & 0xFFu, g[i][j], denom, a.low,
-                                   a.high);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        e[j] = lut[idx[j]];
+        const uint32_t old = (word >> (8 * (j & 3))) & 0xFFu;
+        e[j] = lut[lut_index(old, g[i][j], denom, rcp, a.normalize, a.low, a.high)];
         counts += e[j];
       }
       const uint32_t t01 = __byte_perm(e[0], e[1], 0x7362), t23 = __byte_perm(e[2], e[3], 0x7362);
