@@ -41,6 +41,7 @@ extern "C" {
 #define RT_STATUS_CODE_RANGE 0x4u         /* validate: code escaped [-max_code, max_code]        */
 #define RT_STATUS_PRESSURE_RANGE 0x8u     /* validate: |pressure| > 7                            */
 #define RT_STATUS_SCALE_INVALID 0x10u     /* validate: a row scale is <= 0 or non-finite         */
+#define RT_STATUS_INDEX_RANGE 0x20u       /* a token id / window outside its table (zeros used)  */
 
 int rt_abi_version(void);
 const char *rt_last_error(void);
@@ -332,6 +333,40 @@ int rt_cross_entropy_bwd(const void *logits, int dtype, int64_t ld, int64_t rows
                          const float *row_logsum, const float *grad_loss, const float *count,
                          const float *extra_grad, int64_t ld_extra, void *grad_bf16, int64_t ldo,
                          void *stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Ratchet embedding (ratchet.py:688-749, RatchetEmbedding: rows are tokens) and device-resident
+ * uint16 token shards (data.py:238-287).
+ *
+ * rt_embedding_forward: out[t, :] = float(code(packed[tok[t], :])) * scale[tok[t]], the
+ *   reference's F.embedding(tokens, code.float() * scale[:, None]) without materialising the
+ *   [rows, dim] effective weight.  Tokens outside [0, rows) give zero rows and set
+ *   RT_STATUS_INDEX_RANGE.
+ * rt_embedding_ratchet_update: the embedding's update from its output gradient grad [n_tok, dim]
+ *   (fp32) without a [rows, dim] gradient: sorted_tokens / order are the token ids sorted stably
+ *   and their positions; each distinct token's gradient row is the sum of its positions' rows in
+ *   position order from +0 (the reference's CPU embedding backward), then that row is updated
+ *   exactly as rt_ratchet_update(normalize=1) would; rows of absent tokens have a zero gradient
+ *   in the reference and stay unchanged there, so they are not visited.  workspace:
+ *   rt_embedding_update_workspace_bytes(n_tok, dim) bytes, 256-byte aligned.  counts and rms_sum
+ *   accumulate over the visited rows (the absent rows' rms is zero).
+ * rt_token_windows: inputs[b, t] = data[starts[b] + t], targets[b, t] = data[starts[b] + t + 1]
+ *   (uint16 ids widened to int64), the reference's batch_from_starts; windows past the data give
+ *   zeros and set RT_STATUS_INDEX_RANGE.
+ * ------------------------------------------------------------------------------------------- */
+int rt_embedding_forward(const uint8_t *packed, int64_t ldp, const float *scale, int max_code,
+                         const int64_t *tokens, int64_t n_tok, int64_t rows, int64_t dim,
+                         float *out, int64_t ldo, void *stream);
+int64_t rt_embedding_update_workspace_bytes(int64_t n_tok, int64_t dim);
+int rt_embedding_ratchet_update(const float *grad, int64_t ldg, const int64_t *sorted_tokens,
+                                const int64_t *order, int64_t n_tok, int64_t rows, int64_t dim,
+                                void *workspace, int64_t workspace_bytes, uint8_t *packed,
+                                int64_t ldp, int8_t *code_out, int64_t ldc, float *rms_ema,
+                                double ema_beta, int max_code, int threshold, double bucket_low,
+                                double bucket_high, double eps, int64_t *counts, float *rms_sum,
+                                void *stream);
+int rt_token_windows(const uint16_t *data, int64_t n, const int64_t *starts, int64_t batch,
+                     int64_t block, int64_t *inputs, int64_t *targets, void *stream);
 
 #ifdef __cplusplus
 }

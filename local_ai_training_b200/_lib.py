@@ -22,6 +22,7 @@ STATUS_WAIT_TIMEOUT = 0x2
 STATUS_CODE_RANGE = 0x4
 STATUS_PRESSURE_RANGE = 0x8
 STATUS_SCALE_INVALID = 0x10
+STATUS_INDEX_RANGE = 0x20
 
 _ERR_INVALID, _ERR_DTYPE, _ERR_ALIGN = 1, 2, 3
 ABI_VERSION = 2
@@ -78,6 +79,11 @@ _SIGNATURES = {
                              _p, _i64, _p], _i),
     "rt_heads_gather_sr": ([_p, _p, _i, _i64, _i64, _i64, _i64, _p, _i64, _p, _u64, _u32, _u32,
                             _p, _p, _i64, _p, _p, _i64, _p], _i),
+    "rt_embedding_forward": ([_p, _i64, _p, _i, _p, _i64, _i64, _i64, _p, _i64, _p], _i),
+    "rt_embedding_update_workspace_bytes": ([_i64, _i64], _i64),
+    "rt_embedding_ratchet_update": ([_p, _i64, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _i64, _p,
+                                     _i64, _p, _d, _i, _i, _d, _d, _d, _p, _p, _p], _i),
+    "rt_token_windows": ([_p, _i64, _p, _i64, _i64, _p, _p, _p], _i),
     "rt_cross_entropy_fwd": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p], _i),
     "rt_cross_entropy_bwd": ([_p, _i, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _p,
                               _i64, _p], _i),

@@ -597,6 +597,9 @@ struct UpdateArgs {
   // the gradient is multiplied by grad_mul after the optional bf16 rounding (1: untouched); the
   // mean over ranks / micro-batches of summed gradients, exact for powers of two
   float grad_mul;
+  // optional: gradient row r updates state row row_ids[r] (packed, code, rms_ema, row outputs);
+  // rows with row_ids[r] < 0 are skipped (the row-sparse embedding update)
+  const int64_t *row_ids;
 };
 
 struct Moves {
@@ -752,11 +755,13 @@ __device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a, int64_t
   // by every thread before any thread writes them again
   __syncthreads();
   const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
-  const int64_t row = block * RPC + sub;
-  const bool live = row < a.rows;
+  const int64_t grow = block * RPC + sub;  // gradient row
+  const int64_t srow = (grow < a.rows && a.row_ids != nullptr) ? a.row_ids[grow] : grow;
+  const bool live = grow < a.rows && srow >= 0;
+  const int64_t row = live ? srow : 0;  // state row
   const int64_t nch = a.cols / 8;
-  const G *gr = static_cast<const G *>(a.grad) + (live ? row : 0) * a.ldg;
-  const uint8_t *pr = a.packed + (live ? row : 0) * a.ldp;
+  const G *gr = static_cast<const G *>(a.grad) + (live ? grow : 0) * a.ldg;
+  const uint8_t *pr = a.packed + row * a.ldp;
 
   float g[VPT][8];
   uint2 pk[VPT];
@@ -766,7 +771,7 @@ __device__ __forceinline__ void ratchet_update_body(const UpdateArgs &a, int64_t
     const int64_t c = t + static_cast<int64_t>(i) * RT;
     pk[i] = make_uint2(0, 0);
     if (live && c < nch) {
-      load_grad8<G, WS>(a, gr, row, c, g[i]);
+      load_grad8<G, WS>(a, gr, grow, c, g[i]);
       if (a.round_bf16) {
 #pragma unroll
         for (int j = 0; j < 8; ++j) g[i][j] = bf16_round(g[i][j]);
@@ -919,7 +924,7 @@ __global__ void __launch_bounds__(CTA) ratchet_update_grouped_kernel(const __gri
     a.grad = L.grad, a.ldg = L.ldg, a.rows = L.rows, a.packed = L.packed, a.ldp = L.ldp;
     a.code_out = L.code_out, a.ldc = L.ldc, a.rms_ema = L.rms_ema, a.counts = L.counts;
     a.rms_sum = L.rms_sum, a.grad_mul = L.grad_mul;
-    a.row_rms = nullptr, a.grad_scale = nullptr, a.ws = nullptr;
+    a.row_rms = nullptr, a.grad_scale = nullptr, a.ws = nullptr, a.row_ids = nullptr;
     ratchet_update_body<G, RT, VPT, false>(a, b - L.block0, lut);
   }
 }
@@ -933,7 +938,9 @@ __global__ void __launch_bounds__(CTA) ratchet_update_generic_kernel(UpdateArgs 
   __shared__ float smx[8];
   __shared__ int redi[CTA / 32][4];
   const int t = threadIdx.x;
-  const int64_t row = blockIdx.x;
+  const int64_t grow = blockIdx.x;  // gradient row; the state row is row_ids[grow] if given
+  const int64_t row = a.row_ids != nullptr ? a.row_ids[grow] : grow;
+  if (row < 0) return;  // uniform over the CTA: before any barrier
   const int64_t nch = (a.cols + 7) / 8;
   float ss = 0.0f, gs = 0.0f;
   bool bad = false;
@@ -941,7 +948,7 @@ __global__ void __launch_bounds__(CTA) ratchet_update_generic_kernel(UpdateArgs 
     for (int j = 0; j < 8; ++j) {
       const int64_t k = 8 * c + j;
       if (k >= a.cols) break;
-      float gv = load_elem(a.grad, a.grad_dtype, row * a.ldg + k);
+      float gv = load_elem(a.grad, a.grad_dtype, grow * a.ldg + k);
       if (a.round_bf16) gv = bf16_round(gv);
       if (a.grad_mul != 1.0f) gv = __fmul_rn(gv, a.grad_mul);
       bad |= !isfinite(gv);
@@ -968,7 +975,7 @@ __global__ void __launch_bounds__(CTA) ratchet_update_generic_kernel(UpdateArgs 
   for (int64_t k = t; k < a.cols; k += CTA) {
     uint8_t v = a.packed[row * a.ldp + k];
     if (!bad) {
-      float gv = load_elem(a.grad, a.grad_dtype, row * a.ldg + k);
+      float gv = load_elem(a.grad, a.grad_dtype, grow * a.ldg + k);
       if (a.round_bf16) gv = bf16_round(gv);
       if (a.grad_mul != 1.0f) gv = __fmul_rn(gv, a.grad_mul);
       v = ratchet_one(v, pressure_increment(gv, denom, rcp, a.normalize, a.low, a.high), a, m);
@@ -1764,6 +1771,108 @@ static inline unsigned grid_for(int64_t n, int threads) {
   return static_cast<unsigned>(b);
 }
 
+
+// ===========================================================================================
+// Ratchet embedding (ratchet.py:688-749) and uint16 token windows (data.py:238-287).
+// ===========================================================================================
+// out[t, :] = float(code(packed[tok[t], :])) * scale[tok[t]] -- the reference's
+// F.embedding(tokens, code.float() * scale[:, None]) without the [rows, dim] effective weight.
+// A warp per token; 8 codes per 8-byte load when the rows allow it.  Tokens outside [0, rows)
+// give zero rows and set RT_STATUS_INDEX_RANGE.
+__global__ void __launch_bounds__(256)
+    embedding_forward_kernel(const uint8_t *packed, int64_t ldp, const float *scale, int max_code,
+                             const int64_t *tokens, int64_t n_tok, int64_t rows, int64_t dim,
+                             float *out, int64_t ldo, int vec) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t t = blockIdx.x * 8ll + (threadIdx.x >> 5);
+  if (t >= n_tok) return;
+  const int64_t tok = tokens[t];
+  float *o = out + t * ldo;
+  if (tok < 0 || tok >= rows) {
+    for (int64_t k = lane; k < dim; k += 32) o[k] = 0.0f;
+    if (lane == 0) raise_status(RT_STATUS_INDEX_RANGE);
+    return;
+  }
+  const float sc = __ldg(scale + tok);
+  const uint8_t *pr = packed + tok * ldp;
+  if (vec) {
+    for (int64_t c = lane; c < dim / 8; c += 32) {
+      const uint2 w = __ldg(reinterpret_cast<const uint2 *>(pr + 8 * c));
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t word = j < 4 ? w.x : w.y;
+        v[j] = __fmul_rn(static_cast<float>(code_of(static_cast<uint8_t>(word >> (8 * (j & 3))),
+                                                    max_code)),
+                         sc);
+      }
+      st8(o + 8 * c, v);
+    }
+  } else {
+    for (int64_t k = lane; k < dim; k += 32)
+      o[k] = __fmul_rn(static_cast<float>(code_of(pr[k], max_code)), sc);
+  }
+}
+
+// The embedding's weight gradient, row-sparse: sorted_tokens / order are the token ids sorted
+// stably and their positions (equal tokens keep position order).  The position at sorted index i that starts a
+// run of equal tokens writes, into grad_rows[i], the sum of the run's gradient rows in position
+// order from +0 (the order of the reference's CPU embedding backward, which adds each
+// position's row into its token's row in position order), and row_ids[i] = its token; every
+// other sorted index writes row_ids[i] = -1.  A warp per sorted index.
+__global__ void __launch_bounds__(256)
+    embedding_grad_rows_kernel(const float *grad, int64_t ldg, const int64_t *sorted_tokens,
+                               const int64_t *order, int64_t n_tok, int64_t rows, int64_t dim,
+                               float *grad_rows, int64_t ldr, int64_t *row_ids) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int64_t i = blockIdx.x * 8ll + (threadIdx.x >> 5);
+  if (i >= n_tok) return;
+  const int64_t tok = sorted_tokens[i];
+  const bool start = i == 0 || sorted_tokens[i - 1] != tok;
+  if (!start || tok < 0 || tok >= rows) {
+    if (lane == 0) row_ids[i] = -1;
+    if (start && lane == 0) raise_status(RT_STATUS_INDEX_RANGE);
+    return;
+  }
+  int64_t end = i + 1;
+  while (end < n_tok && sorted_tokens[end] == tok) ++end;
+  float *dst = grad_rows + i * ldr;
+  for (int64_t k = lane; k < dim; k += 32) {
+    float acc = 0.0f;
+    for (int64_t j = i; j < end; ++j) acc = __fadd_rn(acc, __ldg(grad + order[j] * ldg + k));
+    dst[k] = acc;
+  }
+  if (lane == 0) row_ids[i] = tok;
+}
+
+// inputs[b, t] = data[starts[b] + t], targets[b, t] = data[starts[b] + t + 1] (uint16 token ids
+// widened to int64): the reference's batch_from_starts on a device-resident uint16 shard.
+// Windows reaching past the data write zeros and set RT_STATUS_INDEX_RANGE.
+__global__ void token_windows_kernel(const uint16_t *data, int64_t n, const int64_t *starts,
+                                     int64_t batch, int64_t block, int64_t *inputs,
+                                     int64_t *targets) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t total = batch * block;
+  for (int64_t e = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t b = e / block, t = e - b * block;
+    const int64_t idx = starts[b] + t;
+    if (idx < 0 || idx + 1 >= n) {
+      inputs[e] = 0;
+      targets[e] = 0;
+      raise_status(RT_STATUS_INDEX_RANGE);
+      continue;
+    }
+    inputs[e] = data[idx];
+    targets[e] = data[idx + 1];
+  }
+}
+
 }  // namespace rt
 
 // ===========================================================================================
@@ -1846,6 +1955,7 @@ static UpdateArgs update_args(const void *grad, int grad_dtype, int round_bf16, 
   a.counts = reinterpret_cast<unsigned long long *>(counts);
   a.row_rms = row_rms, a.rms_sum = rms_sum, a.grad_scale = grad_scale;
   a.grad_mul = 1.0f;
+  a.row_ids = nullptr;
   return a;
 }
 
@@ -2322,4 +2432,73 @@ extern "C" int rt_heads_gather_sr(const void *const *src, const int64_t *strides
   else
     RT_DISPATCH_ROW(cfg, heads3_sr_kernel, __nv_bfloat16, grid, a);
   return check_launch("rt_heads_gather_sr");
+}
+
+extern "C" int rt_embedding_forward(const uint8_t *packed, int64_t ldp, const float *scale,
+                                    int max_code, const int64_t *tokens, int64_t n_tok,
+                                    int64_t rows, int64_t dim, float *out, int64_t ldo,
+                                    void *stream) {
+  if (n_tok < 0 || rows <= 0 || dim <= 0)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_embedding_forward: shape");
+  if (n_tok == 0) return RT_OK;
+  if (packed == nullptr || scale == nullptr || tokens == nullptr || out == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_embedding_forward: null pointer");
+  const int vec = dim % 8 == 0 && ldp % 8 == 0 && (reinterpret_cast<uintptr_t>(packed) & 7) == 0 &&
+                  aligned16(out) && ldo % 4 == 0;
+  launch_k(embedding_forward_kernel, static_cast<unsigned>((n_tok + 7) / 8), 256, 0,
+           as_stream(stream), packed, ldp, scale, max_code, tokens, n_tok, rows, dim, out, ldo,
+           vec);
+  return check_launch("rt_embedding_forward");
+}
+
+extern "C" int64_t rt_embedding_update_workspace_bytes(int64_t n_tok, int64_t dim) {
+  if (n_tok <= 0 || dim <= 0) return 0;
+  const int64_t grads = ((n_tok * dim * 4 + 255) / 256) * 256;
+  return grads + n_tok * 8;
+}
+
+extern "C" int rt_embedding_ratchet_update(
+    const float *grad, int64_t ldg, const int64_t *sorted_tokens, const int64_t *order,
+    int64_t n_tok, int64_t rows, int64_t dim, void *workspace, int64_t workspace_bytes,
+    uint8_t *packed, int64_t ldp, int8_t *code_out, int64_t ldc, float *rms_ema, double ema_beta,
+    int max_code, int threshold, double bucket_low, double bucket_high, double eps,
+    int64_t *counts, float *rms_sum, void *stream) {
+  if (int rc = ratchet_update_check(rows, dim, max_code, threshold, bucket_low, bucket_high))
+    return rc;
+  if (n_tok < 0) return fail(RT_ERR_INVALID_ARGUMENT, "rt_embedding_ratchet_update: shape");
+  if (n_tok == 0) return RT_OK;
+  if (grad == nullptr || sorted_tokens == nullptr || order == nullptr || packed == nullptr ||
+      workspace == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_embedding_ratchet_update: null pointer");
+  if (workspace_bytes < rt_embedding_update_workspace_bytes(n_tok, dim) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(RT_ERR_INVALID_ARGUMENT,
+                "rt_embedding_ratchet_update: workspace of rt_embedding_update_workspace_bytes, "
+                "256-byte aligned");
+  cudaStream_t s = as_stream(stream);
+  float *grad_rows = static_cast<float *>(workspace);
+  int64_t *row_ids = reinterpret_cast<int64_t *>(
+      static_cast<uint8_t *>(workspace) + ((n_tok * dim * 4 + 255) / 256) * 256);
+  launch_k(embedding_grad_rows_kernel, static_cast<unsigned>((n_tok + 7) / 8), 256, 0, s, grad,
+           ldg, sorted_tokens, order, n_tok, rows, dim, grad_rows, dim, row_ids);
+  if (int rc = check_launch("rt_embedding_ratchet_update")) return rc;
+  // the update over the run-start rows: row r of grad_rows updates state row row_ids[r]
+  UpdateArgs a = update_args(grad_rows, RT_F32, 0, dim, n_tok, dim, packed, ldp, code_out, ldc, 1,
+                             rms_ema, ema_beta, max_code, threshold, bucket_low, bucket_high, eps,
+                             counts, nullptr, rms_sum, nullptr);
+  a.row_ids = row_ids;
+  return ratchet_update_launch(a, s);
+}
+
+extern "C" int rt_token_windows(const uint16_t *data, int64_t n, const int64_t *starts,
+                                int64_t batch, int64_t block, int64_t *inputs, int64_t *targets,
+                                void *stream) {
+  if (n < 0 || batch < 0 || block <= 0)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_token_windows: shape");
+  if (batch == 0) return RT_OK;
+  if (data == nullptr || starts == nullptr || inputs == nullptr || targets == nullptr)
+    return fail(RT_ERR_INVALID_ARGUMENT, "rt_token_windows: null pointer");
+  launch_k(token_windows_kernel, grid_for(batch * block, 256), 256, 0, as_stream(stream), data, n,
+           starts, batch, block, inputs, targets);
+  return check_launch("rt_token_windows");
 }

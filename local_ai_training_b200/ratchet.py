@@ -940,8 +940,50 @@ class DiscreteRatchetLinear(nn.Module):
                 f"states={2 * self.max_code + 1}, threshold={self.pressure_threshold}, bias=False")
 
 
+class _EmbeddingLookup(torch.autograd.Function):
+    """Forward: rows of fp32 `code * scale` gathered straight from `packed` (the
+    reference's F.embedding over the materialised effective weight, ratchet.py:740-747).
+    Backward: the output gradient and the token ids become the layer's pending row-sparse
+    weight gradient (no [rows, dim] gradient tensor)."""
+
+    @staticmethod
+    def forward(ctx, token_ids, anchor, layer):
+        flat = token_ids.reshape(-1).to(torch.int64).contiguous()
+        pk = layer.packed
+        scale = layer.scale.detach().float().contiguous()
+        out = torch.empty((flat.numel(), layer.embedding_dim), device=pk.device,
+                          dtype=torch.float32)
+        ev = _lib.prof_start(pk)
+        _lib.check(_lib.lib().rt_embedding_forward(
+            pk.data_ptr(), pk.stride(0), scale.data_ptr(), layer.max_code, flat.data_ptr(),
+            flat.numel(), layer.num_embeddings, layer.embedding_dim, out.data_ptr(),
+            out.stride(0), _lib.stream_of(pk)))
+        if ev is not None:
+            _lib.prof_stop(ev, "embedding", pk, 0.0, flat.numel() * layer.embedding_dim * 5)
+        ctx.layer = layer
+        ctx.save_for_backward(flat)
+        return out.reshape(*token_ids.shape, layer.embedding_dim)
+
+    @staticmethod
+    def backward(ctx, grad):
+        (flat,) = ctx.saved_tensors
+        layer = ctx.layer
+        g = grad.reshape(-1, layer.embedding_dim)
+        if g.dtype != torch.float32:
+            g = g.float()
+        layer._sparse_gradient = (flat, g.contiguous())
+        return None, None, None
+
+
 class RatchetEmbedding(DiscreteRatchetLinear):
-    """Master-weight-free token embedding (ratchet.py:688-749): rows are tokens."""
+    """Master-weight-free token embedding (ratchet.py:688-749): rows are tokens.
+
+    On CUDA the forward gathers `code * scale` rows straight from `packed` (no [rows, dim]
+    effective weight), backward keeps the output gradient and the token ids, and
+    `ratchet_update` updates only the rows of the tokens seen (rt_embedding_ratchet_update): the
+    other rows have a zero gradient in the reference, which leaves them unchanged.  A trainable
+    scale keeps the reference's dense effective-weight path (its gradient reaches log_scale
+    through autograd)."""
 
     def __init__(self, num_embeddings: int, embedding_dim: int, *, max_code: int,
                  pressure_threshold: int = 8, bucket_low: float = 0.5, bucket_high: float = 1.5,
@@ -961,11 +1003,67 @@ class RatchetEmbedding(DiscreteRatchetLinear):
 
     def forward(self, token_ids: Tensor) -> Tensor:  # type: ignore[override]
         _require_cuda(self.packed, "the ratchet embedding")
+        training = self.training and torch.is_grad_enabled()
+        if not self.trainable_scale:
+            if training:
+                # the gradient of this forward replaces any earlier one (the reference's fresh
+                # effective-weight leaf per forward)
+                self._sparse_gradient = None
+                anchor = torch.empty(0, device=self.packed.device, requires_grad=True)
+                return _EmbeddingLookup.apply(token_ids.to(self.packed.device), anchor, self)
+            with torch.no_grad():
+                return _EmbeddingLookup.apply(token_ids.to(self.packed.device), None, self)
         effective = self.effective_weight()
-        if self.training and torch.is_grad_enabled():
+        if training:
             effective = effective.detach().requires_grad_(True)
             self._effective_weight = effective
         return F.embedding(token_ids, effective)
+
+    @property
+    def has_pending_gradient(self) -> bool:
+        return getattr(self, "_sparse_gradient", None) is not None or super().has_pending_gradient
+
+    def discard_pending_gradient(self) -> None:
+        self._sparse_gradient = None
+        super().discard_pending_gradient()
+
+    @torch.no_grad()
+    def ratchet_update(self, *, validate: bool = True) -> RatchetUpdateStats:
+        pending = getattr(self, "_sparse_gradient", None)
+        if pending is None:
+            return super().ratchet_update(validate=validate)
+        self._sparse_gradient = None
+        tokens, grad = pending
+        if validate and not torch.isfinite(grad).all():
+            raise FloatingPointError("ratchet gradient contains NaN or Inf")
+        pk = self.packed
+        sorted_tokens, order = torch.sort(tokens, stable=True)
+        mirror = self.code_int8()
+        counts = torch.zeros(4, device=pk.device, dtype=torch.int64)
+        rms_sum = torch.zeros(1, device=pk.device, dtype=torch.float32)
+        n, dim = grad.shape
+        need = _lib.lib().rt_embedding_update_workspace_bytes(n, dim)
+        work = _lib.workspace(pk.device, need)
+        ema = self.rms_ema if self.rms_ema_beta > 0.0 else None
+        ev = _lib.prof_start(pk)
+        _lib.check(_lib.lib().rt_embedding_ratchet_update(
+            grad.data_ptr(), grad.stride(0), sorted_tokens.data_ptr(), order.data_ptr(), n,
+            self.num_embeddings, dim, _lib.ptr(work), need, pk.data_ptr(), pk.stride(0),
+            mirror.data_ptr(), mirror.stride(0), _lib.ptr(ema), float(self.rms_ema_beta),
+            self.max_code, self.pressure_threshold, float(self.bucket_low),
+            float(self.bucket_high), float(self.eps), counts.data_ptr(), rms_sum.data_ptr(),
+            _lib.stream_of(pk)))
+        if ev is not None:
+            _lib.prof_stop(ev, "embedding_update", pk, 0.0, n * dim * 4 * 2 + n * dim * 2)
+        if validate:
+            self._validate_state()
+        stats = RatchetUpdateStats(
+            total_weights=self.out_features * self.in_features,
+            positive_moves=counts[0], negative_moves=counts[1],
+            blocked_positive_moves=counts[2], blocked_negative_moves=counts[3],
+            gradient_rms_mean=rms_sum[0] / max(1, self.out_features))
+        self._maybe_leak_pressure()
+        return stats.materialize() if validate else stats
 
     def extra_repr(self) -> str:
         return (f"num_embeddings={self.num_embeddings}, embedding_dim={self.embedding_dim}, "

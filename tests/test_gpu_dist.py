@@ -129,3 +129,68 @@ def test_two_rank_state_stays_replicated(tmp_path):
         assert torch.equal(a, b)
     assert r0["moves"] == r1["moves"] and r0["moves"] > 0
     assert r0["changed"] == r1["changed"] and r0["changed"] > 0
+
+
+def _accum_resume_worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    """Two ranks, two accumulated micro-batches per step: the replicated state agrees across
+    ranks, and a run resumed from rank 0's checkpoint equals the uninterrupted one."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+
+    from local_ai_training_b200 import build_seeded_model
+    from local_ai_training_b200.checkpoint import load_checkpoint, save_checkpoint
+    from local_ai_training_b200.dist import RatchetDataParallel
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    device = torch.device("cuda", rank)
+
+    def build(seed):
+        model = build_seeded_model(_cfg(True), max_code=2, seed=seed).to(device).train()
+        for layer in model.ratchet_layers():
+            layer.sr_seed = 21
+        opt = torch.optim.AdamW(model.parameters(), lr=1e-3)
+        return model, opt, RatchetDataParallel(model, accumulation_steps=2)
+
+    def step(model, ddp, opt, tokens):
+        for chunk in tokens.chunk(2):
+            _, loss = model(chunk[:, :-1], chunk[:, 1:])
+            loss.backward()
+        stats = ddp.step(opt)
+        opt.zero_grad(set_to_none=True)
+        return int(stats.code_moves)
+
+    gen = torch.Generator().manual_seed(200 + rank)
+    batches = [torch.randint(0, 64, (8, 33), generator=gen).to(device) for _ in range(4)]
+    model, opt, ddp = build(9)
+    moves = sum(step(model, ddp, opt, b) for b in batches[:2])
+    save_checkpoint(os.path.join(out_dir, "ck"), model=model, optimizer=opt, step=2, max_code=2,
+                    vocabulary=(), experiment_config={"matmul_mode": "int8"})
+    moves += sum(step(model, ddp, opt, b) for b in batches[2:])
+    resumed, ropt, rddp = build(123)
+    load_checkpoint(os.path.join(out_dir, "ck"), model=resumed, optimizer=ropt, expected_max_code=2,
+                    expected_vocabulary=(), expected_matmul_mode="int8")
+    for b in batches[2:]:
+        step(resumed, rddp, ropt, b)
+    same = all(torch.equal(a, b) for a, b in zip(model.state_dict().values(),
+                                                 resumed.state_dict().values()))
+    torch.save({"packed": [l.packed.cpu() for l in model.ratchet_layers()], "moves": moves,
+                "resume_equal": same}, os.path.join(out_dir, f"acc{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_accumulation_and_resume(tmp_path):
+    pytest.importorskip("safetensors")
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_accum_resume_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       start_method="spawn")
+    r0, r1 = (torch.load(tmp_path / f"acc{r}.pt") for r in range(2))
+    for a, b in zip(r0["packed"], r1["packed"]):
+        assert torch.equal(a, b)
+    assert r0["moves"] == r1["moves"] and r0["moves"] > 0
+    assert r0["resume_equal"] and r1["resume_equal"]
