@@ -240,11 +240,68 @@ def bench_producers(m, k, reps, flush, peaks, dtype=torch.float32):
     _report("transpose_quant_bfloat16", list(xt.shape), t, xt.numel() * 5, 0, 0, peaks)
 
 
+def bench_gelu_bwd(m, k, reps, flush, peaks):
+    from .int8_backward import gelu_backward
+
+    dev = torch.device("cuda")
+    x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+    gy = (torch.randn(m, k, device=dev) * 1e-2).to(torch.bfloat16)
+    t = _time(lambda: gelu_backward(gy, x), reps, flush)
+    return _report("gelu_bwd_bfloat16", [m, k], t, 3 * m * k * 2, 0, 0, peaks)
+
+
+def bench_cross_entropy(m, vocab, reps, flush, peaks):
+    """The lm_head loss kernels: per-row max / log-sum-exp / loss of fp32 logits, then the bf16
+    logit gradient."""
+    from .cross_entropy import cross_entropy_grad_bf16, cross_entropy_rows
+
+    dev = torch.device("cuda")
+    logits = torch.randn(m, vocab, device=dev) * 2.0
+    targets = torch.randint(0, vocab, (m,), device=dev)
+    t = _time(lambda: cross_entropy_rows(logits, targets), reps, flush)
+    _report("ce_fwd_float32", [m, vocab], t, 4 * m * vocab, 0, 0, peaks)
+    row_max, row_logsum, _ = cross_entropy_rows(logits, targets)
+    count = torch.tensor([float(m)], device=dev)
+    gl = torch.ones((), device=dev)
+    t = _time(lambda: cross_entropy_grad_bf16(logits, targets, row_max, row_logsum, gl, count),
+              reps, flush)
+    return _report("ce_bwd_float32", [m, vocab], t, 6 * m * vocab, 0, 0, peaks)
+
+
+def bench_matmul_bf16(m, k, n, reps, flush, peaks):
+    """The lm_head's bf16 grad_input GEMM: [m, k] x [k, n] (k = vocab)."""
+    from .int8_matmul import matmul_bf16
+
+    dev = torch.device("cuda")
+    a = (torch.randn(m, k, device=dev) * 1e-3).to(torch.bfloat16)
+    b = torch.randn(k, n, device=dev).to(torch.bfloat16)
+    t = _time(lambda: matmul_bf16(a, b), reps, flush)
+    return _report("gemm_bf16", [m, k, n], t, 2 * (m * k + k * n + m * n), 2.0 * m * n * k,
+                   peaks["bf16_tflops"], peaks)
+
+
+def bench_unpack(rows, cols, reps, flush, peaks):
+    """The code-mirror refresh after the data-parallel all-gather of `packed`."""
+    dev = torch.device("cuda")
+    packed = (torch.randint(0, 7, (rows, cols), device=dev, dtype=torch.uint8)
+              | (torch.randint(0, 15, (rows, cols), device=dev, dtype=torch.uint8) << 4))
+    code = torch.empty((rows, cols), device=dev, dtype=torch.int8)
+
+    def run():
+        _lib.check(_lib.lib().rt_unpack_code_pressure(
+            packed.data_ptr(), cols, rows, cols, 3, code.data_ptr(), cols, None, 0,
+            _lib.stream_of(packed)))
+
+    t = _time(run, reps, flush)
+    return _report("unpack_codes", [rows, cols], t, 2 * rows * cols, 0, 0, peaks)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("kernel", choices=["all", "all1b", "fwd", "grad_input", "gradw", "quant_sr",
                                            "quant_rn", "dequant", "update", "update_grouped",
-                                           "rmsnorm_bwd", "producers"])
+                                           "rmsnorm_bwd", "producers", "gelu_bwd", "ce",
+                                           "matmul_bf16", "unpack"])
     parser.add_argument("--m", type=int, default=16384)
     parser.add_argument("--k", type=int, default=512)
     parser.add_argument("--n", type=int, default=2048)
@@ -277,6 +334,9 @@ def main() -> None:
                              "ratchet_update_grouped_1b")
         bench_rmsnorm_bwd(m, 512, args.reps, flush, peaks)
         bench_producers(m, 512, args.reps, flush, peaks)
+        bench_gelu_bwd(m, 2048, args.reps, flush, peaks)
+        bench_cross_entropy(m, 8192, args.reps, flush, peaks)
+        bench_matmul_bf16(m, 8192, 512, args.reps, flush, peaks)
         return
     if args.kernel == "all1b":  # the ~1B decoder's layer shapes, M = 16384 tokens
         for k, n in SHAPES_1B:
@@ -313,6 +373,14 @@ def main() -> None:
         bench_rmsnorm_bwd(m, args.k, args.reps, flush, peaks)
     elif args.kernel == "producers":
         bench_producers(m, args.k, args.reps, flush, peaks)
+    elif args.kernel == "gelu_bwd":
+        bench_gelu_bwd(m, args.k, args.reps, flush, peaks)
+    elif args.kernel == "ce":
+        bench_cross_entropy(m, args.n, args.reps, flush, peaks)
+    elif args.kernel == "matmul_bf16":
+        bench_matmul_bf16(m, args.k, args.n, args.reps, flush, peaks)
+    elif args.kernel == "unpack":
+        bench_unpack(args.n, args.k, args.reps, flush, peaks)
 
 
 if __name__ == "__main__":
