@@ -62,16 +62,20 @@ def sequences_per_rank(wl: dict, world: int) -> int:
     return wl["batch_per_rank"]
 
 
-# DRAM bytes (read + write) that ncu measured for one launch of a family's kernel, and that
-# launch's algorithmic bytes (profiles/gemm_i8_fwd_16384x512x2048.md,
-# profiles/quant_rows_sr_bf16_16384x2048.md).  The roofline's `traffic` for the dominant family is
-# this ratio times the family's mean algorithmic bytes per launch (traffic grows in proportion
-# with the rows processed).  Below 1: outputs still resident in L2 when the kernel ends.
+# DRAM bytes (read + write) that ncu measured for one launch of a family's kernel at a shape of the
+# workload, and that launch's algorithmic bytes (the profiles named below).  The roofline's
+# `traffic` for the dominant family is this ratio times the family's mean algorithmic bytes per
+# launch (traffic grows in proportion with the tiles processed).  Below 1: outputs still resident
+# in L2 when the kernel ends; above 1: operand tiles read again by later waves of tiles.
 NCU_TRAFFIC = {
-    ("gemm_i8", "ratchet-decoder-25m"): ((9.59e6 + 9.11e6), 76.6e6,
+    ("gemm_i8", "ratchet-decoder-25m"): ((9.6e6 + 7.8e6), 76.6e6,
                                          "profiles/gemm_i8_fwd_16384x512x2048.md"),
-    ("quant_rows_sr", "ratchet-decoder-25m"): ((67.15e6 + 7.62e6), 100.7e6,
+    ("quant_rows_sr", "ratchet-decoder-25m"): ((67.2e6 + 7.3e6), 100.7e6,
                                                "profiles/quant_rows_sr_bf16_16384x2048.md"),
+    ("gemm_i8", "ratchet-decoder-1b"): ((46.3e6 + 145.8e6), 247.6e6,
+                                        "profiles/gemm_i8_fwd_16384x2048x6144.md"),
+    ("gemm_gradw_bf16", "ratchet-decoder-1b"): ((418.6e6 + 42.4e6), 318.8e6,
+                                                "profiles/gemm_gradw_bf16_16384x6144x2048.md"),
 }
 
 
