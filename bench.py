@@ -291,7 +291,8 @@ def measure(args, wl: dict, rank: int, local_rank: int, world: int, *, steps: in
     device = torch.device("cuda", local_rank)
     config = ModelConfig(vocab_size=wl["vocab"], block_size=wl["block"], n_layer=wl["n_layer"],
                          n_head=wl["n_head"], n_embd=wl["n_embd"], dropout=0.0,
-                         matmul_mode="int8", int8_backward=True)
+                         matmul_mode="int8", int8_backward=True,
+                         fused_grad_quant=args.fused_grad_quant)
     model = build_seeded_model(config, max_code=wl["max_code"], seed=wl["seed"]).to(device).train()
     for layer in model.ratchet_layers():
         layer.sr_seed = wl["seed"] + 7
@@ -614,6 +615,9 @@ def main() -> None:
     parser.add_argument("--no-secondary", action="store_true",
                         help="N = 1, workload 1b: skip the 25m measurement carried in the line")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--fused-grad-quant", action="store_true",
+                        help="ModelConfig(fused_grad_quant=True): the producer backwards also "
+                             "stochastic-round the layer gradients (same results)")
     parser.add_argument("--no-graph", action="store_true", help="time eager steps (no CUDA graph)")
     parser.add_argument("--dp-bucket-layers", type=int, default=4,
                         help="N>1: layers whose grad_W reduce-scatters are batched into one group")
