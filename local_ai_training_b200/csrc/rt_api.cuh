@@ -38,6 +38,13 @@ bool pdl_enabled() {
   return on;
 }
 
+bool staged_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("RT_ROW_STAGED");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
 bool pair_enabled() {
   static const bool on = [] {
     const char *v = getenv("RT_GEMM_PAIR");

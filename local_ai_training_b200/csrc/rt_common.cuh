@@ -47,6 +47,7 @@ __device__ __forceinline__ void pdl_trigger() {
 }
 bool pdl_enabled();
 bool pair_enabled();  // CTA-pair GEMM tiles (RT_GEMM_PAIR=0 turns them off)
+bool staged_enabled();  // shared-memory staged row kernels (RT_ROW_STAGED=0 turns them off)
 template <typename... KArgs, typename... Args>
 inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                      Args &&...args) {
@@ -254,6 +255,20 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void 
 }
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Per-thread asynchronous 16-byte copy global -> shared (cached in L2 only).  A thread that
+// reads back only the slots it filled itself needs no barrier: cp_async_wait<N> makes its own
+// copies of all but the N most recent committed groups visible to it.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 // wait until no committed bulk group of this thread is still reading shared memory
 __device__ __forceinline__ void bulk_wait_read_all() {

@@ -538,11 +538,258 @@ __device__ __forceinline__ void sr_quant_store_row(const QuantArgs &a, uint32_t 
     *reinterpret_cast<uint2 *>(qr + 8 * c) = o;
   }
 }
+// ---- Staged stochastic-rounding quantiser: the layer gradients of the int8 backward.
+// Same results as quant_rows_kernel (floor(RN(RN(v / scale) + u)), clamped), from two changes:
+//  * every thread copies its chunks of the row groups S-1 iterations ahead into its own slots of
+//    shared memory with cp.async, so HBM reads stay in flight while the current rows compute;
+//  * the rounding decision is made in fixed point.  With R = RN(1/scale)·2^15 (exact scaling),
+//    t = fma(v, R, 1.5·2^23 + 2) rounds v·R + 2 to an integer T + 2 (|v·R| < 2^22 keeps t in
+//    [2^23, 2^24), where consecutive integers have consecutive bit patterns).  For the element's
+//    16-bit draw h (u = (h + 1/2)·2^-16),  W = 2·bits(t) + h + 2^23  equals
+//    0x97000000 + Z + 4 (mod 2^32) with Z = 2T + h, the sum RN(v/scale)·2^16 + h + 1/2 estimated
+//    to within 2.25 units (reciprocal 0.25·2, integer rounding 0.5·2, the quotient's rounding
+//    2^-18·2^16).  The reference sum RN(q0 + u) moves by at most 0.5 more, so unless Z lies within
+//    2.75 of a multiple of 2^16 — exactly when the low 16 bits of W are below 7 — floor(sum) is
+//    Z >> 16, whose low byte is byte 2 of W.  Those elements take the IEEE division instead.
+//    |q0| <= 127 + 2^-17 and u <= 1 - 2^-17 bound the sum by 128, and a sum within 2.75 units of
+//    ±127 or 128 is always re-done exactly, so the fast path needs no clamp.
+//    Zero rows take R = 0 (every value 0, t = 2^23·1.5 + 2); rows whose reciprocal exceeds 2^100
+//    (amax below ~1e-28) are done exactly throughout.
+constexpr float kSrFixedMagic = 12582914.0f;  // 1.5·2^23 + 2
+
+// int8 bytes of eight fast-path words (byte 2 of each) and whether any needs the exact path.
+__device__ __forceinline__ uint2 sr_fixed_pack(const uint32_t (&w)[8]) {
+  const uint32_t a = __byte_perm(w[0], w[1], 0x0062), b = __byte_perm(w[2], w[3], 0x0062);
+  const uint32_t c = __byte_perm(w[4], w[5], 0x0062), d = __byte_perm(w[6], w[7], 0x0062);
+  return make_uint2(__byte_perm(a, b, 0x5410), __byte_perm(c, d, 0x5410));
+}
+// (the low 16 bits of each word moved to the top by a multiply, then three-way minima)
+__device__ __forceinline__ bool sr_fixed_ambiguous(const uint32_t (&w)[8]) {
+  uint32_t m = __vimin3_u32(w[0] * 65536u, w[1] * 65536u, w[2] * 65536u);
+  m = __vimin3_u32(m, w[3] * 65536u, w[4] * 65536u);
+  m = __vimin3_u32(m, w[5] * 65536u, w[6] * 65536u);
+  return min(m, w[7] * 65536u) < (7u << 16);
+}
+// h + 2^23 for the low / high 16-bit half of a Philox word (one byte permute each).
+__device__ __forceinline__ uint32_t sr_h_lo(uint32_t word) {
+  return __byte_perm(word, 0x00800000u, 0x7610);
+}
+__device__ __forceinline__ uint32_t sr_h_hi(uint32_t word) {
+  return __byte_perm(word, 0x00800000u, 0x7632);
+}
+// The exact path for one element: the reference's two roundings, floor and clamp.
+__device__ __forceinline__ int sr_exact(float v, float scale, uint32_t hbits) {
+  // hbits = h + 2^23; u = (h + 1/2)·2^-16 built exactly in a float's mantissa
+  const float u = __uint_as_float(0x3F800040u | ((hbits & 0xFFFFu) << 7)) - 1.0f;
+  const float t = __fadd_rn(__fdiv_rn(v, scale), u);
+  return min(max(__float2int_rd(t), -127), 127);
+}
+
+template <typename T, int RT, int VPT, int S>
+__global__ void __launch_bounds__(CTA) quant_sr_staged_kernel(QuantArgs a) {
+  constexpr int RPC = CTA / RT;
+  constexpr int P = static_cast<int>(sizeof(T)) / 2;  // 16-byte pieces per chunk: 1 bf16, 2 fp32
+  extern __shared__ uint4 stage[];                     // [S][VPT][P][CTA] own slots
+  __shared__ float smx[RPC * 8];
+  pdl_wait();
+  pdl_trigger();
+  const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
+  const int64_t nch = a.cols / 8;
+  const int64_t groups = (a.rows + RPC - 1) / RPC;
+  const uint32_t step = sr_step_read(a);
+  const char *xbase = static_cast<const char *>(a.x);
+  const int64_t row_bytes = a.stride_row * static_cast<int64_t>(sizeof(T));
+  // up to two chunks a thread the column scales stay in registers; wider rows re-read them
+  // (L1) for each row
+  constexpr bool kCsRegs = VPT <= 2;
+  float csr[kCsRegs ? VPT : 1][8];
+  if constexpr (kCsRegs) sr_load_col_scales<RT, VPT>(a, t, nch, csr);
+
+  auto issue = [&](int64_t grp, int st) {
+    const int64_t row = grp * RPC + sub;
+    if (grp < groups && row < a.rows) {
+      const char *xr = xbase + row * row_bytes;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t c = t + static_cast<int64_t>(i) * RT;
+        if (c < nch) {
+#pragma unroll
+          for (int p = 0; p < P; ++p)
+            cp_async16(&stage[((st * VPT + i) * P + p) * CTA + threadIdx.x],
+                       xr + c * (8 * static_cast<int64_t>(sizeof(T))) + 16 * p);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int s = 0; s < S - 1; ++s) issue(blockIdx.x + static_cast<int64_t>(s) * gridDim.x, s);
+
+  int st = 0;
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    issue(grp + static_cast<int64_t>(S - 1) * gridDim.x, st == 0 ? S - 1 : st - 1);
+    cp_async_wait<S - 1>();
+    const int64_t row = grp * RPC + sub;
+    const bool live = row < a.rows;
+    float v[VPT][8];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      if (live && c < nch) {
+        const uint4 *slot = &stage[((st * VPT + i) * P) * CTA + threadIdx.x];
+        if constexpr (sizeof(T) == 2) {
+          const uint4 u = slot[0];
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            v[i][2 * j] = __uint_as_float(w[j] << 16);
+            v[i][2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+          }
+        } else {
+          const float4 lo = *reinterpret_cast<const float4 *>(slot);
+          const float4 hi = *reinterpret_cast<const float4 *>(slot + CTA);
+          v[i][0] = lo.x, v[i][1] = lo.y, v[i][2] = lo.z, v[i][3] = lo.w;
+          v[i][4] = hi.x, v[i][5] = hi.y, v[i][6] = hi.z, v[i][7] = hi.w;
+          if (a.round_bf16) {
+            uint32_t pb[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              pb[j] = pack_bf16x2(v[i][2 * j], v[i][2 * j + 1]);
+              v[i][2 * j] = __uint_as_float(pb[j] << 16);
+              v[i][2 * j + 1] = __uint_as_float(pb[j] & 0xFFFF0000u);
+            }
+            if (a.xbf16 != nullptr)
+              *reinterpret_cast<uint4 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c) =
+                  make_uint4(pb[0], pb[1], pb[2], pb[3]);
+          } else if (a.xbf16 != nullptr) {
+            st8(reinterpret_cast<__nv_bfloat16 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c), v[i]);
+          }
+        }
+        if constexpr (sizeof(T) == 2) {
+          if (a.xbf16 != nullptr)
+            *reinterpret_cast<uint4 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c) = slot[0];
+        }
+        if (a.col_scale != nullptr) {
+          float cs[8];
+          if constexpr (kCsRegs) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cs[j] = csr[kCsRegs ? i : 0][j];
+          } else {
+            ld8(a.col_scale + 8 * c, cs);
+          }
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            const float2 r = __fmul2_rn(make_float2(v[i][j], v[i][j + 1]),
+                                        make_float2(cs[j], cs[j + 1]));
+            v[i][j] = r.x, v[i][j + 1] = r.y;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i][j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+      }
+    }
+    amax = row_max<RT>(amax, smx, sub, t);  // CTA-uniform trip count: its barriers are safe
+    const float scale = row_scale_of(amax);
+    const float rcp = __frcp_rn(scale);
+    if (live && t == 0) a.row_scale[row] = scale;
+    const bool row_exact = amax != 0.0f && rcp > 0x1p100f;
+    const float r15 = (amax == 0.0f || row_exact) ? 0.0f : __fmul_rn(rcp, 32768.0f);
+    int8_t *qr = a.q + (live ? row : 0) * a.ldq;
+    uint32_t redo = 0;  // this thread's chunks whose bytes the exact path re-does
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      if (!live || c >= nch) continue;
+      const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;  // multiple of 8
+      const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
+      const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+      uint32_t w[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        w[j] = __float_as_uint(__fmaf_rn(v[i][j], r15, kSrFixedMagic)) * 2u +
+               ((j & 1) ? sr_h_hi(pw[j >> 1]) : sr_h_lo(pw[j >> 1]));
+      if (row_exact || sr_fixed_ambiguous(w)) redo |= 1u << i;
+      *reinterpret_cast<uint2 *>(qr + 8 * c) = sr_fixed_pack(w);
+    }
+    // rare (a few elements in 10^4, or a row of tiny maximum): a warp-uniform pass that draws
+    // the flagged chunks again and overwrites their bytes with the exact result
+    if (__any_sync(0xffffffffu, redo != 0)) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        if (((redo >> i) & 1u) == 0) continue;
+        const int64_t c = t + static_cast<int64_t>(i) * RT;
+        const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;
+        const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
+        const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+        int q[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          q[j] = sr_exact(v[i][j], scale, (j & 1) ? sr_h_hi(pw[j >> 1]) : sr_h_lo(pw[j >> 1]));
+        *reinterpret_cast<uint2 *>(qr + 8 * c) =
+            make_uint2(pack4_i8(q[0], q[1], q[2], q[3]), pack4_i8(q[4], q[5], q[6], q[7]));
+      }
+    }
+    st = st == S - 1 ? 0 : st + 1;
+  }
+  cp_async_wait<0>();
+  sr_step_arrive(a, step);
+}
+
 // Host: the vectorised kernels' layout conditions on the quantiser outputs.
 static inline bool sr_outputs_vec(const QuantArgs &a) {
   return (reinterpret_cast<uintptr_t>(a.q) & 7) == 0 && a.ldq % 8 == 0 &&
          (a.col_scale == nullptr || aligned16(a.col_scale)) &&
          (a.xbf16 == nullptr || (aligned16(a.xbf16) && a.ld_xbf16 % 8 == 0));
+}
+
+// Resident CTAs per SM of one staged-kernel instance (its shared stages and registers), asked of
+// the runtime once per instance (the cache is per template instance: one per kernel).
+template <auto kernel>
+static unsigned staged_resident(size_t smem) {
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    // static and dynamic shared memory together may pass the default 48 KB
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, CTA, smem) != cudaSuccess || n < 1)
+      n = 1;
+    per_sm = n;
+  }
+  int sms = 0;
+  if (rt_sm_count(&sms) != RT_OK || sms <= 0) sms = 148;
+  return static_cast<unsigned>(sms) * static_cast<unsigned>(per_sm);
+}
+template <typename T, int RT, int VPT>
+static void launch_quant_sr_staged(const QuantArgs &a, cudaStream_t s) {
+  constexpr int P = static_cast<int>(sizeof(T)) / 2;
+  constexpr int S = VPT * P <= 2 ? 6 : 3;  // 24-48 KB of stages per CTA
+  constexpr size_t smem = static_cast<size_t>(S) * VPT * P * CTA * 16;
+  const unsigned resident = staged_resident<quant_sr_staged_kernel<T, RT, VPT, S>>(smem);
+  const unsigned groups = row_grid(a.rows, RT);
+  launch_k(quant_sr_staged_kernel<T, RT, VPT, S>, groups < resident ? groups : resident, CTA, smem,
+           s, a);
+}
+// The staged kernel takes the vectorised stochastic cases whose chunks fit 48 KB of stages.
+template <typename T>
+static bool quant_sr_staged(const QuantArgs &a, const RowCfg &cfg, cudaStream_t s) {
+  if (!a.stochastic || !staged_enabled()) return false;
+  switch (cfg.rt * 16 + cfg.vpt * static_cast<int>(sizeof(T)) / 2) {
+    case 32 * 16 + 1: launch_quant_sr_staged<T, 32, 1>(a, s); return true;
+    case 128 * 16 + 1: launch_quant_sr_staged<T, 128, 1>(a, s); return true;
+    case 256 * 16 + 1: launch_quant_sr_staged<T, 256, 1>(a, s); return true;
+    case 32 * 16 + 2: launch_quant_sr_staged<T, 32, sizeof(T) == 2 ? 2 : 1>(a, s); return true;
+    case 128 * 16 + 2: launch_quant_sr_staged<T, 128, sizeof(T) == 2 ? 2 : 1>(a, s); return true;
+    case 256 * 16 + 2: launch_quant_sr_staged<T, 256, sizeof(T) == 2 ? 2 : 1>(a, s); return true;
+    case 32 * 16 + 4: launch_quant_sr_staged<T, 32, sizeof(T) == 2 ? 4 : 2>(a, s); return true;
+    case 128 * 16 + 4: launch_quant_sr_staged<T, 128, sizeof(T) == 2 ? 4 : 2>(a, s); return true;
+    case 256 * 16 + 4: launch_quant_sr_staged<T, 256, sizeof(T) == 2 ? 4 : 2>(a, s); return true;
+    default: return false;
+  }
 }
 
 template <typename T>
@@ -553,7 +800,9 @@ static int quant_rows_dispatch(const QuantArgs &a, cudaStream_t s) {
                    (a.col_scale == nullptr || aligned16(a.col_scale)) &&
                    (a.xbf16 == nullptr || (aligned16(a.xbf16) && a.ld_xbf16 % 8 == 0));
   const RowCfg cfg = vec ? row_cfg(a.cols / 8, a.rows) : RowCfg{0, 0};
-  if (cfg.rt != 0) {
+  if (cfg.rt != 0 && quant_sr_staged<T>(a, cfg, s)) {
+    // launched
+  } else if (cfg.rt != 0) {
     int sms = 0;
     if (int rc = rt_sm_count(&sms)) return rc;
     // CTAs per SM that stay resident (the kernels' launch bounds: 4 up to two chunks a thread)
@@ -618,6 +867,8 @@ __device__ __forceinline__ int pressure_increment(float g, float denom, float rc
     if (fabsf(__fsub_rn(mag, high)) <= win || fabsf(__fsub_rn(mag, low)) <= win)
       mag = fabsf(__fdiv_rn(g, denom));
   }
+  // z rounding to ±0 has sign 0 (and with low = 0 would otherwise reach bucket 1)
+  if (mag == 0.0f) return 0;
   const int bucket = mag >= high ? 2 : (mag >= low ? 1 : 0);
   const int sgn = (g > 0.0f) - (g < 0.0f);
   return -sgn * bucket;
@@ -668,7 +919,7 @@ __device__ __forceinline__ void build_update_lut(uint32_t *lut, const UpdateArgs
   __syncthreads();
 }
 // Table index of one weight: the bucket of |z| (z = g / denom, formed as in pressure_increment)
-// and the sign of g; g == 0 moves nothing (bucket 0).
+// and the sign of g; z == ±0 moves nothing (bucket 0).
 __device__ __forceinline__ uint32_t lut_index(uint32_t old, float g, float denom, float rcp,
                                               int normalize, float low, float high) {
   float mag = normalize ? fabsf(__fmul_rn(g, rcp)) : fabsf(g);
@@ -677,7 +928,8 @@ __device__ __forceinline__ uint32_t lut_index(uint32_t old, float g, float denom
     if (fabsf(__fsub_rn(mag, high)) <= win || fabsf(__fsub_rn(mag, low)) <= win)
       mag = fabsf(__fdiv_rn(g, denom));
   }
-  const uint32_t bucket = g == 0.0f ? 0u : static_cast<uint32_t>(mag >= high) + static_cast<uint32_t>(mag >= low);
+  const uint32_t bucket =
+      mag == 0.0f ? 0u : static_cast<uint32_t>(mag >= high) + static_cast<uint32_t>(mag >= low);
   return (old << 3) | (bucket << 1) | static_cast<uint32_t>(g < 0.0f);
 }
 
@@ -926,6 +1178,348 @@ __global__ void __launch_bounds__(CTA) ratchet_update_grouped_kernel(const __gri
     a.rms_sum = L.rms_sum, a.grad_mul = L.grad_mul;
     a.row_rms = nullptr, a.grad_scale = nullptr, a.ws = nullptr, a.row_ids = nullptr;
     ratchet_update_body<G, RT, VPT, false>(a, b - L.block0, lut);
+  }
+}
+
+// ---- Staged update: the same results as the kernels above, from three changes.
+//  * Exact bucket thresholds per row.  RN(|g| / denom) is non-decreasing in |g|, so "its bucket
+//    reaches low (high)" is |g| >= T_low (T_high) for the least float T with RN(T / denom) >= low
+//    (high).  T lies within a few ulps of RN(low · denom): lanes 0-15 of a warp try the 16 floats
+//    from 8 below it, lanes 16-31 those around RN(high · denom), one IEEE division each, and a
+//    ballot picks the first that reaches the bound.  Each weight then needs two comparisons
+//    instead of a product, a window test and a possible division.  Rows where the candidates
+//    leave the finite positive floats (a denominator of inf, thresholds underflowing) keep the
+//    per-weight path of lut_index.  With normalize off the thresholds are low and high.  A bound
+//    of 0 becomes the least positive float: z = ±0 has sign 0 and moves nothing, so bucket 1
+//    starts where z becomes nonzero (at the least positive |g| when denom <= 1, where g / denom
+//    >= g).
+//  * Non-finite gradients: a row's sum of squares is finite unless some gradient is not finite
+//    or the sum overflows; only when one of the CTA's rows has a non-finite sum are the rows
+//    scanned element by element.
+//  * Every thread copies its chunks of the gradient and packed rows S-1 blocks ahead into its own
+//    shared-memory slots (cp.async); the move counts and rms sums go to the layer's counters once
+//    per CTA and layer instead of once per block.
+// Single-layer calls run as a group of one layer (row_rms, grad_scale and row_ids from common).
+__device__ __forceinline__ void cp_async8(void *smem, const void *gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem)), "l"(gmem)
+               : "memory");
+}
+// Eight table entries of one chunk -> its new packed and code bytes and the move counts.
+__device__ __forceinline__ void store_update_chunk(const GroupLayer &L, int64_t row, int64_t c,
+                                                   const uint32_t (&e)[8], Moves &m) {
+  uint32_t counts = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) counts += e[j];
+  const uint32_t t01 = __byte_perm(e[0], e[1], 0x7362), t23 = __byte_perm(e[2], e[3], 0x7362);
+  const uint32_t t45 = __byte_perm(e[4], e[5], 0x7362), t67 = __byte_perm(e[6], e[7], 0x7362);
+  *reinterpret_cast<uint2 *>(L.packed + row * L.ldp + 8 * c) =
+      make_uint2(__byte_perm(t01, t23, 0x5410), __byte_perm(t45, t67, 0x5410));
+  if (L.code_out != nullptr)
+    *reinterpret_cast<uint2 *>(L.code_out + row * L.ldc + 8 * c) =
+        make_uint2(__byte_perm(t01, t23, 0x7632), __byte_perm(t45, t67, 0x7632));
+  m.pos += counts & 0xF;
+  m.neg += (counts >> 4) & 0xF;
+  m.bpos += (counts >> 8) & 0xF;
+  m.bneg += (counts >> 12) & 0xF;
+}
+// Bucket thresholds of one row (every lane of the warp gets both); false: no exact pair found.
+__device__ __forceinline__ bool bucket_thresholds(float denom, float low, float high,
+                                                  int normalize, float &tlo, float &thi) {
+  constexpr float kLeastPositive = 1.40129846e-45f;
+  if (!normalize) {
+    tlo = fmaxf(low, kLeastPositive), thi = fmaxf(high, kLeastPositive);
+    return true;
+  }
+  const int lane = threadIdx.x & 31;
+  const float lo_bound = low > 0.0f ? low : kLeastPositive;
+  const float hi_bound = high > 0.0f ? high : kLeastPositive;
+  const float bound = lane < 16 ? lo_bound : hi_bound;
+  const float c0 = __fmul_rn(bound, denom);
+  const int32_t b = __float_as_int(c0) + ((lane & 15) - 8);
+  const bool in_range = c0 > 0.0f && __float_as_int(c0) >= 8 && b < 0x7F800000 &&
+                        denom > 0.0f && denom < INFINITY;
+  const float cand = __int_as_float(b);
+  const bool reach = in_range && __fdiv_rn(cand, denom) >= bound;
+  const uint32_t mask = __ballot_sync(0xffffffffu, reach);
+  const uint32_t ok = __ballot_sync(0xffffffffu, in_range);
+  const uint32_t lo = mask & 0xFFFFu, hi = mask >> 16;
+  const int klo = __ffs(lo) - 1, khi = __ffs(hi) - 1;
+  const float tl = __shfl_sync(0xffffffffu, cand, klo < 0 ? 0 : klo);
+  const float th = __shfl_sync(0xffffffffu, cand, khi < 0 ? 16 : 16 + khi);
+  // the candidate range must straddle each threshold: first candidate below, the rest monotone
+  const bool tiny_lo = low <= 0.0f && denom > 0.0f && denom <= 1.0f;
+  const bool lo_ok = tiny_lo || (klo >= 1 && lo == (0xFFFFu & ~((1u << klo) - 1u)) &&
+                                 (ok & 0xFFFFu) == 0xFFFFu);
+  const bool hi_ok = khi >= 1 && hi == (0xFFFFu & ~((1u << khi) - 1u)) && (ok >> 16) == 0xFFFFu;
+  tlo = tiny_lo ? kLeastPositive : tl;
+  thi = th;
+  return lo_ok && hi_ok;
+}
+// Move counts and rms sum of the CTA's blocks of one layer -> its counters (whole CTA).
+__device__ __forceinline__ void publish_layer(Moves m, float rr_acc, unsigned long long *counts,
+                                              float *rms_sum, int (*redi)[4], float *rrs, int sub,
+                                              int t, int rpc) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  m.pos = warp_isum(m.pos), m.neg = warp_isum(m.neg);
+  m.bpos = warp_isum(m.bpos), m.bneg = warp_isum(m.bneg);
+  __syncthreads();
+  if (lane == 0) {
+    redi[warp][0] = m.pos, redi[warp][1] = m.neg, redi[warp][2] = m.bpos, redi[warp][3] = m.bneg;
+  }
+  if (t == 0) rrs[sub] = rr_acc;
+  __syncthreads();
+  if (threadIdx.x < 4 && counts != nullptr) {
+    int sum = 0;
+#pragma unroll
+    for (int w = 0; w < CTA / 32; ++w) sum += redi[w][threadIdx.x];
+    if (sum != 0) atomicAdd(counts + threadIdx.x, static_cast<unsigned long long>(sum));
+  }
+  if (threadIdx.x == 32 && rms_sum != nullptr) {
+    float sum = 0.0f;
+    for (int r = 0; r < rpc; ++r) sum = __fadd_rn(sum, rrs[r]);
+    if (sum != 0.0f) atomicAdd(rms_sum, sum);
+  }
+}
+
+template <typename G, int RT, int VPT, int S>
+__global__ void __launch_bounds__(CTA) ratchet_update_staged_kernel(const __grid_constant__ GroupArgs g) {
+  constexpr int RPC = CTA / RT, NT = CTA / RT;
+  constexpr int P = static_cast<int>(sizeof(G)) / 2;  // 16-byte gradient pieces per chunk
+  __shared__ uint32_t lut[kUpdateLut];
+  __shared__ float sm[RT == 32 ? 1 : RPC * CTA];
+  __shared__ float smb[RPC];
+  __shared__ float smx[RPC * 8];
+  __shared__ int redi[CTA / 32][4];
+  __shared__ float rrs[RPC];
+  extern __shared__ uint4 stage[];  // gradient [S][VPT][P][CTA], then packed [S][VPT][CTA] (8 B)
+  uint2 *pstage = reinterpret_cast<uint2 *>(stage + S * VPT * P * CTA);
+  pdl_trigger();
+  build_update_lut(lut, g.common);  // from the launch arguments only: overlaps the previous kernel
+  pdl_wait();
+  const UpdateArgs &a = g.common;
+  const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
+  const int64_t nch = a.cols / 8;
+
+  int lp = 0;  // layer cursor of the copies (blocks only grow)
+  auto issue = [&](int b, int st) {
+    if (b < g.blocks) {
+      while (lp + 1 < g.n && g.L[lp + 1].block0 <= b) ++lp;
+      const GroupLayer &L = g.L[lp];
+      const int64_t grow = static_cast<int64_t>(b - L.block0) * RPC + sub;
+      if (grow < L.rows) {
+        const int64_t srow = a.row_ids != nullptr ? __ldg(a.row_ids + grow) : grow;
+        if (srow >= 0) {
+          const char *gr = static_cast<const char *>(L.grad) + grow * L.ldg * static_cast<int64_t>(sizeof(G));
+          const uint8_t *pr = L.packed + srow * L.ldp;
+#pragma unroll
+          for (int i = 0; i < VPT; ++i) {
+            const int64_t c = t + static_cast<int64_t>(i) * RT;
+            if (c < nch) {
+#pragma unroll
+              for (int p = 0; p < P; ++p)
+                cp_async16(&stage[((st * VPT + i) * P + p) * CTA + threadIdx.x],
+                           gr + c * (8 * static_cast<int64_t>(sizeof(G))) + 16 * p);
+              cp_async8(&pstage[(st * VPT + i) * CTA + threadIdx.x], pr + 8 * c);
+            }
+          }
+        }
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int s = 0; s < S - 1; ++s) issue(static_cast<int>(blockIdx.x + s * gridDim.x), s);
+
+  int l = 0, cur = -1;
+  Moves m = {0, 0, 0, 0};
+  float rr_acc = 0.0f;
+  int st = 0;
+  for (int b = static_cast<int>(blockIdx.x); b < g.blocks; b += static_cast<int>(gridDim.x)) {
+    issue(b + (S - 1) * static_cast<int>(gridDim.x), st == 0 ? S - 1 : st - 1);
+    while (l + 1 < g.n && g.L[l + 1].block0 <= b) ++l;
+    if (l != cur) {  // CTA-uniform
+      if (cur >= 0)
+        publish_layer(m, rr_acc, g.L[cur].counts, g.L[cur].rms_sum, redi, rrs, sub, t, RPC);
+      m = Moves{0, 0, 0, 0}, rr_acc = 0.0f, cur = l;
+    }
+    const GroupLayer &L = g.L[l];
+    const int64_t grow = static_cast<int64_t>(b - L.block0) * RPC + sub;
+    const int64_t srow = grow < L.rows ? (a.row_ids != nullptr ? __ldg(a.row_ids + grow) : grow) : -1;
+    const bool live = srow >= 0;
+    const int64_t row = live ? srow : 0;
+    const float ema_old = (L.rms_ema != nullptr && live) ? L.rms_ema[row] : 0.0f;
+    cp_async_wait<S - 1>();
+
+    float gv[VPT][8];
+    uint2 pk[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      pk[i] = make_uint2(0, 0);
+      if (live && c < nch) {
+        const uint4 *slot = &stage[((st * VPT + i) * P) * CTA + threadIdx.x];
+        if constexpr (sizeof(G) == 2) {
+          const uint4 u = slot[0];
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            gv[i][2 * j] = __uint_as_float(w[j] << 16);
+            gv[i][2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+          }
+        } else {
+          const float4 lo = *reinterpret_cast<const float4 *>(slot);
+          const float4 hi = *reinterpret_cast<const float4 *>(slot + CTA);
+          gv[i][0] = lo.x, gv[i][1] = lo.y, gv[i][2] = lo.z, gv[i][3] = lo.w;
+          gv[i][4] = hi.x, gv[i][5] = hi.y, gv[i][6] = hi.z, gv[i][7] = hi.w;
+          if (a.round_bf16) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) gv[i][j] = bf16_round(gv[i][j]);
+          }
+        }
+        if (L.grad_mul != 1.0f) {
+#pragma unroll
+          for (int j = 0; j < 8; j += 2) {
+            const float2 r = __fmul2_rn(make_float2(gv[i][j], gv[i][j + 1]),
+                                        make_float2(L.grad_mul, L.grad_mul));
+            gv[i][j] = r.x, gv[i][j + 1] = r.y;
+          }
+        }
+        pk[i] = pstage[(st * VPT + i) * CTA + threadIdx.x];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) gv[i][j] = 0.0f;
+      }
+    }
+    st = st == S - 1 ? 0 : st + 1;
+
+    float ss[NT], gsa[NT];
+#pragma unroll
+    for (int k = 0; k < NT; ++k) ss[k] = 0.0f, gsa[k] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const float2 sq = __fmul2_rn(make_float2(gv[i][j], gv[i][j + 1]),
+                                     make_float2(gv[i][j], gv[i][j + 1]));
+        ss[i % NT] = __fadd_rn(ss[i % NT], sq.x);
+        ss[i % NT] = __fadd_rn(ss[i % NT], sq.y);
+      }
+      if (a.grad_scale != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t word = j < 4 ? pk[i].x : pk[i].y;
+          const float code = static_cast<float>(
+              code_of(static_cast<uint8_t>(word >> (8 * (j & 3))), a.max_code));
+          gsa[i % NT] = __fadd_rn(gsa[i % NT], __fmul_rn(gv[i][j], code));
+        }
+      }
+    }
+    const float total = row_sum<RT>(ss, sm, smb, sub, t);
+    const float gsum = a.grad_scale != nullptr ? row_sum<RT>(gsa, sm, smb, sub, t) : 0.0f;
+    bool bad = false;
+    if (__syncthreads_or(live && !isfinite(total))) {  // rare: scan the CTA's rows
+      bool lb = false;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) lb |= !isfinite(gv[i][j]);
+      bad = row_max<RT>(lb ? 1.0f : 0.0f, smx, sub, t) > 0.0f;
+    }
+    const float ms = __fdiv_rn(total, static_cast<float>(a.cols));
+    UpdateArgs la = a;
+    la.rms_ema = L.rms_ema;
+    const float denom = row_denominator(la, row, ms, ema_old, bad, live && t == 0);
+    float tlo, thi;
+    const bool fast = bucket_thresholds(denom, a.low, a.high, a.normalize, tlo, thi);
+    const float rcp = fast ? 0.0f : __frcp_rn(denom);
+    if (live && t == 0) {
+      const float rr = __fsqrt_rn(ms);
+      if (a.row_rms != nullptr) a.row_rms[row] = rr;
+      rr_acc = __fadd_rn(rr_acc, rr);
+      if (a.grad_scale != nullptr) a.grad_scale[row] = gsum;
+      if (bad) raise_status(RT_STATUS_NONFINITE_GRADIENT);
+    }
+
+    // (fast and bad are uniform over the row's warps: each variant is a loop of its own)
+    if (!bad && fast) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t c = t + static_cast<int64_t>(i) * RT;
+        if (!live || c >= nch) continue;
+        uint32_t e[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t word = j < 4 ? pk[i].x : pk[i].y;
+          const uint32_t old = __byte_perm(word, 0u, 0x4440 + (j & 3));
+          const float ax = fabsf(gv[i][j]);
+          uint32_t idx = (old << 3) | (__float_as_uint(gv[i][j]) >> 31);
+          idx += ax >= tlo ? 2u : 0u;
+          idx += ax >= thi ? 2u : 0u;
+          e[j] = lut[idx];
+        }
+        store_update_chunk(L, row, c, e, m);
+      }
+    } else if (!bad) {
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t c = t + static_cast<int64_t>(i) * RT;
+        if (!live || c >= nch) continue;
+        uint32_t e[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t word = j < 4 ? pk[i].x : pk[i].y;
+          const uint32_t old = __byte_perm(word, 0u, 0x4440 + (j & 3));
+          e[j] = lut[lut_index(old, gv[i][j], denom, rcp, a.normalize, a.low, a.high)];
+        }
+        store_update_chunk(L, row, c, e, m);
+      }
+    }
+    if (bad && L.code_out != nullptr) {  // the row stays; its code mirror is still written
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t c = t + static_cast<int64_t>(i) * RT;
+        if (!live || c >= nch) continue;
+        uint32_t cw[2] = {0, 0};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint32_t word = j < 4 ? pk[i].x : pk[i].y;
+          cw[j >> 2] |= static_cast<uint32_t>(static_cast<uint8_t>(
+                            code_of(static_cast<uint8_t>(word >> (8 * (j & 3))), a.max_code)))
+                        << (8 * (j & 3));
+        }
+        *reinterpret_cast<uint2 *>(L.code_out + row * L.ldc + 8 * c) = make_uint2(cw[0], cw[1]);
+      }
+    }
+  }
+  if (cur >= 0) publish_layer(m, rr_acc, g.L[cur].counts, g.L[cur].rms_sum, redi, rrs, sub, t, RPC);
+  cp_async_wait<0>();
+}
+
+template <typename G, int RT, int VPT>
+static void launch_update_staged(const GroupArgs &g, cudaStream_t s) {
+  constexpr int P = static_cast<int>(sizeof(G)) / 2;
+  constexpr int STAGE = VPT * (16 * P + 8) * CTA;  // one block's gradient and packed chunks
+  constexpr int S = 49152 / STAGE < 2 ? 2 : (49152 / STAGE > 4 ? 4 : 49152 / STAGE);
+  constexpr size_t smem = static_cast<size_t>(S) * STAGE;
+  const unsigned resident = staged_resident<ratchet_update_staged_kernel<G, RT, VPT, S>>(smem);
+  const unsigned blocks = static_cast<unsigned>(g.blocks);
+  launch_k(ratchet_update_staged_kernel<G, RT, VPT, S>, blocks < resident ? blocks : resident, CTA,
+           smem, s, g);
+}
+template <typename G>
+static bool update_staged(const GroupArgs &g, const RowCfg &cfg, cudaStream_t s) {
+  switch (cfg.rt * 16 + cfg.vpt) {
+    case 32 * 16 + 1: launch_update_staged<G, 32, 1>(g, s); return true;
+    case 32 * 16 + 2: launch_update_staged<G, 32, 2>(g, s); return true;
+    case 32 * 16 + 4: launch_update_staged<G, 32, 4>(g, s); return true;
+    case 128 * 16 + 1: launch_update_staged<G, 128, 1>(g, s); return true;
+    case 128 * 16 + 2: launch_update_staged<G, 128, 2>(g, s); return true;
+    case 128 * 16 + 4: launch_update_staged<G, 128, 4>(g, s); return true;
+    case 256 * 16 + 1: launch_update_staged<G, 256, 1>(g, s); return true;
+    case 256 * 16 + 2: launch_update_staged<G, 256, 2>(g, s); return true;
+    case 256 * 16 + 4: launch_update_staged<G, 256, 4>(g, s); return true;
+    case 256 * 16 + 8: launch_update_staged<G, 256, 8>(g, s); return true;
+    default: return false;
   }
 }
 
@@ -1976,6 +2570,18 @@ static int ratchet_update_launch(const UpdateArgs &a, cudaStream_t s) {
     if (cfg.rt == 0)
       return fail(RT_ERR_UNSUPPORTED, "rt_grad_weight_ratchet_update: rows need 8-element chunks");
     RT_DISPATCH_ROW(cfg, ratchet_update_ws_kernel, float, update_grid(row_grid(rows, cfg.rt), cfg.vpt), a);
+  } else if (cfg.rt != 0 && staged_enabled()) {
+    GroupArgs g;
+    g.common = a;
+    g.n = 1;
+    g.blocks = static_cast<int>(row_grid(rows, cfg.rt));
+    GroupLayer &d = g.L[0];
+    d.grad = a.grad, d.ldg = a.ldg, d.rows = rows, d.packed = a.packed, d.ldp = a.ldp;
+    d.code_out = a.code_out, d.ldc = a.ldc, d.rms_ema = a.rms_ema, d.counts = a.counts;
+    d.rms_sum = a.rms_sum, d.grad_mul = a.grad_mul, d.block0 = 0;
+    const bool ok = a.grad_dtype == RT_F32 ? update_staged<float>(g, cfg, s)
+                                           : update_staged<__nv_bfloat16>(g, cfg, s);
+    if (!ok) return fail(RT_ERR_UNSUPPORTED, "rt_ratchet_update: row configuration");
   } else if (cfg.rt != 0) {
     const unsigned grid = update_grid(row_grid(rows, cfg.rt), cfg.vpt);
     if (a.grad_dtype == RT_F32)
@@ -2080,6 +2686,13 @@ extern "C" int rt_ratchet_update_grouped(const rt_update_layer *layers, int n_la
     }
     g.blocks = blocks;
     if (g.n == 0) continue;
+    if (staged_enabled()) {
+      const bool ok = grad_dtype == RT_F32 ? update_staged<float>(g, cfg, s)
+                                           : update_staged<__nv_bfloat16>(g, cfg, s);
+      if (!ok) return fail(RT_ERR_UNSUPPORTED, "rt_ratchet_update_grouped: row configuration");
+      if (int rc = check_launch("rt_ratchet_update_grouped")) return rc;
+      continue;
+    }
     const unsigned grid = update_grid(static_cast<unsigned>(blocks), cfg.vpt);
     if (grad_dtype == RT_F32)
       RT_DISPATCH_ROW(cfg, ratchet_update_grouped_kernel, float, grid, g);
