@@ -292,7 +292,8 @@ def measure(args, wl: dict, rank: int, local_rank: int, world: int, *, steps: in
     config = ModelConfig(vocab_size=wl["vocab"], block_size=wl["block"], n_layer=wl["n_layer"],
                          n_head=wl["n_head"], n_embd=wl["n_embd"], dropout=0.0,
                          matmul_mode="int8", int8_backward=True,
-                         fused_grad_quant=args.fused_grad_quant)
+                         fused_grad_quant=args.fused_grad_quant,
+                         logits_chunk_rows=args.logits_chunk_rows)
     model = build_seeded_model(config, max_code=wl["max_code"], seed=wl["seed"]).to(device).train()
     for layer in model.ratchet_layers():
         layer.sr_seed = wl["seed"] + 7
@@ -568,7 +569,8 @@ def run_ours(args, wl: dict, rank: int, local_rank: int, world: int) -> None:
                    "micro_batch": res["micro_batch"], "micro_batches_per_rank": res["micro_batches"],
                    "codes": 2 * wl["max_code"] + 1, "matmul_mode": "int8", "int8_backward": True,
                    "parallelism": f"dp{world}" if world > 1 else "single",
-                   "l2": "inputs larger than L2: working set (activations, logits) of many GB"},
+                   "logits_chunk_rows": args.logits_chunk_rows,
+                   "l2": "inputs larger than L2: working set (activations, weights) of many GB"},
         "e2e": {"value": tokens * args.steps / res["e_elapsed"], "unit": "tokens/s",
                 "h2d_bytes_per_step": res["h2d"], "d2h_bytes_per_step": 4},
         "roofline": rep["roofline"],
@@ -618,6 +620,9 @@ def main() -> None:
     parser.add_argument("--fused-grad-quant", action="store_true",
                         help="ModelConfig(fused_grad_quant=True): the producer backwards also "
                              "stochastic-round the layer gradients (same results)")
+    parser.add_argument("--logits-chunk-rows", type=int, default=8192,
+                        help="ModelConfig(logits_chunk_rows): the lm_head + loss over blocks of this "
+                             "many tokens, no [tokens, vocab] tensor stored (0: materialised)")
     parser.add_argument("--no-graph", action="store_true", help="time eager steps (no CUDA graph)")
     parser.add_argument("--dp-bucket-layers", type=int, default=4,
                         help="N>1: layers whose grad_W reduce-scatters are batched into one group")

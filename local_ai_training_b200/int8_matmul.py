@@ -214,9 +214,11 @@ def grad_weight_bf16(grad: Tensor, inputs: Tensor, out: Tensor | None = None, *,
     return out
 
 
-def matmul_bf16(a: Tensor, b: Tensor, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+def matmul_bf16(a: Tensor, b: Tensor, out_dtype: torch.dtype = torch.bfloat16, *,
+                out: Tensor | None = None) -> Tensor:
     """a[M, K] @ b[K, N] with bf16 operands and fp32 accumulation on the tcgen05 GEMM (the bf16
-    grad_input matmul of ratchet.py:135-141); output bf16 (RN) or float32."""
+    grad_input matmul of ratchet.py:135-141); output bf16 (RN) or float32, into `out` (a row-major
+    [M, N] view, e.g. a row slice of a larger matrix) when given."""
     if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
         raise TypeError("matmul_bf16 operands must be bfloat16")
     if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0]:
@@ -230,7 +232,12 @@ def matmul_bf16(a: Tensor, b: Tensor, out_dtype: torch.dtype = torch.bfloat16) -
         b = b.contiguous()
     m, k = a.shape
     n = b.shape[1]
-    out = torch.empty((m, n), device=a.device, dtype=out_dtype)
+    if out is None:
+        out = torch.empty((m, n), device=a.device, dtype=out_dtype)
+    elif (out.shape != (m, n) or out.dtype not in (torch.bfloat16, torch.float32)
+          or out.stride(1) != 1 or out.device != a.device):
+        raise ValueError("matmul_bf16 out must be a [M, N] bf16 or float32 view with unit column "
+                         "stride on the operands' device")
     if out.numel() == 0:
         return out
     ev = _lib.prof_start(a)

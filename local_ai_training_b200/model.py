@@ -51,6 +51,10 @@ class ModelConfig:
     # int8 mode with targets: the self-quantising lm_head GEMM and the token cross-entropy run as
     # one autograd step (local_ai_training_b200.cross_entropy); False keeps F.cross_entropy
     fused_cross_entropy: bool = True
+    # with the fused cross-entropy: > 0 runs the lm_head and the loss over blocks of this many
+    # tokens, recomputing each block's logits in backward, and forward returns (None, loss) -- no
+    # [tokens, vocab] logits or logit gradient is stored; 0 returns the logits as the reference does
+    logits_chunk_rows: int = 0
     # int8 mode: the residual adds of each block run in the epilogue of the sublayer's last GEMM
     # and in the RMSNorm backward kernel (TransformerBlock.forward); False keeps `x + f(x)`
     fused_residual: bool = True
@@ -303,7 +307,8 @@ class RatchetGPT(nn.Module):
             from .cross_entropy import fused_lm_head_applies, lm_head_cross_entropy
 
             if fused_lm_head_applies(self.lm_head, normed):
-                return lm_head_cross_entropy(self.lm_head, normed, targets)
+                return lm_head_cross_entropy(self.lm_head, normed, targets,
+                                             chunk_rows=self.config.logits_chunk_rows)
         logits = self.lm_head(normed)
         loss = None
         if targets is not None:

@@ -228,8 +228,16 @@ def _deliver_weight_gradient(gradient_sink, mode: str, fuse_backward_update: boo
                 return grad_scale
         grad_weight = grad_weight_bf16(grad_bf16, inputs_bf16)
         round_bf16 = True
+    return _sink_weight_gradient(gradient_sink, fuse_backward_update, grad_weight, round_bf16,
+                                 code, want_scale)
+
+
+def _sink_weight_gradient(gradient_sink, fuse_backward_update: bool, grad_weight: Tensor,
+                          round_bf16: bool, code: Tensor, want_scale: bool) -> Tensor | None:
+    """A whole [out, in] grad_W (fp32; rounded to bf16 first when round_bf16, as the reference's
+    bf16 GEMM output is) to the fused update or the pending gradient."""
     if fuse_backward_update:
-        return gradient_sink(grad_weight, 0, out_features, round_bf16=round_bf16,
+        return gradient_sink(grad_weight, 0, code.shape[0], round_bf16=round_bf16,
                              want_grad_scale=want_scale)
     if round_bf16:
         grad_weight = grad_weight.to(torch.bfloat16).float()

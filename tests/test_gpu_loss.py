@@ -122,3 +122,79 @@ def test_fused_lm_head_cross_entropy_step_matches_unfused(cuda_device, int8_back
                     for a, b in zip(pf, pp))
     assert mism <= total // 200, (mism, total)
     assert code_mism <= total // 2000, (code_mism, total)
+
+
+def _chunk_model(cuda_device, chunk_rows, vocab=512, block=64, n_embd=64, n_layer=2):
+    from local_ai_training_b200 import ModelConfig, build_seeded_model
+
+    cfg = ModelConfig(vocab_size=vocab, block_size=block, n_layer=n_layer, n_head=2,
+                      n_embd=n_embd, dropout=0.0, pressure_threshold=2, matmul_mode="int8",
+                      int8_backward=True, logits_chunk_rows=chunk_rows)
+    model = build_seeded_model(cfg, max_code=2, seed=3).to(cuda_device).train()
+    for layer in model.ratchet_layers():
+        layer.sr_seed = 5
+    return model
+
+
+@pytest.mark.parametrize("accumulation", [0, 1, 2])
+def test_chunked_lm_head_matches_materialised_step(cuda_device, accumulation):
+    """logits_chunk_rows (ragged last block) against the materialised fused path from the same
+    state: the same loss bit for bit, embedding gradients to bf16 rounding, ratchet states equal
+    up to the fp32 order of the lm_head grad_W sum (boundary weights only); with the deferred
+    data-parallel update at one rank, with and without gradient accumulation."""
+    from local_ai_training_b200.dist import RatchetDataParallel
+    from local_ai_training_b200.ratchet import unpack_code_pressure
+
+    tokens = torch.randint(0, 512, (8, 65), generator=torch.Generator().manual_seed(8))
+    tokens = tokens.to(cuda_device)
+
+    def run(chunk):
+        model = _chunk_model(cuda_device, chunk)
+        ddp = RatchetDataParallel(model, accumulation_steps=accumulation) if accumulation else None
+        parts = tokens.chunk(accumulation) if accumulation else [tokens]
+        losses = []
+        for part in parts:
+            logits, loss = model(part[:, :-1], part[:, 1:])
+            assert (logits is None) == (chunk > 0)
+            loss.backward()
+            losses.append(float(loss))
+        if ddp is not None:
+            ddp.synchronize_gradients()
+        emb_grad = model.token_embedding.weight.grad.clone()
+        if ddp is not None:
+            ddp.ratchet_update()
+        else:
+            model.ratchet_update(validate=False)
+        return losses, emb_grad, [l.packed.clone() for l in model.ratchet_layers()]
+
+    xc, gc, pc = run(96)
+    xm, gm, pm = run(0)
+    assert xc == xm
+    assert torch.allclose(gc, gm, rtol=1e-2, atol=1e-6)
+    total = sum(a.numel() for a in pc)
+    mism = sum(int((a != b).sum()) for a, b in zip(pc, pm))
+    code_mism = sum(int((unpack_code_pressure(a, 2)[0] != unpack_code_pressure(b, 2)[0]).sum())
+                    for a, b in zip(pc, pm))
+    assert mism <= total // 500, (mism, total)
+    assert code_mism <= total // 5000, (code_mism, total)
+
+
+def test_chunked_lm_head_stores_no_token_by_vocab_tensor(cuda_device):
+    """16384 tokens x 8192 classes: with logits_chunk_rows = 2048 the step's peak allocation stays
+    below one bf16 [16384, 8192] tensor (268 MB); materialised, it exceeds the fp32 logits."""
+    tokens = torch.randint(0, 8192, (16, 1025), generator=torch.Generator().manual_seed(2))
+    tokens = tokens.to(cuda_device)
+    full_bf16 = 16384 * 8192 * 2
+    peaks = {}
+    for chunk in (2048, 0):
+        model = _chunk_model(cuda_device, chunk, vocab=8192, block=1024, n_layer=1)
+        torch.cuda.synchronize()
+        torch.cuda.reset_peak_memory_stats()
+        base = torch.cuda.memory_allocated()
+        logits, loss = model(tokens[:, :-1], tokens[:, 1:])
+        loss.backward()
+        torch.cuda.synchronize()
+        peaks[chunk] = torch.cuda.max_memory_allocated() - base
+        del model, logits, loss
+    assert peaks[2048] < full_bf16, peaks
+    assert peaks[0] > 2 * full_bf16, peaks
