@@ -476,73 +476,9 @@ __global__ void __launch_bounds__(CTA) quant_rows_generic_kernel(QuantArgs a) {
   sr_step_arrive(a, step);
 }
 
-// ---- pieces of the stochastic-rounding row quantisation shared by the fused gradient producers
-// (a producer that already holds a layer's output-gradient row in registers quantises it for
-// the layer's int8 grad_input GEMM in the same pass, with the arithmetic of quant_rows_kernel).
-template <int RT, int VPT>
-__device__ __forceinline__ void sr_load_col_scales(const QuantArgs &a, int t, int64_t nch,
-                                                   float (&cs)[VPT][8]) {
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int64_t c = t + static_cast<int64_t>(i) * RT;
-    if (a.col_scale != nullptr && c < nch) {
-      ld8(a.col_scale + 8 * c, cs[i]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) cs[i][j] = 1.0f;
-    }
-  }
-}
-// One chunk of the gradient as the layer receives it -> the value the quantiser rounds: the
-// optional bf16 rounding, the bf16 copy (grad_weight operand), the column scale; amax updated.
-__device__ __forceinline__ void sr_prepare_chunk(const QuantArgs &a, int64_t row, int64_t c,
-                                                 float (&v)[8], const float (&cs)[8],
-                                                 float &amax) {
-  if (a.round_bf16) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = bf16_round(v[j]);
-  }
-  if (a.xbf16 != nullptr)
-    st8(reinterpret_cast<__nv_bfloat16 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c), v);
-  if (a.col_scale != nullptr) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(v[j], cs[j]);
-  }
-#pragma unroll
-  for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
-}
-// Row scale and int8 row from the prepared values (amax already reduced over the row).
-template <int RT, int VPT>
-__device__ __forceinline__ void sr_quant_store_row(const QuantArgs &a, uint32_t step, int64_t row,
-                                                   int t, int64_t nch, const float (&v)[VPT][8],
-                                                   float amax) {
-  const float scale = row_scale_of(amax);
-  const float rcp = __frcp_rn(scale);
-  if (t == 0) a.row_scale[row] = scale;
-  int8_t *qr = a.q + row * a.ldq;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int64_t c = t + static_cast<int64_t>(i) * RT;
-    if (c >= nch) continue;
-    const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;
-    const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
-    uint2 o;
-    o.x = pack4_i8(quant_sr_i(v[i][0], scale, rcp, sr_um_lo(p.x)),
-                   quant_sr_i(v[i][1], scale, rcp, sr_um_hi(p.x)),
-                   quant_sr_i(v[i][2], scale, rcp, sr_um_lo(p.y)),
-                   quant_sr_i(v[i][3], scale, rcp, sr_um_hi(p.y)));
-    o.y = pack4_i8(quant_sr_i(v[i][4], scale, rcp, sr_um_lo(p.z)),
-                   quant_sr_i(v[i][5], scale, rcp, sr_um_hi(p.z)),
-                   quant_sr_i(v[i][6], scale, rcp, sr_um_lo(p.w)),
-                   quant_sr_i(v[i][7], scale, rcp, sr_um_hi(p.w)));
-    *reinterpret_cast<uint2 *>(qr + 8 * c) = o;
-  }
-}
-// ---- Staged stochastic-rounding quantiser: the layer gradients of the int8 backward.
-// Same results as quant_rows_kernel (floor(RN(RN(v / scale) + u)), clamped), from two changes:
-//  * every thread copies its chunks of the row groups S-1 iterations ahead into its own slots of
-//    shared memory with cp.async, so HBM reads stay in flight while the current rows compute;
-//  * the rounding decision is made in fixed point.  With R = RN(1/scale)·2^15 (exact scaling),
+// ---- Fixed-point stochastic rounding (the staged quantiser and the fused producer backwards).
+// Same results as quant_sr_i (floor(RN(RN(v / scale) + u)), clamped), with the rounding decision
+// made in fixed point.  With R = RN(1/scale)·2^15 (exact scaling),
 //    t = fma(v, R, 1.5·2^23 + 2) rounds v·R + 2 to an integer T + 2 (|v·R| < 2^22 keeps t in
 //    [2^23, 2^24), where consecutive integers have consecutive bit patterns).  For the element's
 //    16-bit draw h (u = (h + 1/2)·2^-16),  W = 2·bits(t) + h + 2^23  equals
@@ -585,6 +521,99 @@ __device__ __forceinline__ int sr_exact(float v, float scale, uint32_t hbits) {
   return min(max(__float2int_rd(t), -127), 127);
 }
 
+// ---- pieces of the stochastic-rounding row quantisation shared by the fused gradient producers
+// (a producer that already holds a layer's output-gradient row in registers quantises it for
+// the layer's int8 grad_input GEMM in the same pass, with the arithmetic of quant_rows_kernel).
+template <int RT, int VPT>
+__device__ __forceinline__ void sr_load_col_scales(const QuantArgs &a, int t, int64_t nch,
+                                                   float (&cs)[VPT][8]) {
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (a.col_scale != nullptr && c < nch) {
+      ld8(a.col_scale + 8 * c, cs[i]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cs[i][j] = 1.0f;
+    }
+  }
+}
+// One chunk of the gradient as the layer receives it -> the value the quantiser rounds: the
+// optional bf16 rounding, the bf16 copy (grad_weight operand), the column scale; amax updated.
+__device__ __forceinline__ void sr_prepare_chunk(const QuantArgs &a, int64_t row, int64_t c,
+                                                 float (&v)[8], const float (&cs)[8],
+                                                 float &amax) {
+  if (a.round_bf16) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = bf16_round(v[j]);
+  }
+  if (a.xbf16 != nullptr)
+    st8(reinterpret_cast<__nv_bfloat16 *>(a.xbf16 + row * a.ld_xbf16 + 8 * c), v);
+  if (a.col_scale != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(v[j], cs[j]);
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+}
+// The int8 row of prepared values with the row's scale already known: fixed-point decisions, then
+// a warp-uniform pass that redraws the flagged chunks and overwrites them with the exact result
+// (whole warps call it: RT >= 32 keeps each row's threads in whole warps).
+template <int RT, int VPT>
+__device__ __forceinline__ void sr_fixed_store_row(const QuantArgs &a, uint32_t step, int64_t row,
+                                                   int t, int64_t nch, const float (&v)[VPT][8],
+                                                   float amax, float scale, float rcp, bool live) {
+  const bool row_exact = amax != 0.0f && rcp > 0x1p100f;
+  const float r15 = (amax == 0.0f || row_exact) ? 0.0f : __fmul_rn(rcp, 32768.0f);
+  int8_t *qr = a.q + (live ? row : 0) * a.ldq;
+  uint32_t redo = 0;  // this thread's chunks whose bytes the exact path re-does
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int64_t c = t + static_cast<int64_t>(i) * RT;
+    if (!live || c >= nch) continue;
+    const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;  // multiple of 8
+    const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
+    const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+    uint32_t w[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      w[j] = __float_as_uint(__fmaf_rn(v[i][j], r15, kSrFixedMagic)) * 2u +
+             ((j & 1) ? sr_h_hi(pw[j >> 1]) : sr_h_lo(pw[j >> 1]));
+    if (row_exact || sr_fixed_ambiguous(w)) redo |= 1u << i;
+    *reinterpret_cast<uint2 *>(qr + 8 * c) = sr_fixed_pack(w);
+  }
+  // rare (a few elements in 10^4, or a row of tiny maximum)
+  if (__any_sync(0xffffffffu, redo != 0)) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      if (((redo >> i) & 1u) == 0) continue;
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;
+      const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
+      const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
+      int q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        q[j] = sr_exact(v[i][j], scale, (j & 1) ? sr_h_hi(pw[j >> 1]) : sr_h_lo(pw[j >> 1]));
+      *reinterpret_cast<uint2 *>(qr + 8 * c) =
+          make_uint2(pack4_i8(q[0], q[1], q[2], q[3]), pack4_i8(q[4], q[5], q[6], q[7]));
+    }
+  }
+}
+// Row scale and int8 row from the prepared values (amax already reduced over the row).
+template <int RT, int VPT>
+__device__ __forceinline__ void sr_quant_store_row(const QuantArgs &a, uint32_t step, int64_t row,
+                                                   int t, int64_t nch, const float (&v)[VPT][8],
+                                                   float amax) {
+  const float scale = row_scale_of(amax);
+  const float rcp = __frcp_rn(scale);
+  if (t == 0) a.row_scale[row] = scale;
+  sr_fixed_store_row<RT, VPT>(a, step, row, t, nch, v, amax, scale, rcp, true);
+}
+// ---- Staged stochastic-rounding quantiser: the layer gradients of the int8 backward.
+// Every thread copies its chunks of the row groups S-1 iterations ahead into its own slots of
+// shared memory with cp.async, so HBM reads stay in flight while the current rows compute; the
+// rounding is sr_fixed_store_row's.
 template <typename T, int RT, int VPT, int S>
 __global__ void __launch_bounds__(CTA) quant_sr_staged_kernel(QuantArgs a) {
   constexpr int RPC = CTA / RT;
@@ -696,43 +725,7 @@ __global__ void __launch_bounds__(CTA) quant_sr_staged_kernel(QuantArgs a) {
     const float scale = row_scale_of(amax);
     const float rcp = __frcp_rn(scale);
     if (live && t == 0) a.row_scale[row] = scale;
-    const bool row_exact = amax != 0.0f && rcp > 0x1p100f;
-    const float r15 = (amax == 0.0f || row_exact) ? 0.0f : __fmul_rn(rcp, 32768.0f);
-    int8_t *qr = a.q + (live ? row : 0) * a.ldq;
-    uint32_t redo = 0;  // this thread's chunks whose bytes the exact path re-does
-#pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int64_t c = t + static_cast<int64_t>(i) * RT;
-      if (!live || c >= nch) continue;
-      const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;  // multiple of 8
-      const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
-      const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
-      uint32_t w[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        w[j] = __float_as_uint(__fmaf_rn(v[i][j], r15, kSrFixedMagic)) * 2u +
-               ((j & 1) ? sr_h_hi(pw[j >> 1]) : sr_h_lo(pw[j >> 1]));
-      if (row_exact || sr_fixed_ambiguous(w)) redo |= 1u << i;
-      *reinterpret_cast<uint2 *>(qr + 8 * c) = sr_fixed_pack(w);
-    }
-    // rare (a few elements in 10^4, or a row of tiny maximum): a warp-uniform pass that draws
-    // the flagged chunks again and overwrites their bytes with the exact result
-    if (__any_sync(0xffffffffu, redo != 0)) {
-#pragma unroll
-      for (int i = 0; i < VPT; ++i) {
-        if (((redo >> i) & 1u) == 0) continue;
-        const int64_t c = t + static_cast<int64_t>(i) * RT;
-        const uint64_t e0 = static_cast<uint64_t>(row) * a.cols + 8 * c;
-        const Philox4 p = sr_block(a.seed, step, a.layer, e0 >> 3);
-        const uint32_t pw[4] = {p.x, p.y, p.z, p.w};
-        int q[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          q[j] = sr_exact(v[i][j], scale, (j & 1) ? sr_h_hi(pw[j >> 1]) : sr_h_lo(pw[j >> 1]));
-        *reinterpret_cast<uint2 *>(qr + 8 * c) =
-            make_uint2(pack4_i8(q[0], q[1], q[2], q[3]), pack4_i8(q[4], q[5], q[6], q[7]));
-      }
-    }
+    sr_fixed_store_row<RT, VPT>(a, step, row, t, nch, v, amax, scale, rcp, live);
     st = st == S - 1 ? 0 : st + 1;
   }
   cp_async_wait<0>();
