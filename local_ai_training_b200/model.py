@@ -352,18 +352,15 @@ class RatchetGPT(nn.Module):
                 total_weights=total_weights, positive_moves=counts[0], negative_moves=counts[1],
                 blocked_positive_moves=counts[2], blocked_negative_moves=counts[3],
                 gradient_rms_mean=(rms / self._out_features_dev).mean())
-        updates = [module.ratchet_update(validate=validate) for module in layers]
-        total_weights = sum(update.total_weights for update in updates)
-        aggregated = RatchetUpdateStats(
-            total_weights=total_weights,
-            positive_moves=sum(update.positive_moves for update in updates),
-            negative_moves=sum(update.negative_moves for update in updates),
-            blocked_positive_moves=sum(update.blocked_positive_moves for update in updates),
-            blocked_negative_moves=sum(update.blocked_negative_moves for update in updates),
-            gradient_rms_mean=(sum(update.gradient_rms_mean for update in updates) / len(updates)
-                               if updates else 0.0),
-        )
-        return aggregated.materialize() if validate else aggregated
+        per_layer = [module.ratchet_update(validate=validate) for module in layers]
+        # counters add over layers; the rms statistic is the mean of the layers' means
+        fields = ("total_weights", "positive_moves", "negative_moves", "blocked_positive_moves",
+                  "blocked_negative_moves")
+        totals = {name: sum(getattr(stats, name) for stats in per_layer) for name in fields}
+        rms = [stats.gradient_rms_mean for stats in per_layer]
+        combined = RatchetUpdateStats(**totals,
+                                      gradient_rms_mean=sum(rms) / len(rms) if rms else 0.0)
+        return combined.materialize() if validate else combined
 
     def discard_pending_gradients(self) -> None:
         for module in self.ratchet_layers():
@@ -371,7 +368,9 @@ class RatchetGPT(nn.Module):
 
 
 def build_seeded_model(config: ModelConfig, *, max_code: int | None, seed: int) -> RatchetGPT:
-    """Build matched arms without changing the caller's global CPU RNG state."""
+    """RatchetGPT(config, max_code) initialised from torch.manual_seed(seed) inside a forked CPU
+    RNG, so two calls with one seed give identical models and the caller's generator state is
+    unchanged (the reference's seeded-arm helper, model.py:281-285)."""
     with torch.random.fork_rng(devices=[]):
         torch.manual_seed(seed)
         return RatchetGPT(config, max_code=max_code)
