@@ -198,3 +198,27 @@ def test_chunked_lm_head_stores_no_token_by_vocab_tensor(cuda_device):
         del model, logits, loss
     assert peaks[2048] < full_bf16, peaks
     assert peaks[0] > 2 * full_bf16, peaks
+
+
+def test_chunked_lm_head_ignored_targets_match_materialised(cuda_device):
+    """lm_head_cross_entropy over row blocks (ragged last block, ignore_index rows in several
+    blocks) against the materialised call: the same loss bit for bit, the same grad_input."""
+    from local_ai_training_b200 import DiscreteRatchetLinear
+    from local_ai_training_b200.cross_entropy import IGNORE_INDEX, lm_head_cross_entropy
+
+    torch.manual_seed(21)
+    layer = DiscreteRatchetLinear(256, 1000, matmul_mode="int8", int8_backward=True,
+                                  max_code=2).to(cuda_device)
+    x = torch.randn(700, 256, device=cuda_device)
+    targets = torch.randint(0, 1000, (700,), device=cuda_device)
+    targets[::7] = IGNORE_INDEX
+    out = {}
+    for chunk in (0, 192):
+        xi = x.clone().requires_grad_(True)
+        logits, loss = lm_head_cross_entropy(layer, xi, targets, chunk_rows=chunk)
+        assert (logits is None) == (chunk > 0)
+        loss.backward()
+        layer.discard_pending_gradient()
+        out[chunk] = (loss.detach(), xi.grad.clone())
+    assert torch.equal(out[0][0], out[192][0])
+    torch.testing.assert_close(out[192][1], out[0][1], rtol=0, atol=0)
