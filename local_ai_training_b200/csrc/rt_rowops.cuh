@@ -1825,6 +1825,98 @@ __global__ void __launch_bounds__(CTA) gelu_quant_kernel(ProdArgs a) {
   }
 }
 
+// The same producer over a persistent grid: every thread copies its chunks of the row groups S-1
+// iterations ahead into its own shared-memory slots (cp.async), so the tanh-bound arithmetic of
+// one row runs while the next rows' reads are in flight.  Per element the arithmetic is
+// gelu_quant_kernel's (gelu_tanh, quant_rn_store8): identical results.
+template <typename T, int RT, int VPT, int S>
+__global__ void __launch_bounds__(CTA) gelu_quant_staged_kernel(ProdArgs a) {
+  constexpr int RPC = CTA / RT;
+  constexpr int P = static_cast<int>(sizeof(T)) / 2;  // 16-byte pieces per chunk
+  extern __shared__ uint4 stage[];                     // [S][VPT][P][CTA] own slots
+  __shared__ float smx[RPC * 8];
+  pdl_wait();
+  pdl_trigger();
+  const int sub = threadIdx.x / RT, t = threadIdx.x % RT;
+  const int64_t nch = a.cols / 8;
+  const int64_t groups = (a.rows + RPC - 1) / RPC;
+  const int64_t row_bytes = a.ldx * static_cast<int64_t>(sizeof(T));
+  auto issue = [&](int64_t grp, int st) {
+    const int64_t row = grp * RPC + sub;
+    if (grp < groups && row < a.rows) {
+      const char *xr = static_cast<const char *>(a.x) + row * row_bytes;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t c = t + static_cast<int64_t>(i) * RT;
+        if (c < nch) {
+#pragma unroll
+          for (int p = 0; p < P; ++p)
+            cp_async16(&stage[((st * VPT + i) * P + p) * CTA + threadIdx.x],
+                       xr + c * (8 * static_cast<int64_t>(sizeof(T))) + 16 * p);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int s2 = 0; s2 < S - 1; ++s2) issue(blockIdx.x + static_cast<int64_t>(s2) * gridDim.x, s2);
+  int st = 0;
+  for (int64_t grp = blockIdx.x; grp < groups; grp += gridDim.x) {
+    issue(grp + static_cast<int64_t>(S - 1) * gridDim.x, st == 0 ? S - 1 : st - 1);
+    cp_async_wait<S - 1>();
+    const int64_t row = grp * RPC + sub;
+    const bool live = row < a.rows;
+    float v[VPT][8];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int64_t c = t + static_cast<int64_t>(i) * RT;
+      if (live && c < nch) {
+        const uint4 *slot = &stage[((st * VPT + i) * P) * CTA + threadIdx.x];
+        if constexpr (sizeof(T) == 2) {
+          const uint4 u = slot[0];
+          const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            v[i][2 * j] = __uint_as_float(w[j] << 16);
+            v[i][2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+          }
+        } else {
+          const float4 lo = *reinterpret_cast<const float4 *>(slot);
+          const float4 hi = *reinterpret_cast<const float4 *>(slot + CTA);
+          v[i][0] = lo.x, v[i][1] = lo.y, v[i][2] = lo.z, v[i][3] = lo.w;
+          v[i][4] = hi.x, v[i][5] = hi.y, v[i][6] = hi.z, v[i][7] = hi.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[i][j] = gelu_tanh(v[i][j]);
+          amax = fmaxf(amax, fabsf(v[i][j]));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+      }
+    }
+    amax = row_max<RT>(amax, smx, sub, t);  // CTA-uniform trip count: its barriers are safe
+    if (live) {
+      const float scale = row_scale_of(amax);
+      const float rcp = __frcp_rn(scale);
+      const float sb = bf16_round(scale);
+      if (t == 0) a.row_scale[row] = scale;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int64_t c = t + static_cast<int64_t>(i) * RT;
+        if (c >= nch) continue;
+        quant_rn_store8(a.q + row * a.ldq + 8 * c,
+                        a.xdq == nullptr ? nullptr : a.xdq + row * a.ld_dq + 8 * c, v[i], scale,
+                        rcp, sb);
+      }
+    }
+    st = st == S - 1 ? 0 : st + 1;
+  }
+  cp_async_wait<0>();
+}
+
 // Generic producers: one CTA per row, the row re-read from L2 between passes.
 __global__ void __launch_bounds__(CTA)
     rmsnorm_quant_generic_kernel(ProdArgs a, int dtype) {
@@ -2757,6 +2849,35 @@ extern "C" int rt_rmsnorm_quantize(const void *x, int x_dtype, int64_t ldx, cons
   return check_launch("rt_rmsnorm_quantize");
 }
 
+template <typename T, int RT, int VPT>
+static void launch_gelu_quant_staged(const ProdArgs &a, cudaStream_t s) {
+  constexpr int P = static_cast<int>(sizeof(T)) / 2;
+  constexpr int S = VPT * P <= 2 ? 6 : 3;  // 24-48 KB of stages per CTA
+  constexpr size_t smem = static_cast<size_t>(S) * VPT * P * CTA * 16;
+  const unsigned resident = staged_resident<gelu_quant_staged_kernel<T, RT, VPT, S>>(smem);
+  const unsigned groups = row_grid(a.rows, RT);
+  launch_k(gelu_quant_staged_kernel<T, RT, VPT, S>, groups < resident ? groups : resident, CTA,
+           smem, s, a);
+}
+// The staged producer takes the wide rows (four chunks a thread: 8192 bf16 values and up),
+// where it measured 3 % faster; at 2048-wide rows the one-row-group-per-CTA kernel was as fast.
+template <typename T>
+static bool gelu_quant_staged(const ProdArgs &a, const RowCfg &cfg, cudaStream_t s) {
+  if (cfg.vpt < 4) return false;
+  switch (cfg.rt * 16 + cfg.vpt * static_cast<int>(sizeof(T)) / 2) {
+    case 32 * 16 + 1: launch_gelu_quant_staged<T, 32, 1>(a, s); return true;
+    case 128 * 16 + 1: launch_gelu_quant_staged<T, 128, 1>(a, s); return true;
+    case 256 * 16 + 1: launch_gelu_quant_staged<T, 256, 1>(a, s); return true;
+    case 32 * 16 + 2: launch_gelu_quant_staged<T, 32, sizeof(T) == 2 ? 2 : 1>(a, s); return true;
+    case 128 * 16 + 2: launch_gelu_quant_staged<T, 128, sizeof(T) == 2 ? 2 : 1>(a, s); return true;
+    case 256 * 16 + 2: launch_gelu_quant_staged<T, 256, sizeof(T) == 2 ? 2 : 1>(a, s); return true;
+    case 32 * 16 + 4: launch_gelu_quant_staged<T, 32, sizeof(T) == 2 ? 4 : 2>(a, s); return true;
+    case 128 * 16 + 4: launch_gelu_quant_staged<T, 128, sizeof(T) == 2 ? 4 : 2>(a, s); return true;
+    case 256 * 16 + 4: launch_gelu_quant_staged<T, 256, sizeof(T) == 2 ? 4 : 2>(a, s); return true;
+    default: return false;
+  }
+}
+
 extern "C" int rt_gelu_quantize(const void *x, int x_dtype, int64_t ldx, int64_t rows,
                                 int64_t cols, int8_t *q, int64_t ldq, float *row_scale,
                                 void *dq_out, int64_t ld_dq, void *stream) {
@@ -2771,7 +2892,11 @@ extern "C" int rt_gelu_quantize(const void *x, int x_dtype, int64_t ldx, int64_t
                    (reinterpret_cast<uintptr_t>(q) & 7) == 0 && ldq % 8 == 0 &&
                    (dq_out == nullptr || (aligned16(dq_out) && ld_dq % 8 == 0));
   const RowCfg cfg = vec ? row_cfg(cols / 8) : RowCfg{0, 0};
-  if (cfg.rt != 0) {
+  if (cfg.rt != 0 && staged_enabled() &&
+      (x_dtype == RT_F32 ? gelu_quant_staged<float>(a, cfg, s)
+                         : gelu_quant_staged<__nv_bfloat16>(a, cfg, s))) {
+    // launched
+  } else if (cfg.rt != 0) {
     if (x_dtype == RT_F32)
       RT_DISPATCH_ROW(cfg, gelu_quant_kernel, float, row_grid(rows, cfg.rt), a);
     else

@@ -207,3 +207,22 @@ def test_grouped_update_edges_with_gradient_multiplier(cuda_device):
         np.testing.assert_array_equal(_np(counts), ref["counts"])
         np.testing.assert_allclose(_np(rsum)[0], ref["row_rms"].astype(np.float64).sum(),
                                    rtol=1e-5)
+
+
+@pytest.mark.parametrize("rows,cols,dtype", [(4096, 8192, torch.bfloat16), (1000, 6144, torch.bfloat16),
+                                             (333, 512, torch.bfloat16), (300, 136, torch.float32)])
+def test_gelu_quantize_staged_equals_generic_kernel(cuda_device, rows, cols, dtype):
+    """The GELU -> int8 producer on 16-byte rows (staged for wide rows, one row group per CTA
+    otherwise) against the one-CTA-per-row kernel that a row stride off the 16-byte grid selects,
+    on the same values: int8 rows, scales and the bf16 dequantised copy bit for bit."""
+    from local_ai_training_b200.int8_fused import fused_gelu_quantize
+
+    torch.manual_seed(cols)
+    base = (torch.randn(rows, cols + 1, device=cuda_device) * 2).to(dtype)
+    ragged = base[:, :cols]  # row stride cols + 1
+    packed = ragged.contiguous()
+    q1, s1, d1 = fused_gelu_quantize(packed, dequant_out=True)
+    q2, s2, d2 = fused_gelu_quantize(ragged, dequant_out=True)
+    assert torch.equal(s1, s2)
+    assert torch.equal(q1, q2)
+    assert torch.equal(d1, d2)
