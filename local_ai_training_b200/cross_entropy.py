@@ -157,7 +157,9 @@ class _LMHeadCrossEntropyChunked(torch.autograd.Function):
     one reused logits block, and backward recomputes each block's logits (the int8 GEMM again),
     forms its bf16 logit gradient and runs that block's grad_input rows and its share of grad_W
     before the next.  Per row the loss, the logit gradient and grad_input are those of the
-    unchunked path; grad_W sums the blocks' products in fp32 before its one rounding."""
+    unchunked path; grad_W sums the blocks' products in fp32 before its one rounding.  The block
+    is bf16: the GEMM rounds every logit to bf16 in either output dtype (the reference's bf16
+    GEMM output), so half the bytes hold the same values."""
 
     @staticmethod
     def forward(ctx, inputs, targets, code, scale, gradient_sink, ignore_index, chunk_rows):
@@ -167,9 +169,7 @@ class _LMHeadCrossEntropyChunked(torch.autograd.Function):
         vocab = code.shape[0]
         q, s = quantize_rows(flat_inputs)
         scale_f = scale.float().contiguous()
-        out_dtype = (inputs.dtype if inputs.dtype in (torch.float32, torch.bfloat16)
-                     else torch.float32)
-        block = torch.empty((min(chunk_rows, rows), vocab), device=q.device, dtype=out_dtype)
+        block = torch.empty((min(chunk_rows, rows), vocab), device=q.device, dtype=torch.bfloat16)
         stats = torch.empty((3, rows), device=q.device, dtype=torch.float32)
         row_max, row_logsum, row_loss = stats[0], stats[1], stats[2]
         flat_targets = targets.reshape(-1).to(torch.int64).contiguous()
@@ -190,7 +190,6 @@ class _LMHeadCrossEntropyChunked(torch.autograd.Function):
         ctx.gradient_sink = gradient_sink
         ctx.ignore_index = ignore_index
         ctx.chunk_rows = chunk_rows
-        ctx.out_dtype = out_dtype
         ctx.fuse_backward_update = getattr(gradient_sink.__self__, "fuse_backward_update", True)
         return loss
 
@@ -206,7 +205,7 @@ class _LMHeadCrossEntropyChunked(torch.autograd.Function):
         effective = dequant_rows_bf16(code, scale_f)
         inputs_bf16 = flat_inputs.to(torch.bfloat16)
         grad_input = torch.empty((rows, width), device=q.device, dtype=torch.bfloat16)
-        block = torch.empty((min(chunk_rows, rows), vocab), device=q.device, dtype=ctx.out_dtype)
+        block = torch.empty((min(chunk_rows, rows), vocab), device=q.device, dtype=torch.bfloat16)
         sink = ctx.gradient_sink
         layer = getattr(sink, "__self__", None)
         dp = getattr(layer, "_dp", None)

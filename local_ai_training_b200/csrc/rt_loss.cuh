@@ -63,13 +63,26 @@ struct CeArgs {
   int64_t ldo;
 };
 
-// Register-resident rows: fp32, cols % 4 == 0, cols <= CE_THREADS·4·CE_VEC, 16-byte rows.
+// Four logits as floats: an fp32 float4, or four bf16 widened (exact).
+__device__ __forceinline__ float4 ce_load4(const float *x, int c) {
+  return __ldcs(reinterpret_cast<const float4 *>(x) + c);
+}
+__device__ __forceinline__ float4 ce_load4(const uint16_t *x, int c) {
+  const uint2 u = __ldcs(reinterpret_cast<const uint2 *>(x) + c);
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                     __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+}
+
+// Register-resident rows: cols % 4 == 0, cols <= CE_THREADS·4·CE_VEC, rows aligned to 4 logits
+// (16 bytes fp32, 8 bytes bf16).  Each thread takes the same groups of four in either dtype, so
+// bf16 logits give the bits that fp32 logits of the same values give.
+template <typename T>
 __global__ void __launch_bounds__(CE_THREADS) ce_fwd_vec_kernel(CeArgs a) {
   pdl_wait();
   pdl_trigger();
   __shared__ float sm[CE_THREADS / 32];
   const int64_t row = blockIdx.x;
-  const float *x = static_cast<const float *>(a.logits) + row * a.ld;
+  const T *x = static_cast<const T *>(a.logits) + row * a.ld;
   const int nq = static_cast<int>(a.cols / 4);
   float4 v[CE_VEC];
   float m = -INFINITY;
@@ -77,7 +90,7 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fwd_vec_kernel(CeArgs a) {
   for (int i = 0; i < CE_VEC; ++i) {
     const int c = threadIdx.x + i * CE_THREADS;
     if (c < nq) {
-      v[i] = __ldcs(reinterpret_cast<const float4 *>(x) + c);
+      v[i] = ce_load4(x, c);
       m = fmaxf(m, fmaxf(fmaxf(v[i].x, v[i].y), fmaxf(v[i].z, v[i].w)));
     }
   }
@@ -104,7 +117,7 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fwd_vec_kernel(CeArgs a) {
       if (t < 0 || t >= a.cols) {
         raise_status(RT_STATUS_CODE_RANGE);
       } else {
-        loss = -__fsub_rn(__fsub_rn(x[t], m), logsum);
+        loss = -__fsub_rn(__fsub_rn(ce_load(x + t), m), logsum);
       }
     }
     a.row_loss[row] = loss;
@@ -162,13 +175,25 @@ __global__ void __launch_bounds__(CE_THREADS) ce_bwd_kernel(CeArgs a) {
   const float w = __fdiv_rn(__ldg(a.grad_loss), __ldg(a.count));
   const float m = a.row_max[row], logsum = a.row_logsum[row];
   const auto a16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  const bool vec = sizeof(T) == 4 && a.cols % 8 == 0 && (a.ld % 4) == 0 && (a.ldo % 8) == 0 &&
-                   a16(x) && a16(o) && (e == nullptr || ((a.ld_extra % 4) == 0 && a16(e)));
+  const bool vec = a.cols % 8 == 0 && (a.ld % 8) == 0 && (a.ldo % 8) == 0 && a16(x) && a16(o) &&
+                   (e == nullptr || ((a.ld_extra % 4) == 0 && a16(e)));
   if (vec) {
     for (int64_t c = threadIdx.x; c < a.cols / 8; c += CE_THREADS) {
-      const float4 v0 = __ldcs(reinterpret_cast<const float4 *>(x) + 2 * c);
-      const float4 v1 = __ldcs(reinterpret_cast<const float4 *>(x) + 2 * c + 1);
-      const float xs[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      float xs[8];
+      if constexpr (sizeof(T) == 4) {
+        const float4 v0 = __ldcs(reinterpret_cast<const float4 *>(x) + 2 * c);
+        const float4 v1 = __ldcs(reinterpret_cast<const float4 *>(x) + 2 * c + 1);
+        xs[0] = v0.x, xs[1] = v0.y, xs[2] = v0.z, xs[3] = v0.w;
+        xs[4] = v1.x, xs[5] = v1.y, xs[6] = v1.z, xs[7] = v1.w;
+      } else {
+        const uint4 u = __ldcs(reinterpret_cast<const uint4 *>(x) + c);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          xs[2 * j] = __uint_as_float(w[j] << 16);
+          xs[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+        }
+      }
       float g[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -219,11 +244,14 @@ extern "C" int rt_cross_entropy_fwd(const void *logits, int dtype, int64_t ld, i
   a.ignore_index = ignore_index, a.row_max = row_max, a.row_logsum = row_logsum;
   a.row_loss = row_loss;
   cudaStream_t s = as_stream(stream);
-  const bool vec = dtype == RT_F32 && cols % 4 == 0 && ld % 4 == 0 && aligned16(logits) &&
+  const bool vec = cols % 4 == 0 && ld % 4 == 0 &&
+                   (reinterpret_cast<uintptr_t>(logits) & (dtype == RT_F32 ? 15 : 7)) == 0 &&
                    cols <= static_cast<int64_t>(CE_THREADS) * 4 * CE_VEC;
   const unsigned grid = static_cast<unsigned>(rows);
-  if (vec)
-    launch_k(ce_fwd_vec_kernel, grid, CE_THREADS, 0, s, a);
+  if (vec && dtype == RT_F32)
+    launch_k(ce_fwd_vec_kernel<float>, grid, CE_THREADS, 0, s, a);
+  else if (vec)
+    launch_k(ce_fwd_vec_kernel<uint16_t>, grid, CE_THREADS, 0, s, a);
   else if (dtype == RT_F32)
     launch_k(ce_fwd_generic_kernel<float>, grid, CE_THREADS, 0, s, a);
   else
