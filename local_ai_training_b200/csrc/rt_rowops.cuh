@@ -19,6 +19,7 @@
 #pragma once
 
 #include <cfloat>
+#include <mutex>
 
 #include "rt_common.cuh"
 
@@ -740,22 +741,27 @@ static inline bool sr_outputs_vec(const QuantArgs &a) {
 }
 
 // Resident CTAs per SM of one staged-kernel instance (its shared stages and registers), asked of
-// the runtime once per instance (the cache is per template instance: one per kernel).
+// the runtime once per instance and device (the shared-memory attribute is set on each device
+// the kernel runs on; the cache is per template instance: one per kernel).
 template <auto kernel>
 static unsigned staged_resident(size_t smem) {
-  static int per_sm = 0;
-  if (per_sm == 0) {
+  static std::mutex mu;
+  static int per_sm[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (per_sm[dev] == 0) {
     // static and dynamic shared memory together may pass the default 48 KB
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          static_cast<int>(smem));
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, CTA, smem) != cudaSuccess || n < 1)
       n = 1;
-    per_sm = n;
+    per_sm[dev] = n;
   }
   int sms = 0;
   if (rt_sm_count(&sms) != RT_OK || sms <= 0) sms = 148;
-  return static_cast<unsigned>(sms) * static_cast<unsigned>(per_sm);
+  return static_cast<unsigned>(sms) * static_cast<unsigned>(per_sm[dev]);
 }
 template <typename T, int RT, int VPT>
 static void launch_quant_sr_staged(const QuantArgs &a, cudaStream_t s) {
